@@ -1,0 +1,77 @@
+"""ctypes binding of libnd_denoise.so (include/nd_denoise.h).
+
+This is the Python stand-in for the C# P/Invoke layer: the same C entry
+points a `[LibraryImport("nd_denoise")]` class would bind. Loading fails
+loudly when the library is missing; there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libnd_denoise.so"
+
+ND_OK = 0
+ND_ERR_INVALID = 1
+ND_ERR_OOM = 2
+ND_ERR_CUDA = 3
+ND_ERR_TIMEOUT = 4
+ND_ERR_STATE = 5
+ND_ERR_UNSUPPORTED = 6
+ND_ERR_MISSING_WEIGHT = 7
+
+ND_F32, ND_F16, ND_BF16, ND_I8, ND_I32 = 0, 1, 2, 3, 4
+
+ND_EPI_STORE = 0
+ND_EPI_GELU_TANH = 1
+ND_EPI_GELU_ERF = 2
+ND_EPI_SILU = 3
+ND_EPI_RESIDUAL_GATE = 4
+ND_EPI_STORE_F32 = 5
+ND_EPI_QK_NORM_ROPE = 6
+ND_EPI_RESIDUAL_ADD = 7
+
+
+class NdError(RuntimeError):
+    """A nonzero status from the library, with nd_last_error()'s message."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+
+
+class LinearArgs(C.Structure):
+    _fields_ = [
+        ("dtype", C.c_int), ("epilogue", C.c_int),
+        ("rows", C.c_int64), ("in_features", C.c_int64), ("out_features", C.c_int64),
+        ("x", C.c_void_p), ("ldx", C.c_int64),
+        ("weight", C.c_void_p), ("bias", C.c_void_p), ("group_split", C.c_int64),
+        ("y", C.c_void_p), ("ldy", C.c_int64),
+        ("residual", C.c_void_p), ("ldr", C.c_int64),
+        ("gate", C.c_void_p), ("qk_norm", C.c_void_p),
+        ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
+        ("qk_cols", C.c_int64), ("eps", C.c_float),
+    ]
+
+
+_lib: C.CDLL | None = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing: build it with `python -m naivediffusion_b200.build`")
+        L = C.CDLL(str(LIB_PATH))
+        L.nd_last_error.restype = C.c_char_p
+        L.nd_version.restype = C.c_char_p
+        L.nd_op_linear.argtypes = [C.POINTER(LinearArgs), C.c_void_p]
+        L.nd_op_sync.argtypes = [C.c_void_p]
+        _lib = L
+    return _lib
+
+
+def check(code: int) -> None:
+    if code != ND_OK:
+        raise NdError(code, lib().nd_last_error().decode(errors="replace"))

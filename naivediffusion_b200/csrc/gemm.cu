@@ -1,0 +1,114 @@
+// Host side of the tcgen05 GEMM: argument checks, tensor maps, tile-width
+// choice and launch. The kernel itself is in gemm_sm100.cuh.
+#include <algorithm>
+#include <climits>
+#include <string>
+
+#include "gemm_sm100.cuh"
+#include "nd_internal.h"
+#include "nd_runtime.h"
+
+namespace nd {
+
+namespace {
+
+template <int BN, int STAGES>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
+                cudaStream_t stream) {
+  using L = GemmSmem<BN, STAGES>;
+  static bool configured[64] = {};
+  int dev = 0;
+  ND_CUDA(cudaGetDevice(&dev));
+  if (!configured[dev & 63]) {
+    ND_CUDA(cudaFuncSetAttribute(gemm_sm100_kernel<BN, STAGES>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, L::kLaunchBytes));
+    configured[dev & 63] = true;
+  }
+  const int num_m = (g.M + 127) / 128;
+  const int num_n = (g.N + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int grid = std::min(tiles, sm_count());
+  gemm_sm100_kernel<BN, STAGES><<<grid, 192, L::kLaunchBytes, stream>>>(ta, tb, g);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+}  // namespace
+
+int linear(const nd_linear_args& a, cudaStream_t stream) {
+  if (a.dtype != ND_BF16 && a.dtype != ND_F16) return fail(ND_ERR_INVALID, "linear: dtype must be bf16 or f16");
+  if (a.rows <= 0 || a.in_features <= 0 || a.out_features <= 0)
+    return fail(ND_ERR_INVALID, "linear: empty shape");
+  if (a.rows > INT_MAX || a.in_features > INT_MAX || a.out_features > INT_MAX / 2)
+    return fail(ND_ERR_INVALID, "linear: shape too large");
+  if (a.in_features % 8 != 0) return fail(ND_ERR_INVALID, "linear: in_features must be a multiple of 8");
+  if (a.ldx < a.in_features || a.ldx % 8 != 0) return fail(ND_ERR_INVALID, "linear: ldx must be >= in_features and a multiple of 8");
+  if (!a.x || !a.weight) return fail(ND_ERR_INVALID, "linear: null operand");
+  const bool split = a.group_split < a.rows;
+  if (split && (a.group_split % 128 != 0 || a.group_split <= 0))
+    return fail(ND_ERR_INVALID, "linear: group_split must be a positive multiple of 128");
+  const int epi = a.epilogue;
+  const bool resid = epi == ND_EPI_RESIDUAL_GATE || epi == ND_EPI_RESIDUAL_ADD || epi == ND_EPI_STORE_F32;
+  if (epi < 0 || epi > ND_EPI_RESIDUAL_ADD) return fail(ND_ERR_INVALID, "linear: unknown epilogue");
+  if (resid && (!a.residual || a.ldr < a.out_features || a.ldr % 4 != 0))
+    return fail(ND_ERR_INVALID, "linear: residual epilogue needs residual with ldr >= out_features, ldr % 4 == 0");
+  if (!resid && (!a.y || a.ldy < a.out_features || a.ldy % 8 != 0))
+    return fail(ND_ERR_INVALID, "linear: output needs y with ldy >= out_features, ldy % 8 == 0");
+  if (epi == ND_EPI_RESIDUAL_GATE && !a.gate) return fail(ND_ERR_INVALID, "linear: gate missing");
+  if (epi == ND_EPI_QK_NORM_ROPE) {
+    if (!a.qk_norm || !a.rope_cos || !a.rope_sin)
+      return fail(ND_ERR_INVALID, "linear: qk epilogue needs qk_norm, rope_cos, rope_sin");
+    if (a.qk_cols % 256 != 0 || a.qk_cols > a.out_features)
+      return fail(ND_ERR_INVALID, "linear: qk_cols must be a multiple of 256 and <= out_features");
+    if (a.out_features % 128 != 0) return fail(ND_ERR_INVALID, "linear: qk epilogue needs out_features % 128 == 0");
+  }
+  if (a.bias && (reinterpret_cast<uintptr_t>(a.bias) & 15u))
+    return fail(ND_ERR_INVALID, "linear: bias must be 16-byte aligned");
+  if (a.out_features % 4 != 0 && (a.bias || a.gate))
+    return fail(ND_ERR_INVALID, "linear: bias/gate need out_features % 4 == 0");
+
+  const int groups = split ? 2 : 1;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, a.x, 2, a.rows, a.in_features, a.ldx, 128, 64, true);
+  if (rc) return rc;
+
+  GemmArgs g{};
+  g.M = static_cast<int>(a.rows);
+  g.N = static_cast<int>(a.out_features);
+  g.K = static_cast<int>(a.in_features);
+  g.group_split = split ? static_cast<int>(a.group_split) : INT_MAX;
+  g.epi = epi;
+  g.out_f16 = a.dtype == ND_F16;
+  g.out = a.y;
+  g.ldo = a.ldy;
+  g.resid = a.residual;
+  g.ldr = a.ldr;
+  g.bias = a.bias;
+  g.bias_stride = static_cast<int>(a.out_features);
+  g.gate = a.gate;
+  g.gate_stride = static_cast<int>(a.out_features);
+  g.qk_norm = a.qk_norm;
+  g.rope_cos = a.rope_cos;
+  g.rope_sin = a.rope_sin;
+  g.qk_cols = static_cast<int>(a.qk_cols);
+  g.head_dim = 128;
+  g.norm_eps = a.eps;
+  g.status = device_status();
+  if (!g.status) return fail(ND_ERR_CUDA, "linear: no device status word");
+
+  // Wide tiles when the output is wide enough to fill the machine with them.
+  const int64_t tiles256 = ((a.rows + 127) / 128) * ((a.out_features + 255) / 256);
+  const bool wide = epi == ND_EPI_QK_NORM_ROPE || (a.out_features >= 256 && tiles256 >= sm_count());
+  if (wide) {
+    g.idesc = make_idesc_f16(128, 256, a.dtype == ND_BF16);
+    rc = make_tmap_2d(&tb, a.weight, 2, groups * a.out_features, a.in_features, a.in_features, 256, 64, true);
+    if (rc) return rc;
+    return launch_gemm<256, 4>(ta, tb, g, stream);
+  }
+  g.idesc = make_idesc_f16(128, 128, a.dtype == ND_BF16);
+  rc = make_tmap_2d(&tb, a.weight, 2, groups * a.out_features, a.in_features, a.in_features, 128, 64, true);
+  if (rc) return rc;
+  return launch_gemm<128, 6>(ta, tb, g, stream);
+}
+
+}  // namespace nd

@@ -1,0 +1,429 @@
+// Persistent tcgen05 + TMA GEMM for sm_100a:  C[M, N] = A[M, K] . W[N, K]^T
+//
+// This replaces the reference's `Layers.Linear` (Graph/Layers.cs:131-160),
+// which lowers to DirectML's GEMM with transB (Dml/DmlOps.cs:231-262): the
+// weight is stored [out, in] as nn.Linear keeps it, so both operands are
+// K-major and land in shared memory as 128-byte-swizzled tiles straight from
+// TMA.
+//
+// Work split (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: A tile [128 x 64] + W tile [BN x 64] per stage
+//   warp 1      MMA issuer: tcgen05.mma 128 x BN x 16, accumulating in TMEM;
+//               also allocates the 2 x BN TMEM columns (double buffer)
+//   warps 2..5  epilogue: tcgen05.ld rows out of TMEM, apply the fused
+//               epilogue and write to global memory, while the MMA warp
+//               already fills the other accumulator buffer.
+//
+// Row groups: a dual-stream block (image rows then text rows) runs both
+// streams' projections in one launch. Rows >= group_split take weight rows
+// [N, 2N) and the second group's epilogue vectors. The split is a multiple of
+// the 128-row tile.
+#pragma once
+
+#include "nd_common.cuh"
+
+namespace nd {
+
+enum GemmEpilogue : int {
+  kEpiStore = 0,          // out = acc + bias                       (bf16/f16)
+  kEpiGeluTanh = 1,       // out = gelu_tanh(acc + bias)
+  kEpiGeluErf = 2,        // out = gelu(acc + bias), exact erf form
+  kEpiSilu = 3,           // out = silu(acc + bias)
+  kEpiResidualGate = 4,   // resid(f32) += gate[c] * (acc + bias)
+  kEpiStoreF32 = 5,       // outf(f32) = acc + bias
+  kEpiQkNormRope = 6,     // columns < qk_cols: per-head RMSNorm * w, then RoPE
+  kEpiResidualAdd = 7,    // resid(f32) += acc + bias
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int group_split;  // first row of the second weight group (>= M: one group)
+  int epi;
+  int out_f16;      // 0: bf16 output, 1: fp16 output
+  void* out;        // bf16/f16 output, leading dimension ldo (elements)
+  long long ldo;
+  float* resid;     // fp32 residual / fp32 output, leading dimension ldr
+  long long ldr;
+  const float* bias;  // [groups][bias_stride] or null
+  int bias_stride;
+  const float* gate;  // [groups][gate_stride] (kEpiResidualGate)
+  int gate_stride;
+  const float* qk_norm;   // [groups][2][head_dim]: q weight then k weight
+  const float* rope_cos;  // [M][head_dim / 2]
+  const float* rope_sin;
+  int qk_cols;            // leading columns that are q then k (2 * width)
+  int head_dim;           // 128
+  float norm_eps;
+  uint32_t idesc;
+  unsigned* status;
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kBM = 128;
+  static constexpr int kBK = 64;
+  static constexpr int kABytes = kBM * kBK * 2;  // 16 KB
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTiles = STAGES * kStageBytes;
+  static constexpr int kBarOffset = kTiles;
+  // full[S], empty[S], acc_full[2], acc_empty[2], drain
+  static constexpr int kNumBars = 2 * STAGES + 5;
+  static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
+  static constexpr int kTotal = kMiscOffset + 16;
+  static constexpr int kLaunchBytes = kTotal + 1024;  // + alignment slack
+};
+
+__device__ __forceinline__ void store_chunk32(void* out, long long ldo, int row, int col, int N,
+                                              const float (&v)[32], int out_f16) {
+  uint32_t p[16];
+  if (out_f16) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p[i] = pack_f16(v[2 * i], v[2 * i + 1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+  }
+  uint16_t* base = reinterpret_cast<uint16_t*>(out) + static_cast<long long>(row) * ldo + col;
+  if (col + 32 <= N && ((reinterpret_cast<uintptr_t>(base) & 15u) == 0)) {
+    uint4* dst = reinterpret_cast<uint4*>(base);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (col + i < N) base[i] = static_cast<uint16_t>((p[i >> 1] >> ((i & 1) * 16)) & 0xFFFFu);
+    }
+  }
+}
+
+__device__ __forceinline__ void load_vec32(const float* src, int col, int N, float (&v)[32]) {
+  if (src == nullptr) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    return;
+  }
+  if (col + 32 <= N) {
+    const float4* s = reinterpret_cast<const float4*>(src + col);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float4 t = __ldg(s + i);
+      v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = (col + i < N) ? __ldg(src + col + i) : 0.f;
+  }
+}
+
+// One 32-column chunk of a plain epilogue (everything but kEpiQkNormRope).
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int group, int row, int col,
+                                               const uint32_t (&r)[32]) {
+  float v[32];
+  float b[32];
+  load_vec32(a.bias ? a.bias + group * a.bias_stride : nullptr, col, a.N, b);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + b[i];
+
+  switch (a.epi) {
+    case kEpiGeluTanh:
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+      break;
+    case kEpiGeluErf:
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+      break;
+    case kEpiSilu:
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = silu(v[i]);
+      break;
+    default:
+      break;
+  }
+
+  if (a.epi == kEpiResidualGate || a.epi == kEpiResidualAdd || a.epi == kEpiStoreF32) {
+    float g[32];
+    if (a.epi == kEpiResidualGate) {
+      load_vec32(a.gate + group * a.gate_stride, col, a.N, g);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) g[i] = 1.f;
+    }
+    float* dst = a.resid + static_cast<long long>(row) * a.ldr + col;
+    const bool keep = a.epi != kEpiStoreF32;
+    if (col + 32 <= a.N) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float4 t = keep ? d4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        t.x += g[4 * i] * v[4 * i];
+        t.y += g[4 * i + 1] * v[4 * i + 1];
+        t.z += g[4 * i + 2] * v[4 * i + 2];
+        t.w += g[4 * i + 3] * v[4 * i + 3];
+        d4[i] = t;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (col + i < a.N) dst[i] = (keep ? dst[i] : 0.f) + g[i] * v[i];
+      }
+    }
+    return;
+  }
+  store_chunk32(a.out, a.ldo, row, col, a.N, v, a.out_f16);
+}
+
+// The Q/K projection epilogue for one 128-wide head: RMSNorm over the head's
+// features with the stored per-feature weight, then the rotate-half RoPE with
+// this row's angle tables -- Transformer.HeadNorm + Transformer.Rotate
+// (Graph/Transformer.cs:37-64) fused where the accumulator already sits.
+__device__ __forceinline__ void epilogue_head_norm_rope(const GemmArgs& a, int group, int row,
+                                                        int col0, uint32_t tbase, bool row_ok) {
+  const float* bias = a.bias ? a.bias + group * a.bias_stride + col0 : nullptr;
+  const int which = col0 >= (a.qk_cols >> 1) ? 1 : 0;
+  const float* w = a.qk_norm + (group * 2 + which) * 128;
+  uint32_t r[32];
+  float sumsq = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    tmem_ld32(tbase + c * 32, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float x = __uint_as_float(r[i]) + (bias ? __ldg(bias + c * 32 + i) : 0.f);
+      sumsq += x * x;
+    }
+  }
+  const float scale = rsqrtf(sumsq * (1.0f / 128.0f) + a.norm_eps);
+  const float* cs = a.rope_cos + static_cast<long long>(row_ok ? row : 0) * 64;
+  const float* sn = a.rope_sin + static_cast<long long>(row_ok ? row : 0) * 64;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    uint32_t lo[32], hi[32];
+    tmem_ld32(tbase + c * 32, lo);
+    tmem_ld32(tbase + 64 + c * 32, hi);
+    tmem_ld_wait();
+    float olo[32], ohi[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int f = c * 32 + i;
+      float l = (__uint_as_float(lo[i]) + (bias ? __ldg(bias + f) : 0.f)) * scale * __ldg(w + f);
+      float h = (__uint_as_float(hi[i]) + (bias ? __ldg(bias + 64 + f) : 0.f)) * scale *
+                __ldg(w + 64 + f);
+      const float co = row_ok ? __ldg(cs + f) : 0.f;
+      const float si = row_ok ? __ldg(sn + f) : 0.f;
+      olo[i] = l * co - h * si;
+      ohi[i] = h * co + l * si;
+    }
+    if (row_ok) {
+      store_chunk32(a.out, a.ldo, row, col0 + c * 32, a.N, olo, a.out_f16);
+      store_chunk32(a.out, a.ldo, row, col0 + 64 + c * 32, a.N, ohi, a.out_f16);
+    }
+  }
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + L::kBarOffset;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
+  auto accf_bar = [&](int s) { return bars + 8u * (2 * STAGES + s); };
+  auto acce_bar = [&](int s) { return bars + 8u * (2 * STAGES + 2 + s); };
+  const uint32_t drain_bar = bars + 8u * (2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int num_m = (args.M + 127) / 128;
+  const int num_n = (args.N + BN - 1) / BN;
+  const int total = num_m * num_n;
+  const int num_kb = (args.K + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(accf_bar(s), 1);
+      mbar_init(acce_bar(s), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const int m0 = (t % num_m) * 128;
+        const int n0 = (t / num_m) * BN;
+        const int group = m0 >= args.group_split ? 1 : 0;
+        const int brow = group * args.N + n0;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.status,
+                         kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t a_dst = sbase + stage * L::kStageBytes;
+          const uint32_t b_dst = a_dst + L::kABytes;
+          mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
+          tma_load_2d(a_dst, &tmA, full_bar(stage), kb * 64, m0);
+          tma_load_2d(b_dst, &tmB, full_bar(stage), kb * 64, brow);
+          issued |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Aborted: let every load this thread started land before the CTA
+        // (and its shared memory) goes away.
+        volatile int never = 0;
+        for (int s = 0; s < STAGES; ++s) {
+          if (issued & (1u << s)) {
+            mbar_wait(full_bar(s), (issued_parity >> s) & 1u, &never, nullptr, 0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u, abort_flag, args.status, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, args.status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = sbase + stage * L::kStageBytes;
+          const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = make_sdesc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = make_sdesc_sw128(b_addr + k * 32, 16, 1024);
+            umma_ss(d_tmem, ad, bd, args.idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(empty_bar(stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(accf_bar(acc));
+      }
+      // Wait until every MMA this thread issued has retired before TMEM is
+      // released (bounded, and independent of the abort flag).
+      umma_commit(drain_bar);
+      volatile int never = 0;
+      mbar_wait(drain_bar, 0, &never, args.status, kStatusTimeoutDrain);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp & 3;  // TMEM lane quarter this warp may read
+    const int row_in_tile = ew * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(accf_bar(acc), acc_phase, abort_flag, args.status, kStatusTimeoutEpilogue)) {
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      const int m0 = (t % num_m) * 128;
+      const int n0 = (t / num_m) * BN;
+      const int group = m0 >= args.group_split ? 1 : 0;
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < args.M;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
+
+      if (args.epi == kEpiQkNormRope) {
+#pragma unroll 1
+        for (int h = 0; h < BN / 128; ++h) {
+          const int col0 = n0 + h * 128;
+          if (col0 >= args.N) break;
+          if (col0 < args.qk_cols) {
+            epilogue_head_norm_rope(args, group, row, col0, tbase + h * 128, row_ok);
+          } else {
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+              tmem_ld32(tbase + h * 128 + c * 32, r);
+              tmem_ld_wait();
+              if (row_ok) {
+                GemmArgs plain = args;
+                plain.epi = kEpiStore;
+                epilogue_chunk(plain, group, row, col0 + c * 32, r);
+              }
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          const int col = n0 + c * 32;
+          if (col >= args.N) break;
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_ld_wait();
+          if (row_ok) epilogue_chunk(args, group, row, col, r);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce_bar(acc));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, 2 * BN);
+}
+
+}  // namespace nd

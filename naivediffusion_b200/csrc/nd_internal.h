@@ -1,0 +1,42 @@
+// Host-side internals shared by the translation units of libnd_denoise.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/nd_denoise.h"
+
+namespace nd {
+
+// ----------------------------------------------------------------- errors
+
+// Record a message for nd_last_error() and return `code`.
+int fail(int code, const std::string& msg);
+// Map a CUDA runtime error to a status (ND_ERR_OOM / ND_ERR_CUDA), recording it.
+int cuda_fail(cudaError_t e, const char* what);
+// Current device's SM count (cached per device).
+int sm_count();
+
+#define ND_CUDA(call)                                   \
+  do {                                                  \
+    cudaError_t e_ = (call);                            \
+    if (e_ != cudaSuccess) return ::nd::cuda_fail(e_, #call); \
+  } while (0)
+
+// ----------------------------------------------------------------- TMA
+
+// A 2-D tensor map over a row-major [rows, cols] matrix of `elem_bytes`
+// elements with leading dimension `ld` (elements), box [box_rows, box_cols],
+// 128-byte swizzle (box_cols * elem_bytes must be 128) or none.
+int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, int64_t rows, int64_t cols,
+                 int64_t ld, int box_rows, int box_cols, bool swizzle128);
+
+// ----------------------------------------------------------------- kernels
+
+struct LinearPlan;
+int linear(const nd_linear_args& a, cudaStream_t stream);
+
+}  // namespace nd

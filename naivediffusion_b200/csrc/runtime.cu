@@ -1,0 +1,131 @@
+// Errors, per-device state, tensor-map encoding and the op-level C ABI.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "nd_internal.h"
+#include "nd_runtime.h"
+
+namespace nd {
+
+namespace {
+thread_local std::string g_last_error;
+std::mutex g_dev_mutex;
+unsigned* g_status[64] = {};
+int g_sms[64] = {};
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  return fn;
+}
+}  // namespace
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  std::string msg = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+  return fail(e == cudaErrorMemoryAllocation ? ND_ERR_OOM : ND_ERR_CUDA, msg);
+}
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  if (!g_sms[dev & 63]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_sms[dev & 63] = n > 0 ? n : 148;
+  }
+  return g_sms[dev & 63];
+}
+
+unsigned* device_status() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  if (!g_status[dev & 63]) {
+    unsigned* p = nullptr;
+    if (cudaMalloc(&p, 64) != cudaSuccess) return nullptr;
+    if (cudaMemset(p, 0, 64) != cudaSuccess) return nullptr;
+    g_status[dev & 63] = p;
+  }
+  return g_status[dev & 63];
+}
+
+int check_device_status(cudaStream_t stream) {
+  ND_CUDA(cudaStreamSynchronize(stream));
+  unsigned* st = device_status();
+  if (!st) return fail(ND_ERR_CUDA, "no device status word");
+  unsigned host = 0;
+  ND_CUDA(cudaMemcpy(&host, st, sizeof(host), cudaMemcpyDeviceToHost));
+  if (host != 0) {
+    ND_CUDA(cudaMemset(st, 0, sizeof(unsigned)));
+    char buf[128];
+    snprintf(buf, sizeof(buf), "a kernel's bounded wait ran out (status 0x%x)", host);
+    return fail(ND_ERR_TIMEOUT, buf);
+  }
+  return ND_OK;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, int64_t rows, int64_t cols,
+                 int64_t ld, int box_rows, int box_cols, bool swizzle128) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(ND_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (reinterpret_cast<uintptr_t>(base) & 15u) return fail(ND_ERR_INVALID, "TMA base must be 16-byte aligned");
+  if ((ld * elem_bytes) % 16 != 0) return fail(ND_ERR_INVALID, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
+                           : elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_UINT32
+                                             : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * elem_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[192];
+    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld ld=%lld box=%dx%d",
+             static_cast<int>(r), static_cast<long long>(rows), static_cast<long long>(cols),
+             static_cast<long long>(ld), box_rows, box_cols);
+    return fail(ND_ERR_INVALID, buf);
+  }
+  return ND_OK;
+}
+
+}  // namespace nd
+
+extern "C" {
+
+const char* nd_last_error(void) { return nd::g_last_error.c_str(); }
+
+const char* nd_version(void) { return "nd_denoise 0.1 (sm_100a)"; }
+
+int nd_op_linear(const nd_linear_args* args, void* stream) {
+  if (!args) return nd::fail(ND_ERR_INVALID, "nd_op_linear: null args");
+  return nd::linear(*args, static_cast<cudaStream_t>(stream));
+}
+
+int nd_op_sync(void* stream) { return nd::check_device_status(static_cast<cudaStream_t>(stream)); }
+
+}  // extern "C"
