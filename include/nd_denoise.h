@@ -98,6 +98,83 @@ typedef struct nd_linear_args {
  * the next synchronizing call. */
 ND_API int nd_op_linear(const nd_linear_args* args, void* stream);
 
+/* ------------------------------------------------------------ attention op
+ * O = softmax(Q K^T * scale [+ mask]) V over packed heads, head_dim 128.
+ * Replaces Layers.Attend (src/NaiveDiffusion/Graph/Layers.cs:260-279) ->
+ * DmlOps.MultiheadAttention (src/NaiveDiffusion/Dml/DmlOps.cs:480-524).
+ * Masks: key_limit (keys >= key_limit left out: the KeySequenceLength mask)
+ * and causal (row i sees keys 0..i). Batch items are stacked row blocks:
+ * item b's queries are rows [b*q_rows, (b+1)*q_rows) of q. */
+typedef struct nd_attention_args {
+  int dtype;            /* ND_BF16 or ND_F16 */
+  int heads, head_dim, batch;
+  int64_t q_rows, kv_rows;
+  int64_t key_limit;    /* <= 0: all kv_rows keys */
+  int causal;
+  const void* q; int64_t ldq;  /* head h at columns [h*head_dim, (h+1)*head_dim) */
+  const void* k; int64_t ldk;
+  const void* v; int64_t ldv;
+  void* out; int64_t ldo;
+  float scale;          /* <= 0: 1/sqrt(head_dim) */
+} nd_attention_args;
+
+ND_API int nd_op_attention(const nd_attention_args* args, void* stream);
+
+/* ------------------------------------------------------------ norms
+ * adaLN modulation: y = LayerNorm(x, no affine) * (1 + scale) + shift
+ * (Transformer.Modulate, src/NaiveDiffusion/Graph/Transformer.cs:72-80).
+ * x fp32; scale/shift fp32 vectors [groups][vec_stride]; rows >= group_split
+ * use the second vectors. shift may be NULL. */
+typedef struct nd_modulate_args {
+  const float* x; int64_t ldx;
+  void* y; int64_t ldy; int out_dtype;   /* ND_BF16, ND_F16 or ND_F32 */
+  int64_t rows, width;
+  const float* shift; const float* scale;
+  int64_t vec_stride;   /* 0: width */
+  int64_t group_split;  /* >= rows: one group */
+  float eps;
+} nd_modulate_args;
+
+ND_API int nd_op_modulate(const nd_modulate_args* args, void* stream);
+
+/* RMSNorm over rows: y = x * rsqrt(mean(x^2) + eps) * (weight + plus_one)
+ * (Layers.RmsNorm, src/NaiveDiffusion/Graph/Layers.cs:209-221; CpuMath.RmsNorm).
+ * weight may be NULL (then the factor is 1). */
+typedef struct nd_rmsnorm_args {
+  const void* x; int64_t ldx; int in_dtype;
+  void* y; int64_t ldy; int out_dtype;
+  int64_t rows, width;
+  const float* weight;
+  int plus_one;         /* zero-centred stored weight (QwenImageDit txt_in norm) */
+  float eps;
+} nd_rmsnorm_args;
+
+ND_API int nd_op_rmsnorm(const nd_rmsnorm_args* args, void* stream);
+
+/* ------------------------------------------------------------ GEMV
+ * y[b, n] = act(sum_k W[n, k] * pre(x[b, k]) + bias[n]), W bf16/f16 [n, k],
+ * x and y fp32, batch 1..4. pre_silu applies SiLU to x first; act 0 none,
+ * 1 SiLU, 2 tanh. The modulation vectors (Layers.Linear over 1-2 rows). */
+typedef struct nd_gemv_args {
+  const void* w; int w_dtype;
+  int64_t n, k;
+  const float* x; int batch; int pre_silu;
+  const float* bias; int act;
+  float* y;
+} nd_gemv_args;
+
+ND_API int nd_op_gemv(const nd_gemv_args* args, void* stream);
+
+/* ------------------------------------------------------------ layout
+ * latent [B, C, H, W] fp32 <-> tokens [B * (H/p) * (W/p), C*p*p] (row stride
+ * ldt); feature c*p*p + m*p + n of patch (i, j) is channel c at (p*i+m, p*j+n)
+ * (AnimaDit.Patchify, src/NaiveDiffusion/Models/Anima/AnimaDit.cs:193-247). */
+ND_API int nd_op_patchify(const float* latent, void* tokens, int out_dtype, int batch,
+                          int channels, int height, int width, int patch, int64_t ldt,
+                          void* stream);
+ND_API int nd_op_unpatchify(const float* tokens, int64_t ldt, float* latent, int batch,
+                            int channels, int height, int width, int patch, void* stream);
+
 /* Synchronize `stream` and report any kernel's timed-out wait (ND_ERR_TIMEOUT)
  * or CUDA fault (ND_ERR_CUDA) since the last check on this device. */
 ND_API int nd_op_sync(void* stream);

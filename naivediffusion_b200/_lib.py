@@ -54,6 +54,44 @@ class LinearArgs(C.Structure):
     ]
 
 
+class AttentionArgs(C.Structure):
+    _fields_ = [
+        ("dtype", C.c_int), ("heads", C.c_int), ("head_dim", C.c_int), ("batch", C.c_int),
+        ("q_rows", C.c_int64), ("kv_rows", C.c_int64), ("key_limit", C.c_int64),
+        ("causal", C.c_int),
+        ("q", C.c_void_p), ("ldq", C.c_int64), ("k", C.c_void_p), ("ldk", C.c_int64),
+        ("v", C.c_void_p), ("ldv", C.c_int64), ("out", C.c_void_p), ("ldo", C.c_int64),
+        ("scale", C.c_float),
+    ]
+
+
+class ModulateArgs(C.Structure):
+    _fields_ = [
+        ("x", C.c_void_p), ("ldx", C.c_int64),
+        ("y", C.c_void_p), ("ldy", C.c_int64), ("out_dtype", C.c_int),
+        ("rows", C.c_int64), ("width", C.c_int64),
+        ("shift", C.c_void_p), ("scale", C.c_void_p),
+        ("vec_stride", C.c_int64), ("group_split", C.c_int64), ("eps", C.c_float),
+    ]
+
+
+class RmsNormArgs(C.Structure):
+    _fields_ = [
+        ("x", C.c_void_p), ("ldx", C.c_int64), ("in_dtype", C.c_int),
+        ("y", C.c_void_p), ("ldy", C.c_int64), ("out_dtype", C.c_int),
+        ("rows", C.c_int64), ("width", C.c_int64),
+        ("weight", C.c_void_p), ("plus_one", C.c_int), ("eps", C.c_float),
+    ]
+
+
+class GemvArgs(C.Structure):
+    _fields_ = [
+        ("w", C.c_void_p), ("w_dtype", C.c_int), ("n", C.c_int64), ("k", C.c_int64),
+        ("x", C.c_void_p), ("batch", C.c_int), ("pre_silu", C.c_int),
+        ("bias", C.c_void_p), ("act", C.c_int), ("y", C.c_void_p),
+    ]
+
+
 _lib: C.CDLL | None = None
 
 
@@ -68,6 +106,14 @@ def lib() -> C.CDLL:
         L.nd_version.restype = C.c_char_p
         L.nd_op_linear.argtypes = [C.POINTER(LinearArgs), C.c_void_p]
         L.nd_op_sync.argtypes = [C.c_void_p]
+        L.nd_op_attention.argtypes = [C.POINTER(AttentionArgs), C.c_void_p]
+        L.nd_op_modulate.argtypes = [C.POINTER(ModulateArgs), C.c_void_p]
+        L.nd_op_rmsnorm.argtypes = [C.POINTER(RmsNormArgs), C.c_void_p]
+        L.nd_op_gemv.argtypes = [C.POINTER(GemvArgs), C.c_void_p]
+        L.nd_op_patchify.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     C.c_int, C.c_int, C.c_int64, C.c_void_p]
+        L.nd_op_unpatchify.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                       C.c_int, C.c_int, C.c_void_p]
         _lib = L
     return _lib
 

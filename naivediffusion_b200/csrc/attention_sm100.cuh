@@ -1,0 +1,339 @@
+// Flash attention forward for sm_100a, head_dim 128, bf16/fp16 in, fp32
+// softmax and accumulation:   O = softmax(Q K^T / sqrt(d) + mask) V
+//
+// Replaces DmlOps.MultiheadAttention (Dml/DmlOps.cs:480-524) as Layers.Attend
+// uses it (Graph/Layers.cs:260-279): packed heads ([rows, heads * 128]),
+// unmasked or under a key-count mask (keys >= key_limit are left out, as the
+// KeySequenceLength mask and the reference's CPU check do), optionally causal
+// (row i sees keys 0..i, the text-row table of QwenImageConditioning).
+//
+// One CTA = one head x two 128-row query tiles (A and B) ping-ponging on the
+// tensor core; 10 warps:
+//   warp 0      TMA: Q_A, Q_B once; K_j, V_j per key tile (2 stages)
+//   warp 1      MMA: S_t = Q_t K_j^T (SS, into TMEM); O_t += P_t V_j (TS: P
+//               read from TMEM, V from shared memory as an MN-major operand)
+//   warps 2-5   softmax of tile A (thread = query row), warps 6-9 tile B:
+//               row max / exp2 / row sum in registers, P written back over
+//               S in TMEM as bf16, lazy O rescale (only when the running max
+//               grows by more than 2^8), final 1/l scaling and store.
+// TMEM columns: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512).
+// While tile A's softmax runs, the tensor core does PV_B and S_B of the
+// next step, and the other way round.
+#pragma once
+
+#include "nd_common.cuh"
+
+namespace nd {
+
+struct AttnArgs {
+  int q_rows;       // query rows per batch item
+  int kv_rows;      // key rows per batch item
+  int key_limit;    // keys visible per batch item (<= kv_rows)
+  int causal;       // row i sees keys [0, i]
+  float scale_log2; // softmax scale * log2(e)
+  void* out;        // [batch * q_rows, ldo], head h at columns [h*128, h*128+128)
+  long long ldo;
+  int out_f16;
+  uint32_t idesc_s, idesc_pv;
+  unsigned* status;
+};
+
+struct AttnSmem {
+  static constexpr int kTile = 128 * 128 * 2;  // one [128 x 128] bf16 tile = 32 KB
+  static constexpr int kQ = 0;                  // Q_A, Q_B
+  static constexpr int kK = 2 * kTile;          // K stages
+  static constexpr int kV = 4 * kTile;          // V stages
+  static constexpr int kBar = 6 * kTile;        // 192 KB
+  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], drain
+  static constexpr int kNumBars = 14;
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kTotal = kMisc + 16;
+  static constexpr int kLaunchBytes = kTotal + 1024;
+};
+
+__device__ __forceinline__ void attn_store_row(void* out, long long ldo, long long row, int col,
+                                               const float (&v)[32], int f16) {
+  uint32_t p[16];
+  if (f16) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p[i] = pack_f16(v[2 * i], v[2 * i + 1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+  }
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + row * ldo + col);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
+}
+
+__global__ void __launch_bounds__(320, 1)
+    attention_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
+                           const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+  using L = AttnSmem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + L::kBar;
+  const uint32_t q_full = bars;
+  auto k_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto v_full = [&](int s) { return bars + 8u * (3 + s); };
+  auto kv_empty = [&](int s) { return bars + 8u * (5 + s); };
+  auto s_full = [&](int t) { return bars + 8u * (7 + t); };
+  auto p_full = [&](int t) { return bars + 8u * (9 + t); };
+  auto o_full = [&](int t) { return bars + 8u * (11 + t); };
+  const uint32_t drain_bar = bars + 8u * 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int batch = blockIdx.z;
+  const int q_tile0 = blockIdx.x * 256;                      // within the batch item
+  const long long q_row0 = static_cast<long long>(batch) * a.q_rows + q_tile0;
+  const int kv_row0 = batch * a.kv_rows;
+  // Key tiles this CTA visits: all visible keys, or (causal) up to its last row.
+  int limit = a.key_limit;
+  if (a.causal) limit = min(limit, q_tile0 + 256);
+  const int n_kv = (limit + 127) / 128;
+  const int col0 = head * 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+      mbar_init(s_full(s), 1);
+      mbar_init(p_full(s), 4);
+      mbar_init(o_full(s), 1);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ loads
+    if (elect_one()) {
+      uint32_t issued = 0, issued_parity = 0;  // K/V stages with loads in flight
+      bool q_issued = false;
+      bool ok = true;
+      mbar_arrive_expect_tx(q_full, 2 * L::kTile);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < 2; ++c)
+          tma_load_2d(sbase + L::kQ + t * L::kTile + c * (L::kTile / 2), &tmQ, q_full, col0 + c * 64,
+                      static_cast<int>(q_row0) + t * 128);
+      q_issued = true;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(kv_empty(st), ph ^ 1u, abort_flag, a.status, kStatusTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        const int krow = kv_row0 + j * 128;
+        mbar_arrive_expect_tx(k_full(st), L::kTile);
+        for (int c = 0; c < 2; ++c)
+          tma_load_2d(sbase + L::kK + st * L::kTile + c * (L::kTile / 2), &tmK, k_full(st),
+                      col0 + c * 64, krow);
+        mbar_arrive_expect_tx(v_full(st), L::kTile);
+        for (int c = 0; c < 2; ++c)
+          tma_load_2d(sbase + L::kV + st * L::kTile + c * (L::kTile / 2), &tmV, v_full(st),
+                      col0 + c * 64, krow);
+        issued |= 1u << st;
+        issued_parity = (issued_parity & ~(1u << st)) | (ph << st);
+      }
+      if (!ok) {
+        volatile int never = 0;
+        if (q_issued) mbar_wait(q_full, 0, &never, nullptr, 0);
+        for (int s = 0; s < 2; ++s) {
+          if (issued & (1u << s)) {
+            mbar_wait(k_full(s), (issued_parity >> s) & 1u, &never, nullptr, 0);
+            mbar_wait(v_full(s), (issued_parity >> s) & 1u, &never, nullptr, 0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA
+    if (elect_one()) {
+      bool ok = mbar_wait(q_full, 0, abort_flag, a.status, kStatusTimeoutMma);
+      auto issue_s = [&](int t, int st) {
+        const uint32_t q_addr = sbase + L::kQ + t * L::kTile;
+        const uint32_t k_addr = sbase + L::kK + st * L::kTile;
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t off = c * (L::kTile / 2) + kk * 32;
+            umma_ss(tmem + t * 128, make_sdesc_sw128(q_addr + off, 16, 1024),
+                    make_sdesc_sw128(k_addr + off, 16, 1024), a.idesc_s, (c | kk) != 0 ? 1u : 0u);
+          }
+        umma_commit(s_full(t));
+      };
+      auto issue_pv = [&](int t, int st, bool acc) {
+        const uint32_t v_addr = sbase + L::kV + st * L::kTile;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          // V as the B operand [N = d, K = keys], d contiguous: MN-major,
+          // 64-wide d chunks 16 KB apart (LBO), 8-key groups 1 KB apart (SBO).
+          umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                  make_sdesc_sw128(v_addr + kk * 16 * 128, L::kTile / 2, 1024), a.idesc_pv,
+                  (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      if (ok && n_kv > 0) {
+        ok = mbar_wait(k_full(0), 0, abort_flag, a.status, kStatusTimeoutMma);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0, 0);
+          issue_s(1, 0);
+        }
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        const bool more = j + 1 < n_kv;
+        const int nst = (j + 1) & 1;
+        const uint32_t nph = ((j + 1) >> 1) & 1;
+        if (!mbar_wait(v_full(st), ph, abort_flag, a.status, kStatusTimeoutMma)) break;
+        for (int t = 0; t < 2; ++t) {
+          if (!mbar_wait(p_full(t), j & 1, abort_flag, a.status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(t, st, j > 0);
+          if (t == 1) umma_commit(kv_empty(st));
+          if (more) {
+            if (t == 0 && !mbar_wait(k_full(nst), nph, abort_flag, a.status, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(t, nst);
+          } else {
+            umma_commit(o_full(t));
+          }
+        }
+      }
+      umma_commit(drain_bar);
+      volatile int never = 0;
+      mbar_wait(drain_bar, 0, &never, a.status, kStatusTimeoutDrain);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int t = (warp - 2) >> 2;  // query tile of this warpgroup
+    const int ew = warp & 3;        // TMEM lane quarter
+    const int r = ew * 32 + lane;   // row within the tile
+    const int q_in_batch = q_tile0 + t * 128 + r;
+    const long long q_row = q_row0 + t * 128 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(ew * 32) << 16;
+    const uint32_t s_tm = tmem + lane_off + t * 128;
+    const uint32_t o_tm = tmem + lane_off + 256 + t * 128;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait(s_full(t), j & 1, abort_flag, a.status, kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(s_tm + c * 32, sr[c]);
+      tmem_ld_wait();
+      // Masks: keys past the visible count (and past the end), causal.
+      int vis = limit - j * 128;
+      if (a.causal) vis = min(vis, q_in_batch + 1 - j * 128);
+      if (vis < 128) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i >= vis) sr[c][i] = __float_as_uint(-INFINITY);
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sr[c][i]));
+      mx *= a.scale_log2;
+      const float m_new = fmaxf(m, mx);
+      const bool need = m_new > m + 8.0f;
+      const float m_use = need ? m_new : m;
+      const float factor = fast_exp2(m - m_use);  // 0 on the first tile
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_tm + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+          tmem_st32(o_tm + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      m = m_use;
+      float rowsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * i]), a.scale_log2, -m));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * i + 1]), a.scale_log2, -m));
+          rowsum += p0 + p1;
+          pk[i] = a.out_f16 ? pack_f16(p0, p1) : pack_bf16(p0, p1);
+        }
+        tmem_st16(s_tm + c * 16, pk);
+      }
+      l = l * factor + rowsum;
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full(t));
+    }
+    if (ok && n_kv > 0 && mbar_wait(o_full(t), 0, abort_flag, a.status, kStatusTimeoutEpilogue)) {
+      __syncwarp();
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      const bool row_ok = q_in_batch < a.q_rows;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_tm + c * 32, o);
+        tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]) * inv;
+        if (row_ok) attn_store_row(a.out, a.ldo, q_row, col0 + c * 32, v, a.out_f16);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace nd

@@ -36,7 +36,14 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, int64_t row
 
 // ----------------------------------------------------------------- kernels
 
-struct LinearPlan;
 int linear(const nd_linear_args& a, cudaStream_t stream);
+int attention(const nd_attention_args& a, cudaStream_t stream);
+int modulate(const nd_modulate_args& a, cudaStream_t stream);
+int rmsnorm(const nd_rmsnorm_args& a, cudaStream_t stream);
+int gemv(const nd_gemv_args& a, cudaStream_t stream);
+int patchify(const float* lat, void* tok, int out_dtype, int B, int C, int H, int W, int p,
+             int64_t ldt, cudaStream_t stream);
+int unpatchify(const float* tok, int64_t ldt, float* lat, int B, int C, int H, int W, int p,
+               cudaStream_t stream);
 
 }  // namespace nd

@@ -1,0 +1,357 @@
+// Memory-bound kernels of the denoiser step: adaLN modulation (LayerNorm
+// without affine, x (1 + scale) + shift), RMSNorm, the modulation GEMVs,
+// patchify / unpatchify. All are one pass over HBM with 128-bit accesses and
+// warp-shuffle reductions; their roofline is HBM bandwidth.
+#include <algorithm>
+#include <climits>
+
+#include "nd_common.cuh"
+#include "nd_internal.h"
+#include "nd_runtime.h"
+
+namespace nd {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void store4(void* out, long long idx, float4 v, int out_type) {
+  if (out_type == ND_F32) {
+    reinterpret_cast<float4*>(static_cast<float*>(out) + idx)[0] = v;
+  } else if (out_type == ND_F16) {
+    uint2 p = make_uint2(pack_f16(v.x, v.y), pack_f16(v.z, v.w));
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + idx) = p;
+  } else {
+    uint2 p = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + idx) = p;
+  }
+}
+
+// One warp per row; V float4 per lane hold the row (width <= 128 * V).
+// y = LN(x) * (1 + scale[g]) + shift[g] (Transformer.Modulate,
+// Graph/Transformer.cs:72-80), stats in fp32 over the row held in registers
+// (mean first, then the centred second moment: the two-pass form of
+// CpuMath.LayerNorm, Tensors/CpuMath.cs:100-115).
+template <int V>
+__global__ void __launch_bounds__(256) modulate_kernel(const float* __restrict__ x, long long ldx,
+                                                       void* __restrict__ y, long long ldy,
+                                                       int out_type, int rows, int width,
+                                                       const float* __restrict__ shift,
+                                                       const float* __restrict__ scale,
+                                                       int vec_stride, int split, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int w4 = width >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(warp) * ldx);
+  float4 v[V];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + 32 * i;
+    v[i] = c < w4 ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  const float mean = warp_sum(s) / width;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + 32 * i;
+    if (c < w4) {
+      const float a = v[i].x - mean, b = v[i].y - mean, cc = v[i].z - mean, d = v[i].w - mean;
+      q += (a * a + b * b) + (cc * cc + d * d);
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / width + eps);
+  const int g = warp >= split ? 1 : 0;
+  const float4* sc = reinterpret_cast<const float4*>(scale + g * vec_stride);
+  const float4* sh = shift ? reinterpret_cast<const float4*>(shift + g * vec_stride) : nullptr;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + 32 * i;
+    if (c < w4) {
+      const float4 k = __ldg(sc + c);
+      const float4 b = sh ? __ldg(sh + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 o;
+      o.x = (v[i].x - mean) * rstd * (1.f + k.x) + b.x;
+      o.y = (v[i].y - mean) * rstd * (1.f + k.y) + b.y;
+      o.z = (v[i].z - mean) * rstd * (1.f + k.z) + b.z;
+      o.w = (v[i].w - mean) * rstd * (1.f + k.w) + b.w;
+      store4(y, static_cast<long long>(warp) * ldy + 4 * c, o, out_type);
+    }
+  }
+}
+
+// RMSNorm over rows (CpuMath.RmsNorm, Tensors/CpuMath.cs:128-146):
+// y = x * rsqrt(mean(x^2) + eps) * (w + plus_one). x fp32 or bf16/f16.
+template <int V>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const void* __restrict__ x, int in_type,
+                                                      long long ldx, void* __restrict__ y,
+                                                      long long ldy, int out_type, int rows,
+                                                      int width, const float* __restrict__ w,
+                                                      float plus_one, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int w4 = width >> 2;
+  float4 v[V];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + 32 * i;
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < w4) {
+      if (in_type == ND_F32) {
+        t = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(x) + static_cast<long long>(warp) * ldx) + c);
+      } else {
+        const uint2 p = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + static_cast<long long>(warp) * ldx) + c);
+        if (in_type == ND_F16) {
+          const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&p.x));
+          const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&p.y));
+          t = make_float4(a.x, a.y, b.x, b.y);
+        } else {
+          const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&p.x));
+          const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&p.y));
+          t = make_float4(a.x, a.y, b.x, b.y);
+        }
+      }
+    }
+    v[i] = t;
+    s += (t.x * t.x + t.y * t.y) + (t.z * t.z + t.w * t.w);
+  }
+  const float r = rsqrtf(warp_sum(s) / width + eps);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + 32 * i;
+    if (c < w4) {
+      float4 k = w ? __ldg(reinterpret_cast<const float4*>(w) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (!w) plus_one = 1.f;
+      float4 o;
+      o.x = v[i].x * r * (k.x + plus_one);
+      o.y = v[i].y * r * (k.y + plus_one);
+      o.z = v[i].z * r * (k.z + plus_one);
+      o.w = v[i].w * r * (k.w + plus_one);
+      store4(y, static_cast<long long>(warp) * ldy + 4 * c, o, out_type);
+    }
+  }
+}
+
+int pick_bucket(int width) {
+  const int per_lane = (width / 4 + 31) / 32;
+  if (per_lane <= 2) return 2;
+  if (per_lane <= 4) return 4;
+  if (per_lane <= 8) return 8;
+  if (per_lane <= 16) return 16;
+  if (per_lane <= 24) return 24;
+  if (per_lane <= 32) return 32;
+  return 0;
+}
+
+// y[b][n] = act(sum_k W[n][k] * pre(x[b][k]) + bias[n]); W bf16/f16 [N, K];
+// x fp32 [B, K] (B <= 4); one warp per output row, x staged in shared memory.
+// The modulation vectors of every block at once (one HBM pass over the
+// modulation weights: QwenImageDit's modulation.1, AnimaDit.Modulation).
+__global__ void __launch_bounds__(256) gemv_kernel(const uint16_t* __restrict__ W, int w_f16,
+                                                   long long N, int K, const float* __restrict__ x,
+                                                   int B, int pre, const float* __restrict__ bias,
+                                                   int act, float* __restrict__ y) {
+  extern __shared__ float xs[];
+  for (int i = threadIdx.x; i < B * K; i += blockDim.x) {
+    float v = x[i];
+    if (pre == 1) v = v / (1.0f + __expf(-v));
+    xs[i] = v;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const int k8 = K >> 3;
+  for (long long n = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; n < N;
+       n += warps) {
+    const uint4* wr = reinterpret_cast<const uint4*>(W + n * K);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = lane; c < k8; c += 32) {
+      uint4 p;
+      asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(p.x), "=r"(p.y), "=r"(p.z), "=r"(p.w)
+                   : "l"(wr + c));
+      float wv[8];
+      const uint32_t u[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 f;
+        if (w_f16) f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+        else f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[i]));
+        wv[2 * i] = f.x;
+        wv[2 * i + 1] = f.y;
+      }
+#pragma unroll 4
+      for (int b = 0; b < 4; ++b) {
+        if (b < B) {
+          const float* xb = xs + b * K + 8 * c;
+          float s = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) s += wv[i] * xb[i];
+          acc[b] += s;
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      if (b < B) {
+        float v = warp_sum(acc[b]);
+        if (lane == 0) {
+          if (bias) v += bias[n];
+          if (act == 1) v = v / (1.0f + __expf(-v));
+          else if (act == 2) v = tanhf(v);
+          y[static_cast<long long>(b) * N + n] = v;
+        }
+      }
+    }
+  }
+}
+
+// latent [B][C][H][W] fp32 -> tokens [B][(H/p)(W/p)][C p p] (bf16/f16/fp32);
+// feature c*p*p + m*p + n of patch (i, j) is channel c at (p*i + m, p*j + n)
+// (AnimaDit.Patchify, Models/Anima/AnimaDit.cs:193-247).
+__global__ void patchify_kernel(const float* __restrict__ lat, void* __restrict__ tok, int out_type,
+                                int B, int C, int H, int W, int p, long long ldt) {
+  const long long total = static_cast<long long>(B) * C * H * W;
+  const int rows = H / p, cols = W / p, feat = C * p * p;
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int w = idx % W;
+    const int h = (idx / W) % H;
+    const int c = (idx / (static_cast<long long>(W) * H)) % C;
+    const int b = idx / (static_cast<long long>(W) * H * C);
+    const int i = h / p, m = h % p, j = w / p, n = w % p;
+    const long long t = static_cast<long long>(b) * rows * cols + i * cols + j;
+    const long long o = t * ldt + c * p * p + m * p + n;
+    (void)feat;
+    const float v = lat[idx];
+    if (out_type == ND_F32) static_cast<float*>(tok)[o] = v;
+    else if (out_type == ND_F16) static_cast<__half*>(tok)[o] = __float2half_rn(v);
+    else static_cast<__nv_bfloat16*>(tok)[o] = __float2bfloat16_rn(v);
+  }
+}
+
+// The inverse of patchify_kernel: fp32 tokens -> fp32 latent.
+__global__ void unpatchify_kernel(const float* __restrict__ tok, long long ldt, float* __restrict__ lat,
+                                  int B, int C, int H, int W, int p) {
+  const long long total = static_cast<long long>(B) * C * H * W;
+  const int rows = H / p, cols = W / p;
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int w = idx % W;
+    const int h = (idx / W) % H;
+    const int c = (idx / (static_cast<long long>(W) * H)) % C;
+    const int b = idx / (static_cast<long long>(W) * H * C);
+    const int i = h / p, m = h % p, j = w / p, n = w % p;
+    const long long t = static_cast<long long>(b) * rows * cols + i * cols + j;
+    lat[idx] = tok[t * ldt + c * p * p + m * p + n];
+  }
+  (void)rows;
+}
+
+}  // namespace
+
+int modulate(const nd_modulate_args& a, cudaStream_t stream) {
+  if (a.rows <= 0 || a.width <= 0) return fail(ND_ERR_INVALID, "modulate: empty shape");
+  if (a.width % 4 || a.ldx % 4 || a.ldy % 4) return fail(ND_ERR_INVALID, "modulate: width and strides must be multiples of 4");
+  if (!a.x || !a.y || !a.scale) return fail(ND_ERR_INVALID, "modulate: null operand");
+  if (a.rows > INT_MAX) return fail(ND_ERR_INVALID, "modulate: too many rows");
+  const int bucket = pick_bucket(static_cast<int>(a.width));
+  if (!bucket) return fail(ND_ERR_UNSUPPORTED, "modulate: width above 4096");
+  const int rows = static_cast<int>(a.rows);
+  const int split = a.group_split < a.rows ? static_cast<int>(a.group_split) : INT_MAX;
+  const int vs = a.vec_stride ? static_cast<int>(a.vec_stride) : static_cast<int>(a.width);
+  const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+#define ND_MOD(V) modulate_kernel<V><<<grid, 256, 0, stream>>>(a.x, a.ldx, a.y, a.ldy, a.out_dtype, rows, static_cast<int>(a.width), a.shift, a.scale, vs, split, a.eps)
+  switch (bucket) {
+    case 2: ND_MOD(2); break;
+    case 4: ND_MOD(4); break;
+    case 8: ND_MOD(8); break;
+    case 16: ND_MOD(16); break;
+    case 24: ND_MOD(24); break;
+    default: ND_MOD(32); break;
+  }
+#undef ND_MOD
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int rmsnorm(const nd_rmsnorm_args& a, cudaStream_t stream) {
+  if (a.rows <= 0 || a.width <= 0) return fail(ND_ERR_INVALID, "rmsnorm: empty shape");
+  if (a.width % 4 || a.ldx % 4 || a.ldy % 4) return fail(ND_ERR_INVALID, "rmsnorm: width and strides must be multiples of 4");
+  if (!a.x || !a.y) return fail(ND_ERR_INVALID, "rmsnorm: null operand");
+  const int bucket = pick_bucket(static_cast<int>(a.width));
+  if (!bucket) return fail(ND_ERR_UNSUPPORTED, "rmsnorm: width above 4096");
+  const int rows = static_cast<int>(a.rows);
+  const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+#define ND_RMS(V) rmsnorm_kernel<V><<<grid, 256, 0, stream>>>(a.x, a.in_dtype, a.ldx, a.y, a.ldy, a.out_dtype, rows, static_cast<int>(a.width), a.weight, a.plus_one ? 1.f : 0.f, a.eps)
+  switch (bucket) {
+    case 2: ND_RMS(2); break;
+    case 4: ND_RMS(4); break;
+    case 8: ND_RMS(8); break;
+    case 16: ND_RMS(16); break;
+    case 24: ND_RMS(24); break;
+    default: ND_RMS(32); break;
+  }
+#undef ND_RMS
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int gemv(const nd_gemv_args& a, cudaStream_t stream) {
+  if (a.n <= 0 || a.k <= 0 || a.batch <= 0 || a.batch > 4) return fail(ND_ERR_INVALID, "gemv: bad shape (batch 1..4)");
+  if (a.k % 8) return fail(ND_ERR_INVALID, "gemv: k must be a multiple of 8");
+  if (a.k * a.batch > 12288) return fail(ND_ERR_UNSUPPORTED, "gemv: batch * k above 12288");
+  if (a.w_dtype != ND_BF16 && a.w_dtype != ND_F16) return fail(ND_ERR_INVALID, "gemv: weight must be bf16 or f16");
+  if (!a.w || !a.x || !a.y) return fail(ND_ERR_INVALID, "gemv: null operand");
+  const size_t shmem = static_cast<size_t>(a.k) * a.batch * sizeof(float);
+  if (shmem > 48 * 1024) {
+    static bool configured[64] = {};
+    int dev = 0;
+    ND_CUDA(cudaGetDevice(&dev));
+    if (!configured[dev & 63]) {
+      ND_CUDA(cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 48 * 1024 * 2));
+      configured[dev & 63] = true;
+    }
+  }
+  const long long warps_needed = a.n;
+  long long blocks = (warps_needed + 7) / 8;
+  const long long cap = static_cast<long long>(sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  gemv_kernel<<<static_cast<unsigned>(blocks), 256, shmem, stream>>>(
+      static_cast<const uint16_t*>(a.w), a.w_dtype == ND_F16, a.n, static_cast<int>(a.k), a.x,
+      a.batch, a.pre_silu ? 1 : 0, a.bias, a.act, a.y);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int patchify(const float* lat, void* tok, int out_dtype, int B, int C, int H, int W, int p,
+             int64_t ldt, cudaStream_t stream) {
+  if (B <= 0 || C <= 0 || H <= 0 || W <= 0 || p <= 0 || H % p || W % p)
+    return fail(ND_ERR_INVALID, "patchify: latent does not divide into patches");
+  const long long total = static_cast<long long>(B) * C * H * W;
+  const unsigned grid = static_cast<unsigned>(std::min<long long>((total + 255) / 256, sm_count() * 16LL));
+  patchify_kernel<<<grid, 256, 0, stream>>>(lat, tok, out_dtype, B, C, H, W, p, ldt);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int unpatchify(const float* tok, int64_t ldt, float* lat, int B, int C, int H, int W, int p,
+               cudaStream_t stream) {
+  if (B <= 0 || C <= 0 || H <= 0 || W <= 0 || p <= 0 || H % p || W % p)
+    return fail(ND_ERR_INVALID, "unpatchify: latent does not divide into patches");
+  const long long total = static_cast<long long>(B) * C * H * W;
+  const unsigned grid = static_cast<unsigned>(std::min<long long>((total + 255) / 256, sm_count() * 16LL));
+  unpatchify_kernel<<<grid, 256, 0, stream>>>(tok, ldt, lat, B, C, H, W, p);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+}  // namespace nd

@@ -126,6 +126,38 @@ int nd_op_linear(const nd_linear_args* args, void* stream) {
   return nd::linear(*args, static_cast<cudaStream_t>(stream));
 }
 
+int nd_op_attention(const nd_attention_args* args, void* stream) {
+  if (!args) return nd::fail(ND_ERR_INVALID, "nd_op_attention: null args");
+  return nd::attention(*args, static_cast<cudaStream_t>(stream));
+}
+
+int nd_op_modulate(const nd_modulate_args* args, void* stream) {
+  if (!args) return nd::fail(ND_ERR_INVALID, "nd_op_modulate: null args");
+  return nd::modulate(*args, static_cast<cudaStream_t>(stream));
+}
+
+int nd_op_rmsnorm(const nd_rmsnorm_args* args, void* stream) {
+  if (!args) return nd::fail(ND_ERR_INVALID, "nd_op_rmsnorm: null args");
+  return nd::rmsnorm(*args, static_cast<cudaStream_t>(stream));
+}
+
+int nd_op_gemv(const nd_gemv_args* args, void* stream) {
+  if (!args) return nd::fail(ND_ERR_INVALID, "nd_op_gemv: null args");
+  return nd::gemv(*args, static_cast<cudaStream_t>(stream));
+}
+
+int nd_op_patchify(const float* latent, void* tokens, int out_dtype, int batch, int channels,
+                   int height, int width, int patch, int64_t ldt, void* stream) {
+  return nd::patchify(latent, tokens, out_dtype, batch, channels, height, width, patch, ldt,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int nd_op_unpatchify(const float* tokens, int64_t ldt, float* latent, int batch, int channels,
+                     int height, int width, int patch, void* stream) {
+  return nd::unpatchify(tokens, ldt, latent, batch, channels, height, width, patch,
+                        static_cast<cudaStream_t>(stream));
+}
+
 int nd_op_sync(void* stream) { return nd::check_device_status(static_cast<cudaStream_t>(stream)); }
 
 }  // extern "C"

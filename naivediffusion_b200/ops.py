@@ -13,7 +13,7 @@ import ctypes as C
 import torch
 
 from . import _lib
-from ._lib import LinearArgs, check, lib
+from ._lib import AttentionArgs, GemvArgs, LinearArgs, ModulateArgs, RmsNormArgs, check, lib
 
 _DT = {torch.bfloat16: _lib.ND_BF16, torch.float16: _lib.ND_F16, torch.float32: _lib.ND_F32}
 
@@ -71,3 +71,97 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     a.eps = eps
     check(lib().nd_op_linear(C.byref(a), C.c_void_p(_stream())))
     return residual if resid_epi else out
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *,
+              out: torch.Tensor | None = None, batch: int = 1, key_limit: int = 0,
+              causal: bool = False, scale: float = 0.0) -> torch.Tensor:
+    """Flash attention over packed heads (Layers.Attend, Graph/Layers.cs:260-279).
+
+    q: [batch * q_rows, >= heads*128] (row stride q.stride(0)); k, v likewise
+    with kv_rows per item. Returns out [batch * q_rows, heads * 128].
+    """
+    q_rows = q.shape[0] // batch
+    kv_rows = k.shape[0] // batch
+    if out is None:
+        out = torch.empty(q.shape[0], heads * 128, device=q.device, dtype=q.dtype)
+    a = AttentionArgs()
+    a.dtype = _DT[q.dtype]
+    a.heads, a.head_dim, a.batch = heads, 128, batch
+    a.q_rows, a.kv_rows, a.key_limit, a.causal = q_rows, kv_rows, key_limit, int(causal)
+    a.q, a.ldq = q.data_ptr(), q.stride(0)
+    a.k, a.ldk = k.data_ptr(), k.stride(0)
+    a.v, a.ldv = v.data_ptr(), v.stride(0)
+    a.out, a.ldo = out.data_ptr(), out.stride(0)
+    a.scale = scale
+    check(lib().nd_op_attention(C.byref(a), C.c_void_p(_stream())))
+    return out
+
+
+def modulate(x: torch.Tensor, shift: torch.Tensor | None, scale: torch.Tensor, *,
+             out_dtype=torch.bfloat16, group_split: int | None = None, eps: float = 1e-6,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """LayerNorm(x) * (1 + scale) + shift (Transformer.Modulate, Graph/Transformer.cs:72-80).
+    scale/shift: [width] or [2, width] (second row for rows >= group_split)."""
+    rows, width = x.shape
+    if out is None:
+        out = torch.empty(rows, width, device=x.device, dtype=out_dtype)
+    a = ModulateArgs()
+    a.x, a.ldx = x.data_ptr(), x.stride(0)
+    a.y, a.ldy, a.out_dtype = out.data_ptr(), out.stride(0), _DT[out.dtype]
+    a.rows, a.width = rows, width
+    a.shift = _ptr(shift)
+    a.scale = scale.data_ptr()
+    a.vec_stride = width
+    a.group_split = group_split if group_split is not None else rows
+    a.eps = eps
+    check(lib().nd_op_modulate(C.byref(a), C.c_void_p(_stream())))
+    return out
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor | None, *, out_dtype=None, plus_one=False,
+            eps: float = 1e-6) -> torch.Tensor:
+    """x * rsqrt(mean(x^2) + eps) * (weight [+ 1]) over rows (CpuMath.RmsNorm)."""
+    rows, width = x.shape
+    out = torch.empty(rows, width, device=x.device, dtype=out_dtype or x.dtype)
+    a = RmsNormArgs()
+    a.x, a.ldx, a.in_dtype = x.data_ptr(), x.stride(0), _DT[x.dtype]
+    a.y, a.ldy, a.out_dtype = out.data_ptr(), out.stride(0), _DT[out.dtype]
+    a.rows, a.width = rows, width
+    a.weight = _ptr(weight)
+    a.plus_one = int(plus_one)
+    a.eps = eps
+    check(lib().nd_op_rmsnorm(C.byref(a), C.c_void_p(_stream())))
+    return out
+
+
+def gemv(w: torch.Tensor, x: torch.Tensor, bias: torch.Tensor | None = None, *,
+         pre_silu: bool = False, act: int = 0) -> torch.Tensor:
+    """y[b] = act(W . pre(x[b]) + bias) for 1-4 fp32 rows x; W bf16/f16 [n, k]."""
+    n, k = w.shape
+    x = x.reshape(-1, k).contiguous()
+    y = torch.empty(x.shape[0], n, device=w.device, dtype=torch.float32)
+    a = GemvArgs()
+    a.w, a.w_dtype, a.n, a.k = w.data_ptr(), _DT[w.dtype], n, k
+    a.x, a.batch, a.pre_silu = x.data_ptr(), x.shape[0], int(pre_silu)
+    a.bias, a.act, a.y = _ptr(bias), act, y.data_ptr()
+    check(lib().nd_op_gemv(C.byref(a), C.c_void_p(_stream())))
+    return y
+
+
+def patchify(latent: torch.Tensor, patch: int, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """[B, C, H, W] fp32 -> [B*(H/p)*(W/p), C*p*p] (AnimaDit.Patchify order)."""
+    b, c, h, w = latent.shape
+    tok = torch.empty(b * (h // patch) * (w // patch), c * patch * patch, device=latent.device,
+                      dtype=out_dtype)
+    check(lib().nd_op_patchify(latent.data_ptr(), tok.data_ptr(), _DT[out_dtype], b, c, h, w, patch,
+                               tok.stride(0), C.c_void_p(_stream())))
+    return tok
+
+
+def unpatchify(tokens: torch.Tensor, shape, patch: int) -> torch.Tensor:
+    b, c, h, w = shape
+    lat = torch.empty(b, c, h, w, device=tokens.device, dtype=torch.float32)
+    check(lib().nd_op_unpatchify(tokens.data_ptr(), tokens.stride(0), lat.data_ptr(), b, c, h, w,
+                                 patch, C.c_void_p(_stream())))
+    return lat

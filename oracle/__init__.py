@@ -1,0 +1,287 @@
+"""nd_oracle — TEST INFRASTRUCTURE, NOT PRODUCT CODE.
+
+numpy front end of the C++ restatement of NaiveDiffusion's CPU layer
+arithmetic (oracle/nd_oracle.cpp). Only tests/, __graft_entry__.smoke() and
+bench.py's cpu_baseline / --impl reference legs may import this package, and
+only as the checker or the timed CPU baseline. The product library
+(naivediffusion_b200/libnd_denoise.so) never loads it.
+
+Parity pinning: the reference is C# (.NET) and cannot be built here, so this
+restatement is pinned by the known-answer checks of the reference's own unit
+tests and smoke command, restated in tests/test_oracle.py.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "liboracle.so"
+
+_f = np.float32
+_lib = None
+
+
+def build(force: bool = False) -> Path:
+    """Compile liboracle.so with the Makefile beside this file (g++ + OpenMP)."""
+    src = HERE / "nd_oracle.cpp"
+    if force or not LIB.exists() or LIB.stat().st_mtime < src.stat().st_mtime:
+        subprocess.run(["make", "-s", "-B" if force else "-s", "-C", str(HERE)], check=True,
+                       capture_output=True)
+    return LIB
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        build()
+        _lib = C.CDLL(str(LIB))
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    if a is None:
+        return None
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def _c(a, dtype=_f):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def threads() -> int:
+    return int(lib().nd_oracle_threads())
+
+
+# ------------------------------------------------------------------ dtypes
+
+def to_f16_bits(x) -> np.ndarray:
+    x = _c(x)
+    y = np.empty(x.shape, np.uint16)
+    lib().nd_oracle_f32_to_f16(_p(x), _p(y), C.c_int64(x.size))
+    return y
+
+
+def from_f16_bits(h) -> np.ndarray:
+    h = _c(h, np.uint16)
+    y = np.empty(h.shape, _f)
+    lib().nd_oracle_f16_to_f32(_p(h), _p(y), C.c_int64(h.size))
+    return y
+
+
+def to_bf16_bits(x) -> np.ndarray:
+    x = _c(x)
+    y = np.empty(x.shape, np.uint16)
+    lib().nd_oracle_f32_to_bf16(_p(x), _p(y), C.c_int64(x.size))
+    return y
+
+
+def from_bf16_bits(h) -> np.ndarray:
+    h = _c(h, np.uint16)
+    y = np.empty(h.shape, _f)
+    lib().nd_oracle_bf16_to_f32(_p(h), _p(y), C.c_int64(h.size))
+    return y
+
+
+def round_bf16(x) -> np.ndarray:
+    return from_bf16_bits(to_bf16_bits(x))
+
+
+def round_f16(x) -> np.ndarray:
+    return from_f16_bits(to_f16_bits(x))
+
+
+# ------------------------------------------------------------------ layers
+
+def linear(x, w, b=None) -> np.ndarray:
+    """CpuMath.Linear (Tensors/CpuMath.cs:34-64)."""
+    x = _c(x)
+    w = _c(w)
+    rows, inner = x.shape
+    outer = w.shape[0]
+    y = np.empty((rows, outer), _f)
+    bb = None if b is None else _c(b)
+    lib().nd_oracle_linear(_p(x), rows, inner, _p(w), _p(bb), _p(y), outer)
+    return y
+
+
+def layernorm(x, eps, weight=None, bias=None) -> np.ndarray:
+    """CpuMath.LayerNorm (Tensors/CpuMath.cs:92-122); no affine when weight is None."""
+    x = _c(x)
+    rows, width = x.shape
+    y = np.empty_like(x)
+    w = None if weight is None else _c(weight)
+    b = None if bias is None else _c(bias)
+    lib().nd_oracle_layernorm(_p(x), rows, width, _p(w), _p(b), _p(y), C.c_float(eps))
+    return y
+
+
+def modulate(x, shift, scale, eps) -> np.ndarray:
+    """Transformer.Modulate (Graph/Transformer.cs:72-80)."""
+    x = _c(x)
+    rows, width = x.shape
+    y = np.empty_like(x)
+    sh = None if shift is None else _c(shift)
+    lib().nd_oracle_modulate(_p(x), rows, width, _p(sh), _p(_c(scale)), _p(y), C.c_float(eps))
+    return y
+
+
+def rmsnorm(x, weight, eps) -> np.ndarray:
+    """CpuMath.RmsNorm (Tensors/CpuMath.cs:128-146) over the last axis."""
+    x = _c(x)
+    width = x.shape[-1]
+    rows = x.size // width
+    y = np.empty_like(x)
+    w = None if weight is None else _c(weight)
+    lib().nd_oracle_rmsnorm(_p(x), rows, width, _p(w), _p(y), C.c_float(eps))
+    return y
+
+
+def rope(x, heads, cos, sin) -> np.ndarray:
+    """CpuMath.Rope (Tensors/CpuMath.cs:154-173), rotate-half; returns a copy."""
+    y = _c(x).copy()
+    rows = y.shape[0]
+    dim = y.size // rows // heads
+    lib().nd_oracle_rope(_p(y), rows, heads, dim, _p(_c(cos)), _p(_c(sin)))
+    return y
+
+
+def attention(q, k, v, heads, kv_heads=None, causal=False, key_len=0) -> np.ndarray:
+    """CpuMath.Attention (Tensors/CpuMath.cs:203-248) plus the key-count mask."""
+    q, k, v = _c(q), _c(k), _c(v)
+    kv_heads = kv_heads or heads
+    rows, key_rows = q.shape[0], k.shape[0]
+    dim = q.shape[1] // heads
+    y = np.empty_like(q)
+    lib().nd_oracle_attention(_p(q), _p(k), _p(v), rows, key_rows, heads, kv_heads, dim,
+                              int(causal), int(key_len), _p(y), C.c_int64(0), C.c_int64(0),
+                              C.c_int64(0), C.c_int64(0))
+    return y
+
+
+def gelu(x) -> np.ndarray:
+    y = _c(x).copy()
+    lib().nd_oracle_gelu(_p(y), C.c_int64(y.size))
+    return y
+
+
+def gelu_tanh(x) -> np.ndarray:
+    y = _c(x).copy()
+    lib().nd_oracle_gelu_tanh(_p(y), C.c_int64(y.size))
+    return y
+
+
+def silu(x) -> np.ndarray:
+    y = _c(x).copy()
+    lib().nd_oracle_silu(_p(y), C.c_int64(y.size))
+    return y
+
+
+def sinusoid(time: float, width: int) -> np.ndarray:
+    y = np.empty(width, _f)
+    lib().nd_oracle_sinusoid(C.c_float(time), width, _p(y))
+    return y
+
+
+def qwen_rope_tables(rows, columns, text_len, context_rows):
+    n = rows * columns + context_rows
+    cos = np.empty((n, 64), _f)
+    sin = np.empty((n, 64), _f)
+    lib().nd_oracle_qwen_rope_tables(rows, columns, text_len, context_rows, _p(cos), _p(sin))
+    return cos, sin
+
+
+def anima_rope_tables(rows, columns, head_dim=128):
+    n = rows * columns
+    cos = np.empty((n, head_dim // 2), _f)
+    sin = np.empty((n, head_dim // 2), _f)
+    lib().nd_oracle_anima_rope_tables(rows, columns, head_dim, _p(cos), _p(sin))
+    return cos, sin
+
+
+# ------------------------------------------------------------------ int8
+
+def quantize(w, group=32, scale_f16=True):
+    """BlockQuantizer.Quantize (Tensors/BlockQuantizer.cs:34-105), group-generalised.
+    Returns (q int8 [rows, cols], scales [rows, cols/group] as fp16 bits or fp32)."""
+    w = _c(w)
+    rows, cols = w.shape
+    if group <= 0 or cols % group:
+        raise ValueError(f"{cols} columns do not split into groups of {group}")
+    q = np.empty((rows, cols), np.int8)
+    s = np.empty((rows, cols // group), np.uint16 if scale_f16 else _f)
+    rc = lib().nd_oracle_quantize(_p(w), rows, cols, group, int(scale_f16), _p(q), _p(s))
+    if rc:
+        raise ValueError("quantize: bad shape")
+    return q, s
+
+
+def dequantize(q, scales, group=32) -> np.ndarray:
+    q = _c(q, np.int8)
+    rows, cols = q.shape
+    f16 = scales.dtype == np.uint16
+    s = np.ascontiguousarray(scales)
+    w = np.empty((rows, cols), _f)
+    lib().nd_oracle_dequantize(_p(q), _p(s), int(f16), rows, cols, group, _p(w))
+    return w
+
+
+# ------------------------------------------------------------------ blocks
+
+class _MMDiTStream(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "mod_w", "mod_b", "q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "norm_q", "norm_k",
+        "out_w", "out_b", "up_w", "up_b", "down_w", "down_b")]
+
+
+class _AnimaBlock(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "self_mod1", "self_mod2", "cross_mod1", "cross_mod2", "mlp_mod1", "mlp_mod2",
+        "sq", "sk", "sv", "so", "sq_norm", "sk_norm",
+        "cq", "ck", "cv", "co", "cq_norm", "ck_norm", "fc1", "fc2")]
+
+
+def mmdit_block(img: dict, txt: dict, x, n_img, temb, cos, sin, heads, key_len=0, eps=1e-6):
+    """One dual-stream block (nd_oracle_mmdit_block). img/txt map the
+    _MMDiTStream field names to float32 arrays. Returns the updated x."""
+    keep = []
+
+    def stream(d):
+        s = _MMDiTStream()
+        for name, _ in _MMDiTStream._fields_:
+            a = _c(d[name])
+            keep.append(a)
+            setattr(s, name, a.ctypes.data)
+        return s
+
+    si, st = stream(img), stream(txt)
+    x = _c(x).copy()
+    width = x.shape[1]
+    mlp = img["up_w"].shape[0]
+    head_dim = width // heads
+    lib().nd_oracle_mmdit_block(C.byref(si), C.byref(st), width, heads, head_dim, mlp, _p(x),
+                                n_img, x.shape[0] - n_img, _p(_c(temb)), _p(_c(cos)),
+                                _p(_c(sin)), int(key_len), C.c_float(eps))
+    return x
+
+
+def anima_block(w: dict, x, context, temb, lora, cos, sin, heads, eps=1e-6):
+    keep = []
+    s = _AnimaBlock()
+    for name, _ in _AnimaBlock._fields_:
+        a = _c(w[name])
+        keep.append(a)
+        setattr(s, name, a.ctypes.data)
+    x = _c(x).copy()
+    context = _c(context)
+    width = x.shape[1]
+    rank = w["self_mod1"].shape[0]
+    mlp = w["fc1"].shape[0]
+    lib().nd_oracle_anima_block(C.byref(s), width, heads, width // heads, mlp, rank, _p(x),
+                                x.shape[0], _p(context), context.shape[0], context.shape[1],
+                                _p(_c(temb)), _p(_c(lora)), _p(_c(cos)), _p(_c(sin)),
+                                C.c_float(eps))
+    return x
