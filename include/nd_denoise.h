@@ -55,6 +55,115 @@ ND_API const char* nd_last_error(void);
 /* Library version string. */
 ND_API const char* nd_version(void);
 
+/* ------------------------------------------------------------ denoiser plug-in
+ * The native side of IDenoiser (src/NaiveDiffusion/Pipeline/IDenoiser.cs:10-32):
+ * a model is created from a description, its weights are copied into HBM
+ * once (set_weight), then predict() runs one forward step per call. Weights
+ * stay resident (no streaming); the caller's host buffers are only read
+ * during the call that receives them. One caller at a time per handle, as
+ * the reference's DmlDevice (Dml/DmlDevice.cs:9-14). */
+#define ND_FAMILY_MMDIT 0   /* Qwen-Image-style dual-stream DiT (60 x 3072 at full size) */
+#define ND_FAMILY_ANIMA 1   /* Anima / Cosmos-Predict2 DiT (Models/Anima/AnimaDit.cs) */
+#define ND_FAMILY_SDXL 2    /* SDXL UNet (Models/Sdxl/UNetModel.cs) */
+
+typedef struct nd_device nd_device;
+typedef struct nd_denoiser nd_denoiser;
+
+typedef struct nd_model_desc {
+  int family;                 /* ND_FAMILY_* */
+  int width, heads, head_dim; /* transformer width, heads x head_dim == width */
+  int blocks, mlp_width;
+  int context_rows, context_width; /* text rows per predict and their width */
+  int latent_channels, latent_height, latent_width, patch;
+  int time_width;             /* sinusoid width of the timestep embedder */
+  int batch;                  /* latents per predict (stacked CFG branches) */
+  int compute;                /* ND_BF16 (DiTs), ND_F16 (SDXL) */
+  int weight_dtype;           /* storage: ND_BF16 / ND_F16, or ND_I8 (weight-only) */
+  int quant_group;            /* int8: columns per scale (32 = BlockQuantizer); 0 = per output channel */
+  int quant_scale_dtype;      /* int8: ND_F16 (BlockQuantizer) or ND_F32 */
+  float eps;                  /* norm epsilon (1e-6 for the DiTs) */
+} nd_model_desc;
+
+typedef struct nd_named_tensor {
+  const char* name;
+  int dtype;                  /* ND_F32 / ND_I32 ... */
+  int rank;
+  const int64_t* shape;
+  const void* data;
+} nd_named_tensor;
+
+typedef struct nd_memory {
+  uint64_t persistent_bytes;  /* folded weights, wherever they are */
+  uint64_t streamed_bytes;    /* of those, read from system memory per step (always 0) */
+  uint64_t resident_bytes;    /* of those, in HBM */
+  uint64_t temporary_bytes;   /* scratch one step needs on top */
+  int graph_count;            /* captured CUDA graphs */
+} nd_memory;
+
+/* Open device `ordinal` (its own CUDA stream). */
+ND_API int nd_device_open(int ordinal, nd_device** out);
+ND_API int nd_device_close(nd_device* dev);
+
+/* IModelFamily.BuildDenoiser (Pipeline/IModelFamily.cs:142-143): allocate the
+ * model's resident weights and scratch for `desc`. */
+ND_API int nd_denoiser_create(nd_device* dev, const nd_model_desc* desc, nd_denoiser** out);
+
+/* Name and 2-D shape ([rows, cols]; vectors [n, 1]) of expected tensor
+ * `index` (0-based); ND_ERR_INVALID past the last. `required` is 0 for
+ * tensors that default to zero (biases). */
+ND_API int nd_denoiser_weight_info(const nd_denoiser* d, int index, const char** name,
+                                   int64_t* rows, int64_t* cols, int* required);
+
+/* Copy one tensor into HBM, converting to the storage type. `data` is host
+ * memory (set_weight) or device memory of the same device (set_weight_device);
+ * dtype ND_F32 / ND_F16 / ND_BF16. The shape must match weight_info. */
+ND_API int nd_denoiser_set_weight(nd_denoiser* d, const char* name, int dtype,
+                                  const int64_t* shape, int rank, const void* data);
+ND_API int nd_denoiser_set_weight_device(nd_denoiser* d, const char* name, int dtype,
+                                         const int64_t* shape, int rank, const void* data);
+
+/* Check every required tensor was set and prepare the step (ND_ERR_MISSING_WEIGHT). */
+ND_API int nd_denoiser_finalize(nd_denoiser* d);
+
+/* IDenoiser.Predict: latent [batch, C, H, W] fp32 host memory in, the model's
+ * prediction (same shape, fp32) out. timestep is the training-table index
+ * (UNet), sigma the noise level (flow models' time). Conditioning by name:
+ *   MMDiT: "context" [batch, rows, context_width] f32 (required);
+ *          "cos", "sin" [image tokens + rows, 64] f32 (default: the
+ *          reference's Qwen-Image rotary tables with text length = rows);
+ *          "key_length" i32 [1] (visible keys; default all).
+ * Synchronous. */
+ND_API int nd_denoiser_predict(nd_denoiser* d, const float* latent, double timestep, double sigma,
+                               int n_cond, const nd_named_tensor* cond, float* out);
+
+/* The same with latent, conditioning data and out in device memory, enqueued
+ * on `stream` (NULL: the device's own stream); returns after enqueueing. */
+ND_API int nd_denoiser_predict_device(nd_denoiser* d, const float* latent, double timestep,
+                                      double sigma, int n_cond, const nd_named_tensor* cond,
+                                      float* out, void* stream);
+
+/* Per-kernel-class timing: run `steps` eager forward passes on the last
+ * staged inputs with a CUDA event pair around every launch, and return per
+ * class (e.g. "gemm.qkv", "attention") the launches, device milliseconds,
+ * algorithmic FLOPs and bytes of ONE step (averaged over the steps). The
+ * reference's counterpart is MemoryLog's per-stage report
+ * (src/NaiveDiffusion/Dml/MemoryLog.cs:110-224) and DenoiseCommand's
+ * Stopwatch (NaiveDiffusion.Cli/DenoiseCommand.cs:139-144). */
+typedef struct nd_kernel_time {
+  const char* name;     /* static string owned by the library */
+  int launches;
+  double total_ms;
+  double flops;
+  double bytes;
+} nd_kernel_time;
+
+ND_API int nd_denoiser_profile(nd_denoiser* d, int steps, nd_kernel_time* out, int max_entries,
+                               int* n_entries);
+
+/* IDenoiser's memory figures. */
+ND_API int nd_denoiser_memory(const nd_denoiser* d, nd_memory* out);
+ND_API int nd_denoiser_destroy(nd_denoiser* d);
+
 /* ------------------------------------------------------------ GEMM op
  * y[rows, out] = x[rows, in] . W[out, in]^T (+ bias), with a fused epilogue.
  * Replaces Layers.Linear (src/NaiveDiffusion/Graph/Layers.cs:131-160) ->
@@ -85,7 +194,8 @@ typedef struct nd_linear_args {
   int64_t ldy;
   float* residual;      /* [rows, ldr] fp32 (RESIDUAL_*, STORE_F32) */
   int64_t ldr;
-  const float* gate;    /* [groups * out_features] (RESIDUAL_GATE) */
+  const float* gate;    /* [groups][gate_stride] (RESIDUAL_GATE) */
+  int64_t gate_stride;  /* 0: out_features */
   const float* qk_norm; /* [groups][2][128]: q then k norm weight (QK_NORM_ROPE) */
   const float* rope_cos; /* [rows, 64] */
   const float* rope_sin; /* [rows, 64] */

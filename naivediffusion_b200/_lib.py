@@ -48,7 +48,7 @@ class LinearArgs(C.Structure):
         ("weight", C.c_void_p), ("bias", C.c_void_p), ("group_split", C.c_int64),
         ("y", C.c_void_p), ("ldy", C.c_int64),
         ("residual", C.c_void_p), ("ldr", C.c_int64),
-        ("gate", C.c_void_p), ("qk_norm", C.c_void_p),
+        ("gate", C.c_void_p), ("gate_stride", C.c_int64), ("qk_norm", C.c_void_p),
         ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
         ("qk_cols", C.c_int64), ("eps", C.c_float),
     ]

@@ -1,0 +1,401 @@
+// The denoiser plug-in C ABI: device handles, weight upload, finalize (warm-up
+// run + CUDA-graph capture of the step), predict, memory figures.
+//
+// Replaces, from IDenoiser.Predict (Pipeline/IDenoiser.cs:10-32) down, the
+// reference's ChainDenoiser / GraphChain.Run (Graph/ChainDenoiser.cs,
+// Graph/GraphChain.cs:218-282): instead of ~200 synchronous DirectML
+// submissions per step, one captured graph of kernel launches on one stream.
+#include <algorithm>
+#include <cstring>
+#include <string>
+
+#include "denoiser.h"
+#include "nd_common.cuh"
+#include "nd_runtime.h"
+
+namespace nd {
+
+namespace {
+
+__global__ void convert_kernel(const void* __restrict__ src, int st, void* __restrict__ dst, int dt,
+                               long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float v;
+    if (st == ND_F32) v = static_cast<const float*>(src)[i];
+    else if (st == ND_F16) v = __half2float(static_cast<const __half*>(src)[i]);
+    else v = __bfloat162float(static_cast<const __nv_bfloat16*>(src)[i]);
+    if (dt == ND_F32) static_cast<float*>(dst)[i] = v;
+    else if (dt == ND_F16) static_cast<__half*>(dst)[i] = __float2half_rn(v);
+    else static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn(v);
+  }
+}
+
+int elem_bytes(int dt) { return dt == ND_F32 || dt == ND_I32 ? 4 : dt == ND_I8 ? 1 : 2; }
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int ordinal) {
+    cudaGetDevice(&prev);
+    cudaSetDevice(ordinal);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
+int convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n, cudaStream_t s) {
+  if (n <= 0) return ND_OK;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, sm_count() * 8LL));
+  convert_kernel<<<grid, 256, 0, s>>>(src, src_dtype, dst, dst_dtype, n);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+}  // namespace nd
+
+void nd_denoiser::prof_begin(cudaStream_t s) {
+  if (!profiling) return;
+  if (prof_used + 2 > prof_pool.size()) {
+    for (int i = 0; i < 64; ++i) {
+      cudaEvent_t e;
+      if (cudaEventCreate(&e) != cudaSuccess) return;
+      prof_pool.push_back(e);
+    }
+  }
+  prof_start_ev = prof_pool[prof_used++];
+  cudaEventRecord(prof_start_ev, s);
+}
+
+void nd_denoiser::prof_end(cudaStream_t s, const char* cls, double flops, double bytes) {
+  if (!profiling || !prof_start_ev) return;
+  cudaEvent_t stop = prof_pool[prof_used++];
+  cudaEventRecord(stop, s);
+  prof.push_back(ProfRecord{cls, flops, bytes, prof_start_ev, stop});
+  prof_start_ev = nullptr;
+}
+
+nd_denoiser::~nd_denoiser() {
+  for (cudaEvent_t e : prof_pool) cudaEventDestroy(e);
+  if (exec) cudaGraphExecDestroy(exec);
+  if (graph) cudaGraphDestroy(graph);
+  for (void* p : allocations) cudaFree(p);
+  for (void* p : host_allocations) cudaFreeHost(p);
+  if (staged) cudaEventDestroy(staged);
+  if (staging) cudaFree(staging);
+}
+
+void* nd_denoiser::pinned(size_t bytes) {
+  void* p = nullptr;
+  if (cudaMallocHost(&p, bytes) != cudaSuccess) {
+    alloc_failed = true;
+    return nullptr;
+  }
+  host_allocations.push_back(p);
+  return p;
+}
+
+void* nd_denoiser::alloc(size_t bytes, bool weight) {
+  void* p = nullptr;
+  bytes = (bytes + 255) & ~static_cast<size_t>(255);
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    alloc_failed = true;
+    return nullptr;
+  }
+  if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+    cudaFree(p);
+    alloc_failed = true;
+    return nullptr;
+  }
+  allocations.push_back(p);
+  (weight ? weight_bytes : work_bytes) += bytes;
+  return p;
+}
+
+void nd_denoiser::add_slot(const std::string& name, int kind, int64_t rows, int64_t cols, void* dst,
+                           bool required) {
+  nd::WeightSlot s;
+  s.name = name;
+  s.kind = kind;
+  s.rows = rows;
+  s.cols = cols;
+  s.dst = dst;
+  s.required = required;
+  index[name] = slots.size();
+  slots.push_back(s);
+}
+
+namespace {
+
+int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* shape, int rank,
+                    const void* data, bool device) {
+  using namespace nd;
+  if (!d || !name || !data) return fail(ND_ERR_INVALID, "set_weight: null argument");
+  if (d->finalized) return fail(ND_ERR_STATE, "set_weight: denoiser already finalized");
+  auto it = d->index.find(name);
+  if (it == d->index.end()) return fail(ND_ERR_INVALID, std::string("set_weight: unknown tensor ") + name);
+  WeightSlot& s = d->slots[it->second];
+  if (dtype != ND_F32 && dtype != ND_F16 && dtype != ND_BF16)
+    return fail(ND_ERR_INVALID, std::string("set_weight: ") + name + " must be f32, f16 or bf16");
+  int64_t n = 1;
+  for (int i = 0; i < rank; ++i) n *= shape[i];
+  const bool shape_ok = (rank == 2 && shape[0] == s.rows && shape[1] == s.cols) ||
+                        (rank == 1 && s.cols == 1 && shape[0] == s.rows) ||
+                        (n == s.rows * s.cols && s.kind == kVector);
+  if (!shape_ok) {
+    return fail(ND_ERR_INVALID, std::string("set_weight: ") + name + " has the wrong shape (expected [" +
+                                    std::to_string(s.rows) + ", " + std::to_string(s.cols) + "])");
+  }
+  DeviceGuard g(d->dev->ordinal);
+  cudaStream_t st = d->dev->stream;
+  const int dst_type = s.kind == kMatrix ? d->desc.compute : ND_F32;
+  const size_t src_bytes = static_cast<size_t>(n) * elem_bytes(dtype);
+  if (dtype == dst_type) {
+    ND_CUDA(cudaMemcpyAsync(s.dst, data, src_bytes, device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+  } else {
+    const void* src = data;
+    if (!device) {
+      if (d->staging_bytes < src_bytes) {
+        if (d->staging) cudaFree(d->staging);
+        d->staging = nullptr;
+        d->staging_bytes = 0;
+        ND_CUDA(cudaMalloc(&d->staging, src_bytes));
+        d->staging_bytes = src_bytes;
+      }
+      ND_CUDA(cudaMemcpyAsync(d->staging, data, src_bytes, cudaMemcpyHostToDevice, st));
+      src = d->staging;
+    }
+    int rc = convert(src, dtype, s.dst, dst_type, n, st);
+    if (rc) return rc;
+  }
+  ND_CUDA(cudaStreamSynchronize(st));
+  s.set = true;
+  return ND_OK;
+}
+
+int run_predict(nd_denoiser* d, const float* latent, double timestep, double sigma, int n_cond,
+                const nd_named_tensor* cond, float* out, bool device, cudaStream_t stream) {
+  using namespace nd;
+  if (!d || !latent || !out) return fail(ND_ERR_INVALID, "predict: null argument");
+  if (!d->finalized) return fail(ND_ERR_STATE, "predict: call nd_denoiser_finalize first");
+  if (n_cond < 0 || (n_cond > 0 && !cond)) return fail(ND_ERR_INVALID, "predict: bad conditioning list");
+  DeviceGuard g(d->dev->ordinal);
+  StepInputs in;
+  in.latent = latent;
+  in.device = device;
+  in.timestep = timestep;
+  in.sigma = sigma;
+  int rc = d->check_cond(n_cond, cond, in);
+  if (rc) return rc;
+  cudaStream_t st = stream ? stream : d->dev->stream;
+  rc = d->stage(in, st);
+  if (rc) return rc;
+  // The captured step is specialised on the visible-key count (a kernel
+  // argument): recapture when it changes.
+  if (!d->exec || d->graph_key != in.key_limit) {
+    if (d->exec) {
+      cudaGraphExecDestroy(d->exec);
+      d->exec = nullptr;
+    }
+    if (d->graph) {
+      cudaGraphDestroy(d->graph);
+      d->graph = nullptr;
+    }
+    ND_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    rc = d->forward(st);
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamEndCapture(st, &graph);
+    if (rc) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "predict: graph capture");
+    d->graph = graph;
+    ND_CUDA(cudaGraphInstantiate(&d->exec, d->graph, 0));
+    d->graph_key = in.key_limit;
+  }
+  ND_CUDA(cudaGraphLaunch(d->exec, st));
+  const size_t out_bytes = static_cast<size_t>(d->latent_elems()) * sizeof(float);
+  ND_CUDA(cudaMemcpyAsync(out, d->output(), out_bytes, device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
+  if (!device) return check_device_status(st);
+  return ND_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int nd_device_open(int ordinal, nd_device** out) {
+  if (!out) return nd::fail(ND_ERR_INVALID, "nd_device_open: null out");
+  *out = nullptr;
+  int count = 0;
+  ND_CUDA(cudaGetDeviceCount(&count));
+  if (ordinal < 0 || ordinal >= count) return nd::fail(ND_ERR_INVALID, "nd_device_open: no such device");
+  nd::DeviceGuard g(ordinal);
+  cudaDeviceProp prop;
+  ND_CUDA(cudaGetDeviceProperties(&prop, ordinal));
+  if (prop.major != 10) return nd::fail(ND_ERR_UNSUPPORTED, "nd_device_open: this library runs on sm_100 (B200) only");
+  auto* d = new nd_device();
+  d->ordinal = ordinal;
+  cudaError_t e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete d;
+    return nd::cuda_fail(e, "nd_device_open: stream");
+  }
+  if (!nd::device_status()) {
+    cudaStreamDestroy(d->stream);
+    delete d;
+    return nd::fail(ND_ERR_OOM, "nd_device_open: status word");
+  }
+  *out = d;
+  return ND_OK;
+}
+
+int nd_device_close(nd_device* dev) {
+  if (!dev) return ND_OK;
+  nd::DeviceGuard g(dev->ordinal);
+  cudaStreamSynchronize(dev->stream);
+  cudaStreamDestroy(dev->stream);
+  delete dev;
+  return ND_OK;
+}
+
+int nd_denoiser_create(nd_device* dev, const nd_model_desc* desc, nd_denoiser** out) {
+  if (!dev || !desc || !out) return nd::fail(ND_ERR_INVALID, "nd_denoiser_create: null argument");
+  *out = nullptr;
+  nd::DeviceGuard g(dev->ordinal);
+  nd_denoiser* d = nullptr;
+  switch (desc->family) {
+    case ND_FAMILY_MMDIT: d = nd::make_mmdit(); break;
+    default: return nd::fail(ND_ERR_UNSUPPORTED, "nd_denoiser_create: unknown model family");
+  }
+  d->dev = dev;
+  d->desc = *desc;
+  int rc = d->build();
+  if (rc) {
+    delete d;  // a failed build releases everything (ChainDenoiser.Build)
+    return rc;
+  }
+  *out = d;
+  return ND_OK;
+}
+
+int nd_denoiser_weight_info(const nd_denoiser* d, int index, const char** name, int64_t* rows,
+                            int64_t* cols, int* required) {
+  if (!d) return nd::fail(ND_ERR_INVALID, "weight_info: null denoiser");
+  if (index < 0 || index >= static_cast<int>(d->slots.size())) return ND_ERR_INVALID;
+  const nd::WeightSlot& s = d->slots[index];
+  if (name) *name = s.name.c_str();
+  if (rows) *rows = s.rows;
+  if (cols) *cols = s.cols;
+  if (required) *required = s.required ? 1 : 0;
+  return ND_OK;
+}
+
+int nd_denoiser_set_weight(nd_denoiser* d, const char* name, int dtype, const int64_t* shape, int rank,
+                           const void* data) {
+  return set_weight_impl(d, name, dtype, shape, rank, data, false);
+}
+
+int nd_denoiser_set_weight_device(nd_denoiser* d, const char* name, int dtype, const int64_t* shape,
+                                  int rank, const void* data) {
+  return set_weight_impl(d, name, dtype, shape, rank, data, true);
+}
+
+int nd_denoiser_finalize(nd_denoiser* d) {
+  if (!d) return nd::fail(ND_ERR_INVALID, "finalize: null denoiser");
+  if (d->finalized) return ND_OK;
+  for (const nd::WeightSlot& s : d->slots) {
+    if (s.required && !s.set) return nd::fail(ND_ERR_MISSING_WEIGHT, "finalize: weight not set: " + s.name);
+  }
+  nd::DeviceGuard g(d->dev->ordinal);
+  if (d->staging) {
+    cudaFree(d->staging);
+    d->staging = nullptr;
+    d->staging_bytes = 0;
+  }
+  int rc = d->prepare();
+  if (rc) return rc;
+  // One eager run outside capture: first-use setup (kernel attributes,
+  // status word) happens here, and a broken configuration fails loudly now.
+  rc = d->forward(d->dev->stream);
+  if (rc) return rc;
+  rc = nd::check_device_status(d->dev->stream);
+  if (rc) return rc;
+  d->finalized = true;
+  return ND_OK;
+}
+
+int nd_denoiser_predict(nd_denoiser* d, const float* latent, double timestep, double sigma, int n_cond,
+                        const nd_named_tensor* cond, float* out) {
+  return run_predict(d, latent, timestep, sigma, n_cond, cond, out, false, nullptr);
+}
+
+int nd_denoiser_predict_device(nd_denoiser* d, const float* latent, double timestep, double sigma,
+                               int n_cond, const nd_named_tensor* cond, float* out, void* stream) {
+  return run_predict(d, latent, timestep, sigma, n_cond, cond, out, true, static_cast<cudaStream_t>(stream));
+}
+
+int nd_denoiser_profile(nd_denoiser* d, int steps, nd_kernel_time* out, int max_entries,
+                        int* n_entries) {
+  if (!d || !out || !n_entries || steps <= 0 || max_entries <= 0)
+    return nd::fail(ND_ERR_INVALID, "profile: bad argument");
+  if (!d->finalized) return nd::fail(ND_ERR_STATE, "profile: call nd_denoiser_finalize first");
+  nd::DeviceGuard g(d->dev->ordinal);
+  cudaStream_t st = d->dev->stream;
+  d->prof.clear();
+  d->prof_used = 0;
+  d->profiling = true;
+  int rc = ND_OK;
+  for (int i = 0; i < steps && rc == ND_OK; ++i) rc = d->forward(st);
+  d->profiling = false;
+  if (rc) return rc;
+  rc = nd::check_device_status(st);
+  if (rc) return rc;
+  int n = 0;
+  for (const auto& r : d->prof) {
+    float ms = 0.f;
+    ND_CUDA(cudaEventElapsedTime(&ms, r.start, r.stop));
+    int k = 0;
+    while (k < n && std::strcmp(out[k].name, r.cls) != 0) ++k;
+    if (k == n) {
+      if (n == max_entries) continue;
+      out[k] = nd_kernel_time{r.cls, 0, 0.0, 0.0, 0.0};
+      ++n;
+    }
+    out[k].launches += 1;
+    out[k].total_ms += ms;
+    out[k].flops += r.flops;
+    out[k].bytes += r.bytes;
+  }
+  for (int k = 0; k < n; ++k) {
+    out[k].launches /= steps;
+    out[k].total_ms /= steps;
+    out[k].flops /= steps;
+    out[k].bytes /= steps;
+  }
+  *n_entries = n;
+  return ND_OK;
+}
+
+int nd_denoiser_memory(const nd_denoiser* d, nd_memory* out) {
+  if (!d || !out) return nd::fail(ND_ERR_INVALID, "memory: null argument");
+  out->persistent_bytes = d->weight_bytes;
+  out->streamed_bytes = 0;
+  out->resident_bytes = d->weight_bytes;
+  out->temporary_bytes = d->work_bytes;
+  out->graph_count = d->exec ? 1 : 0;
+  return ND_OK;
+}
+
+int nd_denoiser_destroy(nd_denoiser* d) {
+  if (!d) return ND_OK;
+  nd::DeviceGuard g(d->dev->ordinal);
+  cudaStreamSynchronize(d->dev->stream);
+  delete d;
+  return ND_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,101 @@
+// The denoiser plug-in's C++ side: device handles, the weight registry and
+// the per-family forward step. The C ABI in include/nd_denoise.h wraps it.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "nd_internal.h"
+
+struct nd_device {
+  int ordinal = 0;
+  cudaStream_t stream = nullptr;
+};
+
+namespace nd {
+
+enum SlotKind { kMatrix = 0, kVector = 1 };
+
+struct WeightSlot {
+  std::string name;
+  int kind = kMatrix;
+  int64_t rows = 0, cols = 1;
+  void* dst = nullptr;     // device destination (compute dtype for matrices, fp32 vectors)
+  bool required = true;
+  bool set = false;
+};
+
+// Host-side values of one predict call, already validated.
+struct StepInputs {
+  const float* latent = nullptr;   // [batch, C, H, W]
+  const float* context = nullptr;  // [batch, rows, width]
+  const float* cos = nullptr;      // optional
+  const float* sin = nullptr;
+  int key_limit = 0;               // 0: all keys
+  bool device = false;             // pointers are device memory
+  double timestep = 0, sigma = 0;
+};
+
+// Converts `n` elements of `src` (dtype) into `dst` (dst_dtype) on the device.
+int convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n, cudaStream_t s);
+
+}  // namespace nd
+
+struct nd_denoiser {
+  nd_device* dev = nullptr;
+  nd_model_desc desc{};
+  std::vector<nd::WeightSlot> slots;
+  std::unordered_map<std::string, size_t> index;
+  std::vector<void*> allocations;
+  std::vector<void*> host_allocations;
+  cudaEvent_t staged = nullptr;  // recorded after the last host->device copy of pinned inputs
+  bool alloc_failed = false;
+  uint64_t weight_bytes = 0, work_bytes = 0;
+  bool finalized = false;
+  void* staging = nullptr;
+  size_t staging_bytes = 0;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int graph_key = -1;  // key_limit the captured graph was built for
+
+  // Per-kernel-class CUDA-event timing of eager forward runs (nd_denoiser_profile).
+  struct ProfRecord {
+    const char* cls;
+    double flops, bytes;
+    cudaEvent_t start, stop;
+  };
+  bool profiling = false;
+  std::vector<ProfRecord> prof;
+  std::vector<cudaEvent_t> prof_pool;
+  size_t prof_used = 0;
+  cudaEvent_t prof_start_ev = nullptr;
+  void prof_begin(cudaStream_t s);
+  void prof_end(cudaStream_t s, const char* cls, double flops, double bytes);
+
+  virtual ~nd_denoiser();
+  // Allocate (zeroed) device memory tracked for destroy(); weights count
+  // toward weight_bytes, everything else toward work_bytes.
+  void* alloc(size_t bytes, bool weight);
+  // Pinned host memory, freed with the denoiser (nullptr + alloc_failed on failure).
+  void* pinned(size_t bytes);
+  void add_slot(const std::string& name, int kind, int64_t rows, int64_t cols, void* dst,
+                bool required = true);
+
+  virtual int build() = 0;          // allocate weights + scratch, register slots
+  virtual int prepare() { return ND_OK; }  // after every weight is set
+  // Copy this call's inputs into the model's fixed input buffers.
+  virtual int stage(const nd::StepInputs& in, cudaStream_t s) = 0;
+  // Enqueue the whole forward step on `s` (capturable: no sync, no alloc).
+  virtual int forward(cudaStream_t s) = 0;
+  virtual const float* output() const = 0;
+  virtual int64_t latent_elems() const = 0;
+  virtual int check_cond(int n, const nd_named_tensor* cond, nd::StepInputs& in) = 0;
+};
+
+namespace nd {
+nd_denoiser* make_mmdit();
+}  // namespace nd

@@ -86,7 +86,9 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
   g.bias = a.bias;
   g.bias_stride = static_cast<int>(a.out_features);
   g.gate = a.gate;
-  g.gate_stride = static_cast<int>(a.out_features);
+  g.gate_stride = static_cast<int>(a.gate_stride > 0 ? a.gate_stride : a.out_features);
+  if (a.gate && (g.gate_stride % 4 != 0 || (reinterpret_cast<uintptr_t>(a.gate) & 15u)))
+    return fail(ND_ERR_INVALID, "linear: gate must be 16-byte aligned with gate_stride % 4 == 0");
   g.qk_norm = a.qk_norm;
   g.rope_cos = a.rope_cos;
   g.rope_sin = a.rope_sin;

@@ -1,0 +1,379 @@
+"""Host-side mirror of the reference's denoiser plug-in interface.
+
+`CudaDenoiser` is what the C# `IDenoiser` (src/NaiveDiffusion/Pipeline/
+IDenoiser.cs:10-32) becomes over libnd_denoise: `predict(latent, timestep,
+sigma, conditioning)` plus the memory figures, disposable. `build_denoiser`
+plays `IModelFamily.BuildDenoiser` (Pipeline/IModelFamily.cs:142-143): it
+creates the native model, copies every (LoRA-folded) weight into HBM once and
+finalizes. The C# binding a maintainer would add is in INTEGRATION.md; this
+module calls the same C entry points through ctypes.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import zlib
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _lib
+from ._lib import check, lib
+
+FAMILY_MMDIT, FAMILY_ANIMA, FAMILY_SDXL = 0, 1, 2
+
+
+class ModelDesc(C.Structure):
+    _fields_ = [(n, C.c_int) for n in (
+        "family", "width", "heads", "head_dim", "blocks", "mlp_width",
+        "context_rows", "context_width", "latent_channels", "latent_height", "latent_width",
+        "patch", "time_width", "batch", "compute", "weight_dtype", "quant_group",
+        "quant_scale_dtype")] + [("eps", C.c_float)]
+
+
+class NamedTensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", C.c_int), ("rank", C.c_int),
+                ("shape", C.POINTER(C.c_int64)), ("data", C.c_void_p)]
+
+
+class KernelTime(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("launches", C.c_int), ("total_ms", C.c_double),
+                ("flops", C.c_double), ("bytes", C.c_double)]
+
+
+class Memory(C.Structure):
+    _fields_ = [("persistent_bytes", C.c_uint64), ("streamed_bytes", C.c_uint64),
+                ("resident_bytes", C.c_uint64), ("temporary_bytes", C.c_uint64),
+                ("graph_count", C.c_int)]
+
+
+def _bind() -> C.CDLL:
+    L = lib()
+    if getattr(L, "_nd_denoiser_bound", False):
+        return L
+    P = C.c_void_p
+    L.nd_device_open.argtypes = [C.c_int, C.POINTER(P)]
+    L.nd_device_close.argtypes = [P]
+    L.nd_denoiser_create.argtypes = [P, C.POINTER(ModelDesc), C.POINTER(P)]
+    L.nd_denoiser_weight_info.argtypes = [P, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_int64),
+                                          C.POINTER(C.c_int64), C.POINTER(C.c_int)]
+    L.nd_denoiser_set_weight.argtypes = [P, C.c_char_p, C.c_int, C.POINTER(C.c_int64), C.c_int, P]
+    L.nd_denoiser_set_weight_device.argtypes = [P, C.c_char_p, C.c_int, C.POINTER(C.c_int64), C.c_int, P]
+    L.nd_denoiser_finalize.argtypes = [P]
+    L.nd_denoiser_predict.argtypes = [P, P, C.c_double, C.c_double, C.c_int, C.POINTER(NamedTensor), P]
+    L.nd_denoiser_predict_device.argtypes = [P, P, C.c_double, C.c_double, C.c_int,
+                                             C.POINTER(NamedTensor), P, P]
+    L.nd_denoiser_memory.argtypes = [P, C.POINTER(Memory)]
+    L.nd_denoiser_profile.argtypes = [P, C.c_int, C.POINTER(KernelTime), C.c_int, C.POINTER(C.c_int)]
+    L.nd_denoiser_destroy.argtypes = [P]
+    L._nd_denoiser_bound = True
+    return L
+
+
+@dataclass
+class MMDiTConfig:
+    """A Qwen-Image-style dual-stream DiT. Defaults
+    (60 blocks x 3072, 24 x 128 heads, MLP 12288, 16 x 128 x 168 latent in 2x2
+    patches = 5376 image tokens, 256 text rows of 3584, bf16)."""
+    width: int = 3072
+    heads: int = 24
+    blocks: int = 60
+    mlp_width: int = 12288
+    context_rows: int = 256
+    context_width: int = 3584
+    latent_channels: int = 16
+    latent_height: int = 128
+    latent_width: int = 168
+    patch: int = 2
+    time_width: int = 256
+    compute: int = _lib.ND_BF16
+    eps: float = 1e-6
+
+    @property
+    def image_tokens(self) -> int:
+        return (self.latent_height // self.patch) * (self.latent_width // self.patch)
+
+    @property
+    def tokens(self) -> int:
+        return self.image_tokens + self.context_rows
+
+    def desc(self) -> ModelDesc:
+        d = ModelDesc()
+        d.family = FAMILY_MMDIT
+        d.width, d.heads, d.head_dim = self.width, self.heads, 128
+        d.blocks, d.mlp_width = self.blocks, self.mlp_width
+        d.context_rows, d.context_width = self.context_rows, self.context_width
+        d.latent_channels, d.latent_height, d.latent_width = (
+            self.latent_channels, self.latent_height, self.latent_width)
+        d.patch, d.time_width, d.batch = self.patch, self.time_width, 1
+        d.compute = d.weight_dtype = self.compute
+        d.eps = self.eps
+        return d
+
+    def flops_per_step(self) -> float:
+        """Algorithmic FLOPs of one step (1 MAC = 2 FLOP): block GEMMs, joint
+        attention (QK^T and PV), modulation GEMV, embeddings and final layer."""
+        D, F, N, ni = self.width, self.mlp_width, self.tokens, self.image_tokens
+        gemm = N * (4 * D * D + 2 * D * F)
+        attn = 2 * N * N * D
+        mod = 2 * 6 * D * D
+        per_block = gemm + attn + mod
+        cin = self.latent_channels * self.patch ** 2
+        emb = ni * cin * D + self.context_rows * self.context_width * D + ni * D * cin
+        return 2.0 * (self.blocks * per_block + emb)
+
+
+def _name_seed(name: str, seed: int) -> int:
+    return (zlib.crc32(name.encode()) ^ (seed * 0x9E3779B1)) & 0xFFFFFFFF
+
+
+def synthetic_weights(cfg: MMDiTConfig, seed: int = 0):
+    """Seeded synthetic weights in the storage precision, one generator per
+    tensor name: matrices and biases N(0, 0.02), norm weights 1 + N(0, 0.02).
+    Yields (name, float32 array already rounded to bf16/fp16)."""
+    for name, rows, cols, _req in weight_table(cfg):
+        rng = np.random.default_rng(_name_seed(name, seed))
+        a = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02)
+        if "norm" in name and name.endswith(".weight") and cols == 1:
+            a += np.float32(1.0)
+        if cols == 1:
+            a = a.reshape(rows)
+        else:
+            a = _round(a, cfg.compute)
+        yield name, a
+
+
+def synthetic_weights_device(cfg: MMDiTConfig, seed: int = 0, device="cuda"):
+    """The same distributions as synthetic_weights, drawn on the GPU (a full
+    BASELINE-size model is 20 G parameters): one torch generator per tensor
+    name. Yields (name, CUDA tensor): matrices in the compute dtype, vectors fp32."""
+    import torch
+    dt = torch.bfloat16 if cfg.compute == _lib.ND_BF16 else torch.float16
+    g = torch.Generator(device=device)
+    for name, rows, cols, _req in weight_table(cfg):
+        g.manual_seed(_name_seed(name, seed))
+        if cols == 1:
+            t = torch.randn(rows, device=device, generator=g) * 0.02
+            if "norm" in name and name.endswith(".weight"):
+                t += 1.0
+        else:
+            t = (torch.randn(rows, cols, device=device, generator=g) * 0.02).to(dt)
+        yield name, t
+
+
+def _round(a: np.ndarray, dtype: int) -> np.ndarray:
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    t = t.to(torch.bfloat16 if dtype == _lib.ND_BF16 else torch.float16).float()
+    return t.numpy()
+
+
+def weight_table(cfg: MMDiTConfig):
+    """(name, rows, cols, required) of every tensor the MMDiT family expects,
+    in the order the native registry lists them (vectors have cols == 1)."""
+    D, F, cw, tw = cfg.width, cfg.mlp_width, cfg.context_width, cfg.time_width
+    cin = cfg.latent_channels * cfg.patch ** 2
+    t = [("img_in.weight", D, cin, True), ("img_in.bias", D, 1, False),
+         ("txt_norm.weight", cw, 1, True), ("txt_in.weight", D, cw, True), ("txt_in.bias", D, 1, False),
+         ("time_text_embed.timestep_embedder.linear_1.weight", D, tw, True),
+         ("time_text_embed.timestep_embedder.linear_1.bias", D, 1, False),
+         ("time_text_embed.timestep_embedder.linear_2.weight", D, D, True),
+         ("time_text_embed.timestep_embedder.linear_2.bias", D, 1, False),
+         ("norm_out.linear.weight", 2 * D, D, True), ("norm_out.linear.bias", 2 * D, 1, False),
+         ("proj_out.weight", cin, D, True), ("proj_out.bias", cin, 1, False)]
+    mods = ["img_mod.1", "txt_mod.1"]
+    projs = [["attn.to_q", "attn.to_k", "attn.to_v"], ["attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj"]]
+    norms = [["attn.norm_q", "attn.norm_k"], ["attn.norm_added_q", "attn.norm_added_k"]]
+    outs = ["attn.to_out.0", "attn.to_add_out"]
+    ups = ["img_mlp.net.0.proj", "txt_mlp.net.0.proj"]
+    downs = ["img_mlp.net.2", "txt_mlp.net.2"]
+    for b in range(cfg.blocks):
+        p = f"transformer_blocks.{b}."
+        for s in range(2):
+            t += [(p + mods[s] + ".weight", 6 * D, D, True), (p + mods[s] + ".bias", 6 * D, 1, False)]
+            for j in range(3):
+                t += [(p + projs[s][j] + ".weight", D, D, True), (p + projs[s][j] + ".bias", D, 1, False)]
+            for j in range(2):
+                t += [(p + norms[s][j] + ".weight", 128, 1, True)]
+            t += [(p + outs[s] + ".weight", D, D, True), (p + outs[s] + ".bias", D, 1, False)]
+            t += [(p + ups[s] + ".weight", F, D, True), (p + ups[s] + ".bias", F, 1, False)]
+            t += [(p + downs[s] + ".weight", D, F, True), (p + downs[s] + ".bias", D, 1, False)]
+    return t
+
+
+class Device:
+    """One GPU (nd_device_open)."""
+
+    def __init__(self, ordinal: int = 0):
+        L = _bind()
+        h = C.c_void_p()
+        check(L.nd_device_open(ordinal, C.byref(h)))
+        self.handle = h
+        self.ordinal = ordinal
+
+    def close(self) -> None:
+        if self.handle:
+            _bind().nd_device_close(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+class CudaDenoiser:
+    """IDenoiser over libnd_denoise: Predict + the memory figures, disposable."""
+
+    def __init__(self, device: Device, desc: ModelDesc):
+        L = _bind()
+        h = C.c_void_p()
+        check(L.nd_denoiser_create(device.handle, C.byref(desc), C.byref(h)))
+        self.handle = h
+        self.device = device
+        self.desc = desc
+
+    # --- construction (IModelFamily.BuildDenoiser) ---------------------------
+    def weight_info(self):
+        L = _bind()
+        out = []
+        i = 0
+        while True:
+            name = C.c_char_p()
+            rows, cols, req = C.c_int64(), C.c_int64(), C.c_int()
+            if L.nd_denoiser_weight_info(self.handle, i, C.byref(name), C.byref(rows), C.byref(cols), C.byref(req)):
+                break
+            out.append((name.value.decode(), rows.value, cols.value, bool(req.value)))
+            i += 1
+        return out
+
+    def set_weight(self, name: str, array) -> None:
+        """Copy one tensor into HBM: a numpy array (host) or a torch CUDA tensor."""
+        L = _bind()
+        if hasattr(array, "data_ptr") and getattr(array, "is_cuda", False):
+            import torch
+            dt = {torch.float32: _lib.ND_F32, torch.float16: _lib.ND_F16, torch.bfloat16: _lib.ND_BF16}[array.dtype]
+            t = array.contiguous()
+            # The library copies on its own stream: make torch's producer finish first.
+            torch.cuda.current_stream(t.device).synchronize()
+            shape = (C.c_int64 * t.dim())(*t.shape)
+            check(L.nd_denoiser_set_weight_device(self.handle, name.encode(), dt, shape, t.dim(),
+                                                  C.c_void_p(t.data_ptr())))
+            return
+        a = np.ascontiguousarray(array)
+        dt = {np.dtype(np.float32): _lib.ND_F32, np.dtype(np.float16): _lib.ND_F16}.get(a.dtype)
+        if dt is None:
+            raise TypeError(f"{name}: unsupported dtype {a.dtype}")
+        shape = (C.c_int64 * a.ndim)(*a.shape)
+        check(L.nd_denoiser_set_weight(self.handle, name.encode(), dt, shape, a.ndim,
+                                       a.ctypes.data_as(C.c_void_p)))
+
+    def finalize(self) -> None:
+        check(_bind().nd_denoiser_finalize(self.handle))
+
+    # --- IDenoiser -------------------------------------------------------------
+    @staticmethod
+    def _cond(conditioning: dict, device: bool):
+        keep = []
+        arr = (NamedTensor * max(1, len(conditioning)))()
+        for i, (name, value) in enumerate(conditioning.items()):
+            if device:
+                import torch
+                dt = {torch.float32: _lib.ND_F32, torch.int32: _lib.ND_I32}[value.dtype]
+                shape = (C.c_int64 * value.dim())(*value.shape)
+                ptr, rank = value.data_ptr(), value.dim()
+            else:
+                a = np.ascontiguousarray(value)
+                dt = {np.dtype(np.float32): _lib.ND_F32, np.dtype(np.int32): _lib.ND_I32}[a.dtype]
+                shape = (C.c_int64 * a.ndim)(*a.shape)
+                ptr, rank = a.ctypes.data, a.ndim
+                keep.append(a)
+            keep.append(shape)
+            nm = name.encode()
+            keep.append(nm)
+            arr[i] = NamedTensor(nm, dt, rank, shape, ptr)
+        return arr, keep
+
+    def predict(self, latent: np.ndarray, timestep: float, sigma: float, conditioning: dict,
+                out: np.ndarray | None = None) -> np.ndarray:
+        """One forward step from host memory (IDenoiser.Predict); `out` may be
+        a caller-owned (e.g. pinned) float32 array of the latent's shape."""
+        lat = np.ascontiguousarray(latent, np.float32)
+        if out is None:
+            out = np.empty_like(lat)
+        elif out.shape != lat.shape or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise ValueError("out must be a contiguous float32 array shaped like the latent")
+        arr, keep = self._cond(conditioning, device=False)
+        check(_bind().nd_denoiser_predict(self.handle, lat.ctypes.data_as(C.c_void_p), timestep, sigma,
+                                          len(conditioning), arr, out.ctypes.data_as(C.c_void_p)))
+        del keep
+        return out
+
+    def predict_device(self, latent, timestep: float, sigma: float, conditioning: dict, out, stream=None):
+        """The same over torch CUDA tensors, enqueued on `stream` (cudaStream_t int or None)."""
+        arr, keep = self._cond(conditioning, device=True)
+        check(_bind().nd_denoiser_predict_device(
+            self.handle, C.c_void_p(latent.data_ptr()), timestep, sigma, len(conditioning), arr,
+            C.c_void_p(out.data_ptr()), C.c_void_p(stream or 0)))
+        del keep
+        return out
+
+    def profile(self, steps: int = 1) -> list[dict]:
+        """Per-kernel-class device time of one step (CUDA events around every
+        launch of `steps` eager runs on the last staged inputs)."""
+        arr = (KernelTime * 64)()
+        n = C.c_int()
+        check(_bind().nd_denoiser_profile(self.handle, steps, arr, 64, C.byref(n)))
+        return [dict(name=arr[i].name.decode(), launches=arr[i].launches, ms=arr[i].total_ms,
+                     flops=arr[i].flops, bytes=arr[i].bytes) for i in range(n.value)]
+
+    def memory(self) -> Memory:
+        m = Memory()
+        check(_bind().nd_denoiser_memory(self.handle, C.byref(m)))
+        return m
+
+    @property
+    def persistent_bytes(self) -> int:
+        return self.memory().persistent_bytes
+
+    @property
+    def streamed_bytes(self) -> int:
+        return self.memory().streamed_bytes
+
+    @property
+    def resident_bytes(self) -> int:
+        return self.memory().resident_bytes
+
+    @property
+    def temporary_bytes(self) -> int:
+        return self.memory().temporary_bytes
+
+    @property
+    def graph_count(self) -> int:
+        return self.memory().graph_count
+
+    def close(self) -> None:
+        if self.handle:
+            _bind().nd_denoiser_destroy(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+def build_denoiser(device: Device, cfg: MMDiTConfig, weights) -> CudaDenoiser:
+    """IModelFamily.BuildDenoiser: create, copy every weight in, finalize.
+    `weights` is an iterable of (name, array) or a dict."""
+    d = CudaDenoiser(device, cfg.desc())
+    try:
+        items = weights.items() if isinstance(weights, dict) else weights
+        for name, a in items:
+            d.set_weight(name, a)
+        d.finalize()
+    except Exception:
+        d.close()
+        raise
+    return d

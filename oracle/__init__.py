@@ -285,3 +285,68 @@ def anima_block(w: dict, x, context, temb, lora, cos, sin, heads, eps=1e-6):
                                 _p(_c(temb)), _p(_c(lora)), _p(_c(cos)), _p(_c(sin)),
                                 C.c_float(eps))
     return x
+
+
+# ------------------------------------------------------------------ models
+
+def patchify(latent, p):
+    """[C, H, W] -> [(H/p)(W/p), C p p]; feature c*p*p + m*p + n of patch (i, j)
+    is channel c at (p*i + m, p*j + n) (AnimaDit.Patchify, Models/Anima/AnimaDit.cs:193-247)."""
+    c, h, w = latent.shape
+    r, q = h // p, w // p
+    return np.ascontiguousarray(latent.reshape(c, r, p, q, p).transpose(1, 3, 0, 2, 4).reshape(r * q, c * p * p))
+
+
+def unpatchify(tokens, c, h, w, p):
+    r, q = h // p, w // p
+    return np.ascontiguousarray(tokens.reshape(r, q, c, p, p).transpose(2, 0, 3, 1, 4).reshape(c, h, w))
+
+
+def mmdit_forward(w: dict, cfg, latent, context, sigma, cos=None, sin=None, key_len=0):
+    """The dual-stream (Qwen-Image-style) denoiser step in fp32, composed from
+    the restated primitives in the order of QwenImageDit.Build / .Block
+    (Models/QwenImage/QwenImageDit.cs:309-505) with the dual-stream wiring of
+    nd_oracle_mmdit_block. latent [1, C, H, W]; context [rows, width]."""
+    D, p, eps = cfg.width, cfg.patch, cfg.eps
+    C_, Hl, Wl = cfg.latent_channels, cfg.latent_height, cfg.latent_width
+    n_img = (Hl // p) * (Wl // p)
+    if cos is None:
+        cos, sin = qwen_rope_tables(Hl // p, Wl // p, cfg.context_rows, cfg.context_rows)
+    tok = patchify(np.asarray(latent, np.float32)[0], p)
+    x_img = linear(tok, w["img_in.weight"], w.get("img_in.bias"))
+    ctxn = rmsnorm(np.asarray(context, np.float32).reshape(cfg.context_rows, cfg.context_width),
+                   w["txt_norm.weight"], eps)
+    x_txt = linear(ctxn, w["txt_in.weight"], w.get("txt_in.bias"))
+    x = np.concatenate([x_img, x_txt])
+    tsin = sinusoid(np.float32(sigma * 1000.0), cfg.time_width)
+    pre = "time_text_embed.timestep_embedder."
+    h = silu(linear(tsin[None], w[pre + "linear_1.weight"], w.get(pre + "linear_1.bias")))
+    temb = linear(h, w[pre + "linear_2.weight"], w.get(pre + "linear_2.bias"))[0]
+    z = lambda n: np.zeros(n, np.float32)  # noqa: E731
+    names = {
+        0: dict(mod="img_mod.1", q="attn.to_q", k="attn.to_k", v="attn.to_v", nq="attn.norm_q",
+                nk="attn.norm_k", out="attn.to_out.0", up="img_mlp.net.0.proj", down="img_mlp.net.2"),
+        1: dict(mod="txt_mod.1", q="attn.add_q_proj", k="attn.add_k_proj", v="attn.add_v_proj",
+                nq="attn.norm_added_q", nk="attn.norm_added_k", out="attn.to_add_out",
+                up="txt_mlp.net.0.proj", down="txt_mlp.net.2"),
+    }
+    for b in range(cfg.blocks):
+        pb = f"transformer_blocks.{b}."
+        streams = []
+        for s in range(2):
+            n = names[s]
+            g = lambda key, size: w.get(pb + n[key] + ".bias", z(size))  # noqa: E731
+            streams.append(dict(
+                mod_w=w[pb + n["mod"] + ".weight"], mod_b=g("mod", 6 * D),
+                q_w=w[pb + n["q"] + ".weight"], q_b=g("q", D),
+                k_w=w[pb + n["k"] + ".weight"], k_b=g("k", D),
+                v_w=w[pb + n["v"] + ".weight"], v_b=g("v", D),
+                norm_q=w[pb + n["nq"] + ".weight"], norm_k=w[pb + n["nk"] + ".weight"],
+                out_w=w[pb + n["out"] + ".weight"], out_b=g("out", D),
+                up_w=w[pb + n["up"] + ".weight"], up_b=g("up", cfg.mlp_width),
+                down_w=w[pb + n["down"] + ".weight"], down_b=g("down", D)))
+        x = mmdit_block(streams[0], streams[1], x, n_img, temb, cos, sin, cfg.heads, key_len, eps)
+    emb = linear(silu(temb)[None], w["norm_out.linear.weight"], w.get("norm_out.linear.bias"))[0]
+    y = modulate(x[:n_img], emb[D:], emb[:D], eps)
+    out = linear(y, w["proj_out.weight"], w.get("proj_out.bias"))
+    return unpatchify(out, C_, Hl, Wl, p)[None]

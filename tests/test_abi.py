@@ -1,0 +1,72 @@
+"""CPU checks of the C ABI boundary: the library loads without a GPU, exports
+every entry point include/nd_denoise.h declares, reports errors through
+nd_last_error, and the ctypes mirrors match the header's struct layouts."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+from naivediffusion_b200 import _lib
+from naivediffusion_b200 import denoiser as D
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "nd_denoise.h"
+
+
+def declared():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"ND_API\s+[\w\s\*]+?\b(nd_\w+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported():
+    names = declared()
+    assert len(names) >= 20
+    L = _lib.lib()
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_version_and_error_channel_without_gpu():
+    L = _lib.lib()
+    assert b"sm_100a" in L.nd_version()
+    rc = L.nd_op_linear(None, None)
+    assert rc == _lib.ND_ERR_INVALID
+    assert b"null args" in L.nd_last_error()
+
+
+def test_struct_sizes_match_header_layout():
+    # Field order and widths as declared; int64 fields are 8-byte aligned.
+    assert C.sizeof(_lib.LinearArgs) == 4 * 2 + 8 * 3 + 8 * 2 + 8 * 3 + 8 * 2 + 8 * 2 + 8 * 2 + 8 * 3 + 8 + 8
+    assert C.sizeof(D.ModelDesc) == 19 * 4
+    assert C.sizeof(D.NamedTensor) == 8 + 4 + 4 + 8 + 8
+    assert C.sizeof(D.Memory) == 4 * 8 + 8
+
+
+def test_weight_table_covers_the_checkpoint_layout():
+    cfg = D.MMDiTConfig(blocks=2)
+    t = D.weight_table(cfg)
+    names = [n for n, *_ in t]
+    assert len(names) == len(set(names)) == 13 + 2 * 32
+    assert "transformer_blocks.1.attn.add_k_proj.weight" in names
+    assert "transformer_blocks.0.txt_mlp.net.2.bias" in names
+    shapes = {n: (r, c) for n, r, c, _ in t}
+    assert shapes["transformer_blocks.0.img_mod.1.weight"] == (6 * 3072, 3072)
+    assert shapes["img_in.weight"] == (3072, 64)
+    assert shapes["txt_in.weight"] == (3072, 3584)
+
+
+def test_cfg3_algorithmic_flops():
+    # 99.9 TFLOP per step: GEMMs 76.5 + joint attention 23.4 (+ embeddings).
+    f = D.MMDiTConfig().flops_per_step()
+    assert 99.8e12 < f < 100.1e12
+
+
+def test_device_open_fails_cleanly_without_gpu():
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present")
+    except ImportError:
+        pass
+    with pytest.raises(_lib.NdError):
+        D.Device(0)
