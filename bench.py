@@ -229,9 +229,12 @@ def run_ours(args):
     lat_np, ctx_np, y = lat_h.numpy(), ctx_h.numpy(), out_h.numpy()
     den.predict(lat_np, 0.0, sigma, {"context": ctx_np}, out=y)
     barrier()
+    step_s = []
     t0 = time.perf_counter()
     for _ in range(args.steps):
+        t1 = time.perf_counter()
         den.predict(lat_np, 0.0, sigma, {"context": ctx_np}, out=y)
+        step_s.append(time.perf_counter() - t1)
     e2e_s = torch.tensor([time.perf_counter() - t0], device="cuda", dtype=torch.float64)
     if world > 1:
         dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
@@ -261,6 +264,7 @@ def run_ours(args):
                    "parallelism": f"replicas x{world} (one image per GPU)",
                    "l2": "no flush: each step streams 40.8 GB of weights, far above the 126 MB L2"},
         "e2e": {"value": e2e_value, "unit": UNIT,
+                "ms_per_step_median": statistics.median(step_s) * 1e3,
                 "h2d_bytes_per_step": int(lat_np.nbytes + ctx_np.nbytes + 4 * cfg.time_width),
                 "d2h_bytes_per_step": int(y.nbytes)},
         "gpu_launches": launches * args.steps,

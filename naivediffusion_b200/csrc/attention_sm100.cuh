@@ -270,11 +270,18 @@ __global__ void __launch_bounds__(320, 1)
           for (int i = 0; i < 32; ++i)
             if (c * 32 + i >= vis) sr[c][i] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      // Row max and (below) row sum over 8 independent partials: one serial
+      // chain over 128 values would cost ~4 cycles per element in latency.
+      float m8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m8[k] = fmaxf(__uint_as_float(sr[0][k]), __uint_as_float(sr[0][k + 8]));
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sr[c][i]));
+        for (int i = 0; i < 32; ++i)
+          if (c > 0 || i >= 16) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(sr[c][i]));
+      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       mx *= a.scale_log2;
       const float m_new = fmaxf(m, mx);
       const bool need = m_new > m + 8.0f;
@@ -293,7 +300,9 @@ __global__ void __launch_bounds__(320, 1)
         tmem_st_wait();
       }
       m = m_use;
-      float rowsum = 0.f;
+      float s8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s8[k] = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
@@ -301,11 +310,13 @@ __global__ void __launch_bounds__(320, 1)
         for (int i = 0; i < 16; ++i) {
           const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * i]), a.scale_log2, -m));
           const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * i + 1]), a.scale_log2, -m));
-          rowsum += p0 + p1;
+          s8[(2 * i) & 7] += p0;
+          s8[(2 * i + 1) & 7] += p1;
           pk[i] = a.out_f16 ? pack_f16(p0, p1) : pack_bf16(p0, p1);
         }
         tmem_st16(s_tm + c * 16, pk);
       }
+      const float rowsum = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
       l = l * factor + rowsum;
       tmem_st_wait();
       tc_fence_before();

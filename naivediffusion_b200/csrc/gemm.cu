@@ -13,8 +13,8 @@ namespace nd {
 namespace {
 
 template <int BN, int STAGES>
-int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
-                cudaStream_t stream) {
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                const GemmArgs& g, cudaStream_t stream) {
   using L = GemmSmem<BN, STAGES>;
   static bool configured[64] = {};
   int dev = 0;
@@ -28,7 +28,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
   const int num_n = (g.N + BN - 1) / BN;
   const int tiles = num_m * num_n;
   const int grid = std::min(tiles, sm_count());
-  gemm_sm100_kernel<BN, STAGES><<<grid, 192, L::kLaunchBytes, stream>>>(ta, tb, g);
+  gemm_sm100_kernel<BN, STAGES><<<grid, 192, L::kLaunchBytes, stream>>>(ta, tb, tc, g);
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }
@@ -68,8 +68,18 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
     return fail(ND_ERR_INVALID, "linear: bias/gate need out_features % 4 == 0");
 
   const int groups = split ? 2 : 1;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc;
   int rc = make_tmap_2d(&ta, a.x, 2, a.rows, a.in_features, a.ldx, 128, 64, true);
+  if (rc) return rc;
+  // The epilogue's TMA target: [32 x 32] chunks of the bf16/fp16 output
+  // (64B swizzle) or of the fp32 residual / output (128B swizzle, float add).
+  if (resid) {
+    if (reinterpret_cast<uintptr_t>(a.residual) & 15u) return fail(ND_ERR_INVALID, "linear: residual must be 16-byte aligned");
+    rc = make_tmap_2d_typed(&tc, a.residual, ND_F32, a.rows, a.out_features, a.ldr, 32, 32, 128);
+  } else {
+    if (reinterpret_cast<uintptr_t>(a.y) & 15u) return fail(ND_ERR_INVALID, "linear: y must be 16-byte aligned");
+    rc = make_tmap_2d_typed(&tc, a.y, a.dtype, a.rows, a.out_features, a.ldy, 32, 32, 64);
+  }
   if (rc) return rc;
 
   GemmArgs g{};
@@ -105,12 +115,12 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
     g.idesc = make_idesc_f16(128, 256, a.dtype == ND_BF16);
     rc = make_tmap_2d(&tb, a.weight, 2, groups * a.out_features, a.in_features, a.in_features, 256, 64, true);
     if (rc) return rc;
-    return launch_gemm<256, 4>(ta, tb, g, stream);
+    return launch_gemm<256, 4>(ta, tb, tc, g, stream);
   }
   g.idesc = make_idesc_f16(128, 128, a.dtype == ND_BF16);
   rc = make_tmap_2d(&tb, a.weight, 2, groups * a.out_features, a.in_features, a.in_features, 128, 64, true);
   if (rc) return rc;
-  return launch_gemm<128, 6>(ta, tb, g, stream);
+  return launch_gemm<128, 6>(ta, tb, tc, g, stream);
 }
 
 }  // namespace nd

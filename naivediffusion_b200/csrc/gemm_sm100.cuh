@@ -66,7 +66,10 @@ struct GemmSmem {
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTiles = STAGES * kStageBytes;
-  static constexpr int kBarOffset = kTiles;
+  // Epilogue staging: 4 warps x 2 buffers x [32 rows x 128 B] for TMA stores.
+  static constexpr int kStageBuf = 4096;
+  static constexpr int kEpiOffset = kTiles;
+  static constexpr int kBarOffset = kEpiOffset + 4 * 2 * kStageBuf;
   // full[S], empty[S], acc_full[2], acc_empty[2], drain
   static constexpr int kNumBars = 2 * STAGES + 5;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
@@ -74,28 +77,7 @@ struct GemmSmem {
   static constexpr int kLaunchBytes = kTotal + 1024;  // + alignment slack
 };
 
-__device__ __forceinline__ void store_chunk32(void* out, long long ldo, int row, int col, int N,
-                                              const float (&v)[32], int out_f16) {
-  uint32_t p[16];
-  if (out_f16) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) p[i] = pack_f16(v[2 * i], v[2 * i + 1]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) p[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
-  }
-  uint16_t* base = reinterpret_cast<uint16_t*>(out) + static_cast<long long>(row) * ldo + col;
-  if (col + 32 <= N && ((reinterpret_cast<uintptr_t>(base) & 15u) == 0)) {
-    uint4* dst = reinterpret_cast<uint4*>(base);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) dst[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      if (col + i < N) base[i] = static_cast<uint16_t>((p[i >> 1] >> ((i & 1) * 16)) & 0xFFFFu);
-    }
-  }
-}
+enum EmitKind : int { kEmitBf16 = 0, kEmitF16 = 1, kEmitF32 = 2, kEmitAddF32 = 3 };
 
 __device__ __forceinline__ void load_vec32(const float* src, int col, int N, float (&v)[32]) {
   if (src == nullptr) {
@@ -116,19 +98,65 @@ __device__ __forceinline__ void load_vec32(const float* src, int col, int N, flo
   }
 }
 
+// Stage one warp's [32 rows x 32 columns] chunk (lane = row) in shared memory
+// in the tensor map's swizzled layout and hand it to TMA: a store (bf16, fp16,
+// fp32) or an fp32 reduce-add into global memory. Rows / columns past the
+// tensor's edge are clipped by TMA. Two staging buffers per warp alternate;
+// a buffer is rewritten only after the store issued from it two chunks ago
+// has finished reading it.
+__device__ __forceinline__ void emit_chunk(const CUtensorMap* tm, int kind, uint32_t buf0, int& sb,
+                                           int lane, int row0, int rows, int col,
+                                           const float (&v)[32]) {
+  if (row0 >= rows) return;  // the whole warp's rows are past the tensor's edge
+  const uint32_t buf = buf0 + static_cast<uint32_t>(sb) * 4096u;
+  sb ^= 1;
+  if (lane == 0) bulk_wait_read<1>();
+  __syncwarp();
+  if (kind == kEmitBf16 || kind == kEmitF16) {
+    uint32_t p[16];
+    if (kind == kEmitF16) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) p[i] = pack_f16(v[2 * i], v[2 * i + 1]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) p[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+    }
+    // 64-byte rows, 64B swizzle: 16-byte chunk c of row r at c ^ ((r >> 1) & 3).
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      st_shared_v4(buf + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4), p[4 * c], p[4 * c + 1],
+                   p[4 * c + 2], p[4 * c + 3]);
+  } else {
+    // 128-byte rows, 128B swizzle: 16-byte chunk c of row r at c ^ (r & 7).
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      st_shared_v4(buf + lane * 128 + ((c ^ (lane & 7)) << 4), __float_as_uint(v[4 * c]),
+                   __float_as_uint(v[4 * c + 1]), __float_as_uint(v[4 * c + 2]),
+                   __float_as_uint(v[4 * c + 3]));
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (kind == kEmitAddF32) tma_reduce_add_2d(tm, buf, col, row0);
+    else tma_store_2d(tm, buf, col, row0);
+    bulk_commit();
+  }
+}
+
 // One 32-column chunk of a plain epilogue (everything but kEpiQkNormRope).
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int group, int row, int col,
-                                               const uint32_t (&r)[32]) {
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, const CUtensorMap* tmC, int group,
+                                               int row0, int col, const uint32_t (&r)[32],
+                                               uint32_t buf0, int& sb, int lane) {
   float v[32];
   float b[32];
   load_vec32(a.bias ? a.bias + group * a.bias_stride : nullptr, col, a.N, b);
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + b[i];
-
+  int kind = a.out_f16 ? kEmitF16 : kEmitBf16;
   switch (a.epi) {
     case kEpiGeluTanh:
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+      for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_fast(v[i]);
       break;
     case kEpiGeluErf:
 #pragma unroll
@@ -138,51 +166,38 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int group, int
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = silu(v[i]);
       break;
+    case kEpiResidualGate: {
+      float g[32];
+      load_vec32(a.gate + group * a.gate_stride, col, a.N, g);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= g[i];
+      kind = kEmitAddF32;
+      break;
+    }
+    case kEpiResidualAdd:
+      kind = kEmitAddF32;
+      break;
+    case kEpiStoreF32:
+      kind = kEmitF32;
+      break;
     default:
       break;
   }
-
-  if (a.epi == kEpiResidualGate || a.epi == kEpiResidualAdd || a.epi == kEpiStoreF32) {
-    float g[32];
-    if (a.epi == kEpiResidualGate) {
-      load_vec32(a.gate + group * a.gate_stride, col, a.N, g);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) g[i] = 1.f;
-    }
-    float* dst = a.resid + static_cast<long long>(row) * a.ldr + col;
-    const bool keep = a.epi != kEpiStoreF32;
-    if (col + 32 <= a.N) {
-      float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float4 t = keep ? d4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        t.x += g[4 * i] * v[4 * i];
-        t.y += g[4 * i + 1] * v[4 * i + 1];
-        t.z += g[4 * i + 2] * v[4 * i + 2];
-        t.w += g[4 * i + 3] * v[4 * i + 3];
-        d4[i] = t;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if (col + i < a.N) dst[i] = (keep ? dst[i] : 0.f) + g[i] * v[i];
-      }
-    }
-    return;
-  }
-  store_chunk32(a.out, a.ldo, row, col, a.N, v, a.out_f16);
+  emit_chunk(tmC, kind, buf0, sb, lane, row0, a.M, col, v);
 }
 
 // The Q/K projection epilogue for one 128-wide head: RMSNorm over the head's
 // features with the stored per-feature weight, then the rotate-half RoPE with
 // this row's angle tables -- Transformer.HeadNorm + Transformer.Rotate
 // (Graph/Transformer.cs:37-64) fused where the accumulator already sits.
-__device__ __forceinline__ void epilogue_head_norm_rope(const GemmArgs& a, int group, int row,
-                                                        int col0, uint32_t tbase, bool row_ok) {
+__device__ __forceinline__ void epilogue_head_norm_rope(const GemmArgs& a, const CUtensorMap* tmC,
+                                                        int group, int row0, int row, int col0,
+                                                        uint32_t tbase, bool row_ok, uint32_t buf0,
+                                                        int& sb, int lane) {
   const float* bias = a.bias ? a.bias + group * a.bias_stride + col0 : nullptr;
   const int which = col0 >= (a.qk_cols >> 1) ? 1 : 0;
   const float* w = a.qk_norm + (group * 2 + which) * 128;
+  const int kind = a.out_f16 ? kEmitF16 : kEmitBf16;
   uint32_t r[32];
   float sumsq = 0.f;
 #pragma unroll
@@ -191,14 +206,14 @@ __device__ __forceinline__ void epilogue_head_norm_rope(const GemmArgs& a, int g
     tmem_ld_wait();
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      float x = __uint_as_float(r[i]) + (bias ? __ldg(bias + c * 32 + i) : 0.f);
-      sumsq += x * x;
+      const float x = __uint_as_float(r[i]) + (bias ? __ldg(bias + c * 32 + i) : 0.f);
+      sumsq = fmaf(x, x, sumsq);
     }
   }
   const float scale = rsqrtf(sumsq * (1.0f / 128.0f) + a.norm_eps);
   const float* cs = a.rope_cos + static_cast<long long>(row_ok ? row : 0) * 64;
   const float* sn = a.rope_sin + static_cast<long long>(row_ok ? row : 0) * 64;
-#pragma unroll
+#pragma unroll 1
   for (int c = 0; c < 2; ++c) {
     uint32_t lo[32], hi[32];
     tmem_ld32(tbase + c * 32, lo);
@@ -206,27 +221,31 @@ __device__ __forceinline__ void epilogue_head_norm_rope(const GemmArgs& a, int g
     tmem_ld_wait();
     float olo[32], ohi[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int f = c * 32 + i;
-      float l = (__uint_as_float(lo[i]) + (bias ? __ldg(bias + f) : 0.f)) * scale * __ldg(w + f);
-      float h = (__uint_as_float(hi[i]) + (bias ? __ldg(bias + 64 + f) : 0.f)) * scale *
-                __ldg(w + 64 + f);
-      const float co = row_ok ? __ldg(cs + f) : 0.f;
-      const float si = row_ok ? __ldg(sn + f) : 0.f;
-      olo[i] = l * co - h * si;
-      ohi[i] = h * co + l * si;
+    for (int i = 0; i < 32; i += 4) {
+      const float4 co = row_ok ? __ldg(reinterpret_cast<const float4*>(cs + c * 32 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 si = row_ok ? __ldg(reinterpret_cast<const float4*>(sn + c * 32 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float cv[4] = {co.x, co.y, co.z, co.w};
+      const float sv[4] = {si.x, si.y, si.z, si.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int f = c * 32 + i + u;
+        const float l = (__uint_as_float(lo[i + u]) + (bias ? __ldg(bias + f) : 0.f)) * scale * __ldg(w + f);
+        const float h = (__uint_as_float(hi[i + u]) + (bias ? __ldg(bias + 64 + f) : 0.f)) * scale *
+                        __ldg(w + 64 + f);
+        olo[i + u] = l * cv[u] - h * sv[u];
+        ohi[i + u] = h * cv[u] + l * sv[u];
+      }
     }
-    if (row_ok) {
-      store_chunk32(a.out, a.ldo, row, col0 + c * 32, a.N, olo, a.out_f16);
-      store_chunk32(a.out, a.ldo, row, col0 + 64 + c * 32, a.N, ohi, a.out_f16);
-    }
+    emit_chunk(tmC, kind, buf0, sb, lane, row0, a.M, col0 + c * 32, olo);
+    emit_chunk(tmC, kind, buf0, sb, lane, row0, a.M, col0 + 64 + c * 32, ohi);
   }
 }
 
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
-                      const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+                      const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -265,6 +284,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), 2 * BN);
@@ -366,6 +386,8 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ epilogue
     const int ew = warp & 3;  // TMEM lane quarter this warp may read
     const int row_in_tile = ew * 32 + lane;
+    const uint32_t buf0 = sbase + L::kEpiOffset + (ew * 2) * L::kStageBuf;  // + sb * 4 KB
+    int sb = 0;
     int local = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -378,6 +400,7 @@ __global__ void __launch_bounds__(192, 1)
       const int m0 = (t % num_m) * 128;
       const int n0 = (t / num_m) * BN;
       const int group = m0 >= args.group_split ? 1 : 0;
+      const int row0 = m0 + ew * 32;
       const int row = m0 + row_in_tile;
       const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
@@ -388,18 +411,17 @@ __global__ void __launch_bounds__(192, 1)
           const int col0 = n0 + h * 128;
           if (col0 >= args.N) break;
           if (col0 < args.qk_cols) {
-            epilogue_head_norm_rope(args, group, row, col0, tbase + h * 128, row_ok);
+            epilogue_head_norm_rope(args, &tmC, group, row0, row, col0, tbase + h * 128, row_ok,
+                                    buf0, sb, lane);
           } else {
 #pragma unroll 1
             for (int c = 0; c < 4; ++c) {
               uint32_t r[32];
               tmem_ld32(tbase + h * 128 + c * 32, r);
               tmem_ld_wait();
-              if (row_ok) {
-                GemmArgs plain = args;
-                plain.epi = kEpiStore;
-                epilogue_chunk(plain, group, row, col0 + c * 32, r);
-              }
+              GemmArgs plain = args;
+              plain.epi = kEpiStore;
+              epilogue_chunk(plain, &tmC, group, row0, col0 + c * 32, r, buf0, sb, lane);
             }
           }
         }
@@ -411,13 +433,16 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t r[32];
           tmem_ld32(tbase + c * 32, r);
           tmem_ld_wait();
-          if (row_ok) epilogue_chunk(args, group, row, col, r);
+          epilogue_chunk(args, &tmC, group, row0, col, r, buf0, sb, lane);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar(acc));
     }
+    // Every store this warp handed to TMA must finish before the CTA exits.
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
   }
 
   tc_fence_before();

@@ -134,6 +134,38 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* desc, uint
       : "memory");
 }
 
+// 2-D tiled store / reduce-add from this CTA's shared memory (bulk-group
+// completion). The element type of the add comes from the tensor map.
+__device__ __forceinline__ void tma_store_2d(const void* desc, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const void* desc, uint32_t src, int c0, int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(desc)),
+      "r"(src), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N bulk groups of this thread still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
@@ -267,6 +299,22 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, for the half of the softmax exponentials the SFU
+// does not take. Range reduction by the round-to-nearest magic constant
+// 1.5 * 2^23 (x = j + f, j integer, |f| <= 1/2; j lands in the low mantissa
+// bits of x + 1.5 * 2^23), 2^f by a degree-3 polynomial whose coefficients
+// were fitted here for relative error 7.5e-5 on [-1/2, 1/2], and 2^j added to
+// the exponent field. Relative error <= 1.5e-4 on [-126, 8]; x < -126 gives 0.
+__device__ __forceinline__ float poly_exp2(float x) {
+  const float xc = fmaxf(x, -126.0f);
+  const float t = xc + 12582912.0f;
+  const float j = t - 12582912.0f;
+  const float f = xc - j;
+  const float p = fmaf(fmaf(fmaf(0.0551716648f, f, 0.2426111400f), f, 0.6932609677f), f, 0.9999280572f);
+  const float r = __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+  return x < -126.0f ? 0.0f : r;
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -295,6 +343,20 @@ __device__ __forceinline__ float gelu_erf(float x) {
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+// tanh on the SFU (tanh.approx.f32, relative error ~2^-11: below bf16's).
+__device__ __forceinline__ float fast_tanh(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// GELU-tanh with the SFU tanh, for bf16/fp16 outputs:
+// 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
+__device__ __forceinline__ float gelu_tanh_fast(float x) {
+  const float u = 0.7978845608f * fmaf(0.044715f * x, x * x, x);
+  return 0.5f * x * (1.0f + fast_tanh(u));
+}
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);

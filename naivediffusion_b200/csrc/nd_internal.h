@@ -33,6 +33,10 @@ int sm_count();
 // 128-byte swizzle (box_cols * elem_bytes must be 128) or none.
 int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, int64_t rows, int64_t cols,
                  int64_t ld, int box_rows, int box_cols, bool swizzle128);
+// Same with an explicit element type (ND_F32 for a float reduce-add) and
+// swizzle span in bytes (0, 32, 64 or 128).
+int make_tmap_2d_typed(CUtensorMap* map, const void* base, int nd_dtype, int64_t rows, int64_t cols,
+                       int64_t ld, int box_rows, int box_cols, int swizzle_bytes);
 
 // ----------------------------------------------------------------- kernels
 

@@ -31,11 +31,11 @@ __device__ __forceinline__ void store4(void* out, long long idx, float4 v, int o
   }
 }
 
-// One warp per row; V float4 per lane hold the row (width <= 128 * V).
-// y = LN(x) * (1 + scale[g]) + shift[g] (Transformer.Modulate,
-// Graph/Transformer.cs:72-80), stats in fp32 over the row held in registers
-// (mean first, then the centred second moment: the two-pass form of
-// CpuMath.LayerNorm, Tensors/CpuMath.cs:100-115).
+// 128 threads (4 warps) per row, two rows per 256-thread block; V float4 per
+// thread hold the row (width <= 512 * V). y = LN(x) * (1 + scale[g]) + shift[g]
+// (Transformer.Modulate, Graph/Transformer.cs:72-80), statistics in fp32 over
+// the row held in registers: the mean first, then the centred second moment
+// (the two-pass form of CpuMath.LayerNorm, Tensors/CpuMath.cs:100-115).
 template <int V>
 __global__ void __launch_bounds__(256) modulate_kernel(const float* __restrict__ x, long long ldx,
                                                        void* __restrict__ y, long long ldy,
@@ -43,36 +43,48 @@ __global__ void __launch_bounds__(256) modulate_kernel(const float* __restrict__
                                                        const float* __restrict__ shift,
                                                        const float* __restrict__ scale,
                                                        int vec_stride, int split, float eps) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  __shared__ float red[2][2][4];
+  const int half = threadIdx.x >> 7;        // which of the block's two rows
+  const int t = threadIdx.x & 127;
+  const int w = t >> 5;
   const int lane = threadIdx.x & 31;
-  if (warp >= rows) return;
+  const int row = blockIdx.x * 2 + half;
+  const bool live = row < rows;
   const int w4 = width >> 2;
-  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(warp) * ldx);
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(live ? row : 0) * ldx);
   float4 v[V];
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < V; ++i) {
-    const int c = lane + 32 * i;
-    v[i] = c < w4 ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const int c = t + 128 * i;
+    v[i] = (live && c < w4) ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
   }
-  const float mean = warp_sum(s) / width;
+  s = warp_sum(s);
+  if (lane == 0) red[half][0][w] = s;
+  __syncthreads();
+  const float mean = (red[half][0][0] + red[half][0][1] + red[half][0][2] + red[half][0][3]) / width;
   float q = 0.f;
 #pragma unroll
   for (int i = 0; i < V; ++i) {
-    const int c = lane + 32 * i;
+    const int c = t + 128 * i;
     if (c < w4) {
       const float a = v[i].x - mean, b = v[i].y - mean, cc = v[i].z - mean, d = v[i].w - mean;
       q += (a * a + b * b) + (cc * cc + d * d);
     }
   }
-  const float rstd = rsqrtf(warp_sum(q) / width + eps);
-  const int g = warp >= split ? 1 : 0;
+  q = warp_sum(q);
+  if (lane == 0) red[half][1][w] = q;
+  __syncthreads();
+  if (!live) return;
+  const float var = (red[half][1][0] + red[half][1][1] + red[half][1][2] + red[half][1][3]) / width;
+  const float rstd = rsqrtf(var + eps);
+  const int g = row >= split ? 1 : 0;
   const float4* sc = reinterpret_cast<const float4*>(scale + g * vec_stride);
   const float4* sh = shift ? reinterpret_cast<const float4*>(shift + g * vec_stride) : nullptr;
 #pragma unroll
   for (int i = 0; i < V; ++i) {
-    const int c = lane + 32 * i;
+    const int c = t + 128 * i;
     if (c < w4) {
       const float4 k = __ldg(sc + c);
       const float4 b = sh ? __ldg(sh + c) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -81,7 +93,7 @@ __global__ void __launch_bounds__(256) modulate_kernel(const float* __restrict__
       o.y = (v[i].y - mean) * rstd * (1.f + k.y) + b.y;
       o.z = (v[i].z - mean) * rstd * (1.f + k.z) + b.z;
       o.w = (v[i].w - mean) * rstd * (1.f + k.w) + b.w;
-      store4(y, static_cast<long long>(warp) * ldy + 4 * c, o, out_type);
+      store4(y, static_cast<long long>(row) * ldy + 4 * c, o, out_type);
     }
   }
 }
@@ -263,21 +275,18 @@ int modulate(const nd_modulate_args& a, cudaStream_t stream) {
   if (a.width % 4 || a.ldx % 4 || a.ldy % 4) return fail(ND_ERR_INVALID, "modulate: width and strides must be multiples of 4");
   if (!a.x || !a.y || !a.scale) return fail(ND_ERR_INVALID, "modulate: null operand");
   if (a.rows > INT_MAX) return fail(ND_ERR_INVALID, "modulate: too many rows");
-  const int bucket = pick_bucket(static_cast<int>(a.width));
-  if (!bucket) return fail(ND_ERR_UNSUPPORTED, "modulate: width above 4096");
+  if (a.width > 4096) return fail(ND_ERR_UNSUPPORTED, "modulate: width above 4096");
   const int rows = static_cast<int>(a.rows);
   const int split = a.group_split < a.rows ? static_cast<int>(a.group_split) : INT_MAX;
   const int vs = a.vec_stride ? static_cast<int>(a.vec_stride) : static_cast<int>(a.width);
-  const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+  const unsigned grid = static_cast<unsigned>((rows + 1) / 2);
+  const int per_thread = (static_cast<int>(a.width) / 4 + 127) / 128;
 #define ND_MOD(V) modulate_kernel<V><<<grid, 256, 0, stream>>>(a.x, a.ldx, a.y, a.ldy, a.out_dtype, rows, static_cast<int>(a.width), a.shift, a.scale, vs, split, a.eps)
-  switch (bucket) {
-    case 2: ND_MOD(2); break;
-    case 4: ND_MOD(4); break;
-    case 8: ND_MOD(8); break;
-    case 16: ND_MOD(16); break;
-    case 24: ND_MOD(24); break;
-    default: ND_MOD(32); break;
-  }
+  if (per_thread <= 1) ND_MOD(1);
+  else if (per_thread <= 2) ND_MOD(2);
+  else if (per_thread <= 4) ND_MOD(4);
+  else if (per_thread <= 6) ND_MOD(6);
+  else ND_MOD(8);
 #undef ND_MOD
   ND_CUDA(cudaGetLastError());
   return ND_OK;

@@ -86,6 +86,42 @@ int check_device_status(cudaStream_t stream) {
   return ND_OK;
 }
 
+int make_tmap_2d_typed(CUtensorMap* map, const void* base, int nd_dtype, int64_t rows, int64_t cols,
+                       int64_t ld, int box_rows, int box_cols, int swizzle_bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(ND_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const int elem_bytes = nd_dtype == ND_F32 || nd_dtype == ND_I32 ? 4 : nd_dtype == ND_I8 ? 1 : 2;
+  if (reinterpret_cast<uintptr_t>(base) & 15u) return fail(ND_ERR_INVALID, "TMA base must be 16-byte aligned");
+  if ((ld * elem_bytes) % 16 != 0) return fail(ND_ERR_INVALID, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMapDataType dt;
+  switch (nd_dtype) {
+    case ND_F32: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32; break;
+    case ND_F16: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; break;
+    case ND_BF16: dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; break;
+    case ND_I32: dt = CU_TENSOR_MAP_DATA_TYPE_INT32; break;
+    default: dt = CU_TENSOR_MAP_DATA_TYPE_UINT8; break;
+  }
+  CUtensorMapSwizzle sw = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                          : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                : CU_TENSOR_MAP_SWIZZLE_NONE;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * elem_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[192];
+    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld ld=%lld box=%dx%d",
+             static_cast<int>(r), static_cast<long long>(rows), static_cast<long long>(cols),
+             static_cast<long long>(ld), box_rows, box_cols);
+    return fail(ND_ERR_INVALID, buf);
+  }
+  return ND_OK;
+}
+
 int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, int64_t rows, int64_t cols,
                  int64_t ld, int box_rows, int box_cols, bool swizzle128) {
   EncodeTiledFn fn = encode_fn();
