@@ -201,6 +201,16 @@ typedef struct nd_linear_args {
   const float* rope_sin; /* [rows, 64] */
   int64_t qk_cols;      /* leading columns that are q then k (2 * width) */
   float eps;            /* RMSNorm epsilon */
+  /* int8 weight-only (BlockQuantizer scheme, Tensors/BlockQuantizer.cs:34-105):
+   * weight_dtype ND_I8 makes `weight` int8 [groups * out, in] and widens
+   * w = q * scale inside the GEMM; scales [groups * out, in / quant_group]
+   * (quant_group 32: the reference's blocks) or [groups * out] (quant_group 0:
+   * per output channel), dtype scale_dtype (ND_F16 or ND_F32).
+   * weight_dtype 0 (or == dtype): weights are already bf16 / fp16. */
+  int weight_dtype;
+  const void* scales;
+  int scale_dtype;
+  int64_t quant_group;
 } nd_linear_args;
 
 /* Device pointers; stream is a cudaStream_t (NULL = legacy default stream).
@@ -284,6 +294,14 @@ ND_API int nd_op_patchify(const float* latent, void* tokens, int out_dtype, int 
                           void* stream);
 ND_API int nd_op_unpatchify(const float* tokens, int64_t ldt, float* latent, int batch,
                             int channels, int height, int width, int patch, void* stream);
+
+/* Widen int8 weights: out[r, c] = round(q[r, c] * scale(r, c)) in out_dtype
+ * (ND_BF16 or ND_F16), scale as in nd_linear_args (quant_group 32 or 0). The
+ * same arithmetic the int8 GEMM applies to its tiles (DmlOps.Dequantize,
+ * src/NaiveDiffusion/Dml/DmlOps.cs:208-228). */
+ND_API int nd_op_dequantize(const int8_t* q, const void* scales, int scale_dtype,
+                            int64_t quant_group, int64_t rows, int64_t cols, void* out,
+                            int out_dtype, void* stream);
 
 /* Synchronize `stream` and report any kernel's timed-out wait (ND_ERR_TIMEOUT)
  * or CUDA fault (ND_ERR_CUDA) since the last check on this device. */

@@ -51,6 +51,8 @@ class LinearArgs(C.Structure):
         ("gate", C.c_void_p), ("gate_stride", C.c_int64), ("qk_norm", C.c_void_p),
         ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
         ("qk_cols", C.c_int64), ("eps", C.c_float),
+        ("weight_dtype", C.c_int), ("scales", C.c_void_p), ("scale_dtype", C.c_int),
+        ("quant_group", C.c_int64),
     ]
 
 
@@ -106,6 +108,8 @@ def lib() -> C.CDLL:
         L.nd_version.restype = C.c_char_p
         L.nd_op_linear.argtypes = [C.POINTER(LinearArgs), C.c_void_p]
         L.nd_op_sync.argtypes = [C.c_void_p]
+        L.nd_op_dequantize.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int64,
+                                       C.c_int64, C.c_void_p, C.c_int, C.c_void_p]
         L.nd_op_attention.argtypes = [C.POINTER(AttentionArgs), C.c_void_p]
         L.nd_op_modulate.argtypes = [C.POINTER(ModulateArgs), C.c_void_p]
         L.nd_op_rmsnorm.argtypes = [C.POINTER(RmsNormArgs), C.c_void_p]

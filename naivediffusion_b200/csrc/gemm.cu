@@ -2,9 +2,11 @@
 // choice and launch. The kernel itself is in gemm_sm100.cuh.
 #include <algorithm>
 #include <climits>
+#include <cmath>
 #include <string>
 
 #include "gemm_sm100.cuh"
+#include "gemm_w8_sm100.cuh"
 #include "nd_internal.h"
 #include "nd_runtime.h"
 
@@ -33,6 +35,25 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   return ND_OK;
 }
 
+template <int BN, int STAGES>
+int launch_gemm_w8(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& tc,
+                   const GemmArgs& g, cudaStream_t stream) {
+  using L = GemmW8Smem<BN, STAGES>;
+  static bool configured[64] = {};
+  int dev = 0;
+  ND_CUDA(cudaGetDevice(&dev));
+  if (!configured[dev & 63]) {
+    ND_CUDA(cudaFuncSetAttribute(gemm_w8_sm100_kernel<BN, STAGES>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, L::kLaunchBytes));
+    configured[dev & 63] = true;
+  }
+  const int tiles = ((g.M + 127) / 128) * ((g.N + BN - 1) / BN);
+  const int grid = std::min(tiles, sm_count());
+  gemm_w8_sm100_kernel<BN, STAGES><<<grid, 384, L::kLaunchBytes, stream>>>(ta, tw, tc, g);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
 }  // namespace
 
 int linear(const nd_linear_args& a, cudaStream_t stream) {
@@ -42,6 +63,17 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
   if (a.rows > INT_MAX || a.in_features > INT_MAX || a.out_features > INT_MAX / 2)
     return fail(ND_ERR_INVALID, "linear: shape too large");
   if (a.in_features % 8 != 0) return fail(ND_ERR_INVALID, "linear: in_features must be a multiple of 8");
+  const bool w8 = a.weight_dtype == ND_I8;
+  if (a.weight_dtype != 0 && !w8 && a.weight_dtype != a.dtype)
+    return fail(ND_ERR_INVALID, "linear: weight_dtype must be 0, the activation dtype or ND_I8");
+  if (w8) {
+    if (a.in_features % 16 != 0) return fail(ND_ERR_INVALID, "linear: int8 weights need in_features % 16 == 0");
+    if (!a.scales) return fail(ND_ERR_INVALID, "linear: int8 weights need scales");
+    if (a.scale_dtype != ND_F16 && a.scale_dtype != ND_F32)
+      return fail(ND_ERR_INVALID, "linear: scale_dtype must be ND_F16 or ND_F32");
+    if (a.quant_group < 0 || (a.quant_group > 0 && a.in_features % a.quant_group != 0))
+      return fail(ND_ERR_INVALID, "linear: quant_group must divide in_features (or be 0: per channel)");
+  }
   if (a.ldx < a.in_features || a.ldx % 8 != 0) return fail(ND_ERR_INVALID, "linear: ldx must be >= in_features and a multiple of 8");
   if (!a.x || !a.weight) return fail(ND_ERR_INVALID, "linear: null operand");
   const bool split = a.group_split < a.rows;
@@ -107,20 +139,50 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
   g.norm_eps = a.eps;
   g.status = device_status();
   if (!g.status) return fail(ND_ERR_CUDA, "linear: no device status word");
-
-  // Wide tiles when the output is wide enough to fill the machine with them.
-  const int64_t tiles256 = ((a.rows + 127) / 128) * ((a.out_features + 255) / 256);
-  const bool wide = epi == ND_EPI_QK_NORM_ROPE || (a.out_features >= 256 && tiles256 >= sm_count());
-  if (wide) {
-    g.idesc = make_idesc_f16(128, 256, a.dtype == ND_BF16);
-    rc = make_tmap_2d(&tb, a.weight, 2, groups * a.out_features, a.in_features, a.in_features, 256, 64, true);
-    if (rc) return rc;
-    return launch_gemm<256, 4>(ta, tb, tc, g, stream);
+  if (w8) {
+    const int64_t group = a.quant_group > 0 ? a.quant_group : a.in_features;
+    g.w8_scales = a.scales;
+    g.w8_group = static_cast<int>(group);
+    g.w8_scale_cols = static_cast<int>(a.in_features / group);
+    g.w8_scale_f16 = a.scale_dtype == ND_F16;
   }
-  g.idesc = make_idesc_f16(128, 128, a.dtype == ND_BF16);
-  rc = make_tmap_2d(&tb, a.weight, 2, groups * a.out_features, a.in_features, a.in_features, 128, 64, true);
+
+  // Tile width: 256 unless the grid of 256-wide tiles leaves most SMs idle
+  // (narrow outputs, few rows); then 128. (A 192-wide variant filled the last
+  // wave better at N = 3072 but measured slower per tile on B200.)
+  const int sms = sm_count();
+  const int64_t tiles256 = ((a.rows + 127) / 128) * ((a.out_features + 255) / 256);
+  const int bn = (epi == ND_EPI_QK_NORM_ROPE || (a.out_features >= 256 && tiles256 >= sms)) ? 256 : 128;
+  g.idesc = make_idesc_f16(128, bn, a.dtype == ND_BF16);
+  if (w8) {
+    // Raw int8 tiles [bn rows x 64 bytes], unswizzled (the converters swizzle).
+    rc = make_tmap_2d_typed(&tb, a.weight, ND_I8, groups * a.out_features, a.in_features, a.in_features,
+                            bn, 64, 0);
+    if (rc) return rc;
+    if (bn == 256) return launch_gemm_w8<256, 3>(ta, tb, tc, g, stream);
+    return launch_gemm_w8<128, 4>(ta, tb, tc, g, stream);
+  }
+  rc = make_tmap_2d(&tb, a.weight, 2, groups * a.out_features, a.in_features, a.in_features, bn, 64, true);
   if (rc) return rc;
+  if (bn == 256) return launch_gemm<256, 4>(ta, tb, tc, g, stream);
   return launch_gemm<128, 6>(ta, tb, tc, g, stream);
+}
+
+int dequantize(const int8_t* q, const void* scales, int scale_dtype, int64_t quant_group, int64_t rows,
+               int64_t cols, void* out, int out_dtype, cudaStream_t stream) {
+  if (!q || !scales || !out) return fail(ND_ERR_INVALID, "dequantize: null operand");
+  if (rows <= 0 || cols <= 0 || cols > INT_MAX) return fail(ND_ERR_INVALID, "dequantize: bad shape");
+  if (scale_dtype != ND_F16 && scale_dtype != ND_F32) return fail(ND_ERR_INVALID, "dequantize: scale_dtype");
+  if (out_dtype != ND_BF16 && out_dtype != ND_F16) return fail(ND_ERR_INVALID, "dequantize: out_dtype");
+  const int64_t group = quant_group > 0 ? quant_group : cols;
+  if (cols % group) return fail(ND_ERR_INVALID, "dequantize: quant_group must divide cols");
+  const long long total = rows * cols;
+  const unsigned grid = static_cast<unsigned>(std::min<long long>((total + 255) / 256, sm_count() * 16LL));
+  dequant_w8_kernel<<<grid, 256, 0, stream>>>(q, scales, scale_dtype == ND_F16, static_cast<int>(group),
+                                              static_cast<int>(cols / group), rows, static_cast<int>(cols),
+                                              out, out_dtype == ND_F16);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
 }
 
 }  // namespace nd

@@ -56,6 +56,12 @@ struct GemmArgs {
   float norm_eps;
   uint32_t idesc;
   unsigned* status;
+  // int8 weight-only (gemm_w8_sm100_kernel): scale of weight (n, k) is
+  // w8_scales[n * w8_scale_cols + k / w8_group] (fp16 or fp32).
+  const void* w8_scales;
+  int w8_group;
+  int w8_scale_cols;
+  int w8_scale_f16;
 };
 
 template <int BN, int STAGES>
@@ -75,6 +81,8 @@ struct GemmSmem {
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
   static constexpr int kTotal = kMiscOffset + 16;
   static constexpr int kLaunchBytes = kTotal + 1024;  // + alignment slack
+  // TMEM: two accumulators of BN fp32 columns, allocated as a power of two.
+  static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
 };
 
 enum EmitKind : int { kEmitBf16 = 0, kEmitF16 = 1, kEmitF32 = 2, kEmitAddF32 = 3 };
@@ -287,7 +295,7 @@ __global__ void __launch_bounds__(192, 1)
     tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 2 * BN);
+    tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -448,7 +456,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, 2 * BN);
+  if (warp == 1) tmem_dealloc(tmem_base, L::kTmemCols);
 }
 
 }  // namespace nd

@@ -41,6 +41,8 @@ int make_tmap_2d_typed(CUtensorMap* map, const void* base, int nd_dtype, int64_t
 // ----------------------------------------------------------------- kernels
 
 int linear(const nd_linear_args& a, cudaStream_t stream);
+int dequantize(const int8_t* q, const void* scales, int scale_dtype, int64_t quant_group, int64_t rows,
+               int64_t cols, void* out, int out_dtype, cudaStream_t stream);
 int attention(const nd_attention_args& a, cudaStream_t stream);
 int modulate(const nd_modulate_args& a, cudaStream_t stream);
 int rmsnorm(const nd_rmsnorm_args& a, cudaStream_t stream);

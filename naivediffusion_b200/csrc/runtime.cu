@@ -194,6 +194,12 @@ int nd_op_unpatchify(const float* tokens, int64_t ldt, float* latent, int batch,
                         static_cast<cudaStream_t>(stream));
 }
 
+int nd_op_dequantize(const int8_t* q, const void* scales, int scale_dtype, int64_t quant_group,
+                     int64_t rows, int64_t cols, void* out, int out_dtype, void* stream) {
+  return nd::dequantize(q, scales, scale_dtype, quant_group, rows, cols, out, out_dtype,
+                        static_cast<cudaStream_t>(stream));
+}
+
 int nd_op_sync(void* stream) { return nd::check_device_status(static_cast<cudaStream_t>(stream)); }
 
 }  // extern "C"

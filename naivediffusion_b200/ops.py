@@ -36,11 +36,14 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
            residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
            group_split: int | None = None, qk_norm: torch.Tensor | None = None,
            rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
-           qk_cols: int = 0, eps: float = 1e-6) -> torch.Tensor:
+           qk_cols: int = 0, eps: float = 1e-6, scales: torch.Tensor | None = None,
+           quant_group: int = 32) -> torch.Tensor:
     """y = x . W^T + bias with a fused epilogue (Layers.Linear, Graph/Layers.cs:131-160).
 
     weight is [groups * out, in]; rows >= group_split use the second group.
     Residual epilogues update `residual` (fp32) in place and return it.
+    An int8 weight (with `scales`, fp16 or fp32, `quant_group` 32 or 0 = per
+    output channel) is widened inside the GEMM (BlockQuantizer's scheme).
     """
     rows, k = x.shape
     groups = 1 if group_split is None or group_split >= rows else 2
@@ -69,6 +72,11 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     a.rope_sin = _ptr(rope_sin)
     a.qk_cols = qk_cols
     a.eps = eps
+    if weight.dtype == torch.int8:
+        a.weight_dtype = _lib.ND_I8
+        a.scales = scales.data_ptr()
+        a.scale_dtype = _DT[scales.dtype]
+        a.quant_group = quant_group
     check(lib().nd_op_linear(C.byref(a), C.c_void_p(_stream())))
     return residual if resid_epi else out
 
@@ -165,3 +173,13 @@ def unpatchify(tokens: torch.Tensor, shape, patch: int) -> torch.Tensor:
     check(lib().nd_op_unpatchify(tokens.data_ptr(), tokens.stride(0), lat.data_ptr(), b, c, h, w,
                                  patch, C.c_void_p(_stream())))
     return lat
+
+
+def dequantize(q: torch.Tensor, scales: torch.Tensor, quant_group: int = 32,
+               out_dtype=torch.bfloat16) -> torch.Tensor:
+    """w = round(q * scale) in out_dtype (DmlOps.Dequantize, Dml/DmlOps.cs:208-228)."""
+    rows, cols = q.shape
+    out = torch.empty(rows, cols, device=q.device, dtype=out_dtype)
+    check(lib().nd_op_dequantize(q.data_ptr(), scales.data_ptr(), _DT[scales.dtype], quant_group, rows,
+                                 cols, out.data_ptr(), _DT[out_dtype], C.c_void_p(_stream())))
+    return out

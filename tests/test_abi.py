@@ -34,12 +34,25 @@ def test_version_and_error_channel_without_gpu():
     assert b"null args" in L.nd_last_error()
 
 
-def test_struct_sizes_match_header_layout():
-    # Field order and widths as declared; int64 fields are 8-byte aligned.
-    assert C.sizeof(_lib.LinearArgs) == 4 * 2 + 8 * 3 + 8 * 2 + 8 * 3 + 8 * 2 + 8 * 2 + 8 * 2 + 8 * 3 + 8 + 8
-    assert C.sizeof(D.ModelDesc) == 19 * 4
-    assert C.sizeof(D.NamedTensor) == 8 + 4 + 4 + 8 + 8
-    assert C.sizeof(D.Memory) == 4 * 8 + 8
+def test_struct_layouts_match_the_header(tmp_path):
+    """ctypes mirrors vs the C compiler's view of include/nd_denoise.h."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if not cc:
+        pytest.skip("no C compiler")
+    structs = {"nd_linear_args": _lib.LinearArgs, "nd_attention_args": _lib.AttentionArgs,
+               "nd_modulate_args": _lib.ModulateArgs, "nd_rmsnorm_args": _lib.RmsNormArgs,
+               "nd_gemv_args": _lib.GemvArgs, "nd_model_desc": D.ModelDesc,
+               "nd_named_tensor": D.NamedTensor, "nd_memory": D.Memory, "nd_kernel_time": D.KernelTime}
+    src = tmp_path / "sizes.c"
+    src.write_text('#include <stdio.h>\n#include "nd_denoise.h"\nint main(void){\n' + "".join(
+        f'printf("%zu\\n", sizeof({n}));\n' for n in structs) + "return 0;}\n")
+    exe = tmp_path / "sizes"
+    subprocess.run([cc, "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    sizes = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    for (name, cls), size in zip(structs.items(), sizes):
+        assert C.sizeof(cls) == size, name
 
 
 def test_weight_table_covers_the_checkpoint_layout():
