@@ -122,6 +122,23 @@ ND_API int nd_denoiser_set_weight(nd_denoiser* d, const char* name, int dtype,
 ND_API int nd_denoiser_set_weight_device(nd_denoiser* d, const char* name, int dtype,
                                          const int64_t* shape, int rank, const void* data);
 
+/* A matrix already quantized on the host by BlockQuantizer
+ * (Tensors/BlockQuantizer.cs:34-105): q int8 [rows, cols] and scales
+ * [rows, cols / quant_group] (quant_group 32, scale_dtype ND_F16: the
+ * reference's blocks) or [rows] (quant_group 0, ND_F32: per output channel),
+ * host memory. Only for a model created with weight_dtype ND_I8, whose group
+ * and scale type must match. Matrices given through set_weight instead are
+ * quantized on the device by the same rules, bit for bit. */
+ND_API int nd_denoiser_set_weight_q8(nd_denoiser* d, const char* name, const int64_t* shape, int rank,
+                                     const int8_t* q, int scale_dtype, const void* scales,
+                                     int64_t quant_group);
+
+/* Quantize a matrix on the device (the same rules): src [rows, cols] f32 /
+ * f16 / bf16 device memory -> q int8 [rows, cols] and scales. */
+ND_API int nd_op_quantize(const void* src, int src_dtype, int64_t rows, int64_t cols,
+                          int64_t quant_group, int scale_dtype, int8_t* q, void* scales,
+                          void* stream);
+
 /* Check every required tensor was set and prepare the step (ND_ERR_MISSING_WEIGHT). */
 ND_API int nd_denoiser_finalize(nd_denoiser* d);
 
@@ -276,11 +293,12 @@ ND_API int nd_op_rmsnorm(const nd_rmsnorm_args* args, void* stream);
  * x and y fp32, batch 1..4. pre_silu applies SiLU to x first; act 0 none,
  * 1 SiLU, 2 tanh. The modulation vectors (Layers.Linear over 1-2 rows). */
 typedef struct nd_gemv_args {
-  const void* w; int w_dtype;
+  const void* w; int w_dtype;   /* ND_BF16 / ND_F16, or ND_I8 with scales */
   int64_t n, k;
   const float* x; int batch; int pre_silu;
   const float* bias; int act;
   float* y;
+  const void* scales; int scale_dtype; int64_t quant_group;  /* int8 weights only */
 } nd_gemv_args;
 
 ND_API int nd_op_gemv(const nd_gemv_args* args, void* stream);

@@ -91,6 +91,7 @@ class GemvArgs(C.Structure):
         ("w", C.c_void_p), ("w_dtype", C.c_int), ("n", C.c_int64), ("k", C.c_int64),
         ("x", C.c_void_p), ("batch", C.c_int), ("pre_silu", C.c_int),
         ("bias", C.c_void_p), ("act", C.c_int), ("y", C.c_void_p),
+        ("scales", C.c_void_p), ("scale_dtype", C.c_int), ("quant_group", C.c_int64),
     ]
 
 
@@ -108,6 +109,8 @@ def lib() -> C.CDLL:
         L.nd_version.restype = C.c_char_p
         L.nd_op_linear.argtypes = [C.POINTER(LinearArgs), C.c_void_p]
         L.nd_op_sync.argtypes = [C.c_void_p]
+        L.nd_op_quantize.argtypes = [C.c_void_p, C.c_int, C.c_int64, C.c_int64, C.c_int64, C.c_int,
+                                     C.c_void_p, C.c_void_p, C.c_void_p]
         L.nd_op_dequantize.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int64,
                                        C.c_int64, C.c_void_p, C.c_int, C.c_void_p]
         L.nd_op_attention.argtypes = [C.POINTER(AttentionArgs), C.c_void_p]

@@ -114,14 +114,29 @@ void* nd_denoiser::alloc(size_t bytes, bool weight) {
   return p;
 }
 
+nd::Mat nd_denoiser::alloc_mat(int64_t rows, int64_t cols, int64_t per_rows) {
+  nd::Mat m;
+  m.cols = cols;
+  m.q8 = quantizes(per_rows, cols);
+  if (m.q8) {
+    m.w = alloc(static_cast<size_t>(rows * cols), true);
+    const int64_t sc = cols / qgroup(cols);
+    m.scales = alloc(static_cast<size_t>(rows * sc) * (qf16() ? 2 : 4), true);
+  } else {
+    m.w = alloc(static_cast<size_t>(rows * cols) * 2, true);
+  }
+  return m;
+}
+
 void nd_denoiser::add_slot(const std::string& name, int kind, int64_t rows, int64_t cols, void* dst,
-                           bool required) {
+                           bool required, void* scales) {
   nd::WeightSlot s;
   s.name = name;
   s.kind = kind;
   s.rows = rows;
   s.cols = cols;
   s.dst = dst;
+  s.scales = scales;
   s.required = required;
   index[name] = slots.size();
   slots.push_back(s);
@@ -152,6 +167,27 @@ int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* 
   cudaStream_t st = d->dev->stream;
   const int dst_type = s.kind == kMatrix ? d->desc.compute : ND_F32;
   const size_t src_bytes = static_cast<size_t>(n) * elem_bytes(dtype);
+  if (s.scales) {
+    // int8 storage: quantize on the device (BlockQuantizer's rules).
+    const void* src = data;
+    if (!device) {
+      if (d->staging_bytes < src_bytes) {
+        if (d->staging) cudaFree(d->staging);
+        d->staging = nullptr;
+        d->staging_bytes = 0;
+        ND_CUDA(cudaMalloc(&d->staging, src_bytes));
+        d->staging_bytes = src_bytes;
+      }
+      ND_CUDA(cudaMemcpyAsync(d->staging, data, src_bytes, cudaMemcpyHostToDevice, st));
+      src = d->staging;
+    }
+    int rc = quantize_weights(src, dtype, s.rows, s.cols, d->qgroup(s.cols), d->qf16() ? 1 : 0,
+                              static_cast<int8_t*>(s.dst), s.scales, st);
+    if (rc) return rc;
+    ND_CUDA(cudaStreamSynchronize(st));
+    s.set = true;
+    return ND_OK;
+  }
   if (dtype == dst_type) {
     ND_CUDA(cudaMemcpyAsync(s.dst, data, src_bytes, device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
   } else {
@@ -302,6 +338,30 @@ int nd_denoiser_set_weight(nd_denoiser* d, const char* name, int dtype, const in
 int nd_denoiser_set_weight_device(nd_denoiser* d, const char* name, int dtype, const int64_t* shape,
                                   int rank, const void* data) {
   return set_weight_impl(d, name, dtype, shape, rank, data, true);
+}
+
+int nd_denoiser_set_weight_q8(nd_denoiser* d, const char* name, const int64_t* shape, int rank,
+                              const int8_t* q, int scale_dtype, const void* scales, int64_t quant_group) {
+  using namespace nd;
+  if (!d || !name || !shape || !q || !scales) return fail(ND_ERR_INVALID, "set_weight_q8: null argument");
+  if (d->finalized) return fail(ND_ERR_STATE, "set_weight_q8: denoiser already finalized");
+  auto it = d->index.find(name);
+  if (it == d->index.end()) return fail(ND_ERR_INVALID, std::string("set_weight_q8: unknown tensor ") + name);
+  WeightSlot& s = d->slots[it->second];
+  if (!s.scales) return fail(ND_ERR_INVALID, std::string("set_weight_q8: ") + name + " is not stored as int8");
+  if (rank != 2 || shape[0] != s.rows || shape[1] != s.cols)
+    return fail(ND_ERR_INVALID, std::string("set_weight_q8: ") + name + " has the wrong shape");
+  if ((scale_dtype == ND_F16) != d->qf16() || (quant_group > 0 ? quant_group : s.cols) != d->qgroup(s.cols))
+    return fail(ND_ERR_INVALID, "set_weight_q8: scale type / group differ from the model's");
+  DeviceGuard g(d->dev->ordinal);
+  cudaStream_t st = d->dev->stream;
+  const int64_t sc = s.cols / d->qgroup(s.cols);
+  ND_CUDA(cudaMemcpyAsync(s.dst, q, static_cast<size_t>(s.rows * s.cols), cudaMemcpyHostToDevice, st));
+  ND_CUDA(cudaMemcpyAsync(s.scales, scales, static_cast<size_t>(s.rows * sc) * (d->qf16() ? 2 : 4),
+                          cudaMemcpyHostToDevice, st));
+  ND_CUDA(cudaStreamSynchronize(st));
+  s.set = true;
+  return ND_OK;
 }
 
 int nd_denoiser_finalize(nd_denoiser* d) {

@@ -24,9 +24,23 @@ struct WeightSlot {
   std::string name;
   int kind = kMatrix;
   int64_t rows = 0, cols = 1;
-  void* dst = nullptr;     // device destination (compute dtype for matrices, fp32 vectors)
+  void* dst = nullptr;     // device destination (compute dtype / int8 for matrices, fp32 vectors)
+  void* scales = nullptr;  // int8 matrices: their scales (quant_group / scale type of the model)
   bool required = true;
   bool set = false;
+};
+
+// A matrix kind stored for the GEMM / GEMV: compute dtype, or int8 + scales.
+struct Mat {
+  void* w = nullptr;
+  void* scales = nullptr;
+  bool q8 = false;
+  int64_t cols = 0;
+  // element offset of sub-matrix row `row` in w, and of its scales
+  void* at(int64_t row, int elem_bytes) const { return static_cast<uint8_t*>(w) + row * cols * (q8 ? 1 : elem_bytes); }
+  void* scales_at(int64_t row, int64_t scale_cols, bool f16) const {
+    return scales ? static_cast<uint8_t*>(scales) + row * scale_cols * (f16 ? 2 : 4) : nullptr;
+  }
 };
 
 // Host-side values of one predict call, already validated.
@@ -83,7 +97,20 @@ struct nd_denoiser {
   // Pinned host memory, freed with the denoiser (nullptr + alloc_failed on failure).
   void* pinned(size_t bytes);
   void add_slot(const std::string& name, int kind, int64_t rows, int64_t cols, void* dst,
-                bool required = true);
+                bool required = true, void* scales = nullptr);
+  // int8 storage of matrices (desc.weight_dtype == ND_I8): columns per scale
+  // (0 = per output channel) and whether scales are fp16.
+  bool q8() const { return desc.weight_dtype == ND_I8; }
+  int64_t qgroup(int64_t cols) const { return desc.quant_group > 0 ? desc.quant_group : cols; }
+  bool qf16() const { return desc.quant_scale_dtype == ND_F16; }
+  // Whether a [rows, cols] matrix is stored as int8: the reference's rule
+  // (ModelBuilder.Weight: at least 65,536 elements, whole blocks per row).
+  bool quantizes(int64_t rows, int64_t cols) const {
+    return q8() && rows * cols >= 65536 && cols % qgroup(cols) == 0 && cols % 16 == 0;
+  }
+  // Allocate a matrix kind of `rows` x `cols` (sub-matrices of `per_rows`
+  // rows each stacked; the int8 rule is judged per sub-matrix).
+  nd::Mat alloc_mat(int64_t rows, int64_t cols, int64_t per_rows);
 
   virtual int build() = 0;          // allocate weights + scratch, register slots
   virtual int prepare() { return ND_OK; }  // after every weight is set

@@ -73,10 +73,8 @@ struct MMDiT final : nd_denoiser {
   int n_img = 0, M = 0;
   int dt = ND_BF16;
   float eps = 1e-6f;
-  // weights (compute dtype) and vectors (fp32)
-  void *img_in_w = nullptr, *txt_in_w = nullptr, *t1_w = nullptr, *t2_w = nullptr, *mod_w = nullptr;
-  void *qkv_w = nullptr, *out_w = nullptr, *up_w = nullptr, *down_w = nullptr;
-  void *norm_out_w = nullptr, *proj_out_w = nullptr;
+  // weights (compute dtype or int8 + scales) and vectors (fp32)
+  Mat img_in_w, txt_in_w, t1_w, t2_w, mod_w, qkv_w, out_w, up_w, down_w, norm_out_w, proj_out_w;
   float *img_in_b = nullptr, *txt_norm = nullptr, *txt_in_b = nullptr, *t1_b = nullptr, *t2_b = nullptr;
   float *mod_b = nullptr, *qkv_b = nullptr, *out_b = nullptr, *up_b = nullptr, *down_b = nullptr;
   float *qk_norm = nullptr, *norm_out_b = nullptr, *proj_out_b = nullptr;
@@ -92,13 +90,19 @@ struct MMDiT final : nd_denoiser {
   void *xn = nullptr, *qkv = nullptr, *attn = nullptr, *hid = nullptr, *tok_in = nullptr, *ctx_n = nullptr;
 
   size_t esz() const { return 2; }
-  void* mat(void* base, int64_t elems) const { return static_cast<uint8_t*>(base) + elems * esz(); }
 
   int build() override {
     const nd_model_desc& d = desc;
     if (d.batch != 1) return fail(ND_ERR_UNSUPPORTED, "mmdit: batch must be 1 (shard images across devices)");
     if (d.compute != ND_BF16 && d.compute != ND_F16) return fail(ND_ERR_UNSUPPORTED, "mmdit: compute must be bf16 or f16");
-    if (d.weight_dtype != d.compute) return fail(ND_ERR_UNSUPPORTED, "mmdit: weights must be stored in the compute dtype");
+    if (d.weight_dtype != d.compute && d.weight_dtype != ND_I8)
+      return fail(ND_ERR_UNSUPPORTED, "mmdit: weights must be stored in the compute dtype or int8");
+    if (d.weight_dtype == ND_I8) {
+      if (d.quant_scale_dtype != ND_F16 && d.quant_scale_dtype != ND_F32)
+        return fail(ND_ERR_INVALID, "mmdit: int8 weights need quant_scale_dtype ND_F16 or ND_F32");
+      if (d.quant_group < 0 || (d.quant_group > 0 && d.quant_group % 16))
+        return fail(ND_ERR_INVALID, "mmdit: quant_group must be 0 (per channel) or a multiple of 16");
+    }
     if (d.head_dim != 128 || d.heads * 128 != d.width) return fail(ND_ERR_INVALID, "mmdit: width must be heads x 128");
     if (d.width % 256) return fail(ND_ERR_UNSUPPORTED, "mmdit: width must be a multiple of 256");
     if (d.blocks <= 0 || d.mlp_width <= 0 || d.mlp_width % 8) return fail(ND_ERR_INVALID, "mmdit: bad blocks / mlp_width");
@@ -128,31 +132,30 @@ struct MMDiT final : nd_denoiser {
     const int64_t DD = static_cast<int64_t>(D) * D;
 
     // ---- weights
-    auto W = [&](int64_t elems) { return alloc(static_cast<size_t>(elems) * esz(), true); };
     auto V = [&](int64_t elems) { return static_cast<float*>(alloc(static_cast<size_t>(elems) * 4, true)); };
-    img_in_w = W(static_cast<int64_t>(D) * cin);
+    img_in_w = alloc_mat(D, cin, D);
     img_in_b = V(D);
     txt_norm = V(cw);
-    txt_in_w = W(static_cast<int64_t>(D) * cw);
+    txt_in_w = alloc_mat(D, cw, D);
     txt_in_b = V(D);
-    t1_w = W(static_cast<int64_t>(D) * tw);
+    t1_w = alloc_mat(D, tw, D);
     t1_b = V(D);
-    t2_w = W(DD);
+    t2_w = alloc_mat(D, D, D);
     t2_b = V(D);
-    mod_w = W(static_cast<int64_t>(NB) * 2 * 6 * DD);
+    mod_w = alloc_mat(static_cast<int64_t>(NB) * 2 * 6 * D, D, 6 * D);
     mod_b = V(static_cast<int64_t>(NB) * 2 * 6 * D);
-    qkv_w = W(static_cast<int64_t>(NB) * 2 * 3 * DD);
+    qkv_w = alloc_mat(static_cast<int64_t>(NB) * 2 * 3 * D, D, D);
     qkv_b = V(static_cast<int64_t>(NB) * 2 * 3 * D);
-    out_w = W(static_cast<int64_t>(NB) * 2 * DD);
+    out_w = alloc_mat(static_cast<int64_t>(NB) * 2 * D, D, D);
     out_b = V(static_cast<int64_t>(NB) * 2 * D);
-    up_w = W(static_cast<int64_t>(NB) * 2 * F * D);
+    up_w = alloc_mat(static_cast<int64_t>(NB) * 2 * F, D, F);
     up_b = V(static_cast<int64_t>(NB) * 2 * F);
-    down_w = W(static_cast<int64_t>(NB) * 2 * D * F);
+    down_w = alloc_mat(static_cast<int64_t>(NB) * 2 * D, F, D);
     down_b = V(static_cast<int64_t>(NB) * 2 * D);
     qk_norm = V(static_cast<int64_t>(NB) * 2 * 2 * 128);
-    norm_out_w = W(2 * DD);
+    norm_out_w = alloc_mat(2 * D, D, 2 * D);
     norm_out_b = V(2 * D);
-    proj_out_w = W(static_cast<int64_t>(cin) * D);
+    proj_out_w = alloc_mat(cin, D, cin);
     proj_out_b = V(cin);
     // ---- inputs and scratch
     auto S = [&](size_t bytes) { return alloc(bytes, false); };
@@ -179,18 +182,22 @@ struct MMDiT final : nd_denoiser {
     ND_CUDA(cudaEventCreateWithFlags(&staged, cudaEventDisableTiming));
 
     // ---- registry (dual-stream Qwen-Image tensor names)
-    add_slot("img_in.weight", kMatrix, D, cin, img_in_w);
+    auto M_ = [&](const std::string& name, const Mat& m, int64_t row, int64_t rows) {
+      const int64_t sc = m.q8 ? m.cols / qgroup(m.cols) : 0;
+      add_slot(name, kMatrix, rows, m.cols, m.at(row, 2), true, m.q8 ? m.scales_at(row, sc, qf16()) : nullptr);
+    };
+    M_("img_in.weight", img_in_w, 0, D);
     add_slot("img_in.bias", kVector, D, 1, img_in_b, false);
     add_slot("txt_norm.weight", kVector, cw, 1, txt_norm);
-    add_slot("txt_in.weight", kMatrix, D, cw, txt_in_w);
+    M_("txt_in.weight", txt_in_w, 0, D);
     add_slot("txt_in.bias", kVector, D, 1, txt_in_b, false);
-    add_slot("time_text_embed.timestep_embedder.linear_1.weight", kMatrix, D, tw, t1_w);
+    M_("time_text_embed.timestep_embedder.linear_1.weight", t1_w, 0, D);
     add_slot("time_text_embed.timestep_embedder.linear_1.bias", kVector, D, 1, t1_b, false);
-    add_slot("time_text_embed.timestep_embedder.linear_2.weight", kMatrix, D, D, t2_w);
+    M_("time_text_embed.timestep_embedder.linear_2.weight", t2_w, 0, D);
     add_slot("time_text_embed.timestep_embedder.linear_2.bias", kVector, D, 1, t2_b, false);
-    add_slot("norm_out.linear.weight", kMatrix, 2 * D, D, norm_out_w);
+    M_("norm_out.linear.weight", norm_out_w, 0, 2 * D);
     add_slot("norm_out.linear.bias", kVector, 2 * D, 1, norm_out_b, false);
-    add_slot("proj_out.weight", kMatrix, cin, D, proj_out_w);
+    M_("proj_out.weight", proj_out_w, 0, cin);
     add_slot("proj_out.bias", kVector, cin, 1, proj_out_b, false);
     const char* stream_mod[2] = {"img_mod.1", "txt_mod.1"};
     const char* proj[2][3] = {{"attn.to_q", "attn.to_k", "attn.to_v"},
@@ -203,19 +210,19 @@ struct MMDiT final : nd_denoiser {
       const std::string pre = "transformer_blocks." + std::to_string(b) + ".";
       for (int s = 0; s < 2; ++s) {
         const int64_t g = static_cast<int64_t>(b) * 2 + s;
-        add_slot(pre + stream_mod[s] + ".weight", kMatrix, 6 * D, D, mat(mod_w, g * 6 * DD));
+        M_(pre + stream_mod[s] + ".weight", mod_w, g * 6 * D, 6 * D);
         add_slot(pre + stream_mod[s] + ".bias", kVector, 6 * D, 1, mod_b + g * 6 * D, false);
         for (int j = 0; j < 3; ++j) {
-          add_slot(pre + proj[s][j] + ".weight", kMatrix, D, D, mat(qkv_w, (g * 3 + j) * DD));
+          M_(pre + proj[s][j] + ".weight", qkv_w, (g * 3 + j) * D, D);
           add_slot(pre + proj[s][j] + ".bias", kVector, D, 1, qkv_b + (g * 3 + j) * D, false);
         }
         for (int j = 0; j < 2; ++j)
           add_slot(pre + norms[s][j] + ".weight", kVector, 128, 1, qk_norm + (g * 2 + j) * 128);
-        add_slot(pre + outs[s] + ".weight", kMatrix, D, D, mat(out_w, g * DD));
+        M_(pre + outs[s] + ".weight", out_w, g * D, D);
         add_slot(pre + outs[s] + ".bias", kVector, D, 1, out_b + g * D, false);
-        add_slot(pre + ups[s] + ".weight", kMatrix, F, D, mat(up_w, g * F * static_cast<int64_t>(D)));
+        M_(pre + ups[s] + ".weight", up_w, g * F, F);
         add_slot(pre + ups[s] + ".bias", kVector, F, 1, up_b + g * F, false);
-        add_slot(pre + downs[s] + ".weight", kMatrix, D, F, mat(down_w, g * D * static_cast<int64_t>(F)));
+        M_(pre + downs[s] + ".weight", down_w, g * D, D);
         add_slot(pre + downs[s] + ".bias", kVector, D, 1, down_b + g * D, false);
       }
     }
@@ -294,7 +301,18 @@ struct MMDiT final : nd_denoiser {
     return ND_OK;
   }
 
-  int lin(cudaStream_t s, const void* xin, int64_t rows, int64_t k, int64_t ldx, const void* w,
+  // Point a GEMM at rows [row, ...) of a matrix kind (int8 or compute dtype).
+  void weight_args(nd_linear_args& a, const Mat& m, int64_t row) const {
+    a.weight = m.at(row, 2);
+    if (m.q8) {
+      a.weight_dtype = ND_I8;
+      a.scales = m.scales_at(row, m.cols / qgroup(m.cols), qf16());
+      a.scale_dtype = desc.quant_scale_dtype;
+      a.quant_group = desc.quant_group;
+    }
+  }
+
+  int lin(cudaStream_t s, const void* xin, int64_t rows, int64_t k, int64_t ldx, const Mat& w, int64_t wrow,
           const float* b, int64_t n, int epi, void* y, int64_t ldy, float* resid, int64_t ldr,
           const float* gate, int64_t gate_stride, int64_t split) {
     nd_linear_args a{};
@@ -305,7 +323,7 @@ struct MMDiT final : nd_denoiser {
     a.out_features = n;
     a.x = xin;
     a.ldx = ldx;
-    a.weight = w;
+    weight_args(a, w, wrow);
     a.bias = b;
     a.group_split = split;
     a.y = y;
@@ -335,11 +353,11 @@ struct MMDiT final : nd_denoiser {
     return modulate(m, s);
   }
 
-  int gv(cudaStream_t s, const void* w, int64_t n, int64_t k, const float* xin, const float* b,
+  int gv(cudaStream_t s, const Mat& w, int64_t n, int64_t k, const float* xin, const float* b,
          bool pre_silu, int act, float* y) {
     nd_gemv_args g{};
-    g.w = w;
-    g.w_dtype = dt;
+    g.w = w.w;
+    g.w_dtype = w.q8 ? ND_I8 : dt;
     g.n = n;
     g.k = k;
     g.x = xin;
@@ -348,6 +366,11 @@ struct MMDiT final : nd_denoiser {
     g.bias = b;
     g.act = act;
     g.y = y;
+    if (w.q8) {
+      g.scales = w.scales;
+      g.scale_dtype = desc.quant_scale_dtype;
+      g.quant_group = desc.quant_group;
+    }
     return gemv(g, s);
   }
 
@@ -367,7 +390,6 @@ struct MMDiT final : nd_denoiser {
   }
 
   int block(cudaStream_t s, int b) {
-    const int64_t DD = static_cast<int64_t>(D) * D;
     const int64_t g0 = static_cast<int64_t>(b) * 2;
     const float* mv = mods + g0 * 6 * D;  // [2][6D]: shift1 scale1 gate1 shift2 scale2 gate2
     const double mD = static_cast<double>(M) * D;
@@ -383,7 +405,7 @@ struct MMDiT final : nd_denoiser {
       a.out_features = 3 * D;
       a.x = xn;
       a.ldx = D;
-      a.weight = mat(qkv_w, g0 * 3 * DD);
+      weight_args(a, qkv_w, g0 * 3 * D);
       a.bias = qkv_b + g0 * 3 * D;
       a.group_split = n_img;
       a.y = qkv;
@@ -415,14 +437,14 @@ struct MMDiT final : nd_denoiser {
       ND_OP("attention", 4.0 * M * keys * D, mD * 2 * 4, attention(a, s));
     }
     ND_OP("gemm.out", gemm_flops(M, D, D), gemm_bytes(M, 2.0 * D, D, mD * 8),
-          lin(s, attn, M, D, D, mat(out_w, g0 * DD), out_b + g0 * D, D, ND_EPI_RESIDUAL_GATE, nullptr, 0,
+          lin(s, attn, M, D, D, out_w, g0 * D, out_b + g0 * D, D, ND_EPI_RESIDUAL_GATE, nullptr, 0,
               x, D, mv + 2 * D, 6 * D, n_img));
     ND_OP("modulate", 0.0, mod_bytes, mod(s, mv + 3 * D, mv + 4 * D, M, n_img));
     ND_OP("gemm.up", gemm_flops(M, F, D), gemm_bytes(M, 2.0 * F, D, static_cast<double>(M) * F * 2),
-          lin(s, xn, M, D, D, mat(up_w, g0 * F * static_cast<int64_t>(D)), up_b + g0 * F, F,
+          lin(s, xn, M, D, D, up_w, g0 * F, up_b + g0 * F, F,
               ND_EPI_GELU_TANH, hid, F, nullptr, 0, nullptr, 0, n_img));
     ND_OP("gemm.down", gemm_flops(M, D, F), gemm_bytes(M, 2.0 * D, F, mD * 8),
-          lin(s, hid, M, F, F, mat(down_w, g0 * D * static_cast<int64_t>(F)), down_b + g0 * D, D,
+          lin(s, hid, M, F, F, down_w, g0 * D, down_b + g0 * D, D,
               ND_EPI_RESIDUAL_GATE, nullptr, 0, x, D, mv + 5 * D, 6 * D, n_img));
     return ND_OK;
   }
@@ -432,7 +454,7 @@ struct MMDiT final : nd_denoiser {
     // embeddings: image patches and text rows into one fp32 sequence
     ND_OP("embed", 0.0, ni * cin * 6.0, patchify(in_latent, tok_in, dt, 1, C, Hl, Wl, P, cin, s));
     ND_OP("embed", gemm_flops(ni, dD, cin), gemm_bytes(ni, dD, cin, ni * dD * 4),
-          lin(s, tok_in, n_img, cin, cin, img_in_w, img_in_b, D, ND_EPI_STORE_F32, nullptr, 0, x, D,
+          lin(s, tok_in, n_img, cin, cin, img_in_w, 0, img_in_b, D, ND_EPI_STORE_F32, nullptr, 0, x, D,
               nullptr, 0, n_img));
     {
       nd_rmsnorm_args r{};
@@ -450,7 +472,7 @@ struct MMDiT final : nd_denoiser {
       ND_OP("embed", 0.0, static_cast<double>(ctx) * cw * 6.0, rmsnorm(r, s));
     }
     ND_OP("embed", gemm_flops(ctx, dD, cw), gemm_bytes(ctx, dD, cw, ctx * dD * 4),
-          lin(s, ctx_n, ctx, cw, cw, txt_in_w, txt_in_b, D, ND_EPI_STORE_F32, nullptr, 0,
+          lin(s, ctx_n, ctx, cw, cw, txt_in_w, 0, txt_in_b, D, ND_EPI_STORE_F32, nullptr, 0,
               x + static_cast<int64_t>(n_img) * D, D, nullptr, 0, ctx));
     // time embedding -> every block's modulation vectors in one GEMV pass
     ND_OP("gemv", 2.0 * dD * tw, dD * tw * 2, gv(s, t1_w, D, tw, in_tsin, t1_b, false, 1, temb_h));
@@ -481,7 +503,7 @@ struct MMDiT final : nd_denoiser {
       ND_OP("modulate", 0.0, ni * dD * 6.0, modulate(m, s));
     }
     ND_OP("embed", gemm_flops(ni, cin, dD), gemm_bytes(ni, cin, dD, ni * cin * 4),
-          lin(s, xn, n_img, D, D, proj_out_w, proj_out_b, cin, ND_EPI_STORE_F32, nullptr, 0, out_tok, cin,
+          lin(s, xn, n_img, D, D, proj_out_w, 0, proj_out_b, cin, ND_EPI_STORE_F32, nullptr, 0, out_tok, cin,
               nullptr, 0, n_img));
     ND_OP("embed", 0.0, ni * cin * 8.0, unpatchify(out_tok, cin, out_latent, 1, C, Hl, Wl, P, s));
     return ND_OK;

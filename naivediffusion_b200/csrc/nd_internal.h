@@ -47,6 +47,9 @@ int attention(const nd_attention_args& a, cudaStream_t stream);
 int modulate(const nd_modulate_args& a, cudaStream_t stream);
 int rmsnorm(const nd_rmsnorm_args& a, cudaStream_t stream);
 int gemv(const nd_gemv_args& a, cudaStream_t stream);
+int gemv_w8(const nd_gemv_args& a, cudaStream_t stream);
+int quantize_weights(const void* src, int src_dtype, int64_t rows, int64_t cols, int64_t group,
+                     int scale_f16, int8_t* q, void* scales, cudaStream_t stream);
 int patchify(const float* lat, void* tok, int out_dtype, int B, int C, int H, int W, int p,
              int64_t ldt, cudaStream_t stream);
 int unpatchify(const float* tok, int64_t ldt, float* lat, int B, int C, int H, int W, int p,

@@ -316,6 +316,11 @@ int rmsnorm(const nd_rmsnorm_args& a, cudaStream_t stream) {
 
 int gemv(const nd_gemv_args& a, cudaStream_t stream) {
   if (a.n <= 0 || a.k <= 0 || a.batch <= 0 || a.batch > 4) return fail(ND_ERR_INVALID, "gemv: bad shape (batch 1..4)");
+  if (a.w_dtype == ND_I8) {
+    if (!a.w || !a.x || !a.y) return fail(ND_ERR_INVALID, "gemv: null operand");
+    if (a.k * a.batch > 12288) return fail(ND_ERR_UNSUPPORTED, "gemv: batch * k above 12288");
+    return gemv_w8(a, stream);
+  }
   if (a.k % 8) return fail(ND_ERR_INVALID, "gemv: k must be a multiple of 8");
   if (a.k * a.batch > 12288) return fail(ND_ERR_UNSUPPORTED, "gemv: batch * k above 12288");
   if (a.w_dtype != ND_BF16 && a.w_dtype != ND_F16) return fail(ND_ERR_INVALID, "gemv: weight must be bf16 or f16");

@@ -1,0 +1,167 @@
+// int8 weight storage: the device-side quantizer and the int8 GEMV.
+//
+// quantize_weights restates BlockQuantizer.Quantize
+// (Tensors/BlockQuantizer.cs:34-105) per row and group of `group` columns:
+//   peak   = max |w| over the group
+//   scale  = peak / 127, stored as fp16 (round to nearest even) for the
+//            reference's blocks, or kept fp32 (per-output-channel scheme)
+//   q      = clamp(rint(w * (1 / stored)), -127, 127); a zero stored scale
+//            leaves the group zero
+// with IEEE division and round-half-even, so q and the scales match the host
+// quantizer (and the oracle's restatement) bit for bit.
+#include <algorithm>
+#include <climits>
+
+#include "nd_common.cuh"
+#include "nd_internal.h"
+#include "nd_runtime.h"
+
+namespace nd {
+
+namespace {
+
+__device__ __forceinline__ float load_as_float(const void* src, int dt, long long i) {
+  if (dt == ND_F32) return static_cast<const float*>(src)[i];
+  if (dt == ND_F16) return __half2float(static_cast<const __half*>(src)[i]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(src)[i]);
+}
+
+// One block per row; the row's groups are spread over the block's warps
+// (group <= 32: one lane per element; wider groups: lanes stride the group).
+__global__ void __launch_bounds__(256) quantize_kernel(const void* __restrict__ src, int src_dt,
+                                                       long long rows, int cols, int group,
+                                                       int scale_f16, int8_t* __restrict__ q,
+                                                       void* __restrict__ scales) {
+  const long long r = blockIdx.x;
+  if (r >= rows) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int groups = cols / group;
+  const long long base = r * cols;
+  for (int g = warp; g < groups; g += nwarps) {
+    const long long g0 = base + static_cast<long long>(g) * group;
+    float peak = 0.f;
+    for (int i = lane; i < group; i += 32) peak = fmaxf(peak, fabsf(load_as_float(src, src_dt, g0 + i)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
+    float stored;
+    const long long si = r * groups + g;
+    if (scale_f16) {
+      const __half h = __float2half_rn(__fdiv_rn(peak, 127.0f));
+      stored = __half2float(h);
+      if (lane == 0) static_cast<__half*>(scales)[si] = h;
+    } else {
+      stored = __fdiv_rn(peak, 127.0f);
+      if (lane == 0) static_cast<float*>(scales)[si] = stored;
+    }
+    const float inverse = stored != 0.f ? __fdiv_rn(1.0f, stored) : 0.f;
+    for (int i = lane; i < group; i += 32) {
+      float v = 0.f;
+      if (stored != 0.f) {
+        v = rintf(__fmul_rn(load_as_float(src, src_dt, g0 + i), inverse));
+        v = fmaxf(-127.f, fminf(127.f, v));
+      }
+      q[g0 + i] = static_cast<int8_t>(v);
+    }
+  }
+}
+
+// y[b][n] = act(sum_k q[n][k] * scale(n, k) * pre(x[b][k]) + bias[n]) for int8
+// q; one warp per output row, 16 weights (one 16-byte load) per lane step.
+__global__ void __launch_bounds__(256) gemv_w8_kernel(const int8_t* __restrict__ W, long long N, int K,
+                                                      const void* __restrict__ scales, int scale_f16,
+                                                      int group, int scale_cols,
+                                                      const float* __restrict__ x, int B, int pre,
+                                                      const float* __restrict__ bias, int act,
+                                                      float* __restrict__ y) {
+  extern __shared__ float xs[];
+  for (int i = threadIdx.x; i < B * K; i += blockDim.x) {
+    float v = x[i];
+    if (pre == 1) v = v / (1.0f + __expf(-v));
+    xs[i] = v;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const int k16 = K >> 4;
+  for (long long n = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; n < N;
+       n += warps) {
+    const uint4* wr = reinterpret_cast<const uint4*>(W + n * K);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = lane; c < k16; c += 32) {
+      uint4 p;
+      asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(p.x), "=r"(p.y), "=r"(p.z), "=r"(p.w)
+                   : "l"(wr + c));
+      const long long si = n * scale_cols + (c * 16) / group;
+      const float s = scale_f16 ? __half2float(static_cast<const __half*>(scales)[si])
+                                : static_cast<const float*>(scales)[si];
+      float wv[16];
+      const uint32_t u[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float f[4];
+        i8x4_to_f32(u[i], f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) wv[4 * i + j] = f[j] * s;
+      }
+#pragma unroll 4
+      for (int b = 0; b < 4; ++b) {
+        if (b < B) {
+          const float* xb = xs + b * K + 16 * c;
+          float sum = 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sum += wv[i] * xb[i];
+          acc[b] += sum;
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      if (b < B) {
+        float v = acc[b];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) {
+          if (bias) v += bias[n];
+          if (act == 1) v = v / (1.0f + __expf(-v));
+          else if (act == 2) v = tanhf(v);
+          y[static_cast<long long>(b) * N + n] = v;
+        }
+      }
+    }
+  }
+}
+
+}  // namespace
+
+int quantize_weights(const void* src, int src_dtype, int64_t rows, int64_t cols, int64_t group,
+                     int scale_f16, int8_t* q, void* scales, cudaStream_t stream) {
+  if (!src || !q || !scales) return fail(ND_ERR_INVALID, "quantize: null operand");
+  if (rows <= 0 || cols <= 0 || cols > INT_MAX || rows > INT_MAX) return fail(ND_ERR_INVALID, "quantize: bad shape");
+  const int64_t g = group > 0 ? group : cols;
+  if (cols % g) return fail(ND_ERR_INVALID, "quantize: columns do not split into whole groups");
+  quantize_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(src, src_dtype, rows, static_cast<int>(cols),
+                                                                   static_cast<int>(g), scale_f16, q, scales);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int gemv_w8(const nd_gemv_args& a, cudaStream_t stream) {
+  if (!a.scales) return fail(ND_ERR_INVALID, "gemv: int8 weights need scales");
+  if (a.k % 16) return fail(ND_ERR_INVALID, "gemv: int8 weights need k % 16 == 0");
+  const int64_t group = a.quant_group > 0 ? a.quant_group : a.k;
+  if (group % 16 || a.k % group) return fail(ND_ERR_INVALID, "gemv: quant_group must be a multiple of 16 dividing k");
+  const size_t shmem = static_cast<size_t>(a.k) * a.batch * sizeof(float);
+  long long blocks = (a.n + 7) / 8;
+  const long long cap = static_cast<long long>(sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  gemv_w8_kernel<<<static_cast<unsigned>(blocks), 256, shmem, stream>>>(
+      static_cast<const int8_t*>(a.w), a.n, static_cast<int>(a.k), a.scales, a.scale_dtype == ND_F16,
+      static_cast<int>(group), static_cast<int>(a.k / group), a.x, a.batch, a.pre_silu ? 1 : 0, a.bias,
+      a.act, a.y);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+}  // namespace nd

@@ -200,6 +200,16 @@ int nd_op_dequantize(const int8_t* q, const void* scales, int scale_dtype, int64
                         static_cast<cudaStream_t>(stream));
 }
 
+int nd_op_quantize(const void* src, int src_dtype, int64_t rows, int64_t cols, int64_t quant_group,
+                   int scale_dtype, int8_t* q, void* scales, void* stream) {
+  if (src_dtype != ND_F32 && src_dtype != ND_F16 && src_dtype != ND_BF16)
+    return nd::fail(ND_ERR_INVALID, "nd_op_quantize: src must be f32, f16 or bf16");
+  if (scale_dtype != ND_F16 && scale_dtype != ND_F32)
+    return nd::fail(ND_ERR_INVALID, "nd_op_quantize: scale_dtype must be ND_F16 or ND_F32");
+  return nd::quantize_weights(src, src_dtype, rows, cols, quant_group, scale_dtype == ND_F16, q, scales,
+                              static_cast<cudaStream_t>(stream));
+}
+
 int nd_op_sync(void* stream) { return nd::check_device_status(static_cast<cudaStream_t>(stream)); }
 
 }  // extern "C"

@@ -87,6 +87,9 @@ class MMDiTConfig:
     time_width: int = 256
     compute: int = _lib.ND_BF16
     eps: float = 1e-6
+    weight_dtype: int = 0           # 0: the compute dtype; _lib.ND_I8: int8 weight-only
+    quant_group: int = 32           # int8: columns per scale (0 = per output channel)
+    quant_scale_dtype: int = _lib.ND_F16
 
     @property
     def image_tokens(self) -> int:
@@ -105,9 +108,18 @@ class MMDiTConfig:
         d.latent_channels, d.latent_height, d.latent_width = (
             self.latent_channels, self.latent_height, self.latent_width)
         d.patch, d.time_width, d.batch = self.patch, self.time_width, 1
-        d.compute = d.weight_dtype = self.compute
+        d.compute = self.compute
+        d.weight_dtype = self.weight_dtype or self.compute
+        d.quant_group = self.quant_group
+        d.quant_scale_dtype = self.quant_scale_dtype
         d.eps = self.eps
         return d
+
+    def quantized(self, rows: int, cols: int) -> bool:
+        """Whether a [rows, cols] matrix is stored as int8 (ModelBuilder.Weight's
+        rule: at least 65,536 elements, whole groups per row)."""
+        g = self.quant_group or cols
+        return self.weight_dtype == _lib.ND_I8 and rows * cols >= 65536 and cols % g == 0 and cols % 16 == 0
 
     def flops_per_step(self) -> float:
         """Algorithmic FLOPs of one step (1 MAC = 2 FLOP): block GEMMs, joint
@@ -267,6 +279,19 @@ class CudaDenoiser:
         shape = (C.c_int64 * a.ndim)(*a.shape)
         check(L.nd_denoiser_set_weight(self.handle, name.encode(), dt, shape, a.ndim,
                                        a.ctypes.data_as(C.c_void_p)))
+
+    def set_weight_q8(self, name: str, q: np.ndarray, scales: np.ndarray, quant_group: int) -> None:
+        """A matrix BlockQuantizer already quantized on the host: q int8
+        [rows, cols], scales fp16 (given as uint16 bits or float16) or fp32."""
+        L = _bind()
+        q = np.ascontiguousarray(q, np.int8)
+        s = np.ascontiguousarray(scales)
+        sd = _lib.ND_F32 if s.dtype == np.float32 else _lib.ND_F16
+        shape = (C.c_int64 * 2)(*q.shape)
+        L.nd_denoiser_set_weight_q8.argtypes = [C.c_void_p, C.c_char_p, C.POINTER(C.c_int64), C.c_int,
+                                                C.c_void_p, C.c_int, C.c_void_p, C.c_int64]
+        check(L.nd_denoiser_set_weight_q8(self.handle, name.encode(), shape, 2, q.ctypes.data, sd,
+                                          s.ctypes.data, quant_group))
 
     def finalize(self) -> None:
         check(_bind().nd_denoiser_finalize(self.handle))

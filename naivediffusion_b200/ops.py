@@ -183,3 +183,14 @@ def dequantize(q: torch.Tensor, scales: torch.Tensor, quant_group: int = 32,
     check(lib().nd_op_dequantize(q.data_ptr(), scales.data_ptr(), _DT[scales.dtype], quant_group, rows,
                                  cols, out.data_ptr(), _DT[out_dtype], C.c_void_p(_stream())))
     return out
+
+
+def quantize(w: torch.Tensor, quant_group: int = 32, scale_dtype=torch.float16):
+    """BlockQuantizer on the device: (q int8 [rows, cols], scales [rows, cols / group] or [rows])."""
+    rows, cols = w.shape
+    g = quant_group or cols
+    q = torch.empty(rows, cols, device=w.device, dtype=torch.int8)
+    s = torch.empty(rows, cols // g, device=w.device, dtype=scale_dtype)
+    check(lib().nd_op_quantize(w.data_ptr(), _DT[w.dtype], rows, cols, quant_group, _DT[scale_dtype],
+                               q.data_ptr(), s.data_ptr(), C.c_void_p(_stream())))
+    return q, s
