@@ -242,7 +242,7 @@ def run_ours(args):
     same = bool(np.allclose(y, out.cpu().numpy(), rtol=0, atol=0))
 
     # ---- per-kernel-class profile (eager step, CUDA events per launch)
-    prof = den.profile(steps=1)
+    prof = den.profile(steps=3)
     launches = sum(p["launches"] for p in prof)
     peaks = measured_peaks()
     gemm = [p for p in prof if p["name"].startswith("gemm")]

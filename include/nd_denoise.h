@@ -81,6 +81,7 @@ typedef struct nd_model_desc {
   int weight_dtype;           /* storage: ND_BF16 / ND_F16, or ND_I8 (weight-only) */
   int quant_group;            /* int8: columns per scale (32 = BlockQuantizer); 0 = per output channel */
   int quant_scale_dtype;      /* int8: ND_F16 (BlockQuantizer) or ND_F32 */
+  int adaln_rank;             /* Anima: rank of the low-rank adaLN (256) */
   float eps;                  /* norm epsilon (1e-6 for the DiTs) */
 } nd_model_desc;
 
@@ -159,10 +160,11 @@ ND_API int nd_denoiser_predict_device(nd_denoiser* d, const float* latent, doubl
                                       double sigma, int n_cond, const nd_named_tensor* cond,
                                       float* out, void* stream);
 
-/* Per-kernel-class timing: run `steps` eager forward passes on the last
- * staged inputs with a CUDA event pair around every launch, and return per
- * class (e.g. "gemm.qkv", "attention") the launches, device milliseconds,
- * algorithmic FLOPs and bytes of ONE step (averaged over the steps). The
+/* Per-kernel-class timing: capture the step once more with a CUDA event pair
+ * around every launch (event-record nodes in the graph), replay it `steps`
+ * times on the last staged inputs, and return per class (e.g. "gemm.qkv",
+ * "attention") the launches, device milliseconds, algorithmic FLOPs and bytes
+ * of ONE step (times averaged over the replays). The
  * reference's counterpart is MemoryLog's per-stage report
  * (src/NaiveDiffusion/Dml/MemoryLog.cs:110-224) and DenoiseCommand's
  * Stopwatch (NaiveDiffusion.Cli/DenoiseCommand.cs:139-144). */
@@ -228,6 +230,13 @@ typedef struct nd_linear_args {
   const void* scales;
   int scale_dtype;
   int64_t quant_group;
+  /* QK_NORM_ROPE details: columns [0, qk_cols) are normed, each run of
+   * norm_span columns with its own 128-wide weight (qk_norm[group][col /
+   * norm_span]; 0 = qk_cols / 2: q then k). rope_cos == NULL: norm only, no
+   * rotation (cross-attention). rope_period: table row = row % rope_period
+   * (0 = row), for batch items stacked by rows. */
+  int64_t norm_span;
+  int64_t rope_period;
 } nd_linear_args;
 
 /* Device pointers; stream is a cudaStream_t (NULL = legacy default stream).
@@ -299,6 +308,8 @@ typedef struct nd_gemv_args {
   const float* bias; int act;
   float* y;
   const void* scales; int scale_dtype; int64_t quant_group;  /* int8 weights only */
+  int64_t x_rows_per_vec;  /* > 0: output row n reads input vector n / x_rows_per_vec (batch 1) */
+  int64_t bias_period;     /* > 0: bias index n % bias_period */
 } nd_gemv_args;
 
 ND_API int nd_op_gemv(const nd_gemv_args* args, void* stream);

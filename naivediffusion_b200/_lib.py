@@ -52,7 +52,7 @@ class LinearArgs(C.Structure):
         ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
         ("qk_cols", C.c_int64), ("eps", C.c_float),
         ("weight_dtype", C.c_int), ("scales", C.c_void_p), ("scale_dtype", C.c_int),
-        ("quant_group", C.c_int64),
+        ("quant_group", C.c_int64), ("norm_span", C.c_int64), ("rope_period", C.c_int64),
     ]
 
 
@@ -92,6 +92,7 @@ class GemvArgs(C.Structure):
         ("x", C.c_void_p), ("batch", C.c_int), ("pre_silu", C.c_int),
         ("bias", C.c_void_p), ("act", C.c_int), ("y", C.c_void_p),
         ("scales", C.c_void_p), ("scale_dtype", C.c_int), ("quant_group", C.c_int64),
+        ("x_rows_per_vec", C.c_int64), ("bias_period", C.c_int64),
     ]
 
 

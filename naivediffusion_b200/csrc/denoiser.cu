@@ -8,6 +8,7 @@
 #include <algorithm>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "denoiser.h"
 #include "nd_common.cuh"
@@ -25,6 +26,22 @@ __global__ void convert_kernel(const void* __restrict__ src, int st, void* __res
     if (st == ND_F32) v = static_cast<const float*>(src)[i];
     else if (st == ND_F16) v = __half2float(static_cast<const __half*>(src)[i]);
     else v = __bfloat162float(static_cast<const __nv_bfloat16*>(src)[i]);
+    if (dt == ND_F32) static_cast<float*>(dst)[i] = v;
+    else if (dt == ND_F16) static_cast<__half*>(dst)[i] = __float2half_rn(v);
+    else static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn(v);
+  }
+}
+
+__global__ void convert_cols_kernel(const void* __restrict__ src, int st, long long src_ld,
+                                    void* __restrict__ dst, int dt, long long rows, long long cols) {
+  const long long n = rows * cols;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / cols, c = i % cols, j = r * src_ld + c;
+    float v;
+    if (st == ND_F32) v = static_cast<const float*>(src)[j];
+    else if (st == ND_F16) v = __half2float(static_cast<const __half*>(src)[j]);
+    else v = __bfloat162float(static_cast<const __nv_bfloat16*>(src)[j]);
     if (dt == ND_F32) static_cast<float*>(dst)[i] = v;
     else if (dt == ND_F16) static_cast<__half*>(dst)[i] = __float2half_rn(v);
     else static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn(v);
@@ -54,17 +71,20 @@ int convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n,
   return ND_OK;
 }
 
+int convert_cols(const void* src, int src_dtype, int64_t src_ld, void* dst, int dst_dtype, int64_t rows,
+                 int64_t cols, cudaStream_t s) {
+  const int64_t n = rows * cols;
+  if (n <= 0) return ND_OK;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, sm_count() * 8LL));
+  convert_cols_kernel<<<grid, 256, 0, s>>>(src, src_dtype, src_ld, dst, dst_dtype, rows, cols);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
 }  // namespace nd
 
 void nd_denoiser::prof_begin(cudaStream_t s) {
-  if (!profiling) return;
-  if (prof_used + 2 > prof_pool.size()) {
-    for (int i = 0; i < 64; ++i) {
-      cudaEvent_t e;
-      if (cudaEventCreate(&e) != cudaSuccess) return;
-      prof_pool.push_back(e);
-    }
-  }
+  if (!profiling || prof_used + 2 > prof_pool.size()) return;
   prof_start_ev = prof_pool[prof_used++];
   cudaEventRecord(prof_start_ev, s);
 }
@@ -156,12 +176,36 @@ int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* 
     return fail(ND_ERR_INVALID, std::string("set_weight: ") + name + " must be f32, f16 or bf16");
   int64_t n = 1;
   for (int i = 0; i < rank; ++i) n *= shape[i];
-  const bool shape_ok = (rank == 2 && shape[0] == s.rows && shape[1] == s.cols) ||
+  const bool sliced = s.src_cols > s.cols && rank == 2 && shape[0] == s.rows && shape[1] == s.src_cols;
+  const bool shape_ok = sliced || (rank == 2 && shape[0] == s.rows && shape[1] == s.cols) ||
                         (rank == 1 && s.cols == 1 && shape[0] == s.rows) ||
                         (n == s.rows * s.cols && s.kind == kVector);
   if (!shape_ok) {
     return fail(ND_ERR_INVALID, std::string("set_weight: ") + name + " has the wrong shape (expected [" +
-                                    std::to_string(s.rows) + ", " + std::to_string(s.cols) + "])");
+                                    std::to_string(s.rows) + ", " + std::to_string(s.src_cols > s.cols ? s.src_cols : s.cols) + "])");
+  }
+  if (sliced) {
+    // Keep the first `cols` columns of the checkpoint's wider matrix.
+    DeviceGuard g(d->dev->ordinal);
+    cudaStream_t st = d->dev->stream;
+    const size_t src_bytes = static_cast<size_t>(n) * elem_bytes(dtype);
+    const void* src = data;
+    if (!device) {
+      if (d->staging_bytes < src_bytes) {
+        if (d->staging) cudaFree(d->staging);
+        d->staging = nullptr;
+        d->staging_bytes = 0;
+        ND_CUDA(cudaMalloc(&d->staging, src_bytes));
+        d->staging_bytes = src_bytes;
+      }
+      ND_CUDA(cudaMemcpyAsync(d->staging, data, src_bytes, cudaMemcpyHostToDevice, st));
+      src = d->staging;
+    }
+    int rc = convert_cols(src, dtype, s.src_cols, s.dst, d->desc.compute, s.rows, s.cols, st);
+    if (rc) return rc;
+    ND_CUDA(cudaStreamSynchronize(st));
+    s.set = true;
+    return ND_OK;
   }
   DeviceGuard g(d->dev->ordinal);
   cudaStream_t st = d->dev->stream;
@@ -305,6 +349,7 @@ int nd_denoiser_create(nd_device* dev, const nd_model_desc* desc, nd_denoiser** 
   nd_denoiser* d = nullptr;
   switch (desc->family) {
     case ND_FAMILY_MMDIT: d = nd::make_mmdit(); break;
+    case ND_FAMILY_ANIMA: d = nd::make_anima(); break;
     default: return nd::fail(ND_ERR_UNSUPPORTED, "nd_denoiser_create: unknown model family");
   }
   d->dev = dev;
@@ -405,36 +450,67 @@ int nd_denoiser_profile(nd_denoiser* d, int steps, nd_kernel_time* out, int max_
   if (!d->finalized) return nd::fail(ND_ERR_STATE, "profile: call nd_denoiser_finalize first");
   nd::DeviceGuard g(d->dev->ordinal);
   cudaStream_t st = d->dev->stream;
+  // Capture the step once more with an event pair recorded around every
+  // launch (event-record nodes inside the graph), replay it, and read the
+  // events: per-kernel device times of the same graph execution predict runs.
   d->prof.clear();
   d->prof_used = 0;
+  // Events are created before the capture begins (two per launch).
+  while (d->prof_pool.size() < 4096) {
+    cudaEvent_t ev;
+    ND_CUDA(cudaEventCreate(&ev));
+    d->prof_pool.push_back(ev);
+  }
   d->profiling = true;
-  int rc = ND_OK;
-  for (int i = 0; i < steps && rc == ND_OK; ++i) rc = d->forward(st);
+  ND_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  int rc = d->forward(st);
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(st, &graph);
   d->profiling = false;
+  if (rc) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return nd::cuda_fail(e, "profile: graph capture");
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, graph, 0);
+  if (e != cudaSuccess) {
+    cudaGraphDestroy(graph);
+    return nd::cuda_fail(e, "profile: graph instantiate");
+  }
+  std::vector<double> ms(d->prof.size(), 0.0);
+  for (int i = 0; i < steps && rc == ND_OK; ++i) {
+    e = cudaGraphLaunch(exec, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+      rc = nd::cuda_fail(e, "profile: replay");
+      break;
+    }
+    for (size_t k = 0; k < d->prof.size(); ++k) {
+      float t = 0.f;
+      cudaEventElapsedTime(&t, d->prof[k].start, d->prof[k].stop);
+      ms[k] += t;
+    }
+  }
+  cudaGraphExecDestroy(exec);
+  cudaGraphDestroy(graph);
   if (rc) return rc;
   rc = nd::check_device_status(st);
   if (rc) return rc;
   int n = 0;
-  for (const auto& r : d->prof) {
-    float ms = 0.f;
-    ND_CUDA(cudaEventElapsedTime(&ms, r.start, r.stop));
-    int k = 0;
-    while (k < n && std::strcmp(out[k].name, r.cls) != 0) ++k;
-    if (k == n) {
+  for (size_t k = 0; k < d->prof.size(); ++k) {
+    const auto& r = d->prof[k];
+    int j = 0;
+    while (j < n && std::strcmp(out[j].name, r.cls) != 0) ++j;
+    if (j == n) {
       if (n == max_entries) continue;
-      out[k] = nd_kernel_time{r.cls, 0, 0.0, 0.0, 0.0};
+      out[j] = nd_kernel_time{r.cls, 0, 0.0, 0.0, 0.0};
       ++n;
     }
-    out[k].launches += 1;
-    out[k].total_ms += ms;
-    out[k].flops += r.flops;
-    out[k].bytes += r.bytes;
-  }
-  for (int k = 0; k < n; ++k) {
-    out[k].launches /= steps;
-    out[k].total_ms /= steps;
-    out[k].flops /= steps;
-    out[k].bytes /= steps;
+    out[j].launches += 1;
+    out[j].total_ms += ms[k] / steps;
+    out[j].flops += r.flops;
+    out[j].bytes += r.bytes;
   }
   *n_entries = n;
   return ND_OK;

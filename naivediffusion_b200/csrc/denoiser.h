@@ -26,6 +26,7 @@ struct WeightSlot {
   int64_t rows = 0, cols = 1;
   void* dst = nullptr;     // device destination (compute dtype / int8 for matrices, fp32 vectors)
   void* scales = nullptr;  // int8 matrices: their scales (quant_group / scale type of the model)
+  int64_t src_cols = 0;    // > cols: the checkpoint tensor is wider; keep its first `cols` columns
   bool required = true;
   bool set = false;
 };
@@ -56,6 +57,9 @@ struct StepInputs {
 
 // Converts `n` elements of `src` (dtype) into `dst` (dst_dtype) on the device.
 int convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n, cudaStream_t s);
+// Rows x cols of a row-major src (leading dimension src_ld) into a packed dst.
+int convert_cols(const void* src, int src_dtype, int64_t src_ld, void* dst, int dst_dtype, int64_t rows,
+                 int64_t cols, cudaStream_t s);
 
 }  // namespace nd
 
@@ -125,4 +129,5 @@ struct nd_denoiser {
 
 namespace nd {
 nd_denoiser* make_mmdit();
+nd_denoiser* make_anima();
 }  // namespace nd

@@ -87,12 +87,17 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
   if (!resid && (!a.y || a.ldy < a.out_features || a.ldy % 8 != 0))
     return fail(ND_ERR_INVALID, "linear: output needs y with ldy >= out_features, ldy % 8 == 0");
   if (epi == ND_EPI_RESIDUAL_GATE && !a.gate) return fail(ND_ERR_INVALID, "linear: gate missing");
+  const int64_t span = a.norm_span > 0 ? a.norm_span : a.qk_cols / 2;
   if (epi == ND_EPI_QK_NORM_ROPE) {
-    if (!a.qk_norm || !a.rope_cos || !a.rope_sin)
-      return fail(ND_ERR_INVALID, "linear: qk epilogue needs qk_norm, rope_cos, rope_sin");
-    if (a.qk_cols % 256 != 0 || a.qk_cols > a.out_features)
-      return fail(ND_ERR_INVALID, "linear: qk_cols must be a multiple of 256 and <= out_features");
+    if (!a.qk_norm) return fail(ND_ERR_INVALID, "linear: qk epilogue needs qk_norm");
+    if ((a.rope_cos == nullptr) != (a.rope_sin == nullptr))
+      return fail(ND_ERR_INVALID, "linear: give both rope_cos and rope_sin, or neither");
+    if (a.qk_cols <= 0 || a.qk_cols % 128 != 0 || a.qk_cols > a.out_features)
+      return fail(ND_ERR_INVALID, "linear: qk_cols must be a positive multiple of 128, <= out_features");
+    if (span <= 0 || span % 128 != 0 || a.qk_cols % span != 0)
+      return fail(ND_ERR_INVALID, "linear: norm_span must be a multiple of 128 dividing qk_cols");
     if (a.out_features % 128 != 0) return fail(ND_ERR_INVALID, "linear: qk epilogue needs out_features % 128 == 0");
+    if (a.rope_period < 0) return fail(ND_ERR_INVALID, "linear: rope_period must be >= 0");
   }
   if (a.bias && (reinterpret_cast<uintptr_t>(a.bias) & 15u))
     return fail(ND_ERR_INVALID, "linear: bias must be 16-byte aligned");
@@ -135,6 +140,9 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
   g.rope_cos = a.rope_cos;
   g.rope_sin = a.rope_sin;
   g.qk_cols = static_cast<int>(a.qk_cols);
+  g.norm_span = static_cast<int>(span > 0 ? span : 128);
+  g.norm_sets = static_cast<int>(a.qk_cols > 0 && span > 0 ? a.qk_cols / span : 1);
+  g.rope_period = static_cast<int>(a.rope_period);
   g.head_dim = 128;
   g.norm_eps = a.eps;
   g.status = device_status();

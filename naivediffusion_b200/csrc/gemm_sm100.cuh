@@ -51,7 +51,10 @@ struct GemmArgs {
   const float* qk_norm;   // [groups][2][head_dim]: q weight then k weight
   const float* rope_cos;  // [M][head_dim / 2]
   const float* rope_sin;
-  int qk_cols;            // leading columns that are q then k (2 * width)
+  int qk_cols;            // leading columns that get the head norm
+  int norm_span;          // columns per norm weight set (qk_norm[group][col / norm_span])
+  int norm_sets;          // weight sets per group
+  int rope_period;        // RoPE table row = row % rope_period (rope_cos null: no rotation)
   int head_dim;           // 128
   float norm_eps;
   uint32_t idesc;
@@ -203,8 +206,10 @@ __device__ __forceinline__ void epilogue_head_norm_rope(const GemmArgs& a, const
                                                         uint32_t tbase, bool row_ok, uint32_t buf0,
                                                         int& sb, int lane) {
   const float* bias = a.bias ? a.bias + group * a.bias_stride + col0 : nullptr;
-  const int which = col0 >= (a.qk_cols >> 1) ? 1 : 0;
-  const float* w = a.qk_norm + (group * 2 + which) * 128;
+  const int which = col0 / a.norm_span;
+  const float* w = a.qk_norm + (group * a.norm_sets + which) * 128;
+  const bool rope = a.rope_cos != nullptr;
+  const int trow = row_ok ? (a.rope_period > 0 ? row % a.rope_period : row) : 0;
   const int kind = a.out_f16 ? kEmitF16 : kEmitBf16;
   uint32_t r[32];
   float sumsq = 0.f;
@@ -219,8 +224,8 @@ __device__ __forceinline__ void epilogue_head_norm_rope(const GemmArgs& a, const
     }
   }
   const float scale = rsqrtf(sumsq * (1.0f / 128.0f) + a.norm_eps);
-  const float* cs = a.rope_cos + static_cast<long long>(row_ok ? row : 0) * 64;
-  const float* sn = a.rope_sin + static_cast<long long>(row_ok ? row : 0) * 64;
+  const float* cs = rope ? a.rope_cos + static_cast<long long>(trow) * 64 : nullptr;
+  const float* sn = rope ? a.rope_sin + static_cast<long long>(trow) * 64 : nullptr;
 #pragma unroll 1
   for (int c = 0; c < 2; ++c) {
     uint32_t lo[32], hi[32];
@@ -230,8 +235,10 @@ __device__ __forceinline__ void epilogue_head_norm_rope(const GemmArgs& a, const
     float olo[32], ohi[32];
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
-      const float4 co = row_ok ? __ldg(reinterpret_cast<const float4*>(cs + c * 32 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float4 si = row_ok ? __ldg(reinterpret_cast<const float4*>(sn + c * 32 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 co = (row_ok && rope) ? __ldg(reinterpret_cast<const float4*>(cs + c * 32 + i))
+                                         : make_float4(1.f, 1.f, 1.f, 1.f);
+      const float4 si = (row_ok && rope) ? __ldg(reinterpret_cast<const float4*>(sn + c * 32 + i))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
       const float cv[4] = {co.x, co.y, co.z, co.w};
       const float sv[4] = {si.x, si.y, si.z, si.w};
 #pragma unroll

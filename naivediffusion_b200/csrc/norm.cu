@@ -170,9 +170,10 @@ int pick_bucket(int width) {
 __global__ void __launch_bounds__(256) gemv_kernel(const uint16_t* __restrict__ W, int w_f16,
                                                    long long N, int K, const float* __restrict__ x,
                                                    int B, int pre, const float* __restrict__ bias,
-                                                   int act, float* __restrict__ y) {
+                                                   int act, float* __restrict__ y, long long xrows,
+                                                   int nvec, long long bias_period) {
   extern __shared__ float xs[];
-  for (int i = threadIdx.x; i < B * K; i += blockDim.x) {
+  for (int i = threadIdx.x; i < nvec * K; i += blockDim.x) {
     float v = x[i];
     if (pre == 1) v = v / (1.0f + __expf(-v));
     xs[i] = v;
@@ -203,7 +204,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint16_t* __restrict__ 
 #pragma unroll 4
       for (int b = 0; b < 4; ++b) {
         if (b < B) {
-          const float* xb = xs + b * K + 8 * c;
+          const float* xb = xs + (xrows > 0 ? (n / xrows) : b) * K + 8 * c;
           float s = 0.f;
 #pragma unroll
           for (int i = 0; i < 8; ++i) s += wv[i] * xb[i];
@@ -216,7 +217,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint16_t* __restrict__ 
       if (b < B) {
         float v = warp_sum(acc[b]);
         if (lane == 0) {
-          if (bias) v += bias[n];
+          if (bias) v += bias[bias_period > 0 ? n % bias_period : n];
           if (act == 1) v = v / (1.0f + __expf(-v));
           else if (act == 2) v = tanhf(v);
           y[static_cast<long long>(b) * N + n] = v;
@@ -316,32 +317,25 @@ int rmsnorm(const nd_rmsnorm_args& a, cudaStream_t stream) {
 
 int gemv(const nd_gemv_args& a, cudaStream_t stream) {
   if (a.n <= 0 || a.k <= 0 || a.batch <= 0 || a.batch > 4) return fail(ND_ERR_INVALID, "gemv: bad shape (batch 1..4)");
+  if (a.x_rows_per_vec < 0 || a.bias_period < 0) return fail(ND_ERR_INVALID, "gemv: negative period");
+  if (a.x_rows_per_vec > 0 && a.batch != 1) return fail(ND_ERR_INVALID, "gemv: x_rows_per_vec needs batch 1");
+  const long long nvec = a.x_rows_per_vec > 0 ? (a.n + a.x_rows_per_vec - 1) / a.x_rows_per_vec : a.batch;
+  if (a.k * nvec > 12288) return fail(ND_ERR_UNSUPPORTED, "gemv: input vectors above 12288 floats");
   if (a.w_dtype == ND_I8) {
     if (!a.w || !a.x || !a.y) return fail(ND_ERR_INVALID, "gemv: null operand");
-    if (a.k * a.batch > 12288) return fail(ND_ERR_UNSUPPORTED, "gemv: batch * k above 12288");
     return gemv_w8(a, stream);
   }
   if (a.k % 8) return fail(ND_ERR_INVALID, "gemv: k must be a multiple of 8");
-  if (a.k * a.batch > 12288) return fail(ND_ERR_UNSUPPORTED, "gemv: batch * k above 12288");
   if (a.w_dtype != ND_BF16 && a.w_dtype != ND_F16) return fail(ND_ERR_INVALID, "gemv: weight must be bf16 or f16");
   if (!a.w || !a.x || !a.y) return fail(ND_ERR_INVALID, "gemv: null operand");
-  const size_t shmem = static_cast<size_t>(a.k) * a.batch * sizeof(float);
-  if (shmem > 48 * 1024) {
-    static bool configured[64] = {};
-    int dev = 0;
-    ND_CUDA(cudaGetDevice(&dev));
-    if (!configured[dev & 63]) {
-      ND_CUDA(cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 48 * 1024 * 2));
-      configured[dev & 63] = true;
-    }
-  }
-  const long long warps_needed = a.n;
-  long long blocks = (warps_needed + 7) / 8;
+  const size_t shmem = static_cast<size_t>(a.k) * nvec * sizeof(float);
+  long long blocks = (a.n + 7) / 8;
   const long long cap = static_cast<long long>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
   gemv_kernel<<<static_cast<unsigned>(blocks), 256, shmem, stream>>>(
       static_cast<const uint16_t*>(a.w), a.w_dtype == ND_F16, a.n, static_cast<int>(a.k), a.x,
-      a.batch, a.pre_silu ? 1 : 0, a.bias, a.act, a.y);
+      a.batch, a.pre_silu ? 1 : 0, a.bias, a.act, a.y, a.x_rows_per_vec, static_cast<int>(nvec),
+      a.bias_period);
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }

@@ -73,9 +73,10 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(const int8_t* __restrict__
                                                       int group, int scale_cols,
                                                       const float* __restrict__ x, int B, int pre,
                                                       const float* __restrict__ bias, int act,
-                                                      float* __restrict__ y) {
+                                                      float* __restrict__ y, long long xrows, int nvec,
+                                                      long long bias_period) {
   extern __shared__ float xs[];
-  for (int i = threadIdx.x; i < B * K; i += blockDim.x) {
+  for (int i = threadIdx.x; i < nvec * K; i += blockDim.x) {
     float v = x[i];
     if (pre == 1) v = v / (1.0f + __expf(-v));
     xs[i] = v;
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(const int8_t* __restrict__
 #pragma unroll 4
       for (int b = 0; b < 4; ++b) {
         if (b < B) {
-          const float* xb = xs + b * K + 16 * c;
+          const float* xb = xs + (xrows > 0 ? (n / xrows) : b) * K + 16 * c;
           float sum = 0.f;
 #pragma unroll
           for (int i = 0; i < 16; ++i) sum += wv[i] * xb[i];
@@ -123,7 +124,7 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(const int8_t* __restrict__
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
         if (lane == 0) {
-          if (bias) v += bias[n];
+          if (bias) v += bias[bias_period > 0 ? n % bias_period : n];
           if (act == 1) v = v / (1.0f + __expf(-v));
           else if (act == 2) v = tanhf(v);
           y[static_cast<long long>(b) * N + n] = v;
@@ -152,14 +153,15 @@ int gemv_w8(const nd_gemv_args& a, cudaStream_t stream) {
   if (a.k % 16) return fail(ND_ERR_INVALID, "gemv: int8 weights need k % 16 == 0");
   const int64_t group = a.quant_group > 0 ? a.quant_group : a.k;
   if (group % 16 || a.k % group) return fail(ND_ERR_INVALID, "gemv: quant_group must be a multiple of 16 dividing k");
-  const size_t shmem = static_cast<size_t>(a.k) * a.batch * sizeof(float);
+  const long long nvec = a.x_rows_per_vec > 0 ? (a.n + a.x_rows_per_vec - 1) / a.x_rows_per_vec : a.batch;
+  const size_t shmem = static_cast<size_t>(a.k) * nvec * sizeof(float);
   long long blocks = (a.n + 7) / 8;
   const long long cap = static_cast<long long>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
   gemv_w8_kernel<<<static_cast<unsigned>(blocks), 256, shmem, stream>>>(
       static_cast<const int8_t*>(a.w), a.n, static_cast<int>(a.k), a.scales, a.scale_dtype == ND_F16,
       static_cast<int>(group), static_cast<int>(a.k / group), a.x, a.batch, a.pre_silu ? 1 : 0, a.bias,
-      a.act, a.y);
+      a.act, a.y, a.x_rows_per_vec, static_cast<int>(nvec), a.bias_period);
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }

@@ -27,7 +27,7 @@ class ModelDesc(C.Structure):
         "family", "width", "heads", "head_dim", "blocks", "mlp_width",
         "context_rows", "context_width", "latent_channels", "latent_height", "latent_width",
         "patch", "time_width", "batch", "compute", "weight_dtype", "quant_group",
-        "quant_scale_dtype")] + [("eps", C.c_float)]
+        "quant_scale_dtype", "adaln_rank")] + [("eps", C.c_float)]
 
 
 class NamedTensor(C.Structure):
@@ -134,15 +134,93 @@ class MMDiTConfig:
         return 2.0 * (self.blocks * per_block + emb)
 
 
+@dataclass
+class AnimaConfig:
+    """The Anima (Cosmos-Predict2 2B) DiT. Defaults
+    (28 blocks x 2048, 16 x 128 heads, exact-GELU MLP 8192, low-rank adaLN
+    256, 16 x 128 x 128 latent in 2x2 patches = 4096 tokens, cross-attention
+    to 256 x 1024 text rows, batch 2 = the CFG branches, bf16)."""
+    width: int = 2048
+    heads: int = 16
+    blocks: int = 28
+    mlp_width: int = 8192
+    adaln_rank: int = 256
+    context_rows: int = 256
+    context_width: int = 1024
+    latent_channels: int = 16
+    latent_height: int = 128
+    latent_width: int = 128
+    patch: int = 2
+    batch: int = 2
+    compute: int = _lib.ND_BF16
+    eps: float = 1e-6
+    weight_dtype: int = 0
+    quant_group: int = 32
+    quant_scale_dtype: int = _lib.ND_F16
+
+    @property
+    def tokens(self) -> int:
+        return (self.latent_height // self.patch) * (self.latent_width // self.patch)
+
+    def desc(self) -> ModelDesc:
+        d = ModelDesc()
+        d.family = FAMILY_ANIMA
+        d.width, d.heads, d.head_dim = self.width, self.heads, 128
+        d.blocks, d.mlp_width, d.adaln_rank = self.blocks, self.mlp_width, self.adaln_rank
+        d.context_rows, d.context_width = self.context_rows, self.context_width
+        d.latent_channels, d.latent_height, d.latent_width = (
+            self.latent_channels, self.latent_height, self.latent_width)
+        d.patch, d.time_width, d.batch = self.patch, self.width, self.batch
+        d.compute = self.compute
+        d.weight_dtype = self.weight_dtype or self.compute
+        d.quant_group, d.quant_scale_dtype = self.quant_group, self.quant_scale_dtype
+        d.eps = self.eps
+        return d
+
+    def quantized(self, rows: int, cols: int) -> bool:
+        g = self.quant_group or cols
+        return self.weight_dtype == _lib.ND_I8 and rows * cols >= 65536 and cols % g == 0 and cols % 16 == 0
+
+    def weight_table(self):
+        D, F, R, cw = self.width, self.mlp_width, self.adaln_rank, self.context_width
+        t = [("x_embedder.proj.1.weight", D, 68, True), ("t_embedder.1.linear_1.weight", D, D, True),
+             ("t_embedder.1.linear_2.weight", 3 * D, D, True), ("t_embedding_norm.weight", D, 1, True)]
+        for b in range(self.blocks):
+            p = f"blocks.{b}."
+            for sub in ("adaln_modulation_self_attn", "adaln_modulation_cross_attn", "adaln_modulation_mlp"):
+                t += [(p + sub + ".1.weight", R, D, True), (p + sub + ".2.weight", 3 * D, R, True)]
+            t += [(p + "self_attn.q_proj.weight", D, D, True), (p + "self_attn.k_proj.weight", D, D, True),
+                  (p + "self_attn.v_proj.weight", D, D, True), (p + "self_attn.output_proj.weight", D, D, True),
+                  (p + "self_attn.q_norm.weight", 128, 1, True), (p + "self_attn.k_norm.weight", 128, 1, True),
+                  (p + "cross_attn.q_proj.weight", D, D, True), (p + "cross_attn.k_proj.weight", D, cw, True),
+                  (p + "cross_attn.v_proj.weight", D, cw, True), (p + "cross_attn.output_proj.weight", D, D, True),
+                  (p + "cross_attn.q_norm.weight", 128, 1, True), (p + "cross_attn.k_norm.weight", 128, 1, True),
+                  (p + "mlp.layer1.weight", F, D, True), (p + "mlp.layer2.weight", D, F, True)]
+        t += [("final_layer.adaln_modulation.1.weight", R, D, True),
+              ("final_layer.adaln_modulation.2.weight", 2 * D, R, True),
+              ("final_layer.linear.weight", 64, D, True)]
+        return t
+
+    def flops_per_step(self) -> float:
+        D, F, T, c, R = self.width, self.mlp_width, self.tokens, self.context_rows, self.adaln_rank
+        per_image = (T * (4 * D * D + D * D + D * D + 2 * D * F) + c * self.context_width * 2 * D
+                     + 2 * T * T * D + 2 * T * c * D)
+        return 2.0 * self.batch * self.blocks * per_image
+
+
 def _name_seed(name: str, seed: int) -> int:
     return (zlib.crc32(name.encode()) ^ (seed * 0x9E3779B1)) & 0xFFFFFFFF
 
 
-def synthetic_weights(cfg: MMDiTConfig, seed: int = 0):
+def _table(cfg):
+    return cfg.weight_table() if hasattr(cfg, "weight_table") else weight_table(cfg)
+
+
+def synthetic_weights(cfg, seed: int = 0):
     """Seeded synthetic weights in the storage precision, one generator per
     tensor name: matrices and biases N(0, 0.02), norm weights 1 + N(0, 0.02).
     Yields (name, float32 array already rounded to bf16/fp16)."""
-    for name, rows, cols, _req in weight_table(cfg):
+    for name, rows, cols, _req in _table(cfg):
         rng = np.random.default_rng(_name_seed(name, seed))
         a = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02)
         if "norm" in name and name.endswith(".weight") and cols == 1:
@@ -154,14 +232,14 @@ def synthetic_weights(cfg: MMDiTConfig, seed: int = 0):
         yield name, a
 
 
-def synthetic_weights_device(cfg: MMDiTConfig, seed: int = 0, device="cuda"):
+def synthetic_weights_device(cfg, seed: int = 0, device="cuda"):
     """The same distributions as synthetic_weights, drawn on the GPU (a full
     BASELINE-size model is 20 G parameters): one torch generator per tensor
     name. Yields (name, CUDA tensor): matrices in the compute dtype, vectors fp32."""
     import torch
     dt = torch.bfloat16 if cfg.compute == _lib.ND_BF16 else torch.float16
     g = torch.Generator(device=device)
-    for name, rows, cols, _req in weight_table(cfg):
+    for name, rows, cols, _req in _table(cfg):
         g.manual_seed(_name_seed(name, seed))
         if cols == 1:
             t = torch.randn(rows, device=device, generator=g) * 0.02
@@ -389,7 +467,7 @@ class CudaDenoiser:
         self.close()
 
 
-def build_denoiser(device: Device, cfg: MMDiTConfig, weights) -> CudaDenoiser:
+def build_denoiser(device: Device, cfg, weights) -> CudaDenoiser:
     """IModelFamily.BuildDenoiser: create, copy every weight in, finalize.
     `weights` is an iterable of (name, array) or a dict."""
     d = CudaDenoiser(device, cfg.desc())

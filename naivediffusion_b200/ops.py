@@ -37,7 +37,8 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
            group_split: int | None = None, qk_norm: torch.Tensor | None = None,
            rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
            qk_cols: int = 0, eps: float = 1e-6, scales: torch.Tensor | None = None,
-           quant_group: int = 32) -> torch.Tensor:
+           quant_group: int = 32, norm_span: int = 0, rope_period: int = 0,
+           gate_stride: int = 0) -> torch.Tensor:
     """y = x . W^T + bias with a fused epilogue (Layers.Linear, Graph/Layers.cs:131-160).
 
     weight is [groups * out, in]; rows >= group_split use the second group.
@@ -72,6 +73,9 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     a.rope_sin = _ptr(rope_sin)
     a.qk_cols = qk_cols
     a.eps = eps
+    a.norm_span = norm_span
+    a.rope_period = rope_period
+    a.gate_stride = gate_stride
     if weight.dtype == torch.int8:
         a.weight_dtype = _lib.ND_I8
         a.scales = scales.data_ptr()

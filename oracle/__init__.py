@@ -350,3 +350,41 @@ def mmdit_forward(w: dict, cfg, latent, context, sigma, cos=None, sin=None, key_
     y = modulate(x[:n_img], emb[D:], emb[:D], eps)
     out = linear(y, w["proj_out.weight"], w.get("proj_out.bias"))
     return unpatchify(out, C_, Hl, Wl, p)[None]
+
+
+def anima_forward(w: dict, cfg, latent, context, sigma, cos=None, sin=None):
+    """The Anima denoiser step in fp32 (AnimaDit.Build / .Predict,
+    Models/Anima/AnimaDit.cs:124-134, 360-404), one batch item at a time.
+    latent [B, 16, H, W]; context [B, rows, width]."""
+    D, p, eps = cfg.width, cfg.patch, cfg.eps
+    Hl, Wl = cfg.latent_height, cfg.latent_width
+    if cos is None:
+        cos, sin = anima_rope_tables(Hl // p, Wl // p, 128)
+    tsin = sinusoid(np.float32(sigma), D)
+    temb = rmsnorm(tsin[None], w["t_embedding_norm.weight"], eps)[0]
+    lora = linear(silu(linear(tsin[None], w["t_embedder.1.linear_1.weight"])),
+                  w["t_embedder.1.linear_2.weight"])[0]
+    x_emb = np.ascontiguousarray(np.asarray(w["x_embedder.proj.1.weight"])[:, :64])
+    outs = []
+    for b in range(latent.shape[0]):
+        x = linear(patchify(np.asarray(latent[b], np.float32), p), x_emb)
+        for i in range(cfg.blocks):
+            q = f"blocks.{i}."
+            blk = dict(
+                self_mod1=w[q + "adaln_modulation_self_attn.1.weight"], self_mod2=w[q + "adaln_modulation_self_attn.2.weight"],
+                cross_mod1=w[q + "adaln_modulation_cross_attn.1.weight"], cross_mod2=w[q + "adaln_modulation_cross_attn.2.weight"],
+                mlp_mod1=w[q + "adaln_modulation_mlp.1.weight"], mlp_mod2=w[q + "adaln_modulation_mlp.2.weight"],
+                sq=w[q + "self_attn.q_proj.weight"], sk=w[q + "self_attn.k_proj.weight"],
+                sv=w[q + "self_attn.v_proj.weight"], so=w[q + "self_attn.output_proj.weight"],
+                sq_norm=w[q + "self_attn.q_norm.weight"], sk_norm=w[q + "self_attn.k_norm.weight"],
+                cq=w[q + "cross_attn.q_proj.weight"], ck=w[q + "cross_attn.k_proj.weight"],
+                cv=w[q + "cross_attn.v_proj.weight"], co=w[q + "cross_attn.output_proj.weight"],
+                cq_norm=w[q + "cross_attn.q_norm.weight"], ck_norm=w[q + "cross_attn.k_norm.weight"],
+                fc1=w[q + "mlp.layer1.weight"], fc2=w[q + "mlp.layer2.weight"])
+            x = anima_block(blk, x, context[b], temb, lora, cos, sin, cfg.heads, eps)
+        h = linear(silu(temb)[None], w["final_layer.adaln_modulation.1.weight"])
+        f = linear(h, w["final_layer.adaln_modulation.2.weight"])[0] + lora[:2 * D]
+        y = modulate(x, f[:D], f[D:], eps)
+        out = linear(y, w["final_layer.linear.weight"])
+        outs.append(unpatchify(out, cfg.latent_channels, Hl, Wl, p))
+    return np.stack(outs)

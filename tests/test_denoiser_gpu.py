@@ -119,3 +119,24 @@ def test_plugin_errors(device):
     with pytest.raises(_lib.NdError) as e:
         CudaDenoiser(device, bad)
     assert e.value.code == _lib.ND_ERR_INVALID
+
+
+ANIMA_SMALL = dict(width=256, heads=2, blocks=2, mlp_width=1024, adaln_rank=64, context_rows=96,
+                   context_width=128, latent_height=32, latent_width=16, batch=2)
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+def test_anima_step_matches_oracle(device, batch):
+    """The Anima DiT step (self-attention with 3-D RoPE, cross-attention to the
+    text rows, low-rank adaLN, exact GELU) against the oracle's AnimaDit."""
+    from naivediffusion_b200.denoiser import AnimaConfig
+    cfg = AnimaConfig(**{**ANIMA_SMALL, "batch": batch})
+    w = dict(synthetic_weights(cfg, seed=11))
+    rng = np.random.default_rng(11)
+    lat = rng.standard_normal((batch, 16, cfg.latent_height, cfg.latent_width)).astype(np.float32)
+    ctx = rng.standard_normal((batch, cfg.context_rows, cfg.context_width)).astype(np.float32)
+    with build_denoiser(device, cfg, w) as d:
+        y = d.predict(lat, 0.0, 0.6, {"context": ctx})
+    ref = O.anima_forward(w, cfg, lat, ctx, 0.6)
+    assert y.shape == lat.shape
+    assert rel(y, ref) < 2e-2 and cos(y, ref) > 0.999, (rel(y, ref), cos(y, ref))
