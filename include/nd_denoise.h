@@ -83,6 +83,14 @@ typedef struct nd_model_desc {
   int quant_scale_dtype;      /* int8: ND_F16 (BlockQuantizer) or ND_F32 */
   int adaln_rank;             /* Anima: rank of the low-rank adaLN (256) */
   float eps;                  /* norm epsilon (1e-6 for the DiTs) */
+  /* SDXL UNet levels (UNetModel.cs:20-40): channel multiplier of `width` and
+   * transformer depth per level, resnets per level; 0 levels: SDXL's
+   * {1, 2, 4} x 320, depths {0, 2, 10}, 2 resnets. */
+  int unet_levels;
+  int unet_mult[4];
+  int unet_depth[4];
+  int unet_resnets;
+  int add_width;              /* SDXL: width of the "add" conditioning (2816) */
 } nd_model_desc;
 
 typedef struct nd_named_tensor {
@@ -199,6 +207,7 @@ ND_API int nd_denoiser_destroy(nd_denoiser* d);
 #define ND_EPI_STORE_F32 5       /* residual(f32) = acc + bias              */
 #define ND_EPI_QK_NORM_ROPE 6    /* cols < qk_cols: head RMSNorm * w, RoPE  */
 #define ND_EPI_RESIDUAL_ADD 7    /* residual(f32) += acc + bias             */
+#define ND_EPI_ADD_STORE 8       /* y = acc + bias + addend (like y)        */
 
 typedef struct nd_linear_args {
   int dtype;            /* ND_BF16 or ND_F16: x, W and y */
@@ -237,7 +246,33 @@ typedef struct nd_linear_args {
    * (0 = row), for batch items stacked by rows. */
   int64_t norm_span;
   int64_t rope_period;
+  const void* addend;   /* ADD_STORE: [rows, ld_add], dtype like y */
+  int64_t ld_add;
 } nd_linear_args;
+
+/* ------------------------------------------------------------ conv op
+ * 3x3 convolution, padding 1, stride 1 or 2, NHWC activations, as an
+ * implicit GEMM on the same tcgen05 mainloop: rows = output pixels, K = the
+ * nine taps x input channels, each tap's patch loaded by TMA straight from the
+ * input (borders zero-filled). Replaces Layers.Conv2d
+ * (src/NaiveDiffusion/Graph/Layers.cs:115-128) -> DmlOps.Convolution
+ * (src/NaiveDiffusion/Dml/DmlOps.cs:265). Limits: in_channels % 64 == 0;
+ * output width divides 128; output pixels per image a multiple of 128. */
+typedef struct nd_conv_args {
+  int dtype;            /* ND_F16 or ND_BF16 */
+  int epilogue;         /* ND_EPI_STORE, ND_EPI_ADD_STORE, ND_EPI_STORE_F32, ND_EPI_SILU */
+  int batch, height, width, in_channels, out_channels, stride;
+  const void* x;        /* [batch, height, width, in_channels] */
+  const void* weight;   /* [out_channels, 3, 3, in_channels] */
+  const float* bias;    /* [out_channels], or [batch][out_channels] with per_batch_bias */
+  int per_batch_bias;   /* the ResBlock's time-embedding projection folded into the bias */
+  int64_t bias_stride;  /* per_batch_bias: floats between batch items' bias vectors (0: out_channels) */
+  void* y;              /* [batch, H_out, W_out, out_channels] */
+  float* y_f32;         /* STORE_F32 output */
+  const void* addend;   /* ADD_STORE: like y */
+} nd_conv_args;
+
+ND_API int nd_op_conv2d(const nd_conv_args* args, void* stream);
 
 /* Device pointers; stream is a cudaStream_t (NULL = legacy default stream).
  * Asynchronous: errors of the launch are returned, kernel faults surface at
@@ -279,6 +314,8 @@ typedef struct nd_modulate_args {
   int64_t vec_stride;   /* 0: width */
   int64_t group_split;  /* >= rows: one group */
   float eps;
+  int affine;           /* 1: y = LayerNorm(x) * scale + shift (a plain nn.LayerNorm,
+                           Layers.LayerNorm, Graph/Layers.cs:189-207) */
 } nd_modulate_args;
 
 ND_API int nd_op_modulate(const nd_modulate_args* args, void* stream);
@@ -313,6 +350,21 @@ typedef struct nd_gemv_args {
 } nd_gemv_args;
 
 ND_API int nd_op_gemv(const nd_gemv_args* args, void* stream);
+
+/* ------------------------------------------------------------ UNet ops
+ * GroupNorm over NHWC fp16/bf16: groups of channels normalized over
+ * (pixels, C/groups), then y = n * weight[c] + bias[c], optionally SiLU
+ * (Layers.GroupNorm, src/NaiveDiffusion/Graph/Layers.cs:166-185, and the
+ * ResBlocks' SiLU, Models/Sdxl/UNetModel.cs:230-254). x, y: [batch, pixels,
+ * channels]; weight / bias may be NULL (1 / 0). Uses library-owned device scratch for its partial sums
+ * (allocated on first use per device and grown when a larger shape needs it). */
+ND_API int nd_op_group_norm(const void* x, void* y, int dtype, int batch, int pixels, int channels,
+                            int groups, const float* weight, const float* bias, float eps,
+                            int silu_after, void* stream);
+
+/* GEGLU: in [rows, 2F] -> out [rows, F] = in[:, :F] * gelu(in[:, F:])
+ * (UNetLayers.Geglu, src/NaiveDiffusion/Models/Sdxl/UNetLayers.cs:30-46). */
+ND_API int nd_op_geglu(const void* in, void* out, int dtype, int64_t rows, int64_t F, void* stream);
 
 /* ------------------------------------------------------------ layout
  * latent [B, C, H, W] fp32 <-> tokens [B * (H/p) * (W/p), C*p*p] (row stride

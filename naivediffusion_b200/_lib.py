@@ -30,6 +30,7 @@ ND_EPI_RESIDUAL_GATE = 4
 ND_EPI_STORE_F32 = 5
 ND_EPI_QK_NORM_ROPE = 6
 ND_EPI_RESIDUAL_ADD = 7
+ND_EPI_ADD_STORE = 8
 
 
 class NdError(RuntimeError):
@@ -53,6 +54,18 @@ class LinearArgs(C.Structure):
         ("qk_cols", C.c_int64), ("eps", C.c_float),
         ("weight_dtype", C.c_int), ("scales", C.c_void_p), ("scale_dtype", C.c_int),
         ("quant_group", C.c_int64), ("norm_span", C.c_int64), ("rope_period", C.c_int64),
+        ("addend", C.c_void_p), ("ld_add", C.c_int64),
+    ]
+
+
+class ConvArgs(C.Structure):
+    _fields_ = [
+        ("dtype", C.c_int), ("epilogue", C.c_int),
+        ("batch", C.c_int), ("height", C.c_int), ("width", C.c_int), ("in_channels", C.c_int),
+        ("out_channels", C.c_int), ("stride", C.c_int),
+        ("x", C.c_void_p), ("weight", C.c_void_p), ("bias", C.c_void_p), ("per_batch_bias", C.c_int),
+        ("bias_stride", C.c_int64),
+        ("y", C.c_void_p), ("y_f32", C.c_void_p), ("addend", C.c_void_p),
     ]
 
 
@@ -74,6 +87,7 @@ class ModulateArgs(C.Structure):
         ("rows", C.c_int64), ("width", C.c_int64),
         ("shift", C.c_void_p), ("scale", C.c_void_p),
         ("vec_stride", C.c_int64), ("group_split", C.c_int64), ("eps", C.c_float),
+        ("affine", C.c_int),
     ]
 
 
@@ -114,6 +128,10 @@ def lib() -> C.CDLL:
                                      C.c_void_p, C.c_void_p, C.c_void_p]
         L.nd_op_dequantize.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int64,
                                        C.c_int64, C.c_void_p, C.c_int, C.c_void_p]
+        L.nd_op_group_norm.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                       C.c_void_p, C.c_void_p, C.c_float, C.c_int, C.c_void_p]
+        L.nd_op_geglu.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int64, C.c_void_p]
+        L.nd_op_conv2d.argtypes = [C.POINTER(ConvArgs), C.c_void_p]
         L.nd_op_attention.argtypes = [C.POINTER(AttentionArgs), C.c_void_p]
         L.nd_op_modulate.argtypes = [C.POINTER(ModulateArgs), C.c_void_p]
         L.nd_op_rmsnorm.argtypes = [C.POINTER(RmsNormArgs), C.c_void_p]

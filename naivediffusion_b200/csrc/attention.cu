@@ -10,7 +10,8 @@ namespace nd {
 
 int attention(const nd_attention_args& a, cudaStream_t stream) {
   if (a.dtype != ND_BF16 && a.dtype != ND_F16) return fail(ND_ERR_INVALID, "attention: dtype must be bf16 or f16");
-  if (a.head_dim != 128) return fail(ND_ERR_UNSUPPORTED, "attention: head_dim must be 128");
+  if (a.head_dim != 128 && a.head_dim != 64) return fail(ND_ERR_UNSUPPORTED, "attention: head_dim must be 64 or 128");
+  const int hd = a.head_dim;
   if (a.heads <= 0 || a.batch <= 0 || a.q_rows <= 0 || a.kv_rows <= 0)
     return fail(ND_ERR_INVALID, "attention: empty shape");
   if (a.q_rows > INT_MAX / 4 || a.kv_rows > INT_MAX / 4 || a.batch * a.q_rows > INT_MAX / 2 ||
@@ -18,9 +19,9 @@ int attention(const nd_attention_args& a, cudaStream_t stream) {
     return fail(ND_ERR_INVALID, "attention: shape too large");
   const int64_t limit = a.key_limit <= 0 || a.key_limit > a.kv_rows ? a.kv_rows : a.key_limit;
   if (!a.q || !a.k || !a.v || !a.out) return fail(ND_ERR_INVALID, "attention: null operand");
-  const int64_t width = static_cast<int64_t>(a.heads) * 128;
+  const int64_t width = static_cast<int64_t>(a.heads) * hd;
   if (a.ldq < width || a.ldk < width || a.ldv < width || a.ldo < width)
-    return fail(ND_ERR_INVALID, "attention: leading dimensions must cover heads * 128");
+    return fail(ND_ERR_INVALID, "attention: leading dimensions must cover heads * head_dim");
   if ((a.ldo % 8) || (reinterpret_cast<uintptr_t>(a.out) & 15u))
     return fail(ND_ERR_INVALID, "attention: out must be 16-byte aligned with ldo % 8 == 0");
   if (a.causal && a.q_rows != a.kv_rows) return fail(ND_ERR_INVALID, "attention: causal needs q_rows == kv_rows");
@@ -36,27 +37,37 @@ int attention(const nd_attention_args& a, cudaStream_t stream) {
   g.kv_rows = static_cast<int>(a.kv_rows);
   g.key_limit = static_cast<int>(limit);
   g.causal = a.causal ? 1 : 0;
-  const float scale = a.scale > 0.f ? a.scale : 1.0f / std::sqrt(128.0f);
+  const float scale = a.scale > 0.f ? a.scale : 1.0f / std::sqrt(static_cast<float>(hd));
   g.scale_log2 = scale * 1.4426950408889634f;
   g.out = a.out;
   g.ldo = a.ldo;
   g.out_f16 = a.dtype == ND_F16;
   g.idesc_s = make_idesc_f16(128, 128, a.dtype == ND_BF16);
-  g.idesc_pv = make_idesc_f16(128, 128, a.dtype == ND_BF16, false, true);
+  g.idesc_pv = make_idesc_f16(128, hd, a.dtype == ND_BF16, false, true);
   g.status = device_status();
   if (!g.status) return fail(ND_ERR_CUDA, "attention: no device status word");
 
-  static bool configured[64] = {};
-  int dev = 0;
-  ND_CUDA(cudaGetDevice(&dev));
-  if (!configured[dev & 63]) {
-    ND_CUDA(cudaFuncSetAttribute(attention_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 AttnSmem::kLaunchBytes));
-    configured[dev & 63] = true;
-  }
   dim3 grid(static_cast<unsigned>((a.q_rows + 255) / 256), static_cast<unsigned>(a.heads),
             static_cast<unsigned>(a.batch));
-  attention_sm100_kernel<<<grid, 320, AttnSmem::kLaunchBytes, stream>>>(tq, tk, tv, g);
+  int dev = 0;
+  ND_CUDA(cudaGetDevice(&dev));
+  if (hd == 128) {
+    static bool configured[64] = {};
+    if (!configured[dev & 63]) {
+      ND_CUDA(cudaFuncSetAttribute(attention_sm100_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   AttnSmem<128>::kLaunchBytes));
+      configured[dev & 63] = true;
+    }
+    attention_sm100_kernel<128><<<grid, 320, AttnSmem<128>::kLaunchBytes, stream>>>(tq, tk, tv, g);
+  } else {
+    static bool configured[64] = {};
+    if (!configured[dev & 63]) {
+      ND_CUDA(cudaFuncSetAttribute(attention_sm100_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   AttnSmem<64>::kLaunchBytes));
+      configured[dev & 63] = true;
+    }
+    attention_sm100_kernel<64><<<grid, 320, AttnSmem<64>::kLaunchBytes, stream>>>(tq, tk, tv, g);
+  }
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }

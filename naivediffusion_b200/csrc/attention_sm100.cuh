@@ -1,4 +1,4 @@
-// Flash attention forward for sm_100a, head_dim 128, bf16/fp16 in, fp32
+// Flash attention forward for sm_100a, head_dim 128 or 64, bf16/fp16 in, fp32
 // softmax and accumulation:   O = softmax(Q K^T / sqrt(d) + mask) V
 //
 // Replaces DmlOps.MultiheadAttention (Dml/DmlOps.cs:480-524) as Layers.Attend
@@ -16,7 +16,7 @@
 //               row max / exp2 / row sum in registers, P written back over
 //               S in TMEM as bf16, lazy O rescale (only when the running max
 //               grows by more than 2^8), final 1/l scaling and store.
-// TMEM columns: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512).
+// TMEM columns: S_A [0,128) S_B [128,256) O_A [256, 256+HD) O_B [256+HD, 256+2HD).
 // While tile A's softmax runs, the tensor core does PV_B and S_B of the
 // next step, and the other way round.
 #pragma once
@@ -38,12 +38,14 @@ struct AttnArgs {
   unsigned* status;
 };
 
+template <int HD>
 struct AttnSmem {
-  static constexpr int kTile = 128 * 128 * 2;  // one [128 x 128] bf16 tile = 32 KB
+  static constexpr int kChunks = HD / 64;       // 64-column (128-byte) chunks of a row
+  static constexpr int kTile = 128 * HD * 2;    // one [128 x HD] tile (32 KB at HD 128)
   static constexpr int kQ = 0;                  // Q_A, Q_B
   static constexpr int kK = 2 * kTile;          // K stages
   static constexpr int kV = 4 * kTile;          // V stages
-  static constexpr int kBar = 6 * kTile;        // 192 KB
+  static constexpr int kBar = 6 * kTile;        // 192 KB at HD 128
   // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], drain
   static constexpr int kNumBars = 14;
   static constexpr int kMisc = kBar + kNumBars * 8;
@@ -66,11 +68,12 @@ __device__ __forceinline__ void attn_store_row(void* out, long long ldo, long lo
   for (int i = 0; i < 4; ++i) dst[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
 }
 
+template <int HD>
 __global__ void __launch_bounds__(320, 1)
     attention_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                            const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
-  using L = AttnSmem;
+  using L = AttnSmem<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -98,7 +101,7 @@ __global__ void __launch_bounds__(320, 1)
   int limit = a.key_limit;
   if (a.causal) limit = min(limit, q_tile0 + 256);
   const int n_kv = (limit + 127) / 128;
-  const int col0 = head * 128;
+  const int col0 = head * HD;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -136,8 +139,8 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       mbar_arrive_expect_tx(q_full, 2 * L::kTile);
       for (int t = 0; t < 2; ++t)
-        for (int c = 0; c < 2; ++c)
-          tma_load_2d(sbase + L::kQ + t * L::kTile + c * (L::kTile / 2), &tmQ, q_full, col0 + c * 64,
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_2d(sbase + L::kQ + t * L::kTile + c * 16384, &tmQ, q_full, col0 + c * 64,
                       static_cast<int>(q_row0) + t * 128);
       q_issued = true;
       for (int j = 0; j < n_kv; ++j) {
@@ -149,12 +152,12 @@ __global__ void __launch_bounds__(320, 1)
         }
         const int krow = kv_row0 + j * 128;
         mbar_arrive_expect_tx(k_full(st), L::kTile);
-        for (int c = 0; c < 2; ++c)
-          tma_load_2d(sbase + L::kK + st * L::kTile + c * (L::kTile / 2), &tmK, k_full(st),
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_2d(sbase + L::kK + st * L::kTile + c * 16384, &tmK, k_full(st),
                       col0 + c * 64, krow);
         mbar_arrive_expect_tx(v_full(st), L::kTile);
-        for (int c = 0; c < 2; ++c)
-          tma_load_2d(sbase + L::kV + st * L::kTile + c * (L::kTile / 2), &tmV, v_full(st),
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_2d(sbase + L::kV + st * L::kTile + c * 16384, &tmV, v_full(st),
                       col0 + c * 64, krow);
         issued |= 1u << st;
         issued_parity = (issued_parity & ~(1u << st)) | (ph << st);
@@ -178,10 +181,10 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t q_addr = sbase + L::kQ + t * L::kTile;
         const uint32_t k_addr = sbase + L::kK + st * L::kTile;
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < L::kChunks; ++c)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t off = c * (L::kTile / 2) + kk * 32;
+            const uint32_t off = c * 16384 + kk * 32;
             umma_ss(tmem + t * 128, make_sdesc_sw128(q_addr + off, 16, 1024),
                     make_sdesc_sw128(k_addr + off, 16, 1024), a.idesc_s, (c | kk) != 0 ? 1u : 0u);
           }
@@ -193,8 +196,8 @@ __global__ void __launch_bounds__(320, 1)
         for (int kk = 0; kk < 8; ++kk) {
           // V as the B operand [N = d, K = keys], d contiguous: MN-major,
           // 64-wide d chunks 16 KB apart (LBO), 8-key groups 1 KB apart (SBO).
-          umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                  make_sdesc_sw128(v_addr + kk * 16 * 128, L::kTile / 2, 1024), a.idesc_pv,
+          umma_ts(tmem + 256 + t * HD, tmem + t * 128 + kk * 8,
+                  make_sdesc_sw128(v_addr + kk * 16 * 128, 16384, 1024), a.idesc_pv,
                   (acc || kk > 0) ? 1u : 0u);
         }
       };
@@ -246,7 +249,7 @@ __global__ void __launch_bounds__(320, 1)
     const long long q_row = q_row0 + t * 128 + r;
     const uint32_t lane_off = static_cast<uint32_t>(ew * 32) << 16;
     const uint32_t s_tm = tmem + lane_off + t * 128;
-    const uint32_t o_tm = tmem + lane_off + 256 + t * 128;
+    const uint32_t o_tm = tmem + lane_off + 256 + t * HD;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
@@ -289,7 +292,7 @@ __global__ void __launch_bounds__(320, 1)
       const float factor = fast_exp2(m - m_use);  // 0 on the first tile
       if (j > 0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < HD / 32; ++c) {
           uint32_t o[32];
           tmem_ld32(o_tm + c * 32, o);
           tmem_ld_wait();
@@ -329,7 +332,7 @@ __global__ void __launch_bounds__(320, 1)
       const float inv = 1.0f / l;
       const bool row_ok = q_in_batch < a.q_rows;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
         tmem_ld32(o_tm + c * 32, o);
         tmem_ld_wait();

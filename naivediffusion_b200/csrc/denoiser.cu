@@ -48,6 +48,26 @@ __global__ void convert_cols_kernel(const void* __restrict__ src, int st, long l
   }
 }
 
+__global__ void permute_conv_kernel(const void* __restrict__ src, int st, void* __restrict__ dst, int dt,
+                                    long long cout, int cin, int cin_pad) {
+  const long long n = cout * 9 * cin_pad;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % cin_pad);
+    const int tap = static_cast<int>((i / cin_pad) % 9);
+    const long long o = i / (9LL * cin_pad);
+    float v = 0.f;
+    if (c < cin) {
+      const long long j = (o * cin + c) * 9 + tap;
+      if (st == ND_F32) v = static_cast<const float*>(src)[j];
+      else if (st == ND_F16) v = __half2float(static_cast<const __half*>(src)[j]);
+      else v = __bfloat162float(static_cast<const __nv_bfloat16*>(src)[j]);
+    }
+    if (dt == ND_F16) static_cast<__half*>(dst)[i] = __float2half_rn(v);
+    else static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn(v);
+  }
+}
+
 int elem_bytes(int dt) { return dt == ND_F32 || dt == ND_I32 ? 4 : dt == ND_I8 ? 1 : 2; }
 
 struct DeviceGuard {
@@ -67,6 +87,15 @@ int convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n,
   if (n <= 0) return ND_OK;
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, sm_count() * 8LL));
   convert_kernel<<<grid, 256, 0, s>>>(src, src_dtype, dst, dst_dtype, n);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int permute_conv3x3(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t cout, int cin,
+                    int cin_pad, cudaStream_t s) {
+  const int64_t n = cout * 9 * cin_pad;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, sm_count() * 8LL));
+  permute_conv_kernel<<<grid, 256, 0, s>>>(src, src_dtype, dst, dst_dtype, cout, cin, cin_pad);
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }
@@ -177,12 +206,41 @@ int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* 
   int64_t n = 1;
   for (int i = 0; i < rank; ++i) n *= shape[i];
   const bool sliced = s.src_cols > s.cols && rank == 2 && shape[0] == s.rows && shape[1] == s.src_cols;
-  const bool shape_ok = sliced || (rank == 2 && shape[0] == s.rows && shape[1] == s.cols) ||
+  const bool pointwise = s.kind == kMatrix && rank == 4 && shape[0] == s.rows && shape[1] == s.cols &&
+                         shape[2] == 1 && shape[3] == 1;  // a 1x1 convolution's [out, in, 1, 1]
+  const bool shape_ok = s.kind == kConv3x3 || sliced || pointwise ||
+                        (rank == 2 && shape[0] == s.rows && shape[1] == s.cols) ||
                         (rank == 1 && s.cols == 1 && shape[0] == s.rows) ||
                         (n == s.rows * s.cols && s.kind == kVector);
   if (!shape_ok) {
     return fail(ND_ERR_INVALID, std::string("set_weight: ") + name + " has the wrong shape (expected [" +
                                     std::to_string(s.rows) + ", " + std::to_string(s.src_cols > s.cols ? s.src_cols : s.cols) + "])");
+  }
+  if (s.kind == kConv3x3) {
+    if (!(rank == 4 && shape[0] == s.rows && shape[1] == s.conv_cin && shape[2] == 3 && shape[3] == 3))
+      return fail(ND_ERR_INVALID, std::string("set_weight: ") + name + " must be [" + std::to_string(s.rows) +
+                                      ", " + std::to_string(s.conv_cin) + ", 3, 3]");
+    DeviceGuard g(d->dev->ordinal);
+    cudaStream_t st = d->dev->stream;
+    const size_t src_bytes = static_cast<size_t>(n) * elem_bytes(dtype);
+    const void* src = data;
+    if (!device) {
+      if (d->staging_bytes < src_bytes) {
+        if (d->staging) cudaFree(d->staging);
+        d->staging = nullptr;
+        d->staging_bytes = 0;
+        ND_CUDA(cudaMalloc(&d->staging, src_bytes));
+        d->staging_bytes = src_bytes;
+      }
+      ND_CUDA(cudaMemcpyAsync(d->staging, data, src_bytes, cudaMemcpyHostToDevice, st));
+      src = d->staging;
+    }
+    int rc = permute_conv3x3(src, dtype, s.dst, d->desc.compute, s.rows, s.conv_cin,
+                             static_cast<int>(s.cols / 9), st);
+    if (rc) return rc;
+    ND_CUDA(cudaStreamSynchronize(st));
+    s.set = true;
+    return ND_OK;
   }
   if (sliced) {
     // Keep the first `cols` columns of the checkpoint's wider matrix.
@@ -350,6 +408,7 @@ int nd_denoiser_create(nd_device* dev, const nd_model_desc* desc, nd_denoiser** 
   switch (desc->family) {
     case ND_FAMILY_MMDIT: d = nd::make_mmdit(); break;
     case ND_FAMILY_ANIMA: d = nd::make_anima(); break;
+    case ND_FAMILY_SDXL: d = nd::make_unet(); break;
     default: return nd::fail(ND_ERR_UNSUPPORTED, "nd_denoiser_create: unknown model family");
   }
   d->dev = dev;

@@ -16,9 +16,15 @@ struct nd_device {
   cudaStream_t stream = nullptr;
 };
 
+#define ND_TRY_RC(expr)     \
+  do {                      \
+    int rc_ = (expr);       \
+    if (rc_) return rc_;    \
+  } while (0)
+
 namespace nd {
 
-enum SlotKind { kMatrix = 0, kVector = 1 };
+enum SlotKind { kMatrix = 0, kVector = 1, kConv3x3 = 2 };
 
 struct WeightSlot {
   std::string name;
@@ -27,6 +33,7 @@ struct WeightSlot {
   void* dst = nullptr;     // device destination (compute dtype / int8 for matrices, fp32 vectors)
   void* scales = nullptr;  // int8 matrices: their scales (quant_group / scale type of the model)
   int64_t src_cols = 0;    // > cols: the checkpoint tensor is wider; keep its first `cols` columns
+  int conv_cin = 0;        // kConv3x3: torch [rows, conv_cin, 3, 3] stored as [rows, 3, 3, cols / 9]
   bool required = true;
   bool set = false;
 };
@@ -57,6 +64,9 @@ struct StepInputs {
 
 // Converts `n` elements of `src` (dtype) into `dst` (dst_dtype) on the device.
 int convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n, cudaStream_t s);
+// torch conv weights [cout, cin, 3, 3] -> [cout, 3, 3, cin_pad] (zero padded).
+int permute_conv3x3(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t cout, int cin,
+                    int cin_pad, cudaStream_t s);
 // Rows x cols of a row-major src (leading dimension src_ld) into a packed dst.
 int convert_cols(const void* src, int src_dtype, int64_t src_ld, void* dst, int dst_dtype, int64_t rows,
                  int64_t cols, cudaStream_t s);
@@ -130,4 +140,5 @@ struct nd_denoiser {
 namespace nd {
 nd_denoiser* make_mmdit();
 nd_denoiser* make_anima();
+nd_denoiser* make_unet();
 }  // namespace nd

@@ -14,7 +14,7 @@ namespace nd {
 
 namespace {
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool CONV = false>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                 const GemmArgs& g, cudaStream_t stream) {
   using L = GemmSmem<BN, STAGES>;
@@ -22,7 +22,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   int dev = 0;
   ND_CUDA(cudaGetDevice(&dev));
   if (!configured[dev & 63]) {
-    ND_CUDA(cudaFuncSetAttribute(gemm_sm100_kernel<BN, STAGES>,
+    ND_CUDA(cudaFuncSetAttribute(gemm_sm100_kernel<BN, STAGES, CONV>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, L::kLaunchBytes));
     configured[dev & 63] = true;
   }
@@ -30,7 +30,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   const int num_n = (g.N + BN - 1) / BN;
   const int tiles = num_m * num_n;
   const int grid = std::min(tiles, sm_count());
-  gemm_sm100_kernel<BN, STAGES><<<grid, 192, L::kLaunchBytes, stream>>>(ta, tb, tc, g);
+  gemm_sm100_kernel<BN, STAGES, CONV><<<grid, 192, L::kLaunchBytes, stream>>>(ta, tb, tc, g);
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }
@@ -81,7 +81,9 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
     return fail(ND_ERR_INVALID, "linear: group_split must be a positive multiple of 128");
   const int epi = a.epilogue;
   const bool resid = epi == ND_EPI_RESIDUAL_GATE || epi == ND_EPI_RESIDUAL_ADD || epi == ND_EPI_STORE_F32;
-  if (epi < 0 || epi > ND_EPI_RESIDUAL_ADD) return fail(ND_ERR_INVALID, "linear: unknown epilogue");
+  if (epi < 0 || epi > ND_EPI_ADD_STORE) return fail(ND_ERR_INVALID, "linear: unknown epilogue");
+  if (epi == ND_EPI_ADD_STORE && (!a.addend || a.ld_add < a.out_features || a.ld_add % 8 != 0))
+    return fail(ND_ERR_INVALID, "linear: ADD_STORE needs addend with ld_add >= out_features, ld_add % 8 == 0");
   if (resid && (!a.residual || a.ldr < a.out_features || a.ldr % 4 != 0))
     return fail(ND_ERR_INVALID, "linear: residual epilogue needs residual with ldr >= out_features, ldr % 4 == 0");
   if (!resid && (!a.y || a.ldy < a.out_features || a.ldy % 8 != 0))
@@ -143,6 +145,8 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
   g.norm_span = static_cast<int>(span > 0 ? span : 128);
   g.norm_sets = static_cast<int>(a.qk_cols > 0 && span > 0 ? a.qk_cols / span : 1);
   g.rope_period = static_cast<int>(a.rope_period);
+  g.addend = a.addend;
+  g.ld_add = a.ld_add;
   g.head_dim = 128;
   g.norm_eps = a.eps;
   g.status = device_status();
@@ -174,6 +178,79 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
   if (rc) return rc;
   if (bn == 256) return launch_gemm<256, 4>(ta, tb, tc, g, stream);
   return launch_gemm<128, 6>(ta, tb, tc, g, stream);
+}
+
+int conv2d(const nd_conv_args& c, cudaStream_t stream) {
+  if (c.dtype != ND_F16 && c.dtype != ND_BF16) return fail(ND_ERR_INVALID, "conv2d: dtype must be f16 or bf16");
+  if (c.batch <= 0 || c.height <= 0 || c.width <= 0 || c.in_channels <= 0 || c.out_channels <= 0)
+    return fail(ND_ERR_INVALID, "conv2d: empty shape");
+  if (c.in_channels % 64) return fail(ND_ERR_UNSUPPORTED, "conv2d: in_channels must be a multiple of 64");
+  if (c.stride != 1 && c.stride != 2) return fail(ND_ERR_UNSUPPORTED, "conv2d: stride must be 1 or 2");
+  const int ho = (c.height - 1) / c.stride + 1, wo = (c.width - 1) / c.stride + 1;
+  if (wo > 128 || 128 % wo != 0) return fail(ND_ERR_UNSUPPORTED, "conv2d: output width must divide 128");
+  if ((static_cast<int64_t>(ho) * wo) % 128 != 0) return fail(ND_ERR_UNSUPPORTED, "conv2d: output pixels per image must be a multiple of 128");
+  const int epi = c.epilogue;
+  if (epi != ND_EPI_STORE && epi != ND_EPI_ADD_STORE && epi != ND_EPI_STORE_F32 && epi != ND_EPI_SILU)
+    return fail(ND_ERR_INVALID, "conv2d: epilogue must be STORE, ADD_STORE, STORE_F32 or SILU");
+  if (!c.x || !c.weight) return fail(ND_ERR_INVALID, "conv2d: null operand");
+  if (epi == ND_EPI_STORE_F32 ? !c.y_f32 : !c.y) return fail(ND_ERR_INVALID, "conv2d: null output");
+  if (epi == ND_EPI_ADD_STORE && !c.addend) return fail(ND_ERR_INVALID, "conv2d: ADD_STORE needs addend");
+  if (epi != ND_EPI_STORE_F32 && c.out_channels % 8) return fail(ND_ERR_INVALID, "conv2d: out_channels % 8 for a 16-bit output");
+  if (c.out_channels % 4) return fail(ND_ERR_INVALID, "conv2d: out_channels must be a multiple of 4");
+  const int64_t M = static_cast<int64_t>(c.batch) * ho * wo;
+  const int64_t K = 9LL * c.in_channels;
+  if (M > INT_MAX || K > INT_MAX) return fail(ND_ERR_INVALID, "conv2d: shape too large");
+
+  CUtensorMap ta, tb, tc;
+  const int64_t cin = c.in_channels;
+  const int64_t dims[4] = {cin, c.width, c.height, c.batch};
+  const int64_t strides[3] = {cin * 2, cin * c.width * 2, cin * c.width * c.height * 2};
+  const int rows = 128 / wo;
+  // With a traversal stride s, TMA loads ceil(box / s) elements along a
+  // dimension, so the box spans s x the output extent.
+  const int box[4] = {64, wo * c.stride, rows * c.stride, 1};
+  const int es[4] = {1, c.stride, c.stride, 1};
+  int rc = make_tmap_4d(&ta, c.x, c.dtype, dims, strides, box, es, 128);
+  if (rc) return rc;
+  if (epi == ND_EPI_STORE_F32) {
+    rc = make_tmap_2d_typed(&tc, c.y_f32, ND_F32, M, c.out_channels, c.out_channels, 32, 32, 128);
+  } else {
+    rc = make_tmap_2d_typed(&tc, c.y, c.dtype, M, c.out_channels, c.out_channels, 32, 32, 64);
+  }
+  if (rc) return rc;
+
+  GemmArgs g{};
+  g.M = static_cast<int>(M);
+  g.N = c.out_channels;
+  g.K = static_cast<int>(K);
+  g.epi = epi;
+  g.out_f16 = c.dtype == ND_F16;
+  g.out = c.y;
+  g.ldo = c.out_channels;
+  g.resid = c.y_f32;
+  g.ldr = c.out_channels;
+  g.bias = c.bias;
+  g.bias_stride = static_cast<int>(c.bias_stride > 0 ? c.bias_stride : c.out_channels);
+  g.group_split = c.per_batch_bias ? ho * wo : INT_MAX;
+  g.periodic_groups = c.per_batch_bias ? 1 : 0;
+  g.shared_weights = 1;
+  g.addend = c.addend;
+  g.ld_add = c.out_channels;
+  g.conv_kpc = c.in_channels / 64;
+  g.conv_hw = ho * wo;
+  g.conv_w_out = wo;
+  g.conv_stride = c.stride;
+  g.head_dim = 128;
+  g.status = device_status();
+  if (!g.status) return fail(ND_ERR_CUDA, "conv2d: no device status word");
+  const int sms = sm_count();
+  const int64_t tiles256 = ((M + 127) / 128) * ((c.out_channels + 255) / 256);
+  const int bn = (c.out_channels >= 256 && tiles256 >= sms) ? 256 : 128;
+  g.idesc = make_idesc_f16(128, bn, c.dtype == ND_BF16);
+  rc = make_tmap_2d(&tb, c.weight, 2, c.out_channels, K, K, bn, 64, true);
+  if (rc) return rc;
+  if (bn == 256) return launch_gemm<256, 4, true>(ta, tb, tc, g, stream);
+  return launch_gemm<128, 6, true>(ta, tb, tc, g, stream);
 }
 
 int dequantize(const int8_t* q, const void* scales, int scale_dtype, int64_t quant_group, int64_t rows,

@@ -33,6 +33,7 @@ enum GemmEpilogue : int {
   kEpiStoreF32 = 5,       // outf(f32) = acc + bias
   kEpiQkNormRope = 6,     // columns < qk_cols: per-head RMSNorm * w, then RoPE
   kEpiResidualAdd = 7,    // resid(f32) += acc + bias
+  kEpiAddStore = 8,       // out = acc + bias + addend[row, col]     (bf16/f16)
 };
 
 struct GemmArgs {
@@ -65,7 +66,24 @@ struct GemmArgs {
   int w8_group;
   int w8_scale_cols;
   int w8_scale_f16;
+  // kEpiAddStore: the tensor added to the result, like out (ld_add elements)
+  const void* addend;
+  long long ld_add;
+  // groups of rows: periodic (group = row / group_split: one per batch item)
+  // and weights shared by every group (only bias / gate differ)
+  int periodic_groups;
+  int shared_weights;
+  // implicit-GEMM conv3x3 (pad 1): A rows are output pixels, K = 9 taps x Cin
+  int conv_kpc;      // Cin / 64 channel chunks per tap
+  int conv_hw;       // H_out * W_out pixels per image
+  int conv_w_out;
+  int conv_stride;
 };
+
+__device__ __forceinline__ int row_group(const GemmArgs& a, int m0) {
+  if (a.periodic_groups) return m0 / a.group_split;
+  return m0 >= a.group_split ? 1 : 0;
+}
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -191,6 +209,34 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, const CUtensor
     case kEpiStoreF32:
       kind = kEmitF32;
       break;
+    case kEpiAddStore: {
+      const int row = row0 + lane;
+      if (row < a.M) {
+        const uint16_t* ad = static_cast<const uint16_t*>(a.addend) + static_cast<long long>(row) * a.ld_add + col;
+        if (col + 32 <= a.N) {
+          const uint4* a4 = reinterpret_cast<const uint4*>(ad);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 t = __ldg(a4 + i);
+            const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float2 f = a.out_f16 ? __half22float2(*reinterpret_cast<const __half2*>(&w[j]))
+                                   : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+              v[8 * i + 2 * j] += f.x;
+              v[8 * i + 2 * j + 1] += f.y;
+            }
+          }
+        } else {
+          for (int i = 0; i < 32 && col + i < a.N; ++i) {
+            const uint16_t h = ad[i];
+            v[i] += a.out_f16 ? __half2float(*reinterpret_cast<const __half*>(&h))
+                              : __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(&h));
+          }
+        }
+      }
+      break;
+    }
     default:
       break;
   }
@@ -256,7 +302,7 @@ __device__ __forceinline__ void epilogue_head_norm_rope(const GemmArgs& a, const
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool CONV = false>
 __global__ void __launch_bounds__(192, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
@@ -320,8 +366,13 @@ __global__ void __launch_bounds__(192, 1)
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const int m0 = (t % num_m) * 128;
         const int n0 = (t / num_m) * BN;
-        const int group = m0 >= args.group_split ? 1 : 0;
-        const int brow = group * args.N + n0;
+        const int group = row_group(args, m0);
+        const int brow = (args.shared_weights ? 0 : group * args.N) + n0;
+        int img = 0, y0 = 0;
+        if constexpr (CONV) {
+          img = m0 / args.conv_hw;
+          y0 = (m0 - img * args.conv_hw) / args.conv_w_out;
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.status,
                          kStatusTimeoutProducer)) {
@@ -331,7 +382,16 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t a_dst = sbase + stage * L::kStageBytes;
           const uint32_t b_dst = a_dst + L::kABytes;
           mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
-          tma_load_2d(a_dst, &tmA, full_bar(stage), kb * 64, m0);
+          if constexpr (CONV) {
+            // 128 output pixels x 64 input channels of tap (dy, dx): a 4-D box
+            // (channels, x, y, image) of the NHWC input, borders zero-filled.
+            const int tap = kb / args.conv_kpc;
+            const int c0 = (kb - tap * args.conv_kpc) * 64;
+            const int dy = tap / 3, dx = tap - dy * 3;
+            tma_load_4d(a_dst, &tmA, full_bar(stage), c0, dx - 1, y0 * args.conv_stride + dy - 1, img);
+          } else {
+            tma_load_2d(a_dst, &tmA, full_bar(stage), kb * 64, m0);
+          }
           tma_load_2d(b_dst, &tmB, full_bar(stage), kb * 64, brow);
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -414,7 +474,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int m0 = (t % num_m) * 128;
       const int n0 = (t / num_m) * BN;
-      const int group = m0 >= args.group_split ? 1 : 0;
+      const int group = row_group(args, m0);
       const int row0 = m0 + ew * 32;
       const int row = m0 + row_in_tile;
       const bool row_ok = row < args.M;

@@ -123,8 +123,8 @@ __global__ void __launch_bounds__(384, 1)
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const int m0 = (t % num_m) * 128;
         const int n0 = (t / num_m) * BN;
-        const int group = m0 >= args.group_split ? 1 : 0;
-        const int brow = group * args.N + n0;
+        const int group = row_group(args, m0);
+        const int brow = (args.shared_weights ? 0 : group * args.N) + n0;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.status, kStatusTimeoutProducer)) {
             ok = false;
@@ -199,12 +199,12 @@ __global__ void __launch_bounds__(384, 1)
     uint32_t phase = 0;
     bool ok = true;
     const bool f16_scales = args.w8_scale_f16 != 0;
-    const long long w_rows = (args.group_split < args.M ? 2LL : 1LL) * args.N;
+    const long long w_rows = (args.shared_weights || args.group_split >= args.M ? 1LL : 2LL) * args.N;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       const int m0 = (t % num_m) * 128;
       const int n0 = (t / num_m) * BN;
-      const int group = m0 >= args.group_split ? 1 : 0;
-      const long long wrow0 = static_cast<long long>(group) * args.N + n0;
+      const int group = row_group(args, m0);
+      const long long wrow0 = (args.shared_weights ? 0LL : static_cast<long long>(group) * args.N) + n0;
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!mbar_wait(full_bar(stage), phase, abort_flag, args.status, kStatusTimeoutProducer)) {
           ok = false;
@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(384, 1)
       tc_fence_after();
       const int m0 = (t % num_m) * 128;
       const int n0 = (t / num_m) * BN;
-      const int group = m0 >= args.group_split ? 1 : 0;
+      const int group = row_group(args, m0);
       const int row0 = m0 + ew * 32;
       const int row = m0 + row_in_tile;
       const bool row_ok = row < args.M;

@@ -38,9 +38,15 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, int64_t row
 int make_tmap_2d_typed(CUtensorMap* map, const void* base, int nd_dtype, int64_t rows, int64_t cols,
                        int64_t ld, int box_rows, int box_cols, int swizzle_bytes);
 
+// A 4-D tensor map (innermost first) with a [box] and traversal strides.
+int make_tmap_4d(CUtensorMap* map, const void* base, int nd_dtype, const int64_t dims[4],
+                 const int64_t strides_bytes[3], const int box[4], const int elem_strides[4],
+                 int swizzle_bytes);
+
 // ----------------------------------------------------------------- kernels
 
 int linear(const nd_linear_args& a, cudaStream_t stream);
+int conv2d(const nd_conv_args& c, cudaStream_t stream);
 int dequantize(const int8_t* q, const void* scales, int scale_dtype, int64_t quant_group, int64_t rows,
                int64_t cols, void* out, int out_dtype, cudaStream_t stream);
 int attention(const nd_attention_args& a, cudaStream_t stream);
@@ -54,5 +60,17 @@ int patchify(const float* lat, void* tok, int out_dtype, int B, int C, int H, in
              int64_t ldt, cudaStream_t stream);
 int unpatchify(const float* tok, int64_t ldt, float* lat, int B, int C, int H, int W, int p,
                cudaStream_t stream);
+// UNet (NHWC) kernels
+size_t group_norm_scratch(int B, int HW, int C, int G);
+int group_norm(const void* x, void* y, int dtype, int B, int HW, int C, int G, const float* w,
+               const float* bias, float eps, int silu_after, void* scratch, size_t scratch_bytes,
+               cudaStream_t s);
+int geglu(const void* in, void* out, int dtype, int64_t rows, int64_t F, cudaStream_t s);
+int upsample2x(const void* in, void* out, int B, int H, int W, int C, cudaStream_t s);
+int concat_channels(const void* a, int ca, const void* b, int cb, void* out, int64_t pixels, cudaStream_t s);
+int nchw_to_nhwc(const float* in, void* out, int dtype, int B, int C, int HW, int cpad, cudaStream_t s);
+int nhwc_to_nchw(const float* in, float* out, int B, int C, int HW, cudaStream_t s);
+int add_vectors(float* dst, const float* src, int64_t n, cudaStream_t s);          // dst += src
+int add_vectors2(float* out, const float* a, const float* b, int64_t n, cudaStream_t s);  // out = a + b
 
 }  // namespace nd

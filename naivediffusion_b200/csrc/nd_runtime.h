@@ -9,6 +9,10 @@ namespace nd {
 // when a bounded wait runs out. Allocated on first use per device.
 unsigned* device_status();
 
+// Library-owned device scratch of at least `need` bytes for op-level entry
+// points (grown with cudaMalloc when needed; reused by every call).
+int op_scratch(size_t need, void** ptr, size_t* bytes);
+
 // Read and clear the current device's status word (synchronizes `stream`).
 int check_device_status(cudaStream_t stream);
 

@@ -42,7 +42,8 @@ __global__ void __launch_bounds__(256) modulate_kernel(const float* __restrict__
                                                        int out_type, int rows, int width,
                                                        const float* __restrict__ shift,
                                                        const float* __restrict__ scale,
-                                                       int vec_stride, int split, float eps) {
+                                                       int vec_stride, int split, float eps,
+                                                       int affine) {
   __shared__ float red[2][2][4];
   const int half = threadIdx.x >> 7;        // which of the block's two rows
   const int t = threadIdx.x & 127;
@@ -82,6 +83,7 @@ __global__ void __launch_bounds__(256) modulate_kernel(const float* __restrict__
   const int g = row >= split ? 1 : 0;
   const float4* sc = reinterpret_cast<const float4*>(scale + g * vec_stride);
   const float4* sh = shift ? reinterpret_cast<const float4*>(shift + g * vec_stride) : nullptr;
+  const float one = affine ? 0.f : 1.f;
 #pragma unroll
   for (int i = 0; i < V; ++i) {
     const int c = t + 128 * i;
@@ -89,10 +91,10 @@ __global__ void __launch_bounds__(256) modulate_kernel(const float* __restrict__
       const float4 k = __ldg(sc + c);
       const float4 b = sh ? __ldg(sh + c) : make_float4(0.f, 0.f, 0.f, 0.f);
       float4 o;
-      o.x = (v[i].x - mean) * rstd * (1.f + k.x) + b.x;
-      o.y = (v[i].y - mean) * rstd * (1.f + k.y) + b.y;
-      o.z = (v[i].z - mean) * rstd * (1.f + k.z) + b.z;
-      o.w = (v[i].w - mean) * rstd * (1.f + k.w) + b.w;
+      o.x = (v[i].x - mean) * rstd * (one + k.x) + b.x;
+      o.y = (v[i].y - mean) * rstd * (one + k.y) + b.y;
+      o.z = (v[i].z - mean) * rstd * (one + k.z) + b.z;
+      o.w = (v[i].w - mean) * rstd * (one + k.w) + b.w;
       store4(y, static_cast<long long>(row) * ldy + 4 * c, o, out_type);
     }
   }
@@ -282,7 +284,7 @@ int modulate(const nd_modulate_args& a, cudaStream_t stream) {
   const int vs = a.vec_stride ? static_cast<int>(a.vec_stride) : static_cast<int>(a.width);
   const unsigned grid = static_cast<unsigned>((rows + 1) / 2);
   const int per_thread = (static_cast<int>(a.width) / 4 + 127) / 128;
-#define ND_MOD(V) modulate_kernel<V><<<grid, 256, 0, stream>>>(a.x, a.ldx, a.y, a.ldy, a.out_dtype, rows, static_cast<int>(a.width), a.shift, a.scale, vs, split, a.eps)
+#define ND_MOD(V) modulate_kernel<V><<<grid, 256, 0, stream>>>(a.x, a.ldx, a.y, a.ldy, a.out_dtype, rows, static_cast<int>(a.width), a.shift, a.scale, vs, split, a.eps, a.affine)
   if (per_thread <= 1) ND_MOD(1);
   else if (per_thread <= 2) ND_MOD(2);
   else if (per_thread <= 4) ND_MOD(4);

@@ -71,6 +71,31 @@ unsigned* device_status() {
   return g_status[dev & 63];
 }
 
+namespace {
+void* g_op_scratch[64] = {};
+size_t g_op_scratch_bytes[64] = {};
+}  // namespace
+
+int op_scratch(size_t need, void** ptr, size_t* bytes) {
+  int dev = 0;
+  ND_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  if (g_op_scratch_bytes[dev & 63] < need) {
+    // Growing: wait for work that may still read the old buffer.
+    ND_CUDA(cudaDeviceSynchronize());
+    if (g_op_scratch[dev & 63]) cudaFree(g_op_scratch[dev & 63]);
+    g_op_scratch[dev & 63] = nullptr;
+    g_op_scratch_bytes[dev & 63] = 0;
+    void* p = nullptr;
+    ND_CUDA(cudaMalloc(&p, need));
+    g_op_scratch[dev & 63] = p;
+    g_op_scratch_bytes[dev & 63] = need;
+  }
+  *ptr = g_op_scratch[dev & 63];
+  *bytes = g_op_scratch_bytes[dev & 63];
+  return ND_OK;
+}
+
 int check_device_status(cudaStream_t stream) {
   ND_CUDA(cudaStreamSynchronize(stream));
   unsigned* st = device_status();
@@ -117,6 +142,38 @@ int make_tmap_2d_typed(CUtensorMap* map, const void* base, int nd_dtype, int64_t
     snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld ld=%lld box=%dx%d",
              static_cast<int>(r), static_cast<long long>(rows), static_cast<long long>(cols),
              static_cast<long long>(ld), box_rows, box_cols);
+    return fail(ND_ERR_INVALID, buf);
+  }
+  return ND_OK;
+}
+
+int make_tmap_4d(CUtensorMap* map, const void* base, int nd_dtype, const int64_t dims[4],
+                 const int64_t strides_bytes[3], const int box[4], const int elem_strides[4],
+                 int swizzle_bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(ND_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (reinterpret_cast<uintptr_t>(base) & 15u) return fail(ND_ERR_INVALID, "TMA base must be 16-byte aligned");
+  for (int i = 0; i < 3; ++i)
+    if (strides_bytes[i] % 16) return fail(ND_ERR_INVALID, "TMA strides must be multiples of 16 bytes");
+  CUtensorMapDataType dt = nd_dtype == ND_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                           : nd_dtype == ND_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t d[4], st[3];
+  cuuint32_t b[4], es[4];
+  for (int i = 0; i < 4; ++i) {
+    d[i] = static_cast<cuuint64_t>(dims[i]);
+    b[i] = static_cast<cuuint32_t>(box[i]);
+    es[i] = static_cast<cuuint32_t>(elem_strides[i]);
+  }
+  for (int i = 0; i < 3; ++i) st[i] = static_cast<cuuint64_t>(strides_bytes[i]);
+  CUtensorMapSwizzle sw = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = fn(map, dt, 4, const_cast<void*>(base), d, st, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[160];
+    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled (4-D) failed (%d)", static_cast<int>(r));
     return fail(ND_ERR_INVALID, buf);
   }
   return ND_OK;
@@ -208,6 +265,28 @@ int nd_op_quantize(const void* src, int src_dtype, int64_t rows, int64_t cols, i
     return nd::fail(ND_ERR_INVALID, "nd_op_quantize: scale_dtype must be ND_F16 or ND_F32");
   return nd::quantize_weights(src, src_dtype, rows, cols, quant_group, scale_dtype == ND_F16, q, scales,
                               static_cast<cudaStream_t>(stream));
+}
+
+int nd_op_conv2d(const nd_conv_args* args, void* stream) {
+  if (!args) return nd::fail(ND_ERR_INVALID, "nd_op_conv2d: null args");
+  return nd::conv2d(*args, static_cast<cudaStream_t>(stream));
+}
+
+int nd_op_group_norm(const void* x, void* y, int dtype, int batch, int pixels, int channels, int groups,
+                     const float* weight, const float* bias, float eps, int silu_after, void* stream) {
+  if (batch <= 0 || pixels <= 0 || channels <= 0 || groups <= 0)
+    return nd::fail(ND_ERR_INVALID, "nd_op_group_norm: bad shape");
+  void* scratch = nullptr;
+  size_t bytes = 0;
+  int rc = nd::op_scratch(nd::group_norm_scratch(batch, pixels, channels, groups), &scratch, &bytes);
+  if (rc) return rc;
+  return nd::group_norm(x, y, dtype, batch, pixels, channels, groups, weight, bias, eps, silu_after,
+                        scratch, bytes, static_cast<cudaStream_t>(stream));
+}
+
+int nd_op_geglu(const void* in, void* out, int dtype, int64_t rows, int64_t F, void* stream) {
+  if (!in || !out) return nd::fail(ND_ERR_INVALID, "nd_op_geglu: null operand");
+  return nd::geglu(in, out, dtype, rows, F, static_cast<cudaStream_t>(stream));
 }
 
 int nd_op_sync(void* stream) { return nd::check_device_status(static_cast<cudaStream_t>(stream)); }

@@ -1,0 +1,283 @@
+// The UNet's memory-bound kernels over NHWC fp16 activations: GroupNorm
+// (+ SiLU), GEGLU, nearest 2x upsample, channel concat, NCHW <-> NHWC.
+//
+// GroupNorm (Layers.GroupNorm, Graph/Layers.cs:166-185: mean-variance
+// normalization over (C/G, H, W) of each group, then the per-channel affine)
+// runs in three passes: per-chunk channel sums in fp64, per-group mean and
+// 1/sqrt(var + eps), then one vectorized pass applying it (fused with the SiLU
+// the ResBlocks put after it, UNetModel.ResnetBlock, Models/Sdxl/UNetModel.cs:230-254).
+#include <algorithm>
+#include <climits>
+
+#include "nd_common.cuh"
+#include "nd_internal.h"
+#include "nd_runtime.h"
+
+namespace nd {
+
+namespace {
+
+__device__ __forceinline__ float ld16(const void* p, long long i, int f16) {
+  const uint16_t h = static_cast<const uint16_t*>(p)[i];
+  return f16 ? __half2float(*reinterpret_cast<const __half*>(&h))
+             : __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(&h));
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, int f16, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = f16 ? __half22float2(*reinterpret_cast<const __half2*>(&w[i]))
+                         : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&v)[8], int f16) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = f16 ? pack_f16(v[2 * i], v[2 * i + 1]) : pack_bf16(v[2 * i], v[2 * i + 1]);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Per (image, pixel chunk, channel): sum and sum of squares in fp64.
+__global__ void __launch_bounds__(256) gn_partial_kernel(const void* __restrict__ x, int f16, int hw,
+                                                         int C, int chunk, double2* __restrict__ part) {
+  const int ck = blockIdx.x, b = blockIdx.y;
+  const int p0 = ck * chunk, p1 = min(hw, p0 + chunk);
+  const long long base = static_cast<long long>(b) * hw * C;
+  const int nchunks = gridDim.x;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    double s1 = 0.0, s2 = 0.0;
+    for (int p = p0; p < p1; ++p) {
+      const double v = ld16(x, base + static_cast<long long>(p) * C + c, f16);
+      s1 += v;
+      s2 += v * v;
+    }
+    part[(static_cast<long long>(b) * nchunks + ck) * C + c] = make_double2(s1, s2);
+  }
+}
+
+// Per (image, group): mean and 1/sqrt(var + eps) over hw x C/G values.
+__global__ void gn_finalize_kernel(const double2* __restrict__ part, int nchunks, int C, int G, int hw,
+                                   float eps, float2* __restrict__ stats) {
+  const int b = blockIdx.x / G, g = blockIdx.x % G;
+  const int cg = C / G;
+  double s1 = 0.0, s2 = 0.0;
+  for (int i = threadIdx.x; i < nchunks * cg; i += blockDim.x) {
+    const int ck = i / cg, c = g * cg + i % cg;
+    const double2 v = part[(static_cast<long long>(b) * nchunks + ck) * C + c];
+    s1 += v.x;
+    s2 += v.y;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+  }
+  if (threadIdx.x == 0) {
+    const double n = static_cast<double>(hw) * cg;
+    const double mean = s1 / n;
+    const double var = fmax(s2 / n - mean * mean, 0.0);
+    stats[blockIdx.x] = make_float2(static_cast<float>(mean), static_cast<float>(1.0 / sqrt(var + eps)));
+  }
+}
+
+__global__ void __launch_bounds__(256) gn_apply_kernel(const void* __restrict__ x, void* __restrict__ y,
+                                                       int f16, long long pixels_total, int hw, int C,
+                                                       int G, const float2* __restrict__ stats,
+                                                       const float* __restrict__ w,
+                                                       const float* __restrict__ bias, int silu_after) {
+  const int c8 = C / 8;
+  const int cg = C / G;
+  const long long n = pixels_total * c8;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long pix = i / c8;
+    const int c0 = static_cast<int>(i % c8) * 8;
+    const int b = static_cast<int>(pix / hw);
+    float v[8];
+    unpack8(reinterpret_cast<const uint4*>(x)[i], f16, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int c = c0 + k;
+      const float2 st = stats[b * G + c / cg];
+      float o = (v[k] - st.x) * st.y * (w ? w[c] : 1.0f) + (bias ? bias[c] : 0.0f);
+      if (silu_after) o = o / (1.0f + __expf(-o));
+      v[k] = o;
+    }
+    reinterpret_cast<uint4*>(y)[i] = pack8(v, f16);
+  }
+}
+
+// GEGLU (UNetLayers.Geglu, Models/Sdxl/UNetLayers.cs:30-46): the projection's
+// first half times the exact GELU of its second half.
+__global__ void geglu_kernel(const void* __restrict__ in, void* __restrict__ out, int f16, long long rows,
+                             int F) {
+  const int f8 = F / 8;
+  const long long n = rows * f8;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / f8;
+    const int c = static_cast<int>(i % f8);
+    const uint4* row = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(in) + r * 2 * F);
+    float h[8], g[8];
+    unpack8(row[c], f16, h);
+    unpack8(row[f8 + c], f16, g);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) h[k] *= gelu_erf(g[k]);
+    reinterpret_cast<uint4*>(out)[i] = pack8(h, f16);
+  }
+}
+
+__global__ void upsample2x_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, int B, int H, int W,
+                                  int c8) {
+  const long long n = static_cast<long long>(B) * 2 * H * 2 * W * c8;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % c8);
+    const long long pix = i / c8;
+    const int xo = static_cast<int>(pix % (2 * W));
+    const int yo = static_cast<int>((pix / (2 * W)) % (2 * H));
+    const int b = static_cast<int>(pix / (4LL * H * W));
+    out[i] = in[((static_cast<long long>(b) * H + yo / 2) * W + xo / 2) * c8 + c];
+  }
+}
+
+__global__ void concat_kernel(const uint4* __restrict__ a, int ca8, const uint4* __restrict__ b, int cb8,
+                              uint4* __restrict__ out, long long pixels) {
+  const int c8 = ca8 + cb8;
+  const long long n = pixels * c8;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long p = i / c8;
+    const int c = static_cast<int>(i % c8);
+    out[i] = c < ca8 ? a[p * ca8 + c] : b[p * cb8 + (c - ca8)];
+  }
+}
+
+// NCHW fp32 -> NHWC 16-bit with the channels zero-padded to cpad.
+__global__ void nchw_to_nhwc_kernel(const float* __restrict__ in, void* __restrict__ out, int f16, int B,
+                                    int C, int HW, int cpad) {
+  const long long n = static_cast<long long>(B) * HW * cpad;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % cpad);
+    const long long pix = i / cpad;
+    const int p = static_cast<int>(pix % HW);
+    const int b = static_cast<int>(pix / HW);
+    const float v = c < C ? in[(static_cast<long long>(b) * C + c) * HW + p] : 0.f;
+    if (f16) static_cast<__half*>(out)[i] = __float2half_rn(v);
+    else static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+  }
+}
+
+// NHWC fp32 [B, HW, C] -> NCHW fp32.
+__global__ void nhwc_to_nchw_kernel(const float* __restrict__ in, float* __restrict__ out, int B, int C,
+                                    int HW) {
+  const long long n = static_cast<long long>(B) * C * HW;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int p = static_cast<int>(i % HW);
+    const int c = static_cast<int>((i / HW) % C);
+    const int b = static_cast<int>(i / (static_cast<long long>(HW) * C));
+    out[i] = in[(static_cast<long long>(b) * HW + p) * C + c];
+  }
+}
+
+__global__ void add_vec_kernel(float* __restrict__ dst, const float* __restrict__ a, const float* __restrict__ b,
+                               long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    dst[i] = a[i] + b[i];
+}
+
+unsigned grid_for(long long n) {
+  return static_cast<unsigned>(std::max<long long>(1, std::min<long long>((n + 255) / 256, sm_count() * 16LL)));
+}
+
+}  // namespace
+
+int group_norm(const void* x, void* y, int dtype, int B, int HW, int C, int G, const float* w,
+               const float* bias, float eps, int silu_after, void* scratch, size_t scratch_bytes,
+               cudaStream_t s) {
+  if (dtype != ND_F16 && dtype != ND_BF16) return fail(ND_ERR_INVALID, "group_norm: dtype must be f16 or bf16");
+  if (B <= 0 || HW <= 0 || C <= 0 || G <= 0 || C % G || C % 8) return fail(ND_ERR_INVALID, "group_norm: bad shape");
+  if (!x || !y) return fail(ND_ERR_INVALID, "group_norm: null operand");
+  const int chunk = 256;
+  const int nchunks = (HW + chunk - 1) / chunk;
+  const size_t part_bytes = static_cast<size_t>(B) * nchunks * C * sizeof(double2);
+  const size_t stats_bytes = static_cast<size_t>(B) * G * sizeof(float2);
+  if (scratch_bytes < group_norm_scratch(B, HW, C, G))
+    return fail(ND_ERR_INVALID, "group_norm: scratch too small");
+  double2* part = static_cast<double2*>(scratch);
+  float2* stats = reinterpret_cast<float2*>(static_cast<uint8_t*>(scratch) + part_bytes);
+  (void)stats_bytes;
+  const int f16 = dtype == ND_F16;
+  gn_partial_kernel<<<dim3(nchunks, B), 256, 0, s>>>(x, f16, HW, C, chunk, part);
+  ND_CUDA(cudaGetLastError());
+  gn_finalize_kernel<<<B * G, 32, 0, s>>>(part, nchunks, C, G, HW, eps, stats);
+  ND_CUDA(cudaGetLastError());
+  const long long pixels = static_cast<long long>(B) * HW;
+  gn_apply_kernel<<<grid_for(pixels * (C / 8)), 256, 0, s>>>(x, y, f16, pixels, HW, C, G, stats, w, bias,
+                                                               silu_after);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+size_t group_norm_scratch(int B, int HW, int C, int G) {
+  const int nchunks = (HW + 255) / 256;
+  return static_cast<size_t>(B) * nchunks * C * sizeof(double2) + static_cast<size_t>(B) * G * sizeof(float2) + 256;
+}
+
+int geglu(const void* in, void* out, int dtype, int64_t rows, int64_t F, cudaStream_t s) {
+  if (F % 8 || rows <= 0) return fail(ND_ERR_INVALID, "geglu: bad shape");
+  geglu_kernel<<<grid_for(rows * (F / 8)), 256, 0, s>>>(in, out, dtype == ND_F16, rows, static_cast<int>(F));
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int upsample2x(const void* in, void* out, int B, int H, int W, int C, cudaStream_t s) {
+  if (C % 8) return fail(ND_ERR_INVALID, "upsample2x: channels must be a multiple of 8");
+  const long long n = static_cast<long long>(B) * 4 * H * W * (C / 8);
+  upsample2x_kernel<<<grid_for(n), 256, 0, s>>>(static_cast<const uint4*>(in), static_cast<uint4*>(out), B, H, W, C / 8);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int concat_channels(const void* a, int ca, const void* b, int cb, void* out, int64_t pixels, cudaStream_t s) {
+  if (ca % 8 || cb % 8) return fail(ND_ERR_INVALID, "concat: channels must be multiples of 8");
+  concat_kernel<<<grid_for(pixels * ((ca + cb) / 8)), 256, 0, s>>>(static_cast<const uint4*>(a), ca / 8,
+                                                                    static_cast<const uint4*>(b), cb / 8,
+                                                                    static_cast<uint4*>(out), pixels);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int nchw_to_nhwc(const float* in, void* out, int dtype, int B, int C, int HW, int cpad, cudaStream_t s) {
+  nchw_to_nhwc_kernel<<<grid_for(static_cast<long long>(B) * HW * cpad), 256, 0, s>>>(in, out, dtype == ND_F16, B, C,
+                                                                                         HW, cpad);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int add_vectors(float* dst, const float* src, int64_t n, cudaStream_t s) {
+  add_vec_kernel<<<grid_for(n), 256, 0, s>>>(dst, dst, src, n);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int add_vectors2(float* out, const float* a, const float* b, int64_t n, cudaStream_t s) {
+  add_vec_kernel<<<grid_for(n), 256, 0, s>>>(out, a, b, n);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int nhwc_to_nchw(const float* in, float* out, int B, int C, int HW, cudaStream_t s) {
+  nhwc_to_nchw_kernel<<<grid_for(static_cast<long long>(B) * HW * C), 256, 0, s>>>(in, out, B, C, HW);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+}  // namespace nd

@@ -27,7 +27,9 @@ class ModelDesc(C.Structure):
         "family", "width", "heads", "head_dim", "blocks", "mlp_width",
         "context_rows", "context_width", "latent_channels", "latent_height", "latent_width",
         "patch", "time_width", "batch", "compute", "weight_dtype", "quant_group",
-        "quant_scale_dtype", "adaln_rank")] + [("eps", C.c_float)]
+        "quant_scale_dtype", "adaln_rank")] + [("eps", C.c_float), ("unet_levels", C.c_int),
+        ("unet_mult", C.c_int * 4), ("unet_depth", C.c_int * 4), ("unet_resnets", C.c_int),
+        ("add_width", C.c_int)]
 
 
 class NamedTensor(C.Structure):
@@ -208,6 +210,120 @@ class AnimaConfig:
         return 2.0 * self.batch * self.blocks * per_image
 
 
+@dataclass
+class UNetConfig:
+    """The SDXL UNet. Defaults: BASELINE configuration 5 (levels 320 / 640 /
+    1280 with transformer depths 0 / 2 / 10, 64-wide heads, 2 resnets per
+    level, cross-attention to 77 x 2048 text rows, add embedding 2816, 4 x 128
+    x 128 latent, batch 2 = the CFG branches, fp16)."""
+    width: int = 320
+    mult: tuple = (1, 2, 4)
+    depth: tuple = (0, 2, 10)
+    resnets: int = 2
+    context_rows: int = 77
+    context_width: int = 2048
+    add_width: int = 2816
+    time_width: int = 320
+    latent_height: int = 128
+    latent_width: int = 128
+    batch: int = 2
+    compute: int = _lib.ND_F16
+    latent_channels: int = 4
+
+    def desc(self) -> ModelDesc:
+        d = ModelDesc()
+        d.family = FAMILY_SDXL
+        d.width, d.head_dim = self.width, 64
+        d.context_rows, d.context_width = self.context_rows, self.context_width
+        d.latent_channels, d.latent_height, d.latent_width = 4, self.latent_height, self.latent_width
+        d.time_width, d.batch, d.compute, d.weight_dtype = self.time_width, self.batch, self.compute, self.compute
+        d.unet_levels = len(self.mult)
+        for i, (m, dep) in enumerate(zip(self.mult, self.depth)):
+            d.unet_mult[i], d.unet_depth[i] = m, dep
+        d.unet_resnets, d.add_width = self.resnets, self.add_width
+        return d
+
+    def weight_shapes(self):
+        """(name, checkpoint shape, required) in the library's registry order."""
+        C0, cw, tw, aw = self.width, self.context_width, self.time_width, self.add_width
+        out = []
+
+        def conv(name, co, ci):
+            out.append((name + ".weight", (co, ci, 3, 3), True))
+            out.append((name + ".bias", (co,), False))
+
+        def res(p, ci, co):
+            out.extend([(p + ".norm1.weight", (ci,), True), (p + ".norm1.bias", (ci,), False)])
+            conv(p + ".conv1", co, ci)
+            out.extend([(p + ".norm2.weight", (co,), True), (p + ".norm2.bias", (co,), False)])
+            conv(p + ".conv2", co, co)
+            if ci != co:
+                out.extend([(p + ".conv_shortcut.weight", (co, ci), True), (p + ".conv_shortcut.bias", (co,), False)])
+
+        def t2d(p, c, dep):
+            out.extend([(p + ".norm.weight", (c,), True), (p + ".norm.bias", (c,), False),
+                        (p + ".proj_in.weight", (c, c), True), (p + ".proj_in.bias", (c,), False)])
+            for j in range(dep):
+                q = f"{p}.transformer_blocks.{j}"
+                for n in ("norm1", "norm2", "norm3"):
+                    out.extend([(f"{q}.{n}.weight", (c,), True), (f"{q}.{n}.bias", (c,), False)])
+                out.extend([(q + ".attn1.to_q.weight", (c, c), True), (q + ".attn1.to_k.weight", (c, c), True),
+                            (q + ".attn1.to_v.weight", (c, c), True),
+                            (q + ".attn1.to_out.0.weight", (c, c), True), (q + ".attn1.to_out.0.bias", (c,), False),
+                            (q + ".attn2.to_q.weight", (c, c), True), (q + ".attn2.to_k.weight", (c, cw), True),
+                            (q + ".attn2.to_v.weight", (c, cw), True),
+                            (q + ".attn2.to_out.0.weight", (c, c), True), (q + ".attn2.to_out.0.bias", (c,), False),
+                            (q + ".ff.net.0.proj.weight", (8 * c, c), True), (q + ".ff.net.0.proj.bias", (8 * c,), False),
+                            (q + ".ff.net.2.weight", (c, 4 * c), True), (q + ".ff.net.2.bias", (c,), False)])
+            out.extend([(p + ".proj_out.weight", (c, c), True), (p + ".proj_out.bias", (c,), False)])
+
+        conv("conv_in", C0, self.latent_channels)
+        out.extend([("time_embedding.linear_1.weight", (1280, tw), True), ("time_embedding.linear_1.bias", (1280,), False),
+                    ("time_embedding.linear_2.weight", (1280, 1280), True), ("time_embedding.linear_2.bias", (1280,), False),
+                    ("add_embedding.linear_1.weight", (1280, aw), True), ("add_embedding.linear_1.bias", (1280,), False),
+                    ("add_embedding.linear_2.weight", (1280, 1280), True), ("add_embedding.linear_2.bias", (1280,), False)])
+        L = len(self.mult)
+        chans = [C0]
+        c = C0
+        res_units = []
+        for lvl in range(L):
+            p = f"down_blocks.{lvl}"
+            co = C0 * self.mult[lvl]
+            for i in range(self.resnets):
+                res(f"{p}.resnets.{i}", c, co)
+                res_units.append((f"{p}.resnets.{i}", co))
+                c = co
+                if self.depth[lvl] > 0:
+                    t2d(f"{p}.attentions.{i}", co, self.depth[lvl])
+                chans.append(co)
+            if lvl != L - 1:
+                conv(f"{p}.downsamplers.0.conv", co, co)
+                chans.append(co)
+        res("mid_block.resnets.0", c, c)
+        t2d("mid_block.attentions.0", c, self.depth[L - 1] or 1)
+        res("mid_block.resnets.1", c, c)
+        mid = [("mid_block.resnets.0", c), ("mid_block.resnets.1", c)]
+        ups = []
+        for i in range(L):
+            lvl = L - 1 - i
+            p = f"up_blocks.{i}"
+            co = C0 * self.mult[lvl]
+            for j in range(self.resnets + 1):
+                skip = chans.pop()
+                res(f"{p}.resnets.{j}", c + skip, co)
+                ups.append((f"{p}.resnets.{j}", co))
+                c = co
+                if self.depth[lvl] > 0:
+                    t2d(f"{p}.attentions.{j}", co, self.depth[lvl])
+            if i != L - 1:
+                conv(f"{p}.upsamplers.0.conv", co, co)
+        out.extend([("conv_norm_out.weight", (c,), True), ("conv_norm_out.bias", (c,), False)])
+        conv("conv_out", self.latent_channels, c)
+        for name, co in res_units + mid + ups:
+            out.extend([(name + ".time_emb_proj.weight", (co, 1280), True), (name + ".time_emb_proj.bias", (co,), False)])
+        return out
+
+
 def _name_seed(name: str, seed: int) -> int:
     return (zlib.crc32(name.encode()) ^ (seed * 0x9E3779B1)) & 0xFFFFFFFF
 
@@ -220,6 +336,16 @@ def synthetic_weights(cfg, seed: int = 0):
     """Seeded synthetic weights in the storage precision, one generator per
     tensor name: matrices and biases N(0, 0.02), norm weights 1 + N(0, 0.02).
     Yields (name, float32 array already rounded to bf16/fp16)."""
+    if hasattr(cfg, "weight_shapes"):
+        for name, shape, _req in cfg.weight_shapes():
+            rng = np.random.default_rng(_name_seed(name, seed))
+            a = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+            if len(shape) == 1 and "norm" in name and name.endswith(".weight"):
+                a += np.float32(1.0)
+            if len(shape) > 1:
+                a = _round(a, cfg.compute)
+            yield name, a
+        return
     for name, rows, cols, _req in _table(cfg):
         rng = np.random.default_rng(_name_seed(name, seed))
         a = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02)
@@ -239,6 +365,14 @@ def synthetic_weights_device(cfg, seed: int = 0, device="cuda"):
     import torch
     dt = torch.bfloat16 if cfg.compute == _lib.ND_BF16 else torch.float16
     g = torch.Generator(device=device)
+    if hasattr(cfg, "weight_shapes"):
+        for name, shape, _req in cfg.weight_shapes():
+            g.manual_seed(_name_seed(name, seed))
+            t = torch.randn(*shape, device=device, generator=g) * 0.02
+            if len(shape) == 1 and "norm" in name and name.endswith(".weight"):
+                t += 1.0
+            yield name, (t.to(dt) if len(shape) > 1 else t)
+        return
     for name, rows, cols, _req in _table(cfg):
         g.manual_seed(_name_seed(name, seed))
         if cols == 1:

@@ -87,7 +87,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *,
               out: torch.Tensor | None = None, batch: int = 1, key_limit: int = 0,
-              causal: bool = False, scale: float = 0.0) -> torch.Tensor:
+              causal: bool = False, scale: float = 0.0, head_dim: int = 128) -> torch.Tensor:
     """Flash attention over packed heads (Layers.Attend, Graph/Layers.cs:260-279).
 
     q: [batch * q_rows, >= heads*128] (row stride q.stride(0)); k, v likewise
@@ -96,10 +96,10 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *,
     q_rows = q.shape[0] // batch
     kv_rows = k.shape[0] // batch
     if out is None:
-        out = torch.empty(q.shape[0], heads * 128, device=q.device, dtype=q.dtype)
+        out = torch.empty(q.shape[0], heads * head_dim, device=q.device, dtype=q.dtype)
     a = AttentionArgs()
     a.dtype = _DT[q.dtype]
-    a.heads, a.head_dim, a.batch = heads, 128, batch
+    a.heads, a.head_dim, a.batch = heads, head_dim, batch
     a.q_rows, a.kv_rows, a.key_limit, a.causal = q_rows, kv_rows, key_limit, int(causal)
     a.q, a.ldq = q.data_ptr(), q.stride(0)
     a.k, a.ldk = k.data_ptr(), k.stride(0)
@@ -198,3 +198,52 @@ def quantize(w: torch.Tensor, quant_group: int = 32, scale_dtype=torch.float16):
     check(lib().nd_op_quantize(w.data_ptr(), _DT[w.dtype], rows, cols, quant_group, _DT[scale_dtype],
                                q.data_ptr(), s.data_ptr(), C.c_void_p(_stream())))
     return q, s
+
+
+_EPI_CONV = {"store": 0, "silu": 3, "store_f32": 5, "add_store": 8}
+
+
+def conv2d(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *, stride: int = 1,
+           epilogue: str = "store", addend: torch.Tensor | None = None,
+           per_batch_bias: bool = False) -> torch.Tensor:
+    """3x3 convolution, padding 1, over NHWC activations x [B, H, W, Cin] with
+    weight [Cout, 3, 3, Cin] (Layers.Conv2d, Graph/Layers.cs:115-128).
+    bias: [Cout] fp32, or [B, Cout] with per_batch_bias."""
+    b, h, w, cin = x.shape
+    cout = weight.shape[0]
+    ho, wo = (h + 2 - 3) // stride + 1, (w + 2 - 3) // stride + 1
+    a = _lib.ConvArgs()
+    a.dtype = _DT[x.dtype]
+    a.epilogue = _EPI_CONV[epilogue]
+    a.batch, a.height, a.width, a.in_channels, a.out_channels, a.stride = b, h, w, cin, cout, stride
+    a.x, a.weight, a.bias = x.data_ptr(), weight.data_ptr(), _ptr(bias)
+    a.per_batch_bias = 1 if per_batch_bias else 0
+    a.bias_stride = bias.stride(0) if per_batch_bias else 0
+    if epilogue == "store_f32":
+        y = torch.empty(b, ho, wo, cout, device=x.device, dtype=torch.float32)
+        a.y_f32 = y.data_ptr()
+    else:
+        y = torch.empty(b, ho, wo, cout, device=x.device, dtype=x.dtype)
+        a.y = y.data_ptr()
+    a.addend = _ptr(addend)
+    check(lib().nd_op_conv2d(C.byref(a), C.c_void_p(_stream())))
+    return y
+
+
+def group_norm(x: torch.Tensor, groups: int, weight: torch.Tensor, bias: torch.Tensor | None = None, *,
+               eps: float = 1e-5, silu: bool = False) -> torch.Tensor:
+    """GroupNorm over NHWC x [B, pixels, C] (Layers.GroupNorm, Graph/Layers.cs:166-185),
+    optionally followed by SiLU."""
+    b, p, c = x.shape
+    y = torch.empty_like(x)
+    check(lib().nd_op_group_norm(x.data_ptr(), y.data_ptr(), _DT[x.dtype], b, p, c, groups, weight.data_ptr(),
+                                 _ptr(bias), eps, 1 if silu else 0, C.c_void_p(_stream())))
+    return y
+
+
+def geglu(x: torch.Tensor) -> torch.Tensor:
+    """[rows, 2F] -> [rows, F] = x[:, :F] * gelu(x[:, F:]) (UNetLayers.Geglu, Models/Sdxl/UNetLayers.cs:30-46)."""
+    rows, two_f = x.shape
+    y = torch.empty(rows, two_f // 2, device=x.device, dtype=x.dtype)
+    check(lib().nd_op_geglu(x.data_ptr(), y.data_ptr(), _DT[x.dtype], rows, two_f // 2, C.c_void_p(_stream())))
+    return y

@@ -388,3 +388,122 @@ def anima_forward(w: dict, cfg, latent, context, sigma, cos=None, sin=None):
         out = linear(y, w["final_layer.linear.weight"])
         outs.append(unpatchify(out, cfg.latent_channels, Hl, Wl, p))
     return np.stack(outs)
+
+
+def group_norm(x, groups, weight=None, bias=None, eps=1e-5, silu=False):
+    """GroupNorm over one image x [C, H, W] (or [C, HW])."""
+    x = _c(x)
+    ch = x.shape[0]
+    HW = x.size // ch
+    y = np.empty_like(x)
+    w = None if weight is None else _c(weight)
+    b = None if bias is None else _c(bias)
+    lib().nd_oracle_group_norm(_p(x), ch, HW, groups, _p(w), _p(b), C_float(eps),
+                               int(silu), _p(y))
+    return y
+
+
+def C_float(v):
+    return C.c_float(v)
+
+
+def conv2d(x, w, b=None, stride=1, pad=1):
+    """x [Cin, H, W], w [Cout, Cin, k, k] -> [Cout, Ho, Wo]."""
+    x = _c(x)
+    w = _c(w)
+    Cin, H, W = x.shape
+    Cout, _, k, _ = w.shape
+    Ho, Wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+    y = np.empty((Cout, Ho, Wo), _f)
+    bb = None if b is None else _c(b)
+    lib().nd_oracle_conv2d(_p(x), Cin, H, W, _p(w), _p(bb), Cout, k, stride, pad, _p(y))
+    return y
+
+
+def unet_forward(w: dict, cfg, latent, timestep, add, context):
+    """The SDXL UNet step in fp32, one image at a time (UNetModel.Build,
+    Models/Sdxl/UNetModel.cs:333-437). latent [B, 4, H, W]; add [B, aw];
+    context [B, rows, width]."""
+    from math import cos, exp, log, sin
+
+    def tstep(t, dim):
+        half = dim // 2
+        f = [exp(-log(10000.0) * i / half) for i in range(half)]
+        return np.array([cos(t * x) for x in f] + [sin(t * x) for x in f], np.float32)
+
+    def mlp(x, p):
+        return linear(silu(linear(x, w[p + ".linear_1.weight"], w.get(p + ".linear_1.bias"))),
+                      w[p + ".linear_2.weight"], w.get(p + ".linear_2.bias"))
+
+    def res(x, p, temb):
+        h = group_norm(x, 32, w[p + ".norm1.weight"], w.get(p + ".norm1.bias"), 1e-5, True)
+        h = conv2d(h, w[p + ".conv1.weight"], w.get(p + ".conv1.bias"))
+        proj = linear(silu(temb)[None], w[p + ".time_emb_proj.weight"], w.get(p + ".time_emb_proj.bias"))[0]
+        h = h + proj[:, None, None]
+        h = group_norm(h, 32, w[p + ".norm2.weight"], w.get(p + ".norm2.bias"), 1e-5, True)
+        h = conv2d(h, w[p + ".conv2.weight"], w.get(p + ".conv2.bias"))
+        if p + ".conv_shortcut.weight" in w:
+            sc = w[p + ".conv_shortcut.weight"]
+            x = conv2d(x, sc.reshape(sc.shape[0], sc.shape[1], 1, 1), w.get(p + ".conv_shortcut.bias"), 1, 0)
+        return x + h
+
+    def attn(x, src, p, heads):
+        q = linear(x, w[p + ".to_q.weight"])
+        k = linear(src, w[p + ".to_k.weight"])
+        v = linear(src, w[p + ".to_v.weight"])
+        return linear(attention(q, k, v, heads), w[p + ".to_out.0.weight"], w.get(p + ".to_out.0.bias"))
+
+    def t2d(x, p, ctx):
+        c, h_, w_ = x.shape
+        t = group_norm(x, 32, w[p + ".norm.weight"], w.get(p + ".norm.bias"), 1e-6).reshape(c, -1).T
+        t = linear(np.ascontiguousarray(t), w[p + ".proj_in.weight"], w.get(p + ".proj_in.bias"))
+        j = 0
+        while f"{p}.transformer_blocks.{j}.norm1.weight" in w:
+            q = f"{p}.transformer_blocks.{j}"
+            heads = c // 64
+            n = layernorm(t, 1e-5, w[q + ".norm1.weight"], w.get(q + ".norm1.bias"))
+            t = t + attn(n, n, q + ".attn1", heads)
+            n = layernorm(t, 1e-5, w[q + ".norm2.weight"], w.get(q + ".norm2.bias"))
+            t = t + attn(n, ctx, q + ".attn2", heads)
+            n = layernorm(t, 1e-5, w[q + ".norm3.weight"], w.get(q + ".norm3.bias"))
+            hh = linear(n, w[q + ".ff.net.0.proj.weight"], w.get(q + ".ff.net.0.proj.bias"))
+            inner = hh.shape[1] // 2
+            t = t + linear(hh[:, :inner] * gelu(hh[:, inner:]), w[q + ".ff.net.2.weight"], w.get(q + ".ff.net.2.bias"))
+            j += 1
+        t = linear(t, w[p + ".proj_out.weight"], w.get(p + ".proj_out.bias"))
+        return np.ascontiguousarray(t.T.reshape(c, h_, w_)) + x
+
+    L = len(cfg.mult)
+    outs = []
+    for b in range(latent.shape[0]):
+        temb = mlp(tstep(timestep, cfg.time_width)[None], "time_embedding")[0] + \
+            mlp(np.asarray(add[b], np.float32)[None], "add_embedding")[0]
+        ctx = np.asarray(context[b], np.float32)
+        x = conv2d(np.asarray(latent[b], np.float32), w["conv_in.weight"], w.get("conv_in.bias"))
+        skips = [x]
+        for lvl in range(L):
+            for i in range(cfg.resnets):
+                x = res(x, f"down_blocks.{lvl}.resnets.{i}", temb)
+                if cfg.depth[lvl] > 0:
+                    x = t2d(x, f"down_blocks.{lvl}.attentions.{i}", ctx)
+                skips.append(x)
+            if lvl != L - 1:
+                x = conv2d(x, w[f"down_blocks.{lvl}.downsamplers.0.conv.weight"],
+                           w.get(f"down_blocks.{lvl}.downsamplers.0.conv.bias"), stride=2)
+                skips.append(x)
+        x = res(x, "mid_block.resnets.0", temb)
+        x = t2d(x, "mid_block.attentions.0", ctx)
+        x = res(x, "mid_block.resnets.1", temb)
+        for i in range(L):
+            lvl = L - 1 - i
+            for j in range(cfg.resnets + 1):
+                x = np.concatenate([x, skips.pop()], 0)
+                x = res(x, f"up_blocks.{i}.resnets.{j}", temb)
+                if cfg.depth[lvl] > 0:
+                    x = t2d(x, f"up_blocks.{i}.attentions.{j}", ctx)
+            if i != L - 1:
+                x = x.repeat(2, axis=1).repeat(2, axis=2)
+                x = conv2d(x, w[f"up_blocks.{i}.upsamplers.0.conv.weight"], w.get(f"up_blocks.{i}.upsamplers.0.conv.bias"))
+        x = group_norm(x, 32, w["conv_norm_out.weight"], w.get("conv_norm_out.bias"), 1e-5, True)
+        outs.append(conv2d(x, w["conv_out.weight"], w.get("conv_out.bias")))
+    return np.stack(outs)

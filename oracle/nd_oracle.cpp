@@ -596,3 +596,65 @@ EXPORT void nd_oracle_anima_block(const nd_oracle_anima_block_w* w, int width, i
     for (int64_t i = 0; i < MD; ++i) x[i] += mm[2 * D + i % D] * o[i];
   }
 }
+
+// ------------------------------------------------------------------ UNet
+
+// GroupNorm over one image [C, HW] (Layers.GroupNorm, Graph/Layers.cs:166-185;
+// the smoke check's recipe, NaiveDiffusion.Cli/SmokeTest.cs:208-239): each
+// group of C/G channels normalized over its C/G x HW values with double mean
+// and variance, then y = n * w[c] + b[c] (NULL: 1 / 0), then SiLU if asked
+// (UNetModel.ResnetBlock, Models/Sdxl/UNetModel.cs:230-254).
+EXPORT void nd_oracle_group_norm(const float* x, int C, int HW, int groups, const float* w,
+                                 const float* b, float eps, int silu, float* y) {
+  const int cg = C / groups;
+#pragma omp parallel for schedule(static)
+  for (int g = 0; g < groups; ++g) {
+    const int64_t n = static_cast<int64_t>(cg) * HW;
+    const float* s = x + static_cast<int64_t>(g) * n;
+    double mean = 0;
+    for (int64_t i = 0; i < n; ++i) mean += s[i];
+    mean /= n;
+    double var = 0;
+    for (int64_t i = 0; i < n; ++i) var += (s[i] - mean) * (s[i] - mean);
+    var /= n;
+    const double inv = 1.0 / std::sqrt(var + eps);
+    for (int c = 0; c < cg; ++c) {
+      const int ch = g * cg + c;
+      for (int p = 0; p < HW; ++p) {
+        const int64_t i = static_cast<int64_t>(c) * HW + p;
+        float v = static_cast<float>((s[i] - mean) * inv) * (w ? w[ch] : 1.f) + (b ? b[ch] : 0.f);
+        if (silu) v *= 1.0f / (1.0f + std::exp(-v));
+        y[static_cast<int64_t>(g) * n + i] = v;
+      }
+    }
+  }
+}
+
+// 2-D convolution, NCHW one image (Layers.Conv2d, Graph/Layers.cs:115-128, as
+// the smoke check computes it, SmokeTest.cs:241-281): y[o, r, c] = b[o] +
+// sum over (i, dy, dx) of w[o, i, dy, dx] * x[i, r*s + dy - pad, c*s + dx - pad],
+// zero outside the image; float sums.
+EXPORT void nd_oracle_conv2d(const float* x, int Cin, int H, int W, const float* w, const float* b,
+                             int Cout, int k, int stride, int pad, float* y) {
+  const int Ho = (H + 2 * pad - k) / stride + 1, Wo = (W + 2 * pad - k) / stride + 1;
+#pragma omp parallel for schedule(static)
+  for (int o = 0; o < Cout; ++o) {
+    float* yo = y + static_cast<int64_t>(o) * Ho * Wo;
+    for (int p = 0; p < Ho * Wo; ++p) yo[p] = b ? b[o] : 0.f;
+    for (int i = 0; i < Cin; ++i)
+      for (int dy = 0; dy < k; ++dy)
+        for (int dx = 0; dx < k; ++dx) {
+          const float wv = w[((static_cast<int64_t>(o) * Cin + i) * k + dy) * k + dx];
+          const float* xi = x + static_cast<int64_t>(i) * H * W;
+          for (int r = 0; r < Ho; ++r) {
+            const int yy = r * stride + dy - pad;
+            if (yy < 0 || yy >= H) continue;
+            for (int c = 0; c < Wo; ++c) {
+              const int xx = c * stride + dx - pad;
+              if (xx < 0 || xx >= W) continue;
+              yo[r * Wo + c] += wv * xi[yy * W + xx];
+            }
+          }
+        }
+  }
+}

@@ -41,18 +41,26 @@ def test_struct_layouts_match_the_header(tmp_path):
     cc = shutil.which("gcc") or shutil.which("cc")
     if not cc:
         pytest.skip("no C compiler")
-    structs = {"nd_linear_args": _lib.LinearArgs, "nd_attention_args": _lib.AttentionArgs,
+    structs = {"nd_linear_args": _lib.LinearArgs, "nd_conv_args": _lib.ConvArgs,
+               "nd_attention_args": _lib.AttentionArgs,
                "nd_modulate_args": _lib.ModulateArgs, "nd_rmsnorm_args": _lib.RmsNormArgs,
                "nd_gemv_args": _lib.GemvArgs, "nd_model_desc": D.ModelDesc,
                "nd_named_tensor": D.NamedTensor, "nd_memory": D.Memory, "nd_kernel_time": D.KernelTime}
     src = tmp_path / "sizes.c"
-    src.write_text('#include <stdio.h>\n#include "nd_denoise.h"\nint main(void){\n' + "".join(
-        f'printf("%zu\\n", sizeof({n}));\n' for n in structs) + "return 0;}\n")
+    lines = []
+    for n, cls in structs.items():
+        lines.append(f'printf("%zu\\n", sizeof({n}));\n')
+        lines += [f'printf("%zu\\n", offsetof({n}, {f[0]}));\n' for f in cls._fields_]
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "nd_denoise.h"\nint main(void){\n' +
+                   "".join(lines) + "return 0;}\n")
     exe = tmp_path / "sizes"
     subprocess.run([cc, "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
     sizes = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
-    for (name, cls), size in zip(structs.items(), sizes):
-        assert C.sizeof(cls) == size, name
+    it = iter(sizes)
+    for name, cls in structs.items():
+        assert C.sizeof(cls) == next(it), name
+        for f in cls._fields_:
+            assert getattr(cls, f[0]).offset == next(it), (name, f[0])
 
 
 def test_weight_table_covers_the_checkpoint_layout():

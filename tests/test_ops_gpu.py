@@ -164,3 +164,22 @@ def test_patchify_round_trip(cuda):
     back = ops.unpatchify(t, lat.shape, 2)
     ops.sync()
     np.testing.assert_array_equal(f32(back), lat)
+
+
+@pytest.mark.parametrize("rows,kv_rows,heads,batch", [(4096, 4096, 2, 1), (1024, 77, 4, 2), (300, 300, 3, 1)])
+def test_attention_head_dim_64_fp16(cuda, rows, kv_rows, heads, batch):
+    """SDXL's attention: 64-wide heads, fp16, cross-attention to 77 rows."""
+    from naivediffusion_b200 import ops
+    rng = np.random.default_rng(rows + heads)
+    q = rng.standard_normal((batch * rows, heads * 64)).astype(np.float32)
+    k = rng.standard_normal((batch * kv_rows, heads * 64)).astype(np.float32)
+    v = rng.standard_normal((batch * kv_rows, heads * 64)).astype(np.float32)
+    h = lambda a: torch.from_numpy(a).cuda().half()  # noqa: E731
+    y = ops.attention(h(q), h(k), h(v), heads, batch=batch, head_dim=64)
+    ops.sync()
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    out = f(y)
+    for b in range(batch):
+        sq, sk = slice(b * rows, (b + 1) * rows), slice(b * kv_rows, (b + 1) * kv_rows)
+        ref = O.attention(f(h(q))[sq], f(h(k))[sk], f(h(v))[sk], heads)
+        assert rel(out[sq], ref) < 2e-2 and cos(out[sq], ref) > 0.999

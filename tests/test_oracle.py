@@ -220,3 +220,44 @@ def test_gelu_variants():
     tanh_form = 0.5 * x * (1 + np.tanh(math.sqrt(2 / math.pi) * (x + 0.044715 * x ** 3)))
     assert np.abs(O.gelu_tanh(x) - tanh_form).max() < 1e-5
     assert np.abs(O.silu(x) - x / (1 + np.exp(-x.astype(np.float64)))).max() < 1e-5
+
+
+def test_group_norm_smoke_recipe():
+    # SmokeTest.GroupNormalization (NaiveDiffusion.Cli/SmokeTest.cs:208-239):
+    # [1, 4, 1, 3] in two groups, eps 1e-5, double mean / variance.
+    data = np.array([1, 2, 3, 4, 5, 6, 0, 0, 0, 1, 1, 4], np.float32)
+    y = O.group_norm(data.reshape(4, 1, 3), 2, eps=1e-5).ravel()
+    ref = []
+    for g in range(2):
+        d = data[g * 6:(g + 1) * 6].astype(np.float64)
+        ref += list((d - d.mean()) / np.sqrt(d.var() + 1e-5))
+    assert np.abs(y - np.array(ref)).max() < 1e-6
+
+
+def test_convolution_smoke_recipe():
+    # SmokeTest.Convolution (SmokeTest.cs:241-281): an identity tap plus 0.5
+    # and a 3x3 box sum minus 1 over 0..8, padding 1.
+    x = np.arange(9, dtype=np.float32).reshape(1, 3, 3)
+    f = np.zeros((2, 1, 3, 3), np.float32)
+    f[0, 0, 1, 1] = 1
+    f[1] = 1
+    y = O.conv2d(x, f, np.array([0.5, -1], np.float32))
+    assert np.array_equal(y[0].ravel(), np.arange(9) + 0.5)
+    box = np.pad(x[0], 1)
+    ref = np.array([[box[r:r + 3, c:c + 3].sum() for c in range(3)] for r in range(3)]) - 1
+    assert np.array_equal(y[1], ref)
+
+
+def test_strided_convolution():
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((3, 8, 6)).astype(np.float32)
+    w = rng.standard_normal((4, 3, 3, 3)).astype(np.float32)
+    y = O.conv2d(x, w, None, stride=2, pad=1)
+    assert y.shape == (4, 4, 3)
+    xp = np.pad(x, ((0, 0), (1, 1), (1, 1))).astype(np.float64)
+    ref = np.zeros((4, 4, 3))
+    for o in range(4):
+        for r in range(4):
+            for c in range(3):
+                ref[o, r, c] = (w[o] * xp[:, 2 * r:2 * r + 3, 2 * c:2 * c + 3]).sum()
+    assert np.abs(y - ref).max() < 1e-4
