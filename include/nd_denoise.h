@@ -362,6 +362,26 @@ ND_API int nd_op_group_norm(const void* x, void* y, int dtype, int batch, int pi
                             int groups, const float* weight, const float* bias, float eps,
                             int silu_after, void* stream);
 
+/* nd_op_group_norm that allocates no memory (no counterpart in the reference:
+ * its DirectML graphs own their temporaries). Same arguments, same kernels,
+ * same results. Its scratch is one fixed 4 MiB device array inside the
+ * library, so it suits hosts that cannot let the library allocate: device
+ * memory already fully committed (a serving pool, full weight residency), or
+ * a pipeline that must not meet cudaFree's device-wide wait.
+ *  - Limit: batch * ceil(pixels / 256) * channels * 16 + batch * groups * 8
+ *    + 256 bytes must fit in 4 MiB (SDXL at 1024 x 1024, batch 2, needs
+ *    1.97 MB); larger shapes fail with ND_ERR_INVALID and launch nothing.
+ *  - Nothing needs to start at zero: every partial sum and group statistic
+ *    is written before it is read within the same call.
+ *  - The first call on each device looks up the array's address (with that
+ *    device current); make that first call before any stream capture.
+ *  - One array per device: calls in flight at the same time on one device
+ *    (different streams or host threads) race on it. Calls on one stream,
+ *    or otherwise ordered, are fine. */
+ND_API int nd_op_group_norm_noalloc(const void* x, void* y, int dtype, int batch, int pixels, int channels,
+                                    int groups, const float* weight, const float* bias, float eps,
+                                    int silu_after, void* stream);
+
 /* GEGLU: in [rows, 2F] -> out [rows, F] = in[:, :F] * gelu(in[:, F:])
  * (UNetLayers.Geglu, src/NaiveDiffusion/Models/Sdxl/UNetLayers.cs:30-46). */
 ND_API int nd_op_geglu(const void* in, void* out, int dtype, int64_t rows, int64_t F, void* stream);
