@@ -48,6 +48,14 @@ extern "C" {
 #define ND_BF16 2
 #define ND_I8 3
 #define ND_I32 4
+/* An fp32 tensor carried as a pair of bf16 tensors so that the bf16 tensor
+ * cores can multiply it at fp32 accuracy. A [rows, cols] value v is stored
+ * [rows, 2 * cols]: hi = bf16(v) in columns [0, cols), lo = bf16(v - hi) in
+ * [cols, 2 * cols) (round to nearest even both times; |v - hi - lo| <=
+ * 2^-16 |v|). The GEMM sums hi.hi + hi.lo + lo.hi in fp32 (three passes over
+ * K on the same tcgen05 pipeline); the dropped lo.lo term is below 2^-16 of
+ * each product. This is how model_desc.compute == ND_F32 runs. */
+#define ND_BF16X2 5
 
 /* Message of the last failure on this thread ("" if none). */
 ND_API const char* nd_last_error(void);
@@ -210,7 +218,12 @@ ND_API int nd_denoiser_destroy(nd_denoiser* d);
 #define ND_EPI_ADD_STORE 8       /* y = acc + bias + addend (like y)        */
 
 typedef struct nd_linear_args {
-  int dtype;            /* ND_BF16 or ND_F16: x, W and y */
+  int dtype;            /* ND_BF16 or ND_F16: x, W and y. ND_BF16X2 (fp32
+                           compute): x [rows, 2 * in] and W [groups * out,
+                           2 * in] are hi|lo pairs, in % 64 == 0; STORE, GELU*
+                           and SILU write y as a pair [rows, 2 * out];
+                           QK_NORM_ROPE writes y as fp32 [rows, out] (the
+                           attention input); ADD_STORE is not offered */
   int epilogue;         /* ND_EPI_* */
   int64_t rows, in_features, out_features;
   const void* x;        /* [rows, ldx] */
@@ -287,7 +300,8 @@ ND_API int nd_op_linear(const nd_linear_args* args, void* stream);
  * and causal (row i sees keys 0..i). Batch items are stacked row blocks:
  * item b's queries are rows [b*q_rows, (b+1)*q_rows) of q. */
 typedef struct nd_attention_args {
-  int dtype;            /* ND_BF16 or ND_F16 */
+  int dtype;            /* ND_BF16 or ND_F16 (tensor cores, head_dim 64 / 128), or
+                           ND_F32 (fp32 on the CUDA cores, head_dim 64 / 128) */
   int heads, head_dim, batch;
   int64_t q_rows, kv_rows;
   int64_t key_limit;    /* <= 0: all kv_rows keys */
@@ -297,6 +311,9 @@ typedef struct nd_attention_args {
   const void* v; int64_t ldv;
   void* out; int64_t ldo;
   float scale;          /* <= 0: 1/sqrt(head_dim) */
+  int out_dtype;        /* 0: dtype. With dtype ND_F32 also ND_BF16X2: out is a
+                           hi|lo pair [rows, 2 * heads * head_dim] (ldo counts
+                           bf16 elements) */
 } nd_attention_args;
 
 ND_API int nd_op_attention(const nd_attention_args* args, void* stream);
@@ -308,7 +325,8 @@ ND_API int nd_op_attention(const nd_attention_args* args, void* stream);
  * use the second vectors. shift may be NULL. */
 typedef struct nd_modulate_args {
   const float* x; int64_t ldx;
-  void* y; int64_t ldy; int out_dtype;   /* ND_BF16, ND_F16 or ND_F32 */
+  void* y; int64_t ldy; int out_dtype;   /* ND_BF16, ND_F16, ND_F32, or ND_BF16X2
+                                            (y [rows, 2 * width] hi|lo pair) */
   int64_t rows, width;
   const float* shift; const float* scale;
   int64_t vec_stride;   /* 0: width */
@@ -339,7 +357,8 @@ ND_API int nd_op_rmsnorm(const nd_rmsnorm_args* args, void* stream);
  * x and y fp32, batch 1..4. pre_silu applies SiLU to x first; act 0 none,
  * 1 SiLU, 2 tanh. The modulation vectors (Layers.Linear over 1-2 rows). */
 typedef struct nd_gemv_args {
-  const void* w; int w_dtype;   /* ND_BF16 / ND_F16, or ND_I8 with scales */
+  const void* w; int w_dtype;   /* ND_BF16 / ND_F16, ND_BF16X2 ([n, 2k] hi|lo
+                                   pair), or ND_I8 with scales */
   int64_t n, k;
   const float* x; int batch; int pre_silu;
   const float* bias; int act;
@@ -389,7 +408,8 @@ ND_API int nd_op_geglu(const void* in, void* out, int dtype, int64_t rows, int64
 /* ------------------------------------------------------------ layout
  * latent [B, C, H, W] fp32 <-> tokens [B * (H/p) * (W/p), C*p*p] (row stride
  * ldt); feature c*p*p + m*p + n of patch (i, j) is channel c at (p*i+m, p*j+n)
- * (AnimaDit.Patchify, src/NaiveDiffusion/Models/Anima/AnimaDit.cs:193-247). */
+ * (AnimaDit.Patchify, src/NaiveDiffusion/Models/Anima/AnimaDit.cs:193-247).
+ * out_dtype ND_BF16X2: the lo half of feature f sits at column C*p*p + f. */
 ND_API int nd_op_patchify(const float* latent, void* tokens, int out_dtype, int batch,
                           int channels, int height, int width, int patch, int64_t ldt,
                           void* stream);

@@ -21,6 +21,7 @@ ND_ERR_UNSUPPORTED = 6
 ND_ERR_MISSING_WEIGHT = 7
 
 ND_F32, ND_F16, ND_BF16, ND_I8, ND_I32 = 0, 1, 2, 3, 4
+ND_BF16X2 = 5  # fp32 as a bf16 hi|lo pair: [rows, 2 * cols], hi columns then lo
 
 ND_EPI_STORE = 0
 ND_EPI_GELU_TANH = 1
@@ -76,7 +77,7 @@ class AttentionArgs(C.Structure):
         ("causal", C.c_int),
         ("q", C.c_void_p), ("ldq", C.c_int64), ("k", C.c_void_p), ("ldk", C.c_int64),
         ("v", C.c_void_p), ("ldv", C.c_int64), ("out", C.c_void_p), ("ldo", C.c_int64),
-        ("scale", C.c_float),
+        ("scale", C.c_float), ("out_dtype", C.c_int),
     ]
 
 

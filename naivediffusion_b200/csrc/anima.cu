@@ -74,6 +74,12 @@ struct Anima final : nd_denoiser {
   int D = 0, H = 0, F = 0, NB = 0, R = 0, ctx = 0, cw = 0, Hl = 0, Wl = 0, P = 2, B = 1;
   int T = 0, cin = 0;
   int dt = ND_BF16;
+  // fp32 compute: GEMM operands as bf16 hi|lo pairs (lt = ND_BF16X2, pair
+  // buffers twice as wide), Q/K/V and the attention in fp32.
+  bool f32 = false;
+  int lt = ND_BF16;
+  int pw = 1;      // columns per logical column in GEMM-operand buffers (2: pairs)
+  size_t qe = 2;   // bytes per element of the Q/K/V buffers
   float eps = 1e-6f;
   Mat x_emb, t1, t2, mod1, mod2, sqkv, so, cq, ckv, co, fc1, fc2, fmod1, fmod2, flin;
   float *t_norm = nullptr, *snorm = nullptr, *cqnorm = nullptr, *cknorm = nullptr;
@@ -90,9 +96,10 @@ struct Anima final : nd_denoiser {
 
   int build() override {
     const nd_model_desc& d = desc;
-    if (d.compute != ND_BF16 && d.compute != ND_F16) return fail(ND_ERR_UNSUPPORTED, "anima: compute must be bf16 or f16");
-    if (d.weight_dtype != d.compute && d.weight_dtype != ND_I8)
-      return fail(ND_ERR_UNSUPPORTED, "anima: weights must be stored in the compute dtype or int8");
+    if (d.compute != ND_BF16 && d.compute != ND_F16 && d.compute != ND_F32)
+      return fail(ND_ERR_UNSUPPORTED, "anima: compute must be bf16, f16 or f32");
+    if (d.weight_dtype != d.compute && !(d.weight_dtype == ND_I8 && d.compute != ND_F32))
+      return fail(ND_ERR_UNSUPPORTED, "anima: weights must be stored in the compute dtype (or int8 with 16-bit compute)");
     if (d.weight_dtype == ND_I8 && d.quant_scale_dtype != ND_F16 && d.quant_scale_dtype != ND_F32)
       return fail(ND_ERR_INVALID, "anima: int8 weights need quant_scale_dtype ND_F16 or ND_F32");
     if (d.head_dim != 128 || d.heads * 128 != d.width) return fail(ND_ERR_INVALID, "anima: width must be heads x 128");
@@ -106,6 +113,10 @@ struct Anima final : nd_denoiser {
     if (d.batch < 1 || d.batch > 4) return fail(ND_ERR_INVALID, "anima: batch must be 1..4");
     if (d.time_width != 0 && d.time_width != d.width) return fail(ND_ERR_INVALID, "anima: time_width is the width");
     dt = d.compute;
+    f32 = dt == ND_F32;
+    lt = f32 ? ND_BF16X2 : dt;
+    pw = f32 ? 2 : 1;
+    qe = f32 ? 4 : 2;
     D = d.width;
     H = d.heads;
     F = d.mlp_width;
@@ -159,14 +170,14 @@ struct Anima final : nd_denoiser {
     fmod = static_cast<float*>(S(static_cast<size_t>(2) * D * 4));
     out_tok = static_cast<float*>(S(static_cast<size_t>(M) * cin * 4));
     out_latent = static_cast<float*>(S(static_cast<size_t>(B) * kLatentChannels * Hl * Wl * 4));
-    xn = S(static_cast<size_t>(M) * D * e);
-    qkv = S(static_cast<size_t>(M) * 3 * D * e);
-    attn = S(static_cast<size_t>(M) * D * e);
-    cqb = S(static_cast<size_t>(M) * D * e);
-    kvb = S(static_cast<size_t>(B) * ctx * 2 * D * e);
-    ctxb = S(static_cast<size_t>(B) * ctx * cw * e);
-    hid = S(static_cast<size_t>(M) * F * e);
-    tok_in = S(static_cast<size_t>(M) * cin * e);
+    xn = S(static_cast<size_t>(M) * D * e * pw);
+    qkv = S(static_cast<size_t>(M) * 3 * D * qe);
+    attn = S(static_cast<size_t>(M) * D * e * pw);
+    cqb = S(static_cast<size_t>(M) * D * qe);
+    kvb = S(static_cast<size_t>(B) * ctx * 2 * D * qe);
+    ctxb = S(static_cast<size_t>(B) * ctx * cw * e * pw);
+    hid = S(static_cast<size_t>(M) * F * e * pw);
+    tok_in = S(static_cast<size_t>(M) * cin * e * pw);
     tsin = static_cast<float*>(pinned(static_cast<size_t>(D) * 4));
     if (alloc_failed) return fail(ND_ERR_OOM, "anima: device allocation failed");
     ND_CUDA(cudaEventCreateWithFlags(&staged, cudaEventDisableTiming));
@@ -284,13 +295,13 @@ struct Anima final : nd_denoiser {
   nd_linear_args lin_args(const void* xin, int64_t rows, int64_t k, const Mat& w, int64_t wrow, int64_t n,
                           int epi) const {
     nd_linear_args a{};
-    a.dtype = dt;
+    a.dtype = lt;
     a.epilogue = epi;
     a.rows = rows;
     a.in_features = k;
     a.out_features = n;
     a.x = xin;
-    a.ldx = k;
+    a.ldx = k * pw;
     weight_args(a, w, wrow);
     a.group_split = rows;
     a.eps = eps;
@@ -301,7 +312,7 @@ struct Anima final : nd_denoiser {
          int act, float* y, int64_t x_rows_per_vec = 0, const float* bias = nullptr, int64_t bias_period = 0) {
     nd_gemv_args g{};
     g.w = w.at(row, 2);
-    g.w_dtype = w.q8 ? ND_I8 : dt;
+    g.w_dtype = w.q8 ? ND_I8 : lt;
     g.n = n;
     g.k = k;
     g.x = xin;
@@ -325,8 +336,8 @@ struct Anima final : nd_denoiser {
     m.x = x;
     m.ldx = D;
     m.y = xn;
-    m.ldy = D;
-    m.out_dtype = dt;
+    m.ldy = static_cast<int64_t>(D) * pw;
+    m.out_dtype = lt;
     m.rows = rows;
     m.width = D;
     m.shift = shift;
@@ -341,6 +352,7 @@ struct Anima final : nd_denoiser {
              int q_rows, int kv_rows) {
     nd_attention_args a{};
     a.dtype = dt;
+    a.out_dtype = f32 ? ND_BF16X2 : 0;
     a.heads = H;
     a.head_dim = 128;
     a.batch = B;
@@ -353,7 +365,7 @@ struct Anima final : nd_denoiser {
     a.v = v;
     a.ldv = ldkv;
     a.out = attn;
-    a.ldo = D;
+    a.ldo = static_cast<int64_t>(D) * pw;
     return attention(a, s);
   }
 
@@ -372,7 +384,7 @@ struct Anima final : nd_denoiser {
     const int64_t bD = static_cast<int64_t>(b) * D;
     const float* mv = mods + static_cast<int64_t>(b) * 9 * D;  // self | cross | mlp, each shift scale gate
     const double mD = static_cast<double>(M) * D;
-    const size_t e = 2;
+    const size_t e = qe;
     // ---- self-attention
     ND_OP("modulate", 0.0, mD * 6, mod(s, mv, mv + D, M));
     {
@@ -431,7 +443,7 @@ struct Anima final : nd_denoiser {
     {
       nd_linear_args a = lin_args(xn, M, D, fc1, static_cast<int64_t>(b) * F, F, ND_EPI_GELU_ERF);
       a.y = hid;
-      a.ldy = F;
+      a.ldy = static_cast<int64_t>(F) * pw;
       ND_OP("gemm.up", gf(M, F, D), 0.0, linear(a, s));
     }
     {
@@ -447,14 +459,18 @@ struct Anima final : nd_denoiser {
   int forward(cudaStream_t s) override {
     const int64_t M = static_cast<int64_t>(B) * T;
     const double dD = D;
-    ND_OP("embed", 0.0, 0.0, patchify(in_latent, tok_in, dt, B, kLatentChannels, Hl, Wl, P, cin, s));
+    ND_OP("embed", 0.0, 0.0, patchify(in_latent, tok_in, lt, B, kLatentChannels, Hl, Wl, P, cin * pw, s));
     {
       nd_linear_args a = lin_args(tok_in, M, cin, x_emb, 0, D, ND_EPI_STORE_F32);
       a.residual = x;
       a.ldr = D;
       ND_OP("embed", gf(M, D, cin), 0.0, linear(a, s));
     }
-    ND_OP("embed", 0.0, 0.0, convert(in_ctx, ND_F32, ctxb, dt, static_cast<int64_t>(B) * ctx * cw, s));
+    if (f32) {
+      ND_OP("embed", 0.0, 0.0, convert_cols(in_ctx, ND_F32, cw, ctxb, ND_BF16X2, static_cast<int64_t>(B) * ctx, cw, s));
+    } else {
+      ND_OP("embed", 0.0, 0.0, convert(in_ctx, ND_F32, ctxb, dt, static_cast<int64_t>(B) * ctx * cw, s));
+    }
     // time: temb = RMSNorm(sinusoid); lora = Linear(SiLU(Linear(sinusoid)))
     {
       nd_rmsnorm_args r{};

@@ -9,7 +9,9 @@
 namespace nd {
 
 int attention(const nd_attention_args& a, cudaStream_t stream) {
-  if (a.dtype != ND_BF16 && a.dtype != ND_F16) return fail(ND_ERR_INVALID, "attention: dtype must be bf16 or f16");
+  if (a.dtype == ND_F32) return attention_f32(a, stream);
+  if (a.dtype != ND_BF16 && a.dtype != ND_F16) return fail(ND_ERR_INVALID, "attention: dtype must be bf16, f16 or f32");
+  if (a.out_dtype != 0 && a.out_dtype != a.dtype) return fail(ND_ERR_INVALID, "attention: out_dtype must match a 16-bit dtype");
   if (a.head_dim != 128 && a.head_dim != 64) return fail(ND_ERR_UNSUPPORTED, "attention: head_dim must be 64 or 128");
   const int hd = a.head_dim;
   if (a.heads <= 0 || a.batch <= 0 || a.q_rows <= 0 || a.kv_rows <= 0)

@@ -42,7 +42,13 @@ __global__ void convert_cols_kernel(const void* __restrict__ src, int st, long l
     if (st == ND_F32) v = static_cast<const float*>(src)[j];
     else if (st == ND_F16) v = __half2float(static_cast<const __half*>(src)[j]);
     else v = __bfloat162float(static_cast<const __nv_bfloat16*>(src)[j]);
-    if (dt == ND_F32) static_cast<float*>(dst)[i] = v;
+    if (dt == ND_BF16X2) {
+      // row r of the hi|lo pair: hi at column c, lo at column cols + c
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(dst) + r * 2 * cols + c;
+      o[0] = hi;
+      o[cols] = __float2bfloat16_rn(v - __bfloat162float(hi));
+    } else if (dt == ND_F32) static_cast<float*>(dst)[i] = v;
     else if (dt == ND_F16) static_cast<__half*>(dst)[i] = __float2half_rn(v);
     else static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn(v);
   }
@@ -172,7 +178,8 @@ nd::Mat nd_denoiser::alloc_mat(int64_t rows, int64_t cols, int64_t per_rows) {
     const int64_t sc = cols / qgroup(cols);
     m.scales = alloc(static_cast<size_t>(rows * sc) * (qf16() ? 2 : 4), true);
   } else {
-    m.w = alloc(static_cast<size_t>(rows * cols) * 2, true);
+    m.split = mat_dtype() == ND_BF16X2;
+    m.w = alloc(static_cast<size_t>(rows * cols) * (m.split ? 4 : 2), true);
   }
   return m;
 }
@@ -259,7 +266,7 @@ int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* 
       ND_CUDA(cudaMemcpyAsync(d->staging, data, src_bytes, cudaMemcpyHostToDevice, st));
       src = d->staging;
     }
-    int rc = convert_cols(src, dtype, s.src_cols, s.dst, d->desc.compute, s.rows, s.cols, st);
+    int rc = convert_cols(src, dtype, s.src_cols, s.dst, d->mat_dtype(), s.rows, s.cols, st);
     if (rc) return rc;
     ND_CUDA(cudaStreamSynchronize(st));
     s.set = true;
@@ -267,7 +274,7 @@ int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* 
   }
   DeviceGuard g(d->dev->ordinal);
   cudaStream_t st = d->dev->stream;
-  const int dst_type = s.kind == kMatrix ? d->desc.compute : ND_F32;
+  const int dst_type = s.kind == kMatrix ? d->mat_dtype() : ND_F32;
   const size_t src_bytes = static_cast<size_t>(n) * elem_bytes(dtype);
   if (s.scales) {
     // int8 storage: quantize on the device (BlockQuantizer's rules).
@@ -305,7 +312,8 @@ int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* 
       ND_CUDA(cudaMemcpyAsync(d->staging, data, src_bytes, cudaMemcpyHostToDevice, st));
       src = d->staging;
     }
-    int rc = convert(src, dtype, s.dst, dst_type, n, st);
+    int rc = dst_type == ND_BF16X2 ? convert_cols(src, dtype, s.cols, s.dst, dst_type, s.rows, s.cols, st)
+                                   : convert(src, dtype, s.dst, dst_type, n, st);
     if (rc) return rc;
   }
   ND_CUDA(cudaStreamSynchronize(st));

@@ -43,9 +43,12 @@ struct Mat {
   void* w = nullptr;
   void* scales = nullptr;
   bool q8 = false;
+  bool split = false;  // fp32 compute: rows are bf16 hi|lo pairs, 4 bytes per weight
   int64_t cols = 0;
   // element offset of sub-matrix row `row` in w, and of its scales
-  void* at(int64_t row, int elem_bytes) const { return static_cast<uint8_t*>(w) + row * cols * (q8 ? 1 : elem_bytes); }
+  void* at(int64_t row, int elem_bytes) const {
+    return static_cast<uint8_t*>(w) + row * cols * (q8 ? 1 : split ? 4 : elem_bytes);
+  }
   void* scales_at(int64_t row, int64_t scale_cols, bool f16) const {
     return scales ? static_cast<uint8_t*>(scales) + row * scale_cols * (f16 ? 2 : 4) : nullptr;
   }
@@ -115,6 +118,9 @@ struct nd_denoiser {
   // int8 storage of matrices (desc.weight_dtype == ND_I8): columns per scale
   // (0 = per output channel) and whether scales are fp16.
   bool q8() const { return desc.weight_dtype == ND_I8; }
+  // Storage of the matrices the GEMMs read: the compute dtype, or bf16 hi|lo
+  // pairs when the model computes in fp32.
+  int mat_dtype() const { return desc.compute == ND_F32 ? ND_BF16X2 : desc.compute; }
   int64_t qgroup(int64_t cols) const { return desc.quant_group > 0 ? desc.quant_group : cols; }
   bool qf16() const { return desc.quant_scale_dtype == ND_F16; }
   // Whether a [rows, cols] matrix is stored as int8: the reference's rule

@@ -56,8 +56,110 @@ int launch_gemm_w8(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorM
 
 }  // namespace
 
+namespace {
+
+// fp32 compute on bf16 hi|lo pairs (ND_BF16X2): the same mainloop over three
+// K segments, outputs as pairs (or fp32 for the attention's Q/K/V).
+int linear_split(const nd_linear_args& a, cudaStream_t stream) {
+  if (a.rows <= 0 || a.in_features <= 0 || a.out_features <= 0)
+    return fail(ND_ERR_INVALID, "linear: empty shape");
+  if (a.rows > INT_MAX || a.in_features > INT_MAX / 4 || a.out_features > INT_MAX / 4)
+    return fail(ND_ERR_INVALID, "linear: shape too large");
+  if (a.in_features % 64) return fail(ND_ERR_INVALID, "linear: bf16x2 operands need in_features % 64 == 0");
+  if (a.weight_dtype != 0 && a.weight_dtype != ND_BF16X2)
+    return fail(ND_ERR_INVALID, "linear: bf16x2 activations need bf16x2 weights");
+  if (!a.x || !a.weight) return fail(ND_ERR_INVALID, "linear: null operand");
+  if (a.ldx < 2 * a.in_features || a.ldx % 8) return fail(ND_ERR_INVALID, "linear: bf16x2 x needs ldx >= 2 * in_features, ldx % 8 == 0");
+  const bool split = a.group_split < a.rows;
+  if (split && (a.group_split % 128 != 0 || a.group_split <= 0))
+    return fail(ND_ERR_INVALID, "linear: group_split must be a positive multiple of 128");
+  const int epi = a.epilogue;
+  if (epi < 0 || epi > ND_EPI_RESIDUAL_ADD) return fail(ND_ERR_INVALID, "linear: unknown epilogue (ADD_STORE is not offered for bf16x2)");
+  const bool resid = epi == ND_EPI_RESIDUAL_GATE || epi == ND_EPI_RESIDUAL_ADD || epi == ND_EPI_STORE_F32;
+  const bool qk = epi == ND_EPI_QK_NORM_ROPE;
+  if (resid && (!a.residual || a.ldr < a.out_features || a.ldr % 4 != 0 || (reinterpret_cast<uintptr_t>(a.residual) & 15u)))
+    return fail(ND_ERR_INVALID, "linear: residual epilogue needs a 16-byte aligned residual with ldr >= out_features, ldr % 4 == 0");
+  if (qk && (!a.y || a.ldy < a.out_features || a.ldy % 4 != 0 || (reinterpret_cast<uintptr_t>(a.y) & 15u)))
+    return fail(ND_ERR_INVALID, "linear: bf16x2 QK epilogue writes fp32 y: ldy >= out_features, ldy % 4 == 0, 16-byte aligned");
+  if (!resid && !qk) {
+    if (!a.y || a.ldy < 2 * a.out_features || a.ldy % 8 != 0 || (reinterpret_cast<uintptr_t>(a.y) & 15u))
+      return fail(ND_ERR_INVALID, "linear: bf16x2 output needs a 16-byte aligned y with ldy >= 2 * out_features, ldy % 8 == 0");
+    if (a.out_features % 32) return fail(ND_ERR_INVALID, "linear: bf16x2 output needs out_features % 32 == 0");
+  }
+  if (epi == ND_EPI_RESIDUAL_GATE && !a.gate) return fail(ND_ERR_INVALID, "linear: gate missing");
+  const int64_t span = a.norm_span > 0 ? a.norm_span : a.qk_cols / 2;
+  if (qk) {
+    if (!a.qk_norm) return fail(ND_ERR_INVALID, "linear: qk epilogue needs qk_norm");
+    if ((a.rope_cos == nullptr) != (a.rope_sin == nullptr))
+      return fail(ND_ERR_INVALID, "linear: give both rope_cos and rope_sin, or neither");
+    if (a.qk_cols <= 0 || a.qk_cols % 128 != 0 || a.qk_cols > a.out_features)
+      return fail(ND_ERR_INVALID, "linear: qk_cols must be a positive multiple of 128, <= out_features");
+    if (span <= 0 || span % 128 != 0 || a.qk_cols % span != 0)
+      return fail(ND_ERR_INVALID, "linear: norm_span must be a multiple of 128 dividing qk_cols");
+    if (a.out_features % 128 != 0) return fail(ND_ERR_INVALID, "linear: qk epilogue needs out_features % 128 == 0");
+    if (a.rope_period < 0) return fail(ND_ERR_INVALID, "linear: rope_period must be >= 0");
+  }
+  if (a.bias && (reinterpret_cast<uintptr_t>(a.bias) & 15u))
+    return fail(ND_ERR_INVALID, "linear: bias must be 16-byte aligned");
+  if (a.out_features % 4 != 0 && (a.bias || a.gate))
+    return fail(ND_ERR_INVALID, "linear: bias/gate need out_features % 4 == 0");
+
+  const int groups = split ? 2 : 1;
+  const int64_t K2 = 2 * a.in_features;
+  CUtensorMap ta, tb, tc;
+  int rc = make_tmap_2d(&ta, a.x, 2, a.rows, K2, a.ldx, 128, 64, true);
+  if (rc) return rc;
+  if (resid) rc = make_tmap_2d_typed(&tc, a.residual, ND_F32, a.rows, a.out_features, a.ldr, 32, 32, 128);
+  else if (qk) rc = make_tmap_2d_typed(&tc, a.y, ND_F32, a.rows, a.out_features, a.ldy, 32, 32, 128);
+  else rc = make_tmap_2d_typed(&tc, a.y, ND_BF16, a.rows, 2 * a.out_features, a.ldy, 32, 32, 64);
+  if (rc) return rc;
+
+  GemmArgs g{};
+  g.M = static_cast<int>(a.rows);
+  g.N = static_cast<int>(a.out_features);
+  g.K = static_cast<int>(a.in_features);
+  g.split_kb = static_cast<int>(a.in_features / 64);
+  g.split_koff = static_cast<int>(a.in_features);
+  g.out_kind = resid ? 0 : (qk ? 2 : 1);
+  g.group_split = split ? static_cast<int>(a.group_split) : INT_MAX;
+  g.epi = epi;
+  g.out = a.y;
+  g.ldo = a.ldy;
+  g.resid = a.residual;
+  g.ldr = a.ldr;
+  g.bias = a.bias;
+  g.bias_stride = static_cast<int>(a.out_features);
+  g.gate = a.gate;
+  g.gate_stride = static_cast<int>(a.gate_stride > 0 ? a.gate_stride : a.out_features);
+  if (a.gate && (g.gate_stride % 4 != 0 || (reinterpret_cast<uintptr_t>(a.gate) & 15u)))
+    return fail(ND_ERR_INVALID, "linear: gate must be 16-byte aligned with gate_stride % 4 == 0");
+  g.qk_norm = a.qk_norm;
+  g.rope_cos = a.rope_cos;
+  g.rope_sin = a.rope_sin;
+  g.qk_cols = static_cast<int>(a.qk_cols);
+  g.norm_span = static_cast<int>(span > 0 ? span : 128);
+  g.norm_sets = static_cast<int>(a.qk_cols > 0 && span > 0 ? a.qk_cols / span : 1);
+  g.rope_period = static_cast<int>(a.rope_period);
+  g.head_dim = 128;
+  g.norm_eps = a.eps;
+  g.status = device_status();
+  if (!g.status) return fail(ND_ERR_CUDA, "linear: no device status word");
+
+  const int sms = sm_count();
+  const int64_t tiles256 = ((a.rows + 127) / 128) * ((a.out_features + 255) / 256);
+  const int bn = (qk || (a.out_features >= 256 && tiles256 >= sms)) ? 256 : 128;
+  g.idesc = make_idesc_f16(128, bn, true);
+  rc = make_tmap_2d(&tb, a.weight, 2, groups * a.out_features, K2, K2, bn, 64, true);
+  if (rc) return rc;
+  if (bn == 256) return launch_gemm<256, 4>(ta, tb, tc, g, stream);
+  return launch_gemm<128, 6>(ta, tb, tc, g, stream);
+}
+
+}  // namespace
+
 int linear(const nd_linear_args& a, cudaStream_t stream) {
-  if (a.dtype != ND_BF16 && a.dtype != ND_F16) return fail(ND_ERR_INVALID, "linear: dtype must be bf16 or f16");
+  if (a.dtype == ND_BF16X2) return linear_split(a, stream);
+  if (a.dtype != ND_BF16 && a.dtype != ND_F16) return fail(ND_ERR_INVALID, "linear: dtype must be bf16, f16 or bf16x2");
   if (a.rows <= 0 || a.in_features <= 0 || a.out_features <= 0)
     return fail(ND_ERR_INVALID, "linear: empty shape");
   if (a.rows > INT_MAX || a.in_features > INT_MAX || a.out_features > INT_MAX / 2)

@@ -78,6 +78,12 @@ struct GemmArgs {
   int conv_hw;       // H_out * W_out pixels per image
   int conv_w_out;
   int conv_stride;
+  // fp32 compute on bf16 hi|lo pairs (ND_BF16X2): A is [M, 2K'] and W is
+  // [N, 2K'] with K' = split_kb * 64; the K loop runs three segments,
+  // hi.lo + lo.hi + hi.hi, reading the lo halves split_koff columns along.
+  int split_kb;     // 0: plain operands
+  int split_koff;
+  int out_kind;     // 0: bf16/f16 out, 1: hi|lo pair out (lo at column + N), 2: fp32 out
 };
 
 __device__ __forceinline__ int row_group(const GemmArgs& a, int m0) {
@@ -106,7 +112,14 @@ struct GemmSmem {
   static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
 };
 
-enum EmitKind : int { kEmitBf16 = 0, kEmitF16 = 1, kEmitF32 = 2, kEmitAddF32 = 3 };
+enum EmitKind : int { kEmitBf16 = 0, kEmitF16 = 1, kEmitF32 = 2, kEmitAddF32 = 3, kEmitSplit = 4 };
+
+// The store kind of a 16-bit-class output under the args' out_kind.
+__device__ __forceinline__ int out_emit_kind(const GemmArgs& a) {
+  if (a.out_kind == 1) return kEmitSplit;
+  if (a.out_kind == 2) return kEmitF32;
+  return a.out_f16 ? kEmitF16 : kEmitBf16;
+}
 
 __device__ __forceinline__ void load_vec32(const float* src, int col, int N, float (&v)[32]) {
   if (src == nullptr) {
@@ -129,18 +142,39 @@ __device__ __forceinline__ void load_vec32(const float* src, int col, int N, flo
 
 // Stage one warp's [32 rows x 32 columns] chunk (lane = row) in shared memory
 // in the tensor map's swizzled layout and hand it to TMA: a store (bf16, fp16,
-// fp32) or an fp32 reduce-add into global memory. Rows / columns past the
-// tensor's edge are clipped by TMA. Two staging buffers per warp alternate;
-// a buffer is rewritten only after the store issued from it two chunks ago
-// has finished reading it.
+// fp32, or a bf16 hi|lo pair whose lo chunk goes to column col + lo_off) or
+// an fp32 reduce-add into global memory. Rows / columns past the tensor's
+// edge are clipped by TMA. Two staging buffers per warp alternate; a buffer is
+// rewritten only after the store issued from it two chunks ago has finished
+// reading it.
 __device__ __forceinline__ void emit_chunk(const CUtensorMap* tm, int kind, uint32_t buf0, int& sb,
                                            int lane, int row0, int rows, int col,
-                                           const float (&v)[32]) {
+                                           const float (&v)[32], int lo_off = 0) {
   if (row0 >= rows) return;  // the whole warp's rows are past the tensor's edge
   const uint32_t buf = buf0 + static_cast<uint32_t>(sb) * 4096u;
   sb ^= 1;
   if (lane == 0) bulk_wait_read<1>();
   __syncwarp();
+  if (kind == kEmitSplit) {
+    uint32_t h[16], l[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) pack_split(v[2 * i], v[2 * i + 1], h[i], l[i]);
+    // hi rows in the first 2 KB, lo rows in the second, each 64B-swizzled.
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t off = lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4);
+      st_shared_v4(buf + off, h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+      st_shared_v4(buf + 2048 + off, l[4 * c], l[4 * c + 1], l[4 * c + 2], l[4 * c + 3]);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tm, buf, col, row0);
+      tma_store_2d(tm, buf + 2048, col + lo_off, row0);
+      bulk_commit();
+    }
+    return;
+  }
   if (kind == kEmitBf16 || kind == kEmitF16) {
     uint32_t p[16];
     if (kind == kEmitF16) {
@@ -181,7 +215,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, const CUtensor
   load_vec32(a.bias ? a.bias + group * a.bias_stride : nullptr, col, a.N, b);
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + b[i];
-  int kind = a.out_f16 ? kEmitF16 : kEmitBf16;
+  int kind = out_emit_kind(a);
   switch (a.epi) {
     case kEpiGeluTanh:
 #pragma unroll
@@ -240,7 +274,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, const CUtensor
     default:
       break;
   }
-  emit_chunk(tmC, kind, buf0, sb, lane, row0, a.M, col, v);
+  emit_chunk(tmC, kind, buf0, sb, lane, row0, a.M, col, v, a.N);
 }
 
 // The Q/K projection epilogue for one 128-wide head: RMSNorm over the head's
@@ -256,7 +290,7 @@ __device__ __forceinline__ void epilogue_head_norm_rope(const GemmArgs& a, const
   const float* w = a.qk_norm + (group * a.norm_sets + which) * 128;
   const bool rope = a.rope_cos != nullptr;
   const int trow = row_ok ? (a.rope_period > 0 ? row % a.rope_period : row) : 0;
-  const int kind = a.out_f16 ? kEmitF16 : kEmitBf16;
+  const int kind = out_emit_kind(a);
   uint32_t r[32];
   float sumsq = 0.f;
 #pragma unroll
@@ -297,8 +331,8 @@ __device__ __forceinline__ void epilogue_head_norm_rope(const GemmArgs& a, const
         ohi[i + u] = h * cv[u] + l * sv[u];
       }
     }
-    emit_chunk(tmC, kind, buf0, sb, lane, row0, a.M, col0 + c * 32, olo);
-    emit_chunk(tmC, kind, buf0, sb, lane, row0, a.M, col0 + 64 + c * 32, ohi);
+    emit_chunk(tmC, kind, buf0, sb, lane, row0, a.M, col0 + c * 32, olo, a.N);
+    emit_chunk(tmC, kind, buf0, sb, lane, row0, a.M, col0 + 64 + c * 32, ohi, a.N);
   }
 }
 
@@ -327,7 +361,7 @@ __global__ void __launch_bounds__(192, 1)
   const int num_m = (args.M + 127) / 128;
   const int num_n = (args.N + BN - 1) / BN;
   const int total = num_m * num_n;
-  const int num_kb = (args.K + 63) / 64;
+  const int num_kb = args.split_kb > 0 ? 3 * args.split_kb : (args.K + 63) / 64;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -389,10 +423,20 @@ __global__ void __launch_bounds__(192, 1)
             const int c0 = (kb - tap * args.conv_kpc) * 64;
             const int dy = tap / 3, dx = tap - dy * 3;
             tma_load_4d(a_dst, &tmA, full_bar(stage), c0, dx - 1, y0 * args.conv_stride + dy - 1, img);
+          } else if (args.split_kb > 0) {
+            // segments 0, 1, 2 = (A hi, W lo), (A lo, W hi), (A hi, W hi): the
+            // two small cross terms first, into a still-small accumulator (the
+            // tensor cores' fp32 accumulation loses bits relative to the
+            // accumulator's magnitude at every step, so the small terms are
+            // summed before the large one arrives).
+            const int seg = kb / args.split_kb;
+            const int kc = (kb - seg * args.split_kb) * 64;
+            tma_load_2d(a_dst, &tmA, full_bar(stage), kc + (seg == 1 ? args.split_koff : 0), m0);
+            tma_load_2d(b_dst, &tmB, full_bar(stage), kc + (seg == 0 ? args.split_koff : 0), brow);
           } else {
             tma_load_2d(a_dst, &tmA, full_bar(stage), kb * 64, m0);
           }
-          tma_load_2d(b_dst, &tmB, full_bar(stage), kb * 64, brow);
+          if (CONV || args.split_kb == 0) tma_load_2d(b_dst, &tmB, full_bar(stage), kb * 64, brow);
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {

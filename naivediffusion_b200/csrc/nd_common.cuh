@@ -406,4 +406,20 @@ __device__ __forceinline__ uint32_t pack_f16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Two fp32 values as bf16 hi|lo pairs (the ND_BF16X2 format): hi = bf16(v),
+// lo = bf16(v - hi), both round to nearest even; v - hi is exact in fp32.
+__device__ __forceinline__ void pack_split(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const float2 hf = __bfloat1622float2(h);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+// hi + lo of one packed pair of bf16 pairs, in fp32.
+__device__ __forceinline__ float2 unpack_split(uint32_t hi, uint32_t lo) {
+  const float2 h = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi));
+  const float2 l = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lo));
+  return make_float2(h.x + l.x, h.y + l.y);
+}
+
 }  // namespace nd

@@ -50,6 +50,7 @@ int conv2d(const nd_conv_args& c, cudaStream_t stream);
 int dequantize(const int8_t* q, const void* scales, int scale_dtype, int64_t quant_group, int64_t rows,
                int64_t cols, void* out, int out_dtype, cudaStream_t stream);
 int attention(const nd_attention_args& a, cudaStream_t stream);
+int attention_f32(const nd_attention_args& a, cudaStream_t stream);
 int modulate(const nd_modulate_args& a, cudaStream_t stream);
 int rmsnorm(const nd_rmsnorm_args& a, cudaStream_t stream);
 int gemv(const nd_gemv_args& a, cudaStream_t stream);

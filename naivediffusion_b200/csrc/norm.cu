@@ -19,8 +19,17 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-__device__ __forceinline__ void store4(void* out, long long idx, float4 v, int out_type) {
-  if (out_type == ND_F32) {
+// Four consecutive values at element idx; ND_BF16X2 puts the lo halves
+// lo_off elements further along the row.
+__device__ __forceinline__ void store4(void* out, long long idx, float4 v, int out_type,
+                                       long long lo_off = 0) {
+  if (out_type == ND_BF16X2) {
+    uint2 h, l;
+    pack_split(v.x, v.y, h.x, l.x);
+    pack_split(v.z, v.w, h.y, l.y);
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + idx) = h;
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + idx + lo_off) = l;
+  } else if (out_type == ND_F32) {
     reinterpret_cast<float4*>(static_cast<float*>(out) + idx)[0] = v;
   } else if (out_type == ND_F16) {
     uint2 p = make_uint2(pack_f16(v.x, v.y), pack_f16(v.z, v.w));
@@ -95,7 +104,7 @@ __global__ void __launch_bounds__(256) modulate_kernel(const float* __restrict__
       o.y = (v[i].y - mean) * rstd * (one + k.y) + b.y;
       o.z = (v[i].z - mean) * rstd * (one + k.z) + b.z;
       o.w = (v[i].w - mean) * rstd * (one + k.w) + b.w;
-      store4(y, static_cast<long long>(row) * ldy + 4 * c, o, out_type);
+      store4(y, static_cast<long long>(row) * ldy + 4 * c, o, out_type, width);
     }
   }
 }
@@ -149,7 +158,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const void* __restrict__ x
       o.y = v[i].y * r * (k.y + plus_one);
       o.z = v[i].z * r * (k.z + plus_one);
       o.w = v[i].w * r * (k.w + plus_one);
-      store4(y, static_cast<long long>(warp) * ldy + 4 * c, o, out_type);
+      store4(y, static_cast<long long>(warp) * ldy + 4 * c, o, out_type, width);
     }
   }
 }
@@ -165,11 +174,12 @@ int pick_bucket(int width) {
   return 0;
 }
 
-// y[b][n] = act(sum_k W[n][k] * pre(x[b][k]) + bias[n]); W bf16/f16 [N, K];
+// y[b][n] = act(sum_k W[n][k] * pre(x[b][k]) + bias[n]); W bf16/f16 [N, K]
+// (w_type 0 / 1), or a bf16 hi|lo pair [N, 2K] (w_type 2, fp32 weights);
 // x fp32 [B, K] (B <= 4); one warp per output row, x staged in shared memory.
 // The modulation vectors of every block at once (one HBM pass over the
 // modulation weights: QwenImageDit's modulation.1, AnimaDit.Modulation).
-__global__ void __launch_bounds__(256) gemv_kernel(const uint16_t* __restrict__ W, int w_f16,
+__global__ void __launch_bounds__(256) gemv_kernel(const uint16_t* __restrict__ W, int w_type,
                                                    long long N, int K, const float* __restrict__ x,
                                                    int B, int pre, const float* __restrict__ bias,
                                                    int act, float* __restrict__ y, long long xrows,
@@ -186,19 +196,26 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint16_t* __restrict__ 
   const int k8 = K >> 3;
   for (long long n = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; n < N;
        n += warps) {
-    const uint4* wr = reinterpret_cast<const uint4*>(W + n * K);
+    const bool split = w_type == 2;
+    const uint4* wr = reinterpret_cast<const uint4*>(W + n * K * (split ? 2 : 1));
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int c = lane; c < k8; c += 32) {
-      uint4 p;
+      uint4 p, q = make_uint4(0u, 0u, 0u, 0u);
       asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                    : "=r"(p.x), "=r"(p.y), "=r"(p.z), "=r"(p.w)
                    : "l"(wr + c));
+      if (split)
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w)
+                     : "l"(wr + k8 + c));
       float wv[8];
       const uint32_t u[4] = {p.x, p.y, p.z, p.w};
+      const uint32_t ul[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         float2 f;
-        if (w_f16) f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+        if (split) f = unpack_split(u[i], ul[i]);
+        else if (w_type == 1) f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
         else f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[i]));
         wv[2 * i] = f.x;
         wv[2 * i + 1] = f.y;
@@ -245,9 +262,12 @@ __global__ void patchify_kernel(const float* __restrict__ lat, void* __restrict_
     const int i = h / p, m = h % p, j = w / p, n = w % p;
     const long long t = static_cast<long long>(b) * rows * cols + i * cols + j;
     const long long o = t * ldt + c * p * p + m * p + n;
-    (void)feat;
     const float v = lat[idx];
-    if (out_type == ND_F32) static_cast<float*>(tok)[o] = v;
+    if (out_type == ND_BF16X2) {
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+      static_cast<__nv_bfloat16*>(tok)[o] = hi;
+      static_cast<__nv_bfloat16*>(tok)[o + feat] = __float2bfloat16_rn(v - __bfloat162float(hi));
+    } else if (out_type == ND_F32) static_cast<float*>(tok)[o] = v;
     else if (out_type == ND_F16) static_cast<__half*>(tok)[o] = __float2half_rn(v);
     else static_cast<__nv_bfloat16*>(tok)[o] = __float2bfloat16_rn(v);
   }
@@ -276,6 +296,10 @@ __global__ void unpatchify_kernel(const float* __restrict__ tok, long long ldt, 
 int modulate(const nd_modulate_args& a, cudaStream_t stream) {
   if (a.rows <= 0 || a.width <= 0) return fail(ND_ERR_INVALID, "modulate: empty shape");
   if (a.width % 4 || a.ldx % 4 || a.ldy % 4) return fail(ND_ERR_INVALID, "modulate: width and strides must be multiples of 4");
+  if (a.out_dtype != ND_F32 && a.out_dtype != ND_F16 && a.out_dtype != ND_BF16 && a.out_dtype != ND_BF16X2)
+    return fail(ND_ERR_INVALID, "modulate: out_dtype must be f32, f16, bf16 or bf16x2");
+  if (a.ldy < (a.out_dtype == ND_BF16X2 ? 2 : 1) * a.width)
+    return fail(ND_ERR_INVALID, "modulate: ldy too small (a bf16x2 output needs 2 * width)");
   if (!a.x || !a.y || !a.scale) return fail(ND_ERR_INVALID, "modulate: null operand");
   if (a.rows > INT_MAX) return fail(ND_ERR_INVALID, "modulate: too many rows");
   if (a.width > 4096) return fail(ND_ERR_UNSUPPORTED, "modulate: width above 4096");
@@ -298,6 +322,12 @@ int modulate(const nd_modulate_args& a, cudaStream_t stream) {
 int rmsnorm(const nd_rmsnorm_args& a, cudaStream_t stream) {
   if (a.rows <= 0 || a.width <= 0) return fail(ND_ERR_INVALID, "rmsnorm: empty shape");
   if (a.width % 4 || a.ldx % 4 || a.ldy % 4) return fail(ND_ERR_INVALID, "rmsnorm: width and strides must be multiples of 4");
+  if (a.in_dtype != ND_F32 && a.in_dtype != ND_F16 && a.in_dtype != ND_BF16)
+    return fail(ND_ERR_INVALID, "rmsnorm: in_dtype must be f32, f16 or bf16");
+  if (a.out_dtype != ND_F32 && a.out_dtype != ND_F16 && a.out_dtype != ND_BF16 && a.out_dtype != ND_BF16X2)
+    return fail(ND_ERR_INVALID, "rmsnorm: out_dtype must be f32, f16, bf16 or bf16x2");
+  if (a.ldy < (a.out_dtype == ND_BF16X2 ? 2 : 1) * a.width)
+    return fail(ND_ERR_INVALID, "rmsnorm: ldy too small (a bf16x2 output needs 2 * width)");
   if (!a.x || !a.y) return fail(ND_ERR_INVALID, "rmsnorm: null operand");
   const int bucket = pick_bucket(static_cast<int>(a.width));
   if (!bucket) return fail(ND_ERR_UNSUPPORTED, "rmsnorm: width above 4096");
@@ -328,14 +358,15 @@ int gemv(const nd_gemv_args& a, cudaStream_t stream) {
     return gemv_w8(a, stream);
   }
   if (a.k % 8) return fail(ND_ERR_INVALID, "gemv: k must be a multiple of 8");
-  if (a.w_dtype != ND_BF16 && a.w_dtype != ND_F16) return fail(ND_ERR_INVALID, "gemv: weight must be bf16 or f16");
+  if (a.w_dtype != ND_BF16 && a.w_dtype != ND_F16 && a.w_dtype != ND_BF16X2)
+    return fail(ND_ERR_INVALID, "gemv: weight must be bf16, f16, bf16x2 or int8");
   if (!a.w || !a.x || !a.y) return fail(ND_ERR_INVALID, "gemv: null operand");
   const size_t shmem = static_cast<size_t>(a.k) * nvec * sizeof(float);
   long long blocks = (a.n + 7) / 8;
   const long long cap = static_cast<long long>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
   gemv_kernel<<<static_cast<unsigned>(blocks), 256, shmem, stream>>>(
-      static_cast<const uint16_t*>(a.w), a.w_dtype == ND_F16, a.n, static_cast<int>(a.k), a.x,
+      static_cast<const uint16_t*>(a.w), a.w_dtype == ND_BF16X2 ? 2 : (a.w_dtype == ND_F16 ? 1 : 0), a.n, static_cast<int>(a.k), a.x,
       a.batch, a.pre_silu ? 1 : 0, a.bias, a.act, a.y, a.x_rows_per_vec, static_cast<int>(nvec),
       a.bias_period);
   ND_CUDA(cudaGetLastError());
@@ -346,6 +377,10 @@ int patchify(const float* lat, void* tok, int out_dtype, int B, int C, int H, in
              int64_t ldt, cudaStream_t stream) {
   if (B <= 0 || C <= 0 || H <= 0 || W <= 0 || p <= 0 || H % p || W % p)
     return fail(ND_ERR_INVALID, "patchify: latent does not divide into patches");
+  if (out_dtype != ND_F32 && out_dtype != ND_F16 && out_dtype != ND_BF16 && out_dtype != ND_BF16X2)
+    return fail(ND_ERR_INVALID, "patchify: out_dtype must be f32, f16, bf16 or bf16x2");
+  if (ldt < static_cast<int64_t>(C) * p * p * (out_dtype == ND_BF16X2 ? 2 : 1))
+    return fail(ND_ERR_INVALID, "patchify: ldt smaller than the token width");
   const long long total = static_cast<long long>(B) * C * H * W;
   const unsigned grid = static_cast<unsigned>(std::min<long long>((total + 255) / 256, sm_count() * 16LL));
   patchify_kernel<<<grid, 256, 0, stream>>>(lat, tok, out_dtype, B, C, H, W, p, ldt);

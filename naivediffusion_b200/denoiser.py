@@ -363,7 +363,7 @@ def synthetic_weights_device(cfg, seed: int = 0, device="cuda"):
     BASELINE-size model is 20 G parameters): one torch generator per tensor
     name. Yields (name, CUDA tensor): matrices in the compute dtype, vectors fp32."""
     import torch
-    dt = torch.bfloat16 if cfg.compute == _lib.ND_BF16 else torch.float16
+    dt = {_lib.ND_BF16: torch.bfloat16, _lib.ND_F16: torch.float16}.get(cfg.compute, torch.float32)
     g = torch.Generator(device=device)
     if hasattr(cfg, "weight_shapes"):
         for name, shape, _req in cfg.weight_shapes():
@@ -385,6 +385,8 @@ def synthetic_weights_device(cfg, seed: int = 0, device="cuda"):
 
 
 def _round(a: np.ndarray, dtype: int) -> np.ndarray:
+    if dtype == _lib.ND_F32:
+        return a
     import torch
     t = torch.from_numpy(np.ascontiguousarray(a))
     t = t.to(torch.bfloat16 if dtype == _lib.ND_BF16 else torch.float16).float()

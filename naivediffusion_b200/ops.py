@@ -31,6 +31,20 @@ def sync() -> None:
     check(lib().nd_op_sync(C.c_void_p(_stream())))
 
 
+def to_pairs(t: torch.Tensor) -> torch.Tensor:
+    """fp32 [rows, cols] -> the ND_BF16X2 pair [rows, 2 * cols] (hi = bf16(t),
+    lo = bf16(t - hi)), the operand format of fp32-compute GEMMs."""
+    hi = t.float().bfloat16()
+    lo = (t.float() - hi.float()).bfloat16()
+    return torch.cat([hi, lo], dim=1).contiguous()
+
+
+def from_pairs(p: torch.Tensor) -> torch.Tensor:
+    """The fp32 value hi + lo of an ND_BF16X2 pair [rows, 2 * cols]."""
+    c = p.shape[1] // 2
+    return p[:, :c].float() + p[:, c:].float()
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *,
            epilogue: int = _lib.ND_EPI_STORE, out: torch.Tensor | None = None,
            residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
@@ -38,15 +52,20 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
            rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
            qk_cols: int = 0, eps: float = 1e-6, scales: torch.Tensor | None = None,
            quant_group: int = 32, norm_span: int = 0, rope_period: int = 0,
-           gate_stride: int = 0) -> torch.Tensor:
+           gate_stride: int = 0, pairs: bool = False) -> torch.Tensor:
     """y = x . W^T + bias with a fused epilogue (Layers.Linear, Graph/Layers.cs:131-160).
 
     weight is [groups * out, in]; rows >= group_split use the second group.
     Residual epilogues update `residual` (fp32) in place and return it.
     An int8 weight (with `scales`, fp16 or fp32, `quant_group` 32 or 0 = per
     output channel) is widened inside the GEMM (BlockQuantizer's scheme).
+    pairs=True: fp32 compute on ND_BF16X2 operands (x [rows, 2 * in], weight
+    [groups * out, 2 * in]); the output is a pair [rows, 2 * out], or fp32
+    [rows, out] for QK_NORM_ROPE.
     """
     rows, k = x.shape
+    if pairs:
+        k //= 2
     groups = 1 if group_split is None or group_split >= rows else 2
     n = weight.shape[0] // groups
     resid_epi = epilogue in (_lib.ND_EPI_RESIDUAL_GATE, _lib.ND_EPI_RESIDUAL_ADD, _lib.ND_EPI_STORE_F32)
@@ -54,9 +73,14 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
         if residual is None:
             residual = torch.empty(rows, n, device=x.device, dtype=torch.float32)
     elif out is None:
-        out = torch.empty(rows, n, device=x.device, dtype=x.dtype)
+        if pairs and epilogue == _lib.ND_EPI_QK_NORM_ROPE:
+            out = torch.empty(rows, n, device=x.device, dtype=torch.float32)
+        elif pairs:
+            out = torch.empty(rows, 2 * n, device=x.device, dtype=torch.bfloat16)
+        else:
+            out = torch.empty(rows, n, device=x.device, dtype=x.dtype)
     a = LinearArgs()
-    a.dtype = _DT[x.dtype]
+    a.dtype = _lib.ND_BF16X2 if pairs else _DT[x.dtype]
     a.epilogue = epilogue
     a.rows, a.in_features, a.out_features = rows, k, n
     a.x, a.ldx = x.data_ptr(), x.stride(0)
@@ -87,18 +111,24 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *,
               out: torch.Tensor | None = None, batch: int = 1, key_limit: int = 0,
-              causal: bool = False, scale: float = 0.0, head_dim: int = 128) -> torch.Tensor:
+              causal: bool = False, scale: float = 0.0, head_dim: int = 128,
+              out_pairs: bool = False) -> torch.Tensor:
     """Flash attention over packed heads (Layers.Attend, Graph/Layers.cs:260-279).
 
     q: [batch * q_rows, >= heads*128] (row stride q.stride(0)); k, v likewise
     with kv_rows per item. Returns out [batch * q_rows, heads * 128].
+    fp32 q/k/v run the fp32 attention; out_pairs then writes an ND_BF16X2 pair.
     """
     q_rows = q.shape[0] // batch
     kv_rows = k.shape[0] // batch
     if out is None:
-        out = torch.empty(q.shape[0], heads * head_dim, device=q.device, dtype=q.dtype)
+        if out_pairs:
+            out = torch.empty(q.shape[0], 2 * heads * head_dim, device=q.device, dtype=torch.bfloat16)
+        else:
+            out = torch.empty(q.shape[0], heads * head_dim, device=q.device, dtype=q.dtype)
     a = AttentionArgs()
     a.dtype = _DT[q.dtype]
+    a.out_dtype = _lib.ND_BF16X2 if out_pairs else 0
     a.heads, a.head_dim, a.batch = heads, head_dim, batch
     a.q_rows, a.kv_rows, a.key_limit, a.causal = q_rows, kv_rows, key_limit, int(causal)
     a.q, a.ldq = q.data_ptr(), q.stride(0)
@@ -116,11 +146,13 @@ def modulate(x: torch.Tensor, shift: torch.Tensor | None, scale: torch.Tensor, *
     """LayerNorm(x) * (1 + scale) + shift (Transformer.Modulate, Graph/Transformer.cs:72-80).
     scale/shift: [width] or [2, width] (second row for rows >= group_split)."""
     rows, width = x.shape
+    pairs = out_dtype == "pairs"
     if out is None:
-        out = torch.empty(rows, width, device=x.device, dtype=out_dtype)
+        out = torch.empty(rows, 2 * width if pairs else width, device=x.device,
+                          dtype=torch.bfloat16 if pairs else out_dtype)
     a = ModulateArgs()
     a.x, a.ldx = x.data_ptr(), x.stride(0)
-    a.y, a.ldy, a.out_dtype = out.data_ptr(), out.stride(0), _DT[out.dtype]
+    a.y, a.ldy, a.out_dtype = out.data_ptr(), out.stride(0), (_lib.ND_BF16X2 if pairs else _DT[out.dtype])
     a.rows, a.width = rows, width
     a.shift = _ptr(shift)
     a.scale = scale.data_ptr()
@@ -148,13 +180,16 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor | None, *, out_dtype=None, plu
 
 
 def gemv(w: torch.Tensor, x: torch.Tensor, bias: torch.Tensor | None = None, *,
-         pre_silu: bool = False, act: int = 0) -> torch.Tensor:
-    """y[b] = act(W . pre(x[b]) + bias) for 1-4 fp32 rows x; W bf16/f16 [n, k]."""
+         pre_silu: bool = False, act: int = 0, w_pairs: bool = False) -> torch.Tensor:
+    """y[b] = act(W . pre(x[b]) + bias) for 1-4 fp32 rows x; W bf16/f16 [n, k]
+    (w_pairs: an ND_BF16X2 pair [n, 2k])."""
     n, k = w.shape
+    if w_pairs:
+        k //= 2
     x = x.reshape(-1, k).contiguous()
     y = torch.empty(x.shape[0], n, device=w.device, dtype=torch.float32)
     a = GemvArgs()
-    a.w, a.w_dtype, a.n, a.k = w.data_ptr(), _DT[w.dtype], n, k
+    a.w, a.w_dtype, a.n, a.k = w.data_ptr(), (_lib.ND_BF16X2 if w_pairs else _DT[w.dtype]), n, k
     a.x, a.batch, a.pre_silu = x.data_ptr(), x.shape[0], int(pre_silu)
     a.bias, a.act, a.y = _ptr(bias), act, y.data_ptr()
     check(lib().nd_op_gemv(C.byref(a), C.c_void_p(_stream())))
