@@ -72,6 +72,12 @@ struct MMDiT final : nd_denoiser {
   int D = 0, H = 0, F = 0, NB = 0, ctx = 0, cw = 0, C = 0, Hl = 0, Wl = 0, P = 0, tw = 0, cin = 0;
   int n_img = 0, M = 0;
   int dt = ND_BF16;
+  // fp32 compute: GEMM operands as bf16 hi|lo pairs (lt = ND_BF16X2, pair
+  // buffers twice as wide), Q/K/V and the attention in fp32.
+  bool f32 = false;
+  int lt = ND_BF16;
+  int pw = 1;     // columns per logical column in GEMM-operand buffers
+  size_t qe = 2;  // bytes per element of the Q/K/V buffer
   float eps = 1e-6f;
   // weights (compute dtype or int8 + scales) and vectors (fp32)
   Mat img_in_w, txt_in_w, t1_w, t2_w, mod_w, qkv_w, out_w, up_w, down_w, norm_out_w, proj_out_w;
@@ -94,9 +100,10 @@ struct MMDiT final : nd_denoiser {
   int build() override {
     const nd_model_desc& d = desc;
     if (d.batch != 1) return fail(ND_ERR_UNSUPPORTED, "mmdit: batch must be 1 (shard images across devices)");
-    if (d.compute != ND_BF16 && d.compute != ND_F16) return fail(ND_ERR_UNSUPPORTED, "mmdit: compute must be bf16 or f16");
-    if (d.weight_dtype != d.compute && d.weight_dtype != ND_I8)
-      return fail(ND_ERR_UNSUPPORTED, "mmdit: weights must be stored in the compute dtype or int8");
+    if (d.compute != ND_BF16 && d.compute != ND_F16 && d.compute != ND_F32)
+      return fail(ND_ERR_UNSUPPORTED, "mmdit: compute must be bf16, f16 or f32");
+    if (d.weight_dtype != d.compute && !(d.weight_dtype == ND_I8 && d.compute != ND_F32))
+      return fail(ND_ERR_UNSUPPORTED, "mmdit: weights must be stored in the compute dtype (or int8 with 16-bit compute)");
     if (d.weight_dtype == ND_I8) {
       if (d.quant_scale_dtype != ND_F16 && d.quant_scale_dtype != ND_F32)
         return fail(ND_ERR_INVALID, "mmdit: int8 weights need quant_scale_dtype ND_F16 or ND_F32");
@@ -112,6 +119,10 @@ struct MMDiT final : nd_denoiser {
       return fail(ND_ERR_INVALID, "mmdit: latent does not divide into patches");
     if (d.time_width <= 0 || d.time_width % 8) return fail(ND_ERR_INVALID, "mmdit: time_width must be a multiple of 8");
     dt = d.compute;
+    f32 = dt == ND_F32;
+    lt = f32 ? ND_BF16X2 : dt;
+    pw = f32 ? 2 : 1;
+    qe = f32 ? 4 : 2;
     D = d.width;
     H = d.heads;
     F = d.mlp_width;
@@ -125,6 +136,8 @@ struct MMDiT final : nd_denoiser {
     tw = d.time_width;
     cin = C * P * P;
     if (cin % 8) return fail(ND_ERR_INVALID, "mmdit: channels x patch^2 must be a multiple of 8");
+    if (f32 && (cin % 64 || cw % 64 || F % 64))
+      return fail(ND_ERR_UNSUPPORTED, "mmdit: fp32 compute needs channels x patch^2, context width and mlp width % 64 == 0");
     n_img = (Hl / P) * (Wl / P);
     if (n_img % 128) return fail(ND_ERR_UNSUPPORTED, "mmdit: image tokens must be a multiple of 128");
     M = n_img + ctx;
@@ -171,12 +184,12 @@ struct MMDiT final : nd_denoiser {
     fmod = static_cast<float*>(S(static_cast<size_t>(2) * D * 4));
     out_tok = static_cast<float*>(S(static_cast<size_t>(n_img) * cin * 4));
     out_latent = static_cast<float*>(S(static_cast<size_t>(C) * Hl * Wl * 4));
-    xn = S(static_cast<size_t>(M) * D * esz());
-    qkv = S(static_cast<size_t>(M) * 3 * D * esz());
-    attn = S(static_cast<size_t>(M) * D * esz());
-    hid = S(static_cast<size_t>(M) * F * esz());
-    tok_in = S(static_cast<size_t>(n_img) * cin * esz());
-    ctx_n = S(static_cast<size_t>(ctx) * cw * esz());
+    xn = S(static_cast<size_t>(M) * D * esz() * pw);
+    qkv = S(static_cast<size_t>(M) * 3 * D * qe);
+    attn = S(static_cast<size_t>(M) * D * esz() * pw);
+    hid = S(static_cast<size_t>(M) * F * esz() * pw);
+    tok_in = S(static_cast<size_t>(n_img) * cin * esz() * pw);
+    ctx_n = S(static_cast<size_t>(ctx) * cw * esz() * pw);
     tsin = static_cast<float*>(pinned(static_cast<size_t>(tw) * 4));
     if (alloc_failed) return fail(ND_ERR_OOM, "mmdit: device allocation failed");
     ND_CUDA(cudaEventCreateWithFlags(&staged, cudaEventDisableTiming));
@@ -316,18 +329,18 @@ struct MMDiT final : nd_denoiser {
           const float* b, int64_t n, int epi, void* y, int64_t ldy, float* resid, int64_t ldr,
           const float* gate, int64_t gate_stride, int64_t split) {
     nd_linear_args a{};
-    a.dtype = dt;
+    a.dtype = lt;
     a.epilogue = epi;
     a.rows = rows;
     a.in_features = k;
     a.out_features = n;
     a.x = xin;
-    a.ldx = ldx;
+    a.ldx = ldx * pw;  // pairs: hi then lo columns
     weight_args(a, w, wrow);
     a.bias = b;
     a.group_split = split;
     a.y = y;
-    a.ldy = ldy;
+    a.ldy = ldy * pw;
     a.residual = resid;
     a.ldr = ldr;
     a.gate = gate;
@@ -341,8 +354,8 @@ struct MMDiT final : nd_denoiser {
     m.x = x;
     m.ldx = D;
     m.y = xn;
-    m.ldy = D;
-    m.out_dtype = dt;
+    m.ldy = static_cast<int64_t>(D) * pw;
+    m.out_dtype = lt;
     m.rows = rows;
     m.width = D;
     m.shift = shift;
@@ -357,7 +370,7 @@ struct MMDiT final : nd_denoiser {
          bool pre_silu, int act, float* y) {
     nd_gemv_args g{};
     g.w = w.w;
-    g.w_dtype = w.q8 ? ND_I8 : dt;
+    g.w_dtype = w.q8 ? ND_I8 : lt;
     g.n = n;
     g.k = k;
     g.x = xin;
@@ -398,13 +411,13 @@ struct MMDiT final : nd_denoiser {
     ND_OP("modulate", 0.0, mod_bytes, mod(s, mv, mv + D, M, n_img));
     {
       nd_linear_args a{};
-      a.dtype = dt;
+      a.dtype = lt;
       a.epilogue = ND_EPI_QK_NORM_ROPE;
       a.rows = M;
       a.in_features = D;
       a.out_features = 3 * D;
       a.x = xn;
-      a.ldx = D;
+      a.ldx = static_cast<int64_t>(D) * pw;
       weight_args(a, qkv_w, g0 * 3 * D);
       a.bias = qkv_b + g0 * 3 * D;
       a.group_split = n_img;
@@ -420,6 +433,7 @@ struct MMDiT final : nd_denoiser {
     {
       nd_attention_args a{};
       a.dtype = dt;
+      a.out_dtype = f32 ? ND_BF16X2 : 0;
       a.heads = H;
       a.head_dim = 128;
       a.batch = 1;
@@ -428,12 +442,12 @@ struct MMDiT final : nd_denoiser {
       a.key_limit = key_limit;
       a.q = qkv;
       a.ldq = 3 * D;
-      a.k = static_cast<uint8_t*>(qkv) + static_cast<size_t>(D) * esz();
+      a.k = static_cast<uint8_t*>(qkv) + static_cast<size_t>(D) * qe;
       a.ldk = 3 * D;
-      a.v = static_cast<uint8_t*>(qkv) + static_cast<size_t>(2 * D) * esz();
+      a.v = static_cast<uint8_t*>(qkv) + static_cast<size_t>(2 * D) * qe;
       a.ldv = 3 * D;
       a.out = attn;
-      a.ldo = D;
+      a.ldo = static_cast<int64_t>(D) * pw;
       ND_OP("attention", 4.0 * M * keys * D, mD * 2 * 4, attention(a, s));
     }
     ND_OP("gemm.out", gemm_flops(M, D, D), gemm_bytes(M, 2.0 * D, D, mD * 8),
@@ -452,7 +466,7 @@ struct MMDiT final : nd_denoiser {
   int forward(cudaStream_t s) override {
     const double ni = n_img, dD = D;
     // embeddings: image patches and text rows into one fp32 sequence
-    ND_OP("embed", 0.0, ni * cin * 6.0, patchify(in_latent, tok_in, dt, 1, C, Hl, Wl, P, cin, s));
+    ND_OP("embed", 0.0, ni * cin * 6.0, patchify(in_latent, tok_in, lt, 1, C, Hl, Wl, P, cin * pw, s));
     ND_OP("embed", gemm_flops(ni, dD, cin), gemm_bytes(ni, dD, cin, ni * dD * 4),
           lin(s, tok_in, n_img, cin, cin, img_in_w, 0, img_in_b, D, ND_EPI_STORE_F32, nullptr, 0, x, D,
               nullptr, 0, n_img));
@@ -462,8 +476,8 @@ struct MMDiT final : nd_denoiser {
       r.ldx = cw;
       r.in_dtype = ND_F32;
       r.y = ctx_n;
-      r.ldy = cw;
-      r.out_dtype = dt;
+      r.ldy = static_cast<int64_t>(cw) * pw;
+      r.out_dtype = lt;
       r.rows = ctx;
       r.width = cw;
       r.weight = txt_norm;
@@ -491,8 +505,8 @@ struct MMDiT final : nd_denoiser {
       m.x = x;
       m.ldx = D;
       m.y = xn;
-      m.ldy = D;
-      m.out_dtype = dt;
+      m.ldy = static_cast<int64_t>(D) * pw;
+      m.out_dtype = lt;
       m.rows = n_img;
       m.width = D;
       m.scale = fmod;

@@ -151,3 +151,25 @@ def test_anima_fp32_cfg1_block_within_1e4(device):
         y = d.predict(lat, 0.0, 0.5, {"context": ctx})
     ref = O.anima_forward(w, cfg, lat, ctx, 0.5)
     assert rel(y, ref) < 1e-4, rel(y, ref)
+
+
+@pytest.mark.parametrize("key_len", [0, 5500])
+def test_mmdit_fp32_step_within_1e4(device, key_len):
+    """The dual-stream MMDiT step in fp32 compute (joint attention with 2-D
+    RoPE, GELU-tanh MLP), with and without the key-count mask."""
+    from naivediffusion_b200.denoiser import MMDiTConfig
+    cfg = MMDiTConfig(width=256, heads=2, blocks=2, mlp_width=512, context_rows=64, context_width=64,
+                      latent_height=16, latent_width=32, compute=F32)
+    w = dict(synthetic_weights(cfg, seed=4))
+    rng = np.random.default_rng(4)
+    lat = rng.standard_normal((1, cfg.latent_channels, cfg.latent_height, cfg.latent_width)).astype(np.float32)
+    ctx = rng.standard_normal((1, cfg.context_rows, cfg.context_width)).astype(np.float32)
+    M = (cfg.latent_height // 2) * (cfg.latent_width // 2) + cfg.context_rows
+    kl = min(key_len, M - 7) if key_len else 0
+    cond = {"context": ctx}
+    if kl:
+        cond["key_length"] = np.array([kl], np.int32)
+    with build_denoiser(device, cfg, w) as d:
+        y = d.predict(lat, 500.0, 0.5, cond)
+    ref = O.mmdit_forward(w, cfg, lat, ctx[0], 0.5, key_len=kl)
+    assert rel(y, ref) < 1e-4, rel(y, ref)
