@@ -4,6 +4,7 @@
 MLP 12288, 5376 image + 256 text tokens), per B200, images sharded one per GPU.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config cfg3|cfg1|cfg2|cfg4|cfg5]
 
 Under torchrun (N > 1) each rank drives its own GPU with its own image; the
 only collective is the final NCCL gather of the predicted latents to rank 0.
@@ -13,11 +14,17 @@ Rank 0 prints ONE JSON line.
           already in HBM (device-resident predict replaying the captured step)
   e2e     the same metric through the host C-ABI predict (latent + context
           copied in from pinned host memory, the prediction copied back)
-  roofline  the dominant kernel class (the tcgen05 GEMMs, 77% of the FLOPs)
-          from per-launch CUDA events of a profiled step
+  roofline  the dominant kernel class (the tcgen05 GEMMs -- and for the UNet
+          the implicit-GEMM convolutions) from per-launch CUDA events of a
+          profiled step
   cpu_baseline  the CPU oracle (C++ restatement of the reference's CPU
           layer arithmetic) on a bounded sample: one block at full size,
           extrapolated to a step
+
+--config picks another BASELINE configuration for the same line (default
+cfg3, the headline): cfg1 one Anima block in fp32, cfg2 the 28-block Anima
+step (two CFG branches), cfg4 cfg3 with int8 per-channel weights, cfg5 the
+SDXL UNet (fp16, two CFG branches).
 
 --impl reference times that CPU restatement alone (the reference is C# over
 DirectML and cannot run here or on the GPU box); rank 0 only.
@@ -40,7 +47,6 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "Qwen-Image-style DiT s/step @1024×1344 bf16; images/s at 1/2/4/8 B200"
 UNIT = "images/s (one denoiser step per image)"
-WORKLOAD = "cfg3: Qwen-Image-style MMDiT 60x3072, 24x128 heads, MLP 12288 GELU-tanh, 5376 img + 256 txt tokens, batch 1, guidance 1"
 
 
 def env_rank():
@@ -104,6 +110,44 @@ class Clocks:
                 "samples": len(sm)}
 
 
+def _configs():
+    """BASELINE configurations: (model config, workload text, dtype, metric)."""
+    from naivediffusion_b200 import _lib
+    from naivediffusion_b200.denoiser import AnimaConfig, MMDiTConfig, UNetConfig
+    return {
+        "cfg3": (MMDiTConfig(), "cfg3: Qwen-Image-style MMDiT 60x3072, 24x128 heads, MLP 12288 GELU-tanh, "
+                 "5376 img + 256 txt tokens, batch 1, guidance 1", "bf16", METRIC),
+        "cfg4": (MMDiTConfig(weight_dtype=_lib.ND_I8, quant_group=0, quant_scale_dtype=_lib.ND_F32),
+                 "cfg4: cfg3 with int8 weight-only storage, per-output-channel fp32 scales (absmax/127), "
+                 "dequant fused into the GEMM mainloop, batch 1", "bf16 (int8 weights)",
+                 "Qwen-Image-style DiT int8 weight-only s/step @1024×1344; images/s"),
+        "cfg2": (AnimaConfig(), "cfg2: Anima 28x2048, 16x128 heads, MLP 8192 GELU, 4096 tokens per image, "
+                 "cross-attention to 256x1024, batch 2 (CFG branches of one image)", "bf16",
+                 "Anima DiT s/step @1024×1024 bf16 (2 CFG branches); images/s"),
+        "cfg1": (AnimaConfig(blocks=1, latent_height=64, latent_width=64, batch=1, compute=_lib.ND_F32),
+                 "cfg1: one Anima block 2048 wide, 16x128 heads, 1024 tokens, cross-attention to 256x1024, "
+                 "MLP 8192, fp32 compute (bf16 hi|lo operand pairs on the tensor cores, fp32 attention), "
+                 "with the embedder and final layer", "f32",
+                 "Anima DiT block fp32 s/step (1024 tokens); blocks/s"),
+        "cfg5": (UNetConfig(), "cfg5: SDXL UNet 320/640/1280, transformer depths 0/2/10, 4x128x128 latent, "
+                 "context 77x2048, add 2816, batch 2 (CFG branches of one image)", "f16",
+                 "SDXL UNet s/step @1024×1024 fp16 (2 CFG branches); images/s"),
+    }
+
+
+def _inputs(cfg, rank):
+    """Seeded device inputs of one step: latent, conditioning dict, timestep."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    b = getattr(cfg, "batch", 1)
+    latent = torch.randn(b, cfg.latent_channels, cfg.latent_height, cfg.latent_width, device="cuda", generator=g)
+    context = torch.randn(b, cfg.context_rows, cfg.context_width, device="cuda", generator=g)
+    cond = {"context": context}
+    if hasattr(cfg, "add_width"):
+        cond["add"] = torch.randn(b, cfg.add_width, device="cuda", generator=g)
+    return latent, cond, 500.0
+
+
 def cpu_block_sample(cfg, repeats: int = 1, budget_s: float = 150.0):
     """Time one full-size dual-stream block on the CPU oracle (the reference's
     CPU layer arithmetic, all host threads) and extrapolate to a whole step:
@@ -139,21 +183,59 @@ def cpu_block_sample(cfg, repeats: int = 1, budget_s: float = 150.0):
     return per_step, sample, O.threads()
 
 
+def cpu_anima_sample(cfg, repeats: int = 1, budget_s: float = 150.0):
+    """One full-size Anima block (batch 1, with the embedder and final layer)
+    through the CPU oracle's AnimaDit step, extrapolated by FLOPs to the
+    configuration's whole step (x blocks x batch)."""
+    import numpy as np
+    import oracle as O
+    from dataclasses import replace
+    from naivediffusion_b200.denoiser import synthetic_weights
+    one = replace(cfg, blocks=1, batch=1)
+    w = dict(synthetic_weights(one, seed=0))
+    rng = np.random.default_rng(0)
+    lat = rng.standard_normal((1, 16, one.latent_height, one.latent_width)).astype(np.float32)
+    ctx = rng.standard_normal((1, one.context_rows, one.context_width)).astype(np.float32)
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(max(1, repeats)):
+        t0 = time.perf_counter()
+        O.anima_forward(w, one, lat, ctx, 0.5)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    scale = cfg.flops_per_step() / one.flops_per_step()
+    sample = (f"one full-size Anima block ({one.tokens} tokens, width {one.width}, batch 1) through the CPU "
+              f"oracle's step, median of {len(times)}" + (f", extrapolated x{scale:.0f} by FLOPs" if scale > 1 else ""))
+    return statistics.median(times) * scale, sample, O.threads()
+
+
+def cpu_sample(name, cfg, repeats=1, budget_s=150.0):
+    if name in ("cfg3", "cfg4"):
+        return cpu_block_sample(cfg, repeats, budget_s)
+    if name in ("cfg1", "cfg2"):
+        return cpu_anima_sample(cfg, repeats, budget_s)
+    return None  # cfg5: no bounded full-size sample of the UNet on the oracle
+
+
 def run_reference(args):
     rank, world, _ = env_rank()
     if rank != 0:
         return 0
-    from naivediffusion_b200.denoiser import MMDiTConfig
-    cfg = MMDiTConfig()
-    cpu_block_sample(cfg, repeats=1, budget_s=1e9) if args.warmup > 0 else None  # warm-up (one block)
-    per_step, sample, threads = cpu_block_sample(cfg, repeats=args.steps, budget_s=150.0)
+    cfg, workload, _dt, metric = _configs()[args.config]
+    if args.config == "cfg5":
+        print(json.dumps({"impl": "reference", "unavailable": "cfg5 has no bounded CPU sample of the UNet step"}))
+        return 0
+    if args.warmup > 0:
+        cpu_sample(args.config, cfg, 1, 1e9)  # warm-up: one sample
+    per_step, sample, threads = cpu_sample(args.config, cfg, args.steps, 150.0)
     value = 1.0 / per_step
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "impl": "reference", "metric": metric, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-        "config": {"workload": WORKLOAD, "sample": "one block, extrapolated"},
+        "config": {"workload": workload, "sample": "one block, extrapolated"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference is C# over DirectML/D3D12 (Windows); its CPU layer arithmetic is timed "
@@ -169,13 +251,13 @@ def run_ours(args):
     import torch.distributed as dist
     from datetime import timedelta
 
-    from naivediffusion_b200.denoiser import CudaDenoiser, Device, MMDiTConfig, synthetic_weights_device
+    from naivediffusion_b200.denoiser import CudaDenoiser, Device, synthetic_weights_device
 
     rank, world, local = env_rank()
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
-    cfg = MMDiTConfig()
+    cfg, workload, dtype, metric = _configs()[args.config]
     dev = Device(local)
     den = CudaDenoiser(dev, cfg.desc())
     for name, t in synthetic_weights_device(cfg, seed=0):
@@ -183,12 +265,13 @@ def run_ours(args):
     den.finalize()
     torch.cuda.synchronize()
 
-    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
-    latent = torch.randn(1, cfg.latent_channels, cfg.latent_height, cfg.latent_width, device="cuda", generator=g)
-    context = torch.randn(1, cfg.context_rows, cfg.context_width, device="cuda", generator=g)
+    # One explicit stream for the inputs, the library's launches and the
+    # timing events (a null stream handle would mean the library's own
+    # stream, which the events below would not be ordered with).
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    latent, cond, timestep = _inputs(cfg, rank)
     out = torch.empty_like(latent)
-    stream = torch.cuda.current_stream()
-    cond = {"context": context}
     sigma = 0.75
 
     def barrier():
@@ -198,14 +281,14 @@ def run_ours(args):
 
     # ---- device-resident step (the kernels' number)
     for _ in range(max(3, args.warmup)):
-        den.predict_device(latent, 0.0, sigma, cond, out, stream=stream.cuda_stream)
+        den.predict_device(latent, timestep, sigma, cond, out, stream=stream.cuda_stream)
     barrier()
     clocks = Clocks(local)
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        den.predict_device(latent, 0.0, sigma, cond, out, stream=stream.cuda_stream)
+        den.predict_device(latent, timestep, sigma, cond, out, stream=stream.cuda_stream)
     if world > 1:  # the run's one collective: gather every rank's prediction on rank 0
         gathered = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(gathered, out)
@@ -222,18 +305,21 @@ def run_ours(args):
 
     # ---- end to end through the host C ABI (pinned host buffers)
     lat_h = torch.empty(latent.shape, dtype=torch.float32, pin_memory=True)
-    ctx_h = torch.empty(context.shape, dtype=torch.float32, pin_memory=True)
     lat_h.copy_(latent.cpu())
-    ctx_h.copy_(context.cpu())
+    cond_h = {}
+    for k, v in cond.items():
+        h = torch.empty(v.shape, dtype=torch.float32, pin_memory=True)
+        h.copy_(v.cpu())
+        cond_h[k] = h.numpy()
     out_h = torch.empty(latent.shape, dtype=torch.float32, pin_memory=True)
-    lat_np, ctx_np, y = lat_h.numpy(), ctx_h.numpy(), out_h.numpy()
-    den.predict(lat_np, 0.0, sigma, {"context": ctx_np}, out=y)
+    lat_np, y = lat_h.numpy(), out_h.numpy()
+    den.predict(lat_np, timestep, sigma, cond_h, out=y)
     barrier()
     step_s = []
     t0 = time.perf_counter()
     for _ in range(args.steps):
         t1 = time.perf_counter()
-        den.predict(lat_np, 0.0, sigma, {"context": ctx_np}, out=y)
+        den.predict(lat_np, timestep, sigma, cond_h, out=y)
         step_s.append(time.perf_counter() - t1)
     e2e_s = torch.tensor([time.perf_counter() - t0], device="cuda", dtype=torch.float64)
     if world > 1:
@@ -241,48 +327,64 @@ def run_ours(args):
     e2e_value = world * args.steps / e2e_s.item()
     same = bool(np.allclose(y, out.cpu().numpy(), rtol=0, atol=0))
 
-    # ---- per-kernel-class profile (eager step, CUDA events per launch)
+    # ---- per-kernel-class profile (a captured step with an event pair around every launch)
     prof = den.profile(steps=3)
     launches = sum(p["launches"] for p in prof)
     peaks = measured_peaks()
-    gemm = [p for p in prof if p["name"].startswith("gemm")]
-    g_ms = sum(p["ms"] for p in gemm)
-    g_fl = sum(p["flops"] for p in gemm)
-    g_n = sum(p["launches"] for p in gemm)
+    tensor_classes = [p for p in prof if p["name"].startswith("gemm") or p["name"] == "conv3x3"]
+    g_ms = sum(p["ms"] for p in tensor_classes)
+    g_fl = sum(p["flops"] for p in tensor_classes)
+    g_n = sum(p["launches"] for p in tensor_classes)
     achieved = g_fl / (g_ms / 1e3) / 1e12
+    step_flops = cfg.flops_per_step() if hasattr(cfg, "flops_per_step") else sum(p["flops"] for p in prof)
+    long_step = ms_per_step > 50.0
+    peak = peaks["bf16_sustained"] if long_step else peaks["bf16"]
     traffic = None
     tpath = ROOT / "profiles" / "gemm_traffic.json"
-    if tpath.exists():
+    if args.config == "cfg3" and tpath.exists():
         traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
+    kernel = "gemm_sm100_kernel (tcgen05, all GEMM launches of a step)"
+    if args.config == "cfg5":
+        kernel = "gemm_sm100_kernel (tcgen05: conv3x3 implicit GEMMs and the linear layers)"
+    elif args.config == "cfg4":
+        kernel = "gemm_w8_sm100_kernel (tcgen05, int8 weights widened in the mainloop)"
+    elif args.config == "cfg1":
+        kernel = ("gemm_sm100_kernel on bf16 hi|lo pairs (3 MMA passes per logical product; "
+                  "achieved counts the logical fp32 FLOPs)")
 
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,0.02) bf16 weights generated on device, N(0,1) latent and text states)",
-        "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": cfg.tokens,
+        "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+        "data": "synthetic (seeded N(0,0.02) weights generated on device, N(0,1) latent and conditioning)",
+        "config": {"workload": workload, "global_batch": world * getattr(cfg, "batch", 1),
                    "parallelism": f"replicas x{world} (one image per GPU)",
-                   "l2": "no flush: each step streams 40.8 GB of weights, far above the 126 MB L2"},
+                   "l2": "no flush: each step streams its weights and activations, far above the 126 MB L2"},
         "e2e": {"value": e2e_value, "unit": UNIT,
                 "ms_per_step_median": statistics.median(step_s) * 1e3,
-                "h2d_bytes_per_step": int(lat_np.nbytes + ctx_np.nbytes + 4 * cfg.time_width),
+                "h2d_bytes_per_step": int(lat_np.nbytes + sum(v.nbytes for v in cond_h.values())),
                 "d2h_bytes_per_step": int(y.nbytes)},
         "gpu_launches": launches * args.steps,
-        "roofline": {"bound": "tensor", "kernel": "gemm_sm100_kernel (tcgen05, all GEMM launches of a step)",
-                     "achieved": achieved, "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
-                     "frac": achieved / peaks["bf16_sustained"], "traffic": traffic,
-                     "peak_source": f"{peaks['source']} bf16 sustained (kernel timed inside a long step)",
+        "roofline": {"bound": "tensor", "kernel": kernel,
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": f"{peaks['source']} bf16 " + ("sustained (kernel timed inside a long step)"
+                                                                   if long_step else "burst (short step)"),
                      "launches_per_step": g_n},
-        "step_tflops": cfg.flops_per_step() / (ms_per_step / 1e3) / 1e12,
-        "step_frac_of_peak": cfg.flops_per_step() / (ms_per_step / 1e3) / 1e12 / peaks["bf16"],
+        "step_tflops": step_flops / (ms_per_step / 1e3) / 1e12,
+        "step_frac_of_peak": step_flops / (ms_per_step / 1e3) / 1e12 / peaks["bf16"],
         "kernels": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in p.items()} for p in prof],
         "clocks": clk,
         "output_finite": finite, "e2e_matches_device_path": same,
     }
+    if args.config in ("cfg3", "cfg4"):
+        line["config"]["seq_len"] = cfg.tokens
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        per_step, sample, threads = cpu_block_sample(cfg, repeats=1)
-        line["cpu_baseline"] = {"value": 1.0 / per_step, "unit": UNIT, "cores": threads, "kind": "port",
-                                "sample": sample}
+        got = cpu_sample(args.config, cfg, 1)
+        if got is not None:
+            per_step, sample, threads = got
+            line["cpu_baseline"] = {"value": 1.0 / per_step, "unit": UNIT, "cores": threads, "kind": "port",
+                                    "sample": sample}
     if rank == 0:
         print(json.dumps(line), flush=True)
     den.close()
@@ -299,6 +401,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["cfg3", "cfg1", "cfg2", "cfg4", "cfg5"], default="cfg3",
+                    help="BASELINE configuration (default cfg3, the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle sample")
     args = ap.parse_args()
     if args.impl == "reference":

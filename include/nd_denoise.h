@@ -176,11 +176,11 @@ ND_API int nd_denoiser_predict_device(nd_denoiser* d, const float* latent, doubl
                                       double sigma, int n_cond, const nd_named_tensor* cond,
                                       float* out, void* stream);
 
-/* Per-kernel-class timing: capture the step once more with a CUDA event pair
- * around every launch (event-record nodes in the graph), replay it `steps`
- * times on the last staged inputs, and return per class (e.g. "gemm.qkv",
- * "attention") the launches, device milliseconds, algorithmic FLOPs and bytes
- * of ONE step (times averaged over the replays). The
+/* Per-kernel-class timing: run the step `steps` times eagerly on the last
+ * staged inputs with a CUDA event pair around every launch, and return per
+ * class (e.g. "gemm.qkv", "attention") the launches, device milliseconds,
+ * algorithmic FLOPs and bytes of ONE step (times averaged over the runs).
+ * Launches shorter than the host's enqueue time read long. The
  * reference's counterpart is MemoryLog's per-stage report
  * (src/NaiveDiffusion/Dml/MemoryLog.cs:110-224) and DenoiseCommand's
  * Stopwatch (NaiveDiffusion.Cli/DenoiseCommand.cs:139-144). */

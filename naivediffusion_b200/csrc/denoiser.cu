@@ -517,56 +517,57 @@ int nd_denoiser_profile(nd_denoiser* d, int steps, nd_kernel_time* out, int max_
   if (!d->finalized) return nd::fail(ND_ERR_STATE, "profile: call nd_denoiser_finalize first");
   nd::DeviceGuard g(d->dev->ordinal);
   cudaStream_t st = d->dev->stream;
-  // Capture the step once more with an event pair recorded around every
-  // launch (event-record nodes inside the graph), replay it, and read the
-  // events: per-kernel device times of the same graph execution predict runs.
-  d->prof.clear();
-  d->prof_used = 0;
-  // Events are created before the capture begins (two per launch).
-  while (d->prof_pool.size() < 4096) {
+  // Run the step eagerly with an event pair recorded around every launch and
+  // read the events. The host enqueues a step in a few milliseconds while the
+  // GPU needs far longer, so after the first launches the queue runs ahead
+  // and each pair brackets its kernel alone. (Event-record nodes inside a
+  // captured graph were measured to add tens of microseconds per launch.)
+  // Events are created once, two per launch.
+  while (d->prof_pool.size() < 8192) {
     cudaEvent_t ev;
     ND_CUDA(cudaEventCreate(&ev));
     d->prof_pool.push_back(ev);
   }
-  d->profiling = true;
-  ND_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-  int rc = d->forward(st);
-  cudaGraph_t graph = nullptr;
-  cudaError_t e = cudaStreamEndCapture(st, &graph);
-  d->profiling = false;
-  if (rc) {
-    if (graph) cudaGraphDestroy(graph);
-    return rc;
-  }
-  if (e != cudaSuccess) return nd::cuda_fail(e, "profile: graph capture");
-  cudaGraphExec_t exec = nullptr;
-  e = cudaGraphInstantiate(&exec, graph, 0);
-  if (e != cudaSuccess) {
-    cudaGraphDestroy(graph);
-    return nd::cuda_fail(e, "profile: graph instantiate");
-  }
-  std::vector<double> ms(d->prof.size(), 0.0);
+  std::vector<double> ms;
+  std::vector<nd_denoiser::ProfRecord> first;
+  int rc = ND_OK;
   for (int i = 0; i < steps && rc == ND_OK; ++i) {
-    e = cudaGraphLaunch(exec, st);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    d->prof.clear();
+    d->prof_used = 0;
+    d->profiling = true;
+    rc = d->forward(st);
+    d->profiling = false;
+    if (rc) break;
+    cudaError_t e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) {
-      rc = nd::cuda_fail(e, "profile: replay");
+      rc = nd::cuda_fail(e, "profile: step");
       break;
     }
-    for (size_t k = 0; k < d->prof.size(); ++k) {
+    if (i == 0) {
+      first = d->prof;
+      ms.assign(first.size(), 0.0);
+    } else if (d->prof.size() != first.size()) {
+      rc = nd::fail(ND_ERR_STATE, "profile: the step's launch list changed between runs");
+      break;
+    }
+    for (size_t k = 0; k < d->prof.size() && rc == ND_OK; ++k) {
       float t = 0.f;
-      cudaEventElapsedTime(&t, d->prof[k].start, d->prof[k].stop);
+      e = cudaEventElapsedTime(&t, d->prof[k].start, d->prof[k].stop);
+      if (e != cudaSuccess) {
+        cudaGetLastError();  // not sticky: keep it from surfacing in a later call
+        rc = nd::cuda_fail(e, (std::string("profile: event time of ") + d->prof[k].cls + " launch " +
+                               std::to_string(k)).c_str());
+        break;
+      }
       ms[k] += t;
     }
   }
-  cudaGraphExecDestroy(exec);
-  cudaGraphDestroy(graph);
   if (rc) return rc;
   rc = nd::check_device_status(st);
   if (rc) return rc;
   int n = 0;
-  for (size_t k = 0; k < d->prof.size(); ++k) {
-    const auto& r = d->prof[k];
+  for (size_t k = 0; k < first.size(); ++k) {
+    const auto& r = first[k];
     int j = 0;
     while (j < n && std::strcmp(out[j].name, r.cls) != 0) ++j;
     if (j == n) {

@@ -140,3 +140,21 @@ def test_anima_step_matches_oracle(device, batch):
     ref = O.anima_forward(w, cfg, lat, ctx, 0.6)
     assert y.shape == lat.shape
     assert rel(y, ref) < 2e-2 and cos(y, ref) > 0.999, (rel(y, ref), cos(y, ref))
+
+
+def test_profile_times_every_kernel_class(device):
+    """nd_denoiser_profile replays a captured step with an event pair around
+    every launch: every class gets a positive device time, and the launch
+    count matches between two calls."""
+    cfg = MMDiTConfig(**SMALL)
+    w = dict(synthetic_weights(cfg, seed=2))
+    lat, ctx = _inputs(cfg, seed=2)
+    with build_denoiser(device, cfg, w) as d:
+        d.predict(lat, 500.0, 0.5, {"context": ctx})
+        p1 = d.profile(steps=2)
+        p2 = d.profile(steps=1)
+        y = d.predict(lat, 500.0, 0.5, {"context": ctx})  # the plug-in still works afterwards
+    assert {p["name"] for p in p1} >= {"gemm.qkv", "attention", "gemm.out", "modulate", "gemm.up", "gemm.down"}
+    assert all(p["ms"] > 0 for p in p1), p1
+    assert [p["launches"] for p in p1] == [p["launches"] for p in p2]
+    assert np.isfinite(y).all()
