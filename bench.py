@@ -252,6 +252,7 @@ def run_ours(args):
     from datetime import timedelta
 
     from naivediffusion_b200.denoiser import CudaDenoiser, Device, synthetic_weights_device
+    from naivediffusion_b200.multigpu import gather_latents, max_over_ranks
 
     rank, world, local = env_rank()
     torch.cuda.set_device(local)
@@ -289,19 +290,14 @@ def run_ours(args):
     e0.record(stream)
     for _ in range(args.steps):
         den.predict_device(latent, timestep, sigma, cond, out, stream=stream.cuda_stream)
-    if world > 1:  # the run's one collective: gather every rank's prediction on rank 0
-        gathered = [torch.empty_like(out) for _ in range(world)]
-        dist.all_gather(gathered, out)
+    gathered = gather_latents(out, world)  # the run's one collective (world > 1)
     e1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    ms = torch.tensor([e0.elapsed_time(e1)], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    total_ms = ms.item()
+    total_ms = max_over_ranks(e0.elapsed_time(e1), device="cuda")
     ms_per_step = total_ms / args.steps
     value = world * args.steps / (total_ms / 1e3)
-    finite = bool(torch.isfinite(out).all().item())
+    finite = bool(all(torch.isfinite(g).all().item() for g in gathered))
 
     # ---- end to end through the host C ABI (pinned host buffers)
     lat_h = torch.empty(latent.shape, dtype=torch.float32, pin_memory=True)
@@ -321,10 +317,8 @@ def run_ours(args):
         t1 = time.perf_counter()
         den.predict(lat_np, timestep, sigma, cond_h, out=y)
         step_s.append(time.perf_counter() - t1)
-    e2e_s = torch.tensor([time.perf_counter() - t0], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
-    e2e_value = world * args.steps / e2e_s.item()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, device="cuda")
+    e2e_value = world * args.steps / e2e_s
     same = bool(np.allclose(y, out.cpu().numpy(), rtol=0, atol=0))
 
     # ---- per-kernel-class profile (a captured step with an event pair around every launch)

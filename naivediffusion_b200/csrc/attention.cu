@@ -56,19 +56,25 @@ int attention(const nd_attention_args& a, cudaStream_t stream) {
   if (hd == 128) {
     static bool configured[64] = {};
     if (!configured[dev & 63]) {
+      int rc = check_register_split(reinterpret_cast<const void*>(attention_sm100_kernel<128>), kAttnThreads,
+                                    kAttnRegsNeeded, "attention");
+      if (rc) return rc;
       ND_CUDA(cudaFuncSetAttribute(attention_sm100_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    AttnSmem<128>::kLaunchBytes));
       configured[dev & 63] = true;
     }
-    attention_sm100_kernel<128><<<grid, 320, AttnSmem<128>::kLaunchBytes, stream>>>(tq, tk, tv, g);
+    attention_sm100_kernel<128><<<grid, kAttnThreads, AttnSmem<128>::kLaunchBytes, stream>>>(tq, tk, tv, g);
   } else {
     static bool configured[64] = {};
     if (!configured[dev & 63]) {
+      int rc = check_register_split(reinterpret_cast<const void*>(attention_sm100_kernel<64>), kAttnThreads,
+                                    kAttnRegsNeeded, "attention");
+      if (rc) return rc;
       ND_CUDA(cudaFuncSetAttribute(attention_sm100_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    AttnSmem<64>::kLaunchBytes));
       configured[dev & 63] = true;
     }
-    attention_sm100_kernel<64><<<grid, 320, AttnSmem<64>::kLaunchBytes, stream>>>(tq, tk, tv, g);
+    attention_sm100_kernel<64><<<grid, kAttnThreads, AttnSmem<64>::kLaunchBytes, stream>>>(tq, tk, tv, g);
   }
   ND_CUDA(cudaGetLastError());
   return ND_OK;

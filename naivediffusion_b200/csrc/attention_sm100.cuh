@@ -8,11 +8,13 @@
 // (row i sees keys 0..i, the text-row table of QwenImageConditioning).
 //
 // One CTA = one head x two 128-row query tiles (A and B) ping-ponging on the
-// tensor core; 10 warps:
+// tensor core; 12 warps in three warpgroups:
 //   warp 0      TMA: Q_A, Q_B once; K_j, V_j per key tile (2 stages)
 //   warp 1      MMA: S_t = Q_t K_j^T (SS, into TMEM); O_t += P_t V_j (TS: P
 //               read from TMEM, V from shared memory as an MN-major operand)
-//   warps 2-5   softmax of tile A (thread = query row), warps 6-9 tile B:
+//   warps 2-3   idle; the first warpgroup gives up registers (setmaxnreg) so
+//               the softmax warpgroups hold a whole 128-value score row each
+//   warps 4-7   softmax of tile A (thread = query row), warps 8-11 tile B:
 //               row max / exp2 / row sum in registers, P written back over
 //               S in TMEM as bf16, lazy O rescale (only when the running max
 //               grows by more than 2^8), final 1/l scaling and store.
@@ -68,8 +70,16 @@ __device__ __forceinline__ void attn_store_row(void* out, long long ldo, long lo
   for (int i = 0; i < 4; ++i) dst[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
 }
 
+// Register split: 384 threads x 168 at launch = 64512 = 128 x 72 (first
+// warpgroup) + 256 x 216 (the two softmax warpgroups). The host checks the
+// launch count before every launch.
+constexpr int kAttnThreads = 384;
+constexpr int kAttnRegsLow = 72;
+constexpr int kAttnRegsHigh = 216;
+constexpr int kAttnRegsNeeded = 128 * kAttnRegsLow + 256 * kAttnRegsHigh;
+
 template <int HD>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(kAttnThreads, 1)
     attention_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                            const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
@@ -131,6 +141,10 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Each role's code sits inside its warpgroup's setmaxnreg branch, so the
+  // compiler budgets each region with that branch's register count.
+  if (warp < 4) {
+    reg_dealloc<kAttnRegsLow>();
   if (warp == 0) {
     // ------------------------------------------------------------ loads
     if (elect_one()) {
@@ -240,9 +254,11 @@ __global__ void __launch_bounds__(320, 1)
       volatile int never = 0;
       mbar_wait(drain_bar, 0, &never, a.status, kStatusTimeoutDrain);
     }
+  }
   } else {
+    reg_alloc<kAttnRegsHigh>();
     // ------------------------------------------------------------ softmax
-    const int t = (warp - 2) >> 2;  // query tile of this warpgroup
+    const int t = (warp - 4) >> 2;  // query tile of this warpgroup
     const int ew = warp & 3;        // TMEM lane quarter
     const int r = ew * 32 + lane;   // row within the tile
     const int q_in_batch = q_tile0 + t * 128 + r;
@@ -273,18 +289,19 @@ __global__ void __launch_bounds__(320, 1)
           for (int i = 0; i < 32; ++i)
             if (c * 32 + i >= vis) sr[c][i] = __float_as_uint(-INFINITY);
       }
-      // Row max and (below) row sum over 8 independent partials: one serial
-      // chain over 128 values would cost ~4 cycles per element in latency.
+      // Row max and (below) row sum over 8 / 4 independent partials (one serial
+      // chain over 128 values would cost its full latency per element); the
+      // loop is issue-bound, so the max takes three inputs and the scale and
+      // sum run as paired f32x2 operations.
       float m8[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m8[k] = fmaxf(__uint_as_float(sr[0][k]), __uint_as_float(sr[0][k + 8]));
+      for (int k = 0; k < 8; ++k) m8[k] = fmaxf(__uint_as_float(sr[0][2 * k]), __uint_as_float(sr[0][2 * k + 1]));
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c > 0 || i >= 16) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(sr[c][i]));
-      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        for (int i = (c == 0 ? 16 : 0); i < 32; i += 2)
+          m8[(i >> 1) & 7] = fmax3(m8[(i >> 1) & 7], __uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]));
+      float mx = fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(fmax3(m8[3], m8[4], m8[5]), m8[6], m8[7]));
       mx *= a.scale_log2;
       const float m_new = fmaxf(m, mx);
       const bool need = m_new > m + 8.0f;
@@ -303,23 +320,25 @@ __global__ void __launch_bounds__(320, 1)
         tmem_st_wait();
       }
       m = m_use;
-      float s8[8];
+      float2 s4[4];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) s8[k] = 0.f;
+      for (int k = 0; k < 4; ++k) s4[k] = make_float2(0.f, 0.f);
+      const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
+      const float2 nm2 = make_float2(-m, -m);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * i]), a.scale_log2, -m));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * i + 1]), a.scale_log2, -m));
-          s8[(2 * i) & 7] += p0;
-          s8[(2 * i + 1) & 7] += p1;
-          pk[i] = a.out_f16 ? pack_f16(p0, p1) : pack_bf16(p0, p1);
+          const float2 x = ffma2(make_float2(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])),
+                                 sc2, nm2);
+          const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          s4[i & 3] = fadd2(s4[i & 3], p);
+          pk[i] = a.out_f16 ? pack_f16(p.x, p.y) : pack_bf16(p.x, p.y);
         }
         tmem_st16(s_tm + c * 16, pk);
       }
-      const float rowsum = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+      const float rowsum = ((s4[0].x + s4[0].y) + (s4[1].x + s4[1].y)) + ((s4[2].x + s4[2].y) + (s4[3].x + s4[3].y));
       l = l * factor + rowsum;
       tmem_st_wait();
       tc_fence_before();

@@ -49,6 +49,10 @@ int linear(const nd_linear_args& a, cudaStream_t stream);
 int conv2d(const nd_conv_args& c, cudaStream_t stream);
 int dequantize(const int8_t* q, const void* scales, int scale_dtype, int64_t quant_group, int64_t rows,
                int64_t cols, void* out, int out_dtype, cudaStream_t stream);
+// A kernel that moves registers between its warpgroups (setmaxnreg) may only
+// hand out what it was launched with: fail unless the compiled per-thread
+// count x threads covers `needed`.
+int check_register_split(const void* kernel, int threads, int needed, const char* what);
 int attention(const nd_attention_args& a, cudaStream_t stream);
 int attention_f32(const nd_attention_args& a, cudaStream_t stream);
 int modulate(const nd_modulate_args& a, cudaStream_t stream);

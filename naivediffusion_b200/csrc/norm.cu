@@ -199,35 +199,56 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint16_t* __restrict__ 
     const bool split = w_type == 2;
     const uint4* wr = reinterpret_cast<const uint4*>(W + n * K * (split ? 2 : 1));
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int c = lane; c < k8; c += 32) {
-      uint4 p, q = make_uint4(0u, 0u, 0u, 0u);
-      asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(p.x), "=r"(p.y), "=r"(p.z), "=r"(p.w)
-                   : "l"(wr + c));
-      if (split)
-        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w)
-                     : "l"(wr + k8 + c));
-      float wv[8];
-      const uint32_t u[4] = {p.x, p.y, p.z, p.w};
-      const uint32_t ul[4] = {q.x, q.y, q.z, q.w};
+    // Four 16-byte loads per lane in flight before any arithmetic: the
+    // weight stream is read once, so the loop is bound by bytes in flight.
+    for (int c0 = lane; c0 < k8; c0 += 128) {
+      uint4 p[4], q[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float2 f;
-        if (split) f = unpack_split(u[i], ul[i]);
-        else if (w_type == 1) f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
-        else f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[i]));
-        wv[2 * i] = f.x;
-        wv[2 * i + 1] = f.y;
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + 32 * u;
+        p[u] = q[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (c < k8) {
+          asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(p[u].x), "=r"(p[u].y), "=r"(p[u].z), "=r"(p[u].w)
+                       : "l"(wr + c));
+          if (split)
+            asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(q[u].x), "=r"(q[u].y), "=r"(q[u].z), "=r"(q[u].w)
+                         : "l"(wr + k8 + c));
+        }
       }
-#pragma unroll 4
-      for (int b = 0; b < 4; ++b) {
-        if (b < B) {
-          const float* xb = xs + (xrows > 0 ? (n / xrows) : b) * K + 8 * c;
-          float s = 0.f;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) s += wv[i] * xb[i];
-          acc[b] += s;
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + 32 * u;
+        if (c >= k8) break;
+        float wv[8];
+        const uint32_t uh[4] = {p[u].x, p[u].y, p[u].z, p[u].w};
+        const uint32_t ul[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float2 f;
+          if (split) f = unpack_split(uh[i], ul[i]);
+          else if (w_type == 1) f = __half22float2(*reinterpret_cast<const __half2*>(&uh[i]));
+          else f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uh[i]));
+          wv[2 * i] = f.x;
+          wv[2 * i + 1] = f.y;
+        }
+#pragma unroll 4
+        for (int b = 0; b < 4; ++b) {
+          if (b < B) {
+            const float* xb = xs + (xrows > 0 ? (n / xrows) : b) * K + 8 * c;
+            const float4 x0 = *reinterpret_cast<const float4*>(xb);
+            const float4 x1 = *reinterpret_cast<const float4*>(xb + 4);
+            float s0 = wv[0] * x0.x;
+            s0 = fmaf(wv[1], x0.y, s0);
+            s0 = fmaf(wv[2], x0.z, s0);
+            s0 = fmaf(wv[3], x0.w, s0);
+            float s1 = wv[4] * x1.x;
+            s1 = fmaf(wv[5], x1.y, s1);
+            s1 = fmaf(wv[6], x1.z, s1);
+            s1 = fmaf(wv[7], x1.w, s1);
+            acc[b] += s0 + s1;
+          }
         }
       }
     }

@@ -89,31 +89,47 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(const int8_t* __restrict__
        n += warps) {
     const uint4* wr = reinterpret_cast<const uint4*>(W + n * K);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int c = lane; c < k16; c += 32) {
-      uint4 p;
-      asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(p.x), "=r"(p.y), "=r"(p.z), "=r"(p.w)
-                   : "l"(wr + c));
-      const long long si = n * scale_cols + (c * 16) / group;
-      const float s = scale_f16 ? __half2float(static_cast<const __half*>(scales)[si])
-                                : static_cast<const float*>(scales)[si];
-      float wv[16];
-      const uint32_t u[4] = {p.x, p.y, p.z, p.w};
+    // Four 16-byte loads (and their scales) per lane in flight before any
+    // arithmetic: the weight stream is read once, bound by bytes in flight.
+    for (int c0 = lane; c0 < k16; c0 += 128) {
+      uint4 p[4];
+      float sc[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float f[4];
-        i8x4_to_f32(u[i], f);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) wv[4 * i + j] = f[j] * s;
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + 32 * u;
+        p[u] = make_uint4(0u, 0u, 0u, 0u);
+        sc[u] = 0.f;
+        if (c < k16) {
+          asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(p[u].x), "=r"(p[u].y), "=r"(p[u].z), "=r"(p[u].w)
+                       : "l"(wr + c));
+          const long long si = n * scale_cols + (c * 16) / group;
+          sc[u] = scale_f16 ? __half2float(static_cast<const __half*>(scales)[si])
+                            : static_cast<const float*>(scales)[si];
+        }
       }
-#pragma unroll 4
-      for (int b = 0; b < 4; ++b) {
-        if (b < B) {
-          const float* xb = xs + (xrows > 0 ? (n / xrows) : b) * K + 16 * c;
-          float sum = 0.f;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) sum += wv[i] * xb[i];
-          acc[b] += sum;
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + 32 * u;
+        if (c >= k16) break;
+        float wv[16];
+        const uint32_t w4[4] = {p[u].x, p[u].y, p[u].z, p[u].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float f[4];
+          i8x4_to_f32(w4[i], f);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) wv[4 * i + j] = f[j] * sc[u];
+        }
+#pragma unroll 4
+        for (int b = 0; b < 4; ++b) {
+          if (b < B) {
+            const float* xb = xs + (xrows > 0 ? (n / xrows) : b) * K + 16 * c;
+            float sum = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum += wv[i] * xb[i];
+            acc[b] += sum;
+          }
         }
       }
     }

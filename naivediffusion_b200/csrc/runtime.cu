@@ -46,6 +46,16 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(e == cudaErrorMemoryAllocation ? ND_ERR_OOM : ND_ERR_CUDA, msg);
 }
 
+int check_register_split(const void* kernel, int threads, int needed, const char* what) {
+  cudaFuncAttributes fa{};
+  cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
+  if (static_cast<long long>(fa.numRegs) * threads < needed)
+    return fail(ND_ERR_UNSUPPORTED, std::string(what) + ": kernel compiled with " + std::to_string(fa.numRegs) +
+                                        " registers per thread, fewer than its warpgroups' register split needs");
+  return ND_OK;
+}
+
 int sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
