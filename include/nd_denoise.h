@@ -387,9 +387,10 @@ ND_API int nd_op_group_norm(const void* x, void* y, int dtype, int batch, int pi
  * library, so it suits hosts that cannot let the library allocate: device
  * memory already fully committed (a serving pool, full weight residency), or
  * a pipeline that must not meet cudaFree's device-wide wait.
- *  - Limit: batch * ceil(pixels / 256) * channels * 16 + batch * groups * 8
- *    + 256 bytes must fit in 4 MiB (SDXL at 1024 x 1024, batch 2, needs
- *    1.97 MB); larger shapes fail with ND_ERR_INVALID and launch nothing.
+ *  - Limit: batch * ceil(pixels / 32) * groups * 8 (rounded up to 256)
+ *    + batch * groups * 8 + 256 bytes must fit in 4 MiB (SDXL at 1024 x
+ *    1024, batch 2: 0.26 MB; at 32 groups up to about 512 K pixels over the
+ *    batch); larger shapes fail with ND_ERR_INVALID and launch nothing.
  *  - Nothing needs to start at zero: every partial sum and group statistic
  *    is written before it is read within the same call.
  *  - The first call on each device looks up the array's address (with that

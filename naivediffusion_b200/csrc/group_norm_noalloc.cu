@@ -19,10 +19,10 @@
 namespace nd {
 namespace {
 
-// Fixed scratch: batch x ceil(pixels / 256) x channels fp64 pairs (16 bytes)
-// plus batch x groups float pairs (8 bytes) plus 256 bytes of slack. 4 MiB
-// holds the SDXL UNet's largest GroupNorm at a 1024 x 1024 image and batch 2
-// (2 x 64 x 960 x 16 bytes = 1.97 MB).
+// Fixed scratch: batch x ceil(pixels / 32) x groups float pairs (8 bytes,
+// rounded up to 256) plus batch x groups float pairs plus 256 bytes of slack.
+// 4 MiB holds the SDXL UNet's GroupNorms at a 1024 x 1024 image and batch 2
+// (2 x 512 x 32 x 8 bytes = 0.26 MB) with room to spare.
 constexpr size_t kNoAllocScratchBytes = size_t{4} << 20;
 __device__ __align__(256) unsigned char g_gn_scratch[kNoAllocScratchBytes];
 
@@ -59,7 +59,7 @@ extern "C" int nd_op_group_norm_noalloc(const void* x, void* y, int dtype, int b
     return nd::fail(ND_ERR_INVALID, "nd_op_group_norm_noalloc: this shape needs " + std::to_string(need) +
                                         " bytes of scratch, more than the fixed " +
                                         std::to_string(nd::kNoAllocScratchBytes) +
-                                        " (batch x ceil(pixels / 256) x channels x 16 + batch x groups x 8 + 256)");
+                                        " (batch x ceil(pixels / 32) x groups x 8, rounded up to 256, + batch x groups x 8 + 256)");
   void* scratch = nullptr;
   int rc = nd::scratch_for_current_device(&scratch);
   if (rc) return rc;

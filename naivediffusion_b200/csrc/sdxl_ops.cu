@@ -41,33 +41,91 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8], int f16) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// Per (image, pixel chunk, channel): sum and sum of squares in fp64.
+// Per (image, chunk of kGnChunk pixels, group): sum and sum of squares.
+// Threads read 16-byte vectors (8 channels), consecutive threads on
+// consecutive vectors of a pixel row and several rows per pass, so every load
+// is coalesced; each thread sums its 8 channels in fp32, the block adds the
+// rows' sums per channel in shared memory and then each group's channels.
+// Small chunks give every SM blocks to run even at the UNet's smallest
+// levels; the per-group partials are combined in fp64 by gn_finalize_kernel.
+constexpr int kGnChunk = 32;
+constexpr int kGnMaxSlab = 2048;  // channels per block (static shared memory: 16 KB of channel sums)
+
+// grid (pixel chunks, channel slabs, images): a slab is a run of whole groups
+// and whole 8-channel vectors, [slab * slab_c, ...) clipped to C.
 __global__ void __launch_bounds__(256) gn_partial_kernel(const void* __restrict__ x, int f16, int hw,
-                                                         int C, int chunk, double2* __restrict__ part) {
-  const int ck = blockIdx.x, b = blockIdx.y;
-  const int p0 = ck * chunk, p1 = min(hw, p0 + chunk);
-  const long long base = static_cast<long long>(b) * hw * C;
+                                                         int C, int G, int slab_c, float2* __restrict__ part) {
+  __shared__ float red[256][17];
+  __shared__ float chs[2][kGnMaxSlab];
+  const int ck = blockIdx.x, b = blockIdx.z;
+  const int c_lo = blockIdx.y * slab_c, c_hi = min(C, c_lo + slab_c);
+  const int p0 = ck * kGnChunk, p1 = min(hw, p0 + kGnChunk);
   const int nchunks = gridDim.x;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    double s1 = 0.0, s2 = 0.0;
-    for (int p = p0; p < p1; ++p) {
-      const double v = ld16(x, base + static_cast<long long>(p) * C + c, f16);
-      s1 += v;
-      s2 += v * v;
+  const int c8 = C / 8;
+  const int v_lo = c_lo / 8, nv = (c_hi - c_lo) / 8;  // this slab's vectors
+  const int tpr = min(nv, 256);                        // threads per pixel row
+  const int rows = 256 / tpr;                          // pixel rows per pass
+  const int t = threadIdx.x;
+  const int pr = t / tpr;
+  const uint4* xv = reinterpret_cast<const uint4*>(x) + static_cast<long long>(b) * hw * c8;
+  for (int j0 = 0; j0 < nv; j0 += tpr) {
+    const int j = j0 + t % tpr;  // vector within the slab
+    float s1[8], s2[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s1[k] = s2[k] = 0.f;
+    if (pr < rows && j < nv) {
+      for (int p = p0 + pr; p < p1; p += rows) {
+        float v[8];
+        unpack8(__ldg(xv + static_cast<long long>(p) * c8 + v_lo + j), f16, v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          s1[k] += v[k];
+          s2[k] = fmaf(v[k], v[k], s2[k]);
+        }
+      }
     }
-    part[(static_cast<long long>(b) * nchunks + ck) * C + c] = make_double2(s1, s2);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      red[t][k] = s1[k];
+      red[t][8 + k] = s2[k];
+    }
+    __syncthreads();
+    if (pr == 0 && j < nv) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float a = 0.f, q = 0.f;
+        for (int r = 0; r < rows; ++r) {
+          a += red[r * tpr + t][k];
+          q += red[r * tpr + t][8 + k];
+        }
+        chs[0][j * 8 + k] = a;
+        chs[1][j * 8 + k] = q;
+      }
+    }
+    __syncthreads();
+  }
+  const int cg = C / G;
+  const int g_lo = c_lo / cg, g_hi = c_hi / cg;
+  for (int g = g_lo + t; g < g_hi; g += 256) {
+    float a = 0.f, q = 0.f;
+    for (int c = g * cg; c < (g + 1) * cg; ++c) {
+      a += chs[0][c - c_lo];
+      q += chs[1][c - c_lo];
+    }
+    part[(static_cast<long long>(b) * nchunks + ck) * G + g] = make_float2(a, q);
   }
 }
 
-// Per (image, group): mean and 1/sqrt(var + eps) over hw x C/G values.
-__global__ void gn_finalize_kernel(const double2* __restrict__ part, int nchunks, int C, int G, int hw,
+// Per (image, group): mean and 1/sqrt(var + eps) over hw x C/G values, the
+// chunks' partial sums added in fp64.
+__global__ void gn_finalize_kernel(const float2* __restrict__ part, int nchunks, int C, int G, int hw,
                                    float eps, float2* __restrict__ stats) {
   const int b = blockIdx.x / G, g = blockIdx.x % G;
-  const int cg = C / G;
+  __shared__ double red[2][8];
   double s1 = 0.0, s2 = 0.0;
-  for (int i = threadIdx.x; i < nchunks * cg; i += blockDim.x) {
-    const int ck = i / cg, c = g * cg + i % cg;
-    const double2 v = part[(static_cast<long long>(b) * nchunks + ck) * C + c];
+#pragma unroll 4
+  for (int i = threadIdx.x; i < nchunks; i += blockDim.x) {
+    const float2 v = part[(static_cast<long long>(b) * nchunks + i) * G + g];
     s1 += v.x;
     s2 += v.y;
   }
@@ -76,38 +134,68 @@ __global__ void gn_finalize_kernel(const double2* __restrict__ part, int nchunks
     s1 += __shfl_xor_sync(0xffffffffu, s1, o);
     s2 += __shfl_xor_sync(0xffffffffu, s2, o);
   }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    red[0][w] = s1;
+    red[1][w] = s2;
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
-    const double n = static_cast<double>(hw) * cg;
+    s1 = s2 = 0.0;
+    for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) {
+      s1 += red[0][k];
+      s2 += red[1][k];
+    }
+    const double n = static_cast<double>(hw) * (C / G);
     const double mean = s1 / n;
     const double var = fmax(s2 / n - mean * mean, 0.0);
     stats[blockIdx.x] = make_float2(static_cast<float>(mean), static_cast<float>(1.0 / sqrt(var + eps)));
   }
 }
 
+// y = (x - mean_g) * rstd_g * w_c + b_c (then SiLU), one block per
+// (kGnApplyPixels pixels, image): each thread owns fixed 8-channel vectors, so
+// the per-channel factors are formed once and the loop is loads, 8 FMAs and
+// stores, with no index division.
+constexpr int kGnApplyPixels = 64;  // upper bound; the host picks fewer for enough blocks
+
 __global__ void __launch_bounds__(256) gn_apply_kernel(const void* __restrict__ x, void* __restrict__ y,
-                                                       int f16, long long pixels_total, int hw, int C,
-                                                       int G, const float2* __restrict__ stats,
+                                                       int f16, int hw, int C, int G, int pix_per_block,
+                                                       const float2* __restrict__ stats,
                                                        const float* __restrict__ w,
                                                        const float* __restrict__ bias, int silu_after) {
+  const int b = blockIdx.y;
+  const int p0 = blockIdx.x * pix_per_block, p1 = min(hw, p0 + pix_per_block);
   const int c8 = C / 8;
+  const int tpr = min(c8, 256);
+  const int rows = 256 / tpr;
+  const int t = threadIdx.x;
+  const int pr = t / tpr;
+  if (pr >= rows) return;
   const int cg = C / G;
-  const long long n = pixels_total * c8;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long pix = i / c8;
-    const int c0 = static_cast<int>(i % c8) * 8;
-    const int b = static_cast<int>(pix / hw);
-    float v[8];
-    unpack8(reinterpret_cast<const uint4*>(x)[i], f16, v);
+  const long long base = static_cast<long long>(b) * hw * c8;
+  for (int cv = t % tpr; cv < c8; cv += tpr) {
+    float sc[8], sh[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const int c = c0 + k;
+      const int c = cv * 8 + k;
       const float2 st = stats[b * G + c / cg];
-      float o = (v[k] - st.x) * st.y * (w ? w[c] : 1.0f) + (bias ? bias[c] : 0.0f);
-      if (silu_after) o = o / (1.0f + __expf(-o));
-      v[k] = o;
+      const float wc = w ? __ldg(w + c) : 1.0f;
+      sc[k] = st.y * wc;
+      sh[k] = (bias ? __ldg(bias + c) : 0.0f) - st.x * st.y * wc;
     }
-    reinterpret_cast<uint4*>(y)[i] = pack8(v, f16);
+    for (int p = p0 + pr; p < p1; p += rows) {
+      const long long i = base + static_cast<long long>(p) * c8 + cv;
+      float v[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(x) + i), f16, v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float o = fmaf(v[k], sc[k], sh[k]);
+        if (silu_after) o = o / (1.0f + __expf(-o));
+        v[k] = o;
+      }
+      reinterpret_cast<uint4*>(y)[i] = pack8(v, f16);
+    }
   }
 }
 
@@ -205,30 +293,45 @@ int group_norm(const void* x, void* y, int dtype, int B, int HW, int C, int G, c
   if (dtype != ND_F16 && dtype != ND_BF16) return fail(ND_ERR_INVALID, "group_norm: dtype must be f16 or bf16");
   if (B <= 0 || HW <= 0 || C <= 0 || G <= 0 || C % G || C % 8) return fail(ND_ERR_INVALID, "group_norm: bad shape");
   if (!x || !y) return fail(ND_ERR_INVALID, "group_norm: null operand");
-  const int chunk = 256;
-  const int nchunks = (HW + chunk - 1) / chunk;
-  const size_t part_bytes = static_cast<size_t>(B) * nchunks * C * sizeof(double2);
-  const size_t stats_bytes = static_cast<size_t>(B) * G * sizeof(float2);
+  const int nchunks = (HW + kGnChunk - 1) / kGnChunk;
+  // Channel slabs: whole groups and whole vectors (multiples of lcm(C/G, 8)),
+  // as many as it takes for ~4 blocks per SM, at most kGnMaxSlab channels.
+  const int cg = C / G;
+  int base = cg;
+  while (base % 8) base += cg;
+  if (base > kGnMaxSlab) return fail(ND_ERR_UNSUPPORTED, "group_norm: groups too wide");
+  const long long want = 4LL * sm_count();
+  long long slabs = std::max<long long>(1, std::min<long long>(C / base, (want + static_cast<long long>(nchunks) * B - 1) /
+                                                                            (static_cast<long long>(nchunks) * B)));
+  int slab_c = static_cast<int>(((C / base + slabs - 1) / slabs) * base);
+  while (slab_c > kGnMaxSlab) slab_c -= base;
+  slabs = (C + slab_c - 1) / slab_c;
+  if (B > 65535) return fail(ND_ERR_INVALID, "group_norm: batch above 65535");
+  const size_t part_bytes = static_cast<size_t>(B) * nchunks * G * sizeof(float2);
   if (scratch_bytes < group_norm_scratch(B, HW, C, G))
     return fail(ND_ERR_INVALID, "group_norm: scratch too small");
-  double2* part = static_cast<double2*>(scratch);
-  float2* stats = reinterpret_cast<float2*>(static_cast<uint8_t*>(scratch) + part_bytes);
-  (void)stats_bytes;
+  float2* part = static_cast<float2*>(scratch);
+  float2* stats = reinterpret_cast<float2*>(static_cast<uint8_t*>(scratch) + ((part_bytes + 255) & ~size_t{255}));
   const int f16 = dtype == ND_F16;
-  gn_partial_kernel<<<dim3(nchunks, B), 256, 0, s>>>(x, f16, HW, C, chunk, part);
+  gn_partial_kernel<<<dim3(nchunks, static_cast<unsigned>(slabs), B), 256, 0, s>>>(x, f16, HW, C, G, slab_c, part);
   ND_CUDA(cudaGetLastError());
-  gn_finalize_kernel<<<B * G, 32, 0, s>>>(part, nchunks, C, G, HW, eps, stats);
+  gn_finalize_kernel<<<B * G, 256, 0, s>>>(part, nchunks, C, G, HW, eps, stats);
   ND_CUDA(cudaGetLastError());
-  const long long pixels = static_cast<long long>(B) * HW;
-  gn_apply_kernel<<<grid_for(pixels * (C / 8)), 256, 0, s>>>(x, y, f16, pixels, HW, C, G, stats, w, bias,
-                                                               silu_after);
+  const long long vectors = static_cast<long long>(B) * HW * (C / 8);
+  const int rows = 256 / std::min(C / 8, 256);  // pixel rows a block covers per pass
+  const int ppb = static_cast<int>(std::max<long long>(
+      rows, std::min<long long>(kGnApplyPixels, vectors / (want * 256 * 2))));
+  gn_apply_kernel<<<dim3((HW + ppb - 1) / ppb, B), 256, 0, s>>>(x, y, f16, HW, C, G, ppb, stats, w, bias,
+                                                                silu_after);
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }
 
 size_t group_norm_scratch(int B, int HW, int C, int G) {
-  const int nchunks = (HW + 255) / 256;
-  return static_cast<size_t>(B) * nchunks * C * sizeof(double2) + static_cast<size_t>(B) * G * sizeof(float2) + 256;
+  (void)C;
+  const size_t nchunks = (static_cast<size_t>(HW) + kGnChunk - 1) / kGnChunk;
+  const size_t part = static_cast<size_t>(B) * nchunks * G * sizeof(float2);
+  return ((part + 255) & ~size_t{255}) + static_cast<size_t>(B) * G * sizeof(float2) + 256;
 }
 
 int geglu(const void* in, void* out, int dtype, int64_t rows, int64_t F, cudaStream_t s) {

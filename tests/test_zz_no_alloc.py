@@ -75,9 +75,9 @@ def test_noalloc_leaves_free_memory_unchanged(cuda):
 
 
 def test_noalloc_rejects_shapes_beyond_its_fixed_scratch(cuda):
-    # 2 x 64 x 2048 x 16 bytes = 4 MiB of partial sums alone: over the limit.
-    x = torch.zeros(2, 16384, 2048, dtype=torch.float16, device="cuda")
-    w = torch.ones(2048, device="cuda")
+    # 4 x 8192 x 32 x 8 bytes = 8 MiB of partial sums alone: over the limit.
+    x = torch.zeros(4, 262144, 64, dtype=torch.float16, device="cuda")
+    w = torch.ones(64, device="cuda")
     y = torch.empty_like(x)
     rc = _call("nd_op_group_norm_noalloc", x, y, 32, w, None, 1e-5, False)
     assert rc == _lib.ND_ERR_INVALID
