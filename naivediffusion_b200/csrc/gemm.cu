@@ -43,13 +43,16 @@ int launch_gemm_w8(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorM
   int dev = 0;
   ND_CUDA(cudaGetDevice(&dev));
   if (!configured[dev & 63]) {
+    int rc = check_register_split(reinterpret_cast<const void*>(gemm_w8_sm100_kernel<BN, STAGES>), kW8Threads,
+                                  kW8RegsNeeded, "int8 linear");
+    if (rc) return rc;
     ND_CUDA(cudaFuncSetAttribute(gemm_w8_sm100_kernel<BN, STAGES>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, L::kLaunchBytes));
     configured[dev & 63] = true;
   }
   const int tiles = ((g.M + 127) / 128) * ((g.N + BN - 1) / BN);
   const int grid = std::min(tiles, sm_count());
-  gemm_w8_sm100_kernel<BN, STAGES><<<grid, 384, L::kLaunchBytes, stream>>>(ta, tw, tc, g);
+  gemm_w8_sm100_kernel<BN, STAGES><<<grid, kW8Threads, L::kLaunchBytes, stream>>>(ta, tw, tc, g);
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }

@@ -15,15 +15,19 @@
 // whose mantissa product still fits) is formed exactly in fp32, so the
 // widened weight is the oracle's dequantized weight rounded once.
 //
-// Warp roles (384 threads, one CTA per SM, persistent over tiles):
+// Warp roles (512 threads, one CTA per SM, persistent over tiles):
 //   warp 0       TMA: A tile [128 x 64] bf16 + raw W tile [BN x 64] int8
 //   warp 1       tcgen05.mma issuer (as in gemm_sm100_kernel)
-//   warps 2-7    converters: raw int8 -> bf16 * scale into the 128B-swizzled
-//                K-major operand layout, then release the stage to the MMA
-//   warps 8-11   epilogue (shared with gemm_sm100_kernel)
-// Registers are rebalanced per warpgroup with setmaxnreg: 104 + 104 + 232
-// per thread of warpgroups 0 / 1 / 2, summing to 56,320 of the 64,512 the
-// block is launched with (384 x 168).
+//   warps 4-11   converters (two per SM sub-partition): raw int8 -> bf16 *
+//                scale into the 128B-swizzled K-major operand layout, then
+//                release the stage to the MMA. A thread converts 16-byte
+//                pieces (16 weights), so its shared-memory reads and writes
+//                are free of bank conflicts; per-channel scales are loaded
+//                once per tile, group scales once per k block.
+//   warps 12-15  epilogue (shared with gemm_sm100_kernel)
+// Registers are rebalanced per warpgroup with setmaxnreg: 56 / 104 / 104 /
+// 200 per thread of warpgroups 0-3, summing to 59,392 of what the block is
+// launched with (512 x its compiled count; the host checks it covers this).
 #pragma once
 
 #include "gemm_sm100.cuh"
@@ -46,11 +50,14 @@ struct GemmW8Smem {
   static constexpr int kTotal = kMiscOffset + 16;
   static constexpr int kLaunchBytes = kTotal + 1024;
   static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
-  static constexpr int kConverters = 6;          // warps 2..7
+  static constexpr int kConverters = 8;          // warps 4..11
 };
 
+constexpr int kW8Threads = 512;
+constexpr int kW8RegsNeeded = 128 * (56 + 104 + 104 + 200);
+
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(kW8Threads, 1)
     gemm_w8_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmW,
                          const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
@@ -107,12 +114,10 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp < 8) {
-    reg_dealloc<104>();
-  } else {
-    reg_alloc<232>();
-  }
-
+  // Each role's code sits inside its warpgroup's setmaxnreg branch so the
+  // compiler budgets each region with that branch's register count.
+  if (warp < 4) {
+    reg_dealloc<56>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one()) {
@@ -188,62 +193,82 @@ __global__ void __launch_bounds__(384, 1)
       volatile int never = 0;
       mbar_wait(drain_bar, 0, &never, args.status, kStatusTimeoutDrain);
     }
-  } else if (warp < 8) {
+  }
+  } else if (warp < 12) {
+    reg_dealloc<104>();
     // ------------------------------------------------------------ converters
-    // Unit u = (row r of the W tile, half h of the 64-column k block): 32
-    // int8 at raw[r * 64 + h * 32] -> 32 bf16 at 16-byte chunks 4h..4h+3 of
-    // the operand row r, chunk c stored at position c ^ (r & 7) (128B swizzle).
-    const int ct = threadIdx.x - 64;  // 0 .. 191
-    const int n_conv = L::kConverters * 32;
+    // Unit u = (row r of the W tile, quarter q of the 64-column k block): 16
+    // int8 at raw[r * 64 + q * 16] -> 16 bf16, the 16-byte chunks 2q and
+    // 2q + 1 of operand row r, chunk c stored at c ^ (r & 7) (128B swizzle).
+    // A warp's 32 units are 8 rows x 4 quarters: 512 contiguous bytes read,
+    // 4 x 128 bytes written per store, no bank conflicts either way.
+    constexpr int kUnits = BN * 4;
+    constexpr int kPer = kUnits / (L::kConverters * 32);  // units per thread (4 or 2)
+    static_assert(kUnits % (L::kConverters * 32) == 0, "tile rows must fill the converters");
+    const int ct = threadIdx.x - 128;  // 0 .. 255
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
     const bool f16_scales = args.w8_scale_f16 != 0;
+    const bool per_channel = args.w8_scale_cols == 1;
     const long long w_rows = (args.shared_weights || args.group_split >= args.M ? 1LL : 2LL) * args.N;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       const int m0 = (t % num_m) * 128;
       const int n0 = (t / num_m) * BN;
       const int group = row_group(args, m0);
       const long long wrow0 = (args.shared_weights ? 0LL : static_cast<long long>(group) * args.N) + n0;
+      auto load_scale = [&](long long wrow, int kcol) {
+        if (wrow >= w_rows || kcol >= args.K) return 0.f;
+        const long long si = wrow * args.w8_scale_cols + (per_channel ? 0 : kcol / args.w8_group);
+        return f16_scales ? __half2float(__ldg(static_cast<const __half*>(args.w8_scales) + si))
+                          : __ldg(static_cast<const float*>(args.w8_scales) + si);
+      };
+      float sc[kPer];
+      if (per_channel) {
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) sc[j] = load_scale(wrow0 + ((ct + j * 256) >> 2), 0);
+      }
       for (int kb = 0; kb < num_kb; ++kb) {
+        if (!per_channel) {
+#pragma unroll
+          for (int j = 0; j < kPer; ++j) {
+            const int u = ct + j * 256;
+            sc[j] = load_scale(wrow0 + (u >> 2), kb * 64 + (u & 3) * 16);
+          }
+        }
         if (!mbar_wait(full_bar(stage), phase, abort_flag, args.status, kStatusTimeoutProducer)) {
           ok = false;
           break;
         }
-        for (int u = ct; u < BN * 2; u += n_conv) {
-          const int r = u >> 1;
-          const int h = u & 1;
-          const long long wrow = wrow0 + r;
-          const int kcol = kb * 64 + h * 32;
-          float sc = 0.f;
-          if (wrow < w_rows && kcol < args.K) {
-            const long long si = wrow * args.w8_scale_cols + kcol / args.w8_group;
-            sc = f16_scales ? __half2float(__ldg(static_cast<const __half*>(args.w8_scales) + si))
-                            : __ldg(static_cast<const float*>(args.w8_scales) + si);
-          }
-          uint32_t w[8];
-          const uint32_t src = raw_buf(stage) + r * 64 + h * 32;
-          ld_shared_v4(src, w[0], w[1], w[2], w[3]);
-          ld_shared_v4(src + 16, w[4], w[5], w[6], w[7]);
-          uint32_t p[16];
+        uint4 raw[kPer];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float f[4];
-            i8x4_to_f32(w[i], f);
-            if (args.out_f16) {
-              p[2 * i] = pack_f16(f[0] * sc, f[1] * sc);
-              p[2 * i + 1] = pack_f16(f[2] * sc, f[3] * sc);
-            } else {
-              p[2 * i] = pack_bf16(f[0] * sc, f[1] * sc);
-              p[2 * i + 1] = pack_bf16(f[2] * sc, f[3] * sc);
-            }
+        for (int j = 0; j < kPer; ++j) {
+          const int u = ct + j * 256;
+          ld_shared_v4(raw_buf(stage) + (u >> 2) * 64 + (u & 3) * 16, raw[j].x, raw[j].y, raw[j].z, raw[j].w);
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+          const int u = ct + j * 256;
+          const int r = u >> 2, q = u & 3;
+          const uint32_t w4[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+          const float2 s2 = make_float2(sc[j], sc[j]);
+          const float2 m2 = make_float2(-8388736.0f, -8388736.0f);
+          uint32_t p[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            // exact int8 -> fp32 (magic 2^23 + 128 offset), fp32 product, one RNE rounding
+            const uint32_t x = w4[i] ^ 0x80808080u;
+            const float2 lo = fadd2(make_float2(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540u)),
+                                                __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7541u))), m2);
+            const float2 hi = fadd2(make_float2(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7542u)),
+                                                __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7543u))), m2);
+            const float2 a = fmul2(lo, s2), b = fmul2(hi, s2);
+            p[2 * i] = args.out_f16 ? pack_f16(a.x, a.y) : pack_bf16(a.x, a.y);
+            p[2 * i + 1] = args.out_f16 ? pack_f16(b.x, b.y) : pack_bf16(b.x, b.y);
           }
           const uint32_t dst = b_buf(stage) + r * 128;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int c = h * 4 + j;
-            st_shared_v4(dst + ((c ^ (r & 7)) << 4), p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
-          }
+          st_shared_v4(dst + (((2 * q) ^ (r & 7)) << 4), p[0], p[1], p[2], p[3]);
+          st_shared_v4(dst + (((2 * q + 1) ^ (r & 7)) << 4), p[4], p[5], p[6], p[7]);
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -255,6 +280,7 @@ __global__ void __launch_bounds__(384, 1)
       }
     }
   } else {
+    reg_alloc<200>();
     // ------------------------------------------------------------ epilogue
     const int ew = warp & 3;
     const int row_in_tile = ew * 32 + lane;
