@@ -276,8 +276,8 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
     rc = make_tmap_2d_typed(&tb, a.weight, ND_I8, groups * a.out_features, a.in_features, a.in_features,
                             bn, 64, 0);
     if (rc) return rc;
-    if (bn == 256) return launch_gemm_w8<256, 3>(ta, tb, tc, g, stream);
-    return launch_gemm_w8<128, 4>(ta, tb, tc, g, stream);
+    if (bn == 256) return launch_gemm_w8<256, 4>(ta, tb, tc, g, stream);
+    return launch_gemm_w8<128, 6>(ta, tb, tc, g, stream);
   }
   rc = make_tmap_2d(&tb, a.weight, 2, groups * a.out_features, a.in_features, a.in_features, bn, 64, true);
   if (rc) return rc;

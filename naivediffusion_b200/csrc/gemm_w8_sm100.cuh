@@ -34,18 +34,23 @@
 
 namespace nd {
 
+// Two rings: STAGES slots of (A tile + raw int8 W tile) fed by TMA, deep
+// enough to cover the load latency, and kBStages slots of widened bf16 W
+// tiles between the converters and the tensor core.
 template <int BN, int STAGES>
 struct GemmW8Smem {
   static constexpr int kABytes = 128 * 64 * 2;   // 16 KB
   static constexpr int kRawBytes = BN * 64;      // int8 tile
   static constexpr int kBBytes = BN * 64 * 2;    // widened bf16 tile
-  static constexpr int kStageBytes = kABytes + kRawBytes + kBBytes;
-  static constexpr int kTiles = STAGES * kStageBytes;
+  static constexpr int kBStages = 2;
+  static constexpr int kStageBytes = kABytes + kRawBytes;
+  static constexpr int kBOffset = STAGES * kStageBytes;
+  static constexpr int kTiles = kBOffset + kBStages * kBBytes;
   static constexpr int kStageBuf = 4096;
   static constexpr int kEpiOffset = kTiles;
   static constexpr int kBarOffset = kEpiOffset + 4 * 2 * kStageBuf;
-  // full[S], conv[S], empty[S], acc_full[2], acc_empty[2], drain
-  static constexpr int kNumBars = 3 * STAGES + 5;
+  // full[S], empty[S], conv[BS], bempty[BS], acc_full[2], acc_empty[2], drain
+  static constexpr int kNumBars = 2 * STAGES + 2 * kBStages + 5;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
   static constexpr int kTotal = kMiscOffset + 16;
   static constexpr int kLaunchBytes = kTotal + 1024;
@@ -67,17 +72,19 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bars = sbase + L::kBarOffset;
+  constexpr int BS = L::kBStages;
   auto full_bar = [&](int s) { return bars + 8u * s; };
-  auto conv_bar = [&](int s) { return bars + 8u * (STAGES + s); };
-  auto empty_bar = [&](int s) { return bars + 8u * (2 * STAGES + s); };
-  auto accf_bar = [&](int s) { return bars + 8u * (3 * STAGES + s); };
-  auto acce_bar = [&](int s) { return bars + 8u * (3 * STAGES + 2 + s); };
-  const uint32_t drain_bar = bars + 8u * (3 * STAGES + 4);
+  auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
+  auto conv_bar = [&](int s) { return bars + 8u * (2 * STAGES + s); };
+  auto bempty_bar = [&](int s) { return bars + 8u * (2 * STAGES + BS + s); };
+  auto accf_bar = [&](int s) { return bars + 8u * (2 * STAGES + 2 * BS + s); };
+  auto acce_bar = [&](int s) { return bars + 8u * (2 * STAGES + 2 * BS + 2 + s); };
+  const uint32_t drain_bar = bars + 8u * (2 * STAGES + 2 * BS + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
   auto a_buf = [&](int s) { return sbase + s * L::kStageBytes; };
   auto raw_buf = [&](int s) { return sbase + s * L::kStageBytes + L::kABytes; };
-  auto b_buf = [&](int s) { return sbase + s * L::kStageBytes + L::kABytes + L::kRawBytes; };
+  auto b_buf = [&](int s) { return sbase + L::kBOffset + s * L::kBBytes; };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -89,8 +96,11 @@ __global__ void __launch_bounds__(kW8Threads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);
-      mbar_init(conv_bar(s), L::kConverters);
       mbar_init(empty_bar(s), 1);
+    }
+    for (int s = 0; s < BS; ++s) {
+      mbar_init(conv_bar(s), L::kConverters);
+      mbar_init(bempty_bar(s), 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(accf_bar(s), 1);
@@ -155,8 +165,8 @@ __global__ void __launch_bounds__(kW8Threads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
-      int stage = 0;
-      uint32_t phase = 0;
+      int stage = 0, bstage = 0;
+      uint32_t phase = 0, bphase = 0;
       int local = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
@@ -169,7 +179,8 @@ __global__ void __launch_bounds__(kW8Threads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(conv_bar(stage), phase, abort_flag, args.status, kStatusTimeoutMma)) {
+          // the widened tile is ready only after its A + raw slot landed
+          if (!mbar_wait(conv_bar(bstage), bphase, abort_flag, args.status, kStatusTimeoutMma)) {
             ok = false;
             break;
           }
@@ -177,13 +188,18 @@ __global__ void __launch_bounds__(kW8Threads, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = make_sdesc_sw128(a_buf(stage) + k * 32, 16, 1024);
-            const uint64_t bd = make_sdesc_sw128(b_buf(stage) + k * 32, 16, 1024);
+            const uint64_t bd = make_sdesc_sw128(b_buf(bstage) + k * 32, 16, 1024);
             umma_ss(d_tmem, ad, bd, args.idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(empty_bar(stage));
+          umma_commit(bempty_bar(bstage));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
+          }
+          if (++bstage == BS) {
+            bstage = 0;
+            bphase ^= 1u;
           }
         }
         if (!ok) break;
@@ -206,8 +222,8 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     constexpr int kPer = kUnits / (L::kConverters * 32);  // units per thread (4 or 2)
     static_assert(kUnits % (L::kConverters * 32) == 0, "tile rows must fill the converters");
     const int ct = threadIdx.x - 128;  // 0 .. 255
-    int stage = 0;
-    uint32_t phase = 0;
+    int stage = 0, bstage = 0;
+    uint32_t phase = 0, bphase = 0;
     bool ok = true;
     const bool f16_scales = args.w8_scale_f16 != 0;
     const bool per_channel = args.w8_scale_cols == 1;
@@ -240,6 +256,11 @@ __global__ void __launch_bounds__(kW8Threads, 1)
           ok = false;
           break;
         }
+        // the widened slot must have been read by the MMAs of two k blocks ago
+        if (!mbar_wait(bempty_bar(bstage), bphase ^ 1u, abort_flag, args.status, kStatusTimeoutProducer)) {
+          ok = false;
+          break;
+        }
         uint4 raw[kPer];
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
@@ -266,16 +287,20 @@ __global__ void __launch_bounds__(kW8Threads, 1)
             p[2 * i] = args.out_f16 ? pack_f16(a.x, a.y) : pack_bf16(a.x, a.y);
             p[2 * i + 1] = args.out_f16 ? pack_f16(b.x, b.y) : pack_bf16(b.x, b.y);
           }
-          const uint32_t dst = b_buf(stage) + r * 128;
+          const uint32_t dst = b_buf(bstage) + r * 128;
           st_shared_v4(dst + (((2 * q) ^ (r & 7)) << 4), p[0], p[1], p[2], p[3]);
           st_shared_v4(dst + (((2 * q + 1) ^ (r & 7)) << 4), p[4], p[5], p[6], p[7]);
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(conv_bar(stage));
+        if (lane == 0) mbar_arrive(conv_bar(bstage));
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
+        }
+        if (++bstage == BS) {
+          bstage = 0;
+          bphase ^= 1u;
         }
       }
     }
