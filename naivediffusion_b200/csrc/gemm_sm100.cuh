@@ -86,6 +86,22 @@ struct GemmArgs {
   int out_kind;     // 0: bf16/f16 out, 1: hi|lo pair out (lo at column + N), 2: fp32 out
 };
 
+// Tile order of the persistent loop: bands of kTileBandM row tiles, each
+// band walked column tile by column tile. The ~148 tiles in flight at once
+// then share a few A row panels and W column panels, which stay in L2,
+// instead of every CTA streaming its own panels from HBM.
+constexpr int kTileBandM = 16;
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mt, int& nt) {
+  const int per_band = kTileBandM * num_n;
+  const int band = t / per_band;
+  const int first = band * kTileBandM;
+  const int rows = min(kTileBandM, num_m - first);
+  const int r = t - band * per_band;
+  mt = first + r % rows;
+  nt = r / rows;
+}
+
 __device__ __forceinline__ int row_group(const GemmArgs& a, int m0) {
   if (a.periodic_groups) return m0 / a.group_split;
   return m0 >= a.group_split ? 1 : 0;
@@ -398,8 +414,10 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t issued = 0, issued_parity = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const int m0 = (t % num_m) * 128;
-        const int n0 = (t / num_m) * BN;
+        int mt, nt;
+        tile_coords(t, num_m, num_n, mt, nt);
+        const int m0 = mt * 128;
+        const int n0 = nt * BN;
         const int group = row_group(args, m0);
         const int brow = (args.shared_weights ? 0 : group * args.N) + n0;
         int img = 0, y0 = 0;
@@ -516,8 +534,10 @@ __global__ void __launch_bounds__(192, 1)
       }
       __syncwarp();
       tc_fence_after();
-      const int m0 = (t % num_m) * 128;
-      const int n0 = (t / num_m) * BN;
+      int mt, nt;
+      tile_coords(t, num_m, num_n, mt, nt);
+      const int m0 = mt * 128;
+      const int n0 = nt * BN;
       const int group = row_group(args, m0);
       const int row0 = m0 + ew * 32;
       const int row = m0 + row_in_tile;

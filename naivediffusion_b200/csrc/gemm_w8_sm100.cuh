@@ -136,8 +136,10 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       uint32_t issued = 0, issued_parity = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const int m0 = (t % num_m) * 128;
-        const int n0 = (t / num_m) * BN;
+        int mt, nt;
+        tile_coords(t, num_m, num_n, mt, nt);
+        const int m0 = mt * 128;
+        const int n0 = nt * BN;
         const int group = row_group(args, m0);
         const int brow = (args.shared_weights ? 0 : group * args.N) + n0;
         for (int kb = 0; kb < num_kb; ++kb) {
@@ -229,8 +231,10 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     const bool per_channel = args.w8_scale_cols == 1;
     const long long w_rows = (args.shared_weights || args.group_split >= args.M ? 1LL : 2LL) * args.N;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      const int m0 = (t % num_m) * 128;
-      const int n0 = (t / num_m) * BN;
+      int mt, nt;
+      tile_coords(t, num_m, num_n, mt, nt);
+      const int m0 = mt * 128;
+      const int n0 = nt * BN;
       const int group = row_group(args, m0);
       const long long wrow0 = (args.shared_weights ? 0LL : static_cast<long long>(group) * args.N) + n0;
       auto load_scale = [&](long long wrow, int kcol) {
@@ -318,8 +322,10 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       if (!mbar_wait(accf_bar(acc), acc_phase, abort_flag, args.status, kStatusTimeoutEpilogue)) break;
       __syncwarp();
       tc_fence_after();
-      const int m0 = (t % num_m) * 128;
-      const int n0 = (t / num_m) * BN;
+      int mt, nt;
+      tile_coords(t, num_m, num_n, mt, nt);
+      const int m0 = mt * 128;
+      const int n0 = nt * BN;
       const int group = row_group(args, m0);
       const int row0 = m0 + ew * 32;
       const int row = m0 + row_in_tile;
