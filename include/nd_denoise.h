@@ -85,8 +85,9 @@ typedef struct nd_model_desc {
   int latent_channels, latent_height, latent_width, patch;
   int time_width;             /* sinusoid width of the timestep embedder */
   int batch;                  /* latents per predict (stacked CFG branches) */
-  int compute;                /* ND_BF16 (DiTs), ND_F16 (SDXL) */
-  int weight_dtype;           /* storage: ND_BF16 / ND_F16, or ND_I8 (weight-only) */
+  int compute;                /* ND_BF16 (DiTs), ND_F16 (SDXL), or ND_F32 (the DiTs' fp32
+                                 mode: bf16 hi|lo operand pairs on the tensor cores) */
+  int weight_dtype;           /* storage: the compute dtype, or ND_I8 (weight-only, 16-bit compute) */
   int quant_group;            /* int8: columns per scale (32 = BlockQuantizer); 0 = per output channel */
   int quant_scale_dtype;      /* int8: ND_F16 (BlockQuantizer) or ND_F32 */
   int adaln_rank;             /* Anima: rank of the low-rank adaLN (256) */
