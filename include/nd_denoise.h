@@ -426,6 +426,56 @@ ND_API int nd_op_dequantize(const int8_t* q, const void* scales, int scale_dtype
                             int64_t quant_group, int64_t rows, int64_t cols, void* out,
                             int out_dtype, void* stream);
 
+/* ------------------------------------------------------------ sampler step
+ * One solver step on the device, fused with the guidance combine, so the
+ * latent never leaves HBM between denoiser calls: per element
+ *   prediction = branches == 2 ? uncond + guidance * (cond - uncond) : out
+ *   sample     = the sampler's update of `sample` with that prediction
+ * in the reference's arithmetic, operation by operation (float where it
+ * computes in float, double where it does), so a step is bit-identical to
+ * the reference's CPU one:
+ *   ClassifierFreeGuidance.Combine (Pipeline/GuidanceStrategy.cs:32-41),
+ *   EulerScheduler / EulerAncestralScheduler / DpmPlusPlus2MScheduler /
+ *   DpmPlusPlus2MSdeScheduler.Step (Sampling/Schedulers.cs:263-445), with the
+ *   prediction types' Denoise / Derivative / Renoise (Sampling/Prediction.cs).
+ * The per-step scalars the reference computes in double (log, sqrt of the
+ * sigmas) are passed in, computed on the host as it does: see the comments. */
+#define ND_SAMPLER_EULER 0
+#define ND_SAMPLER_EULER_A 1
+#define ND_SAMPLER_DPMPP_2M 2
+#define ND_SAMPLER_DPMPP_2M_SDE 3
+#define ND_PRED_EPSILON 0
+#define ND_PRED_VELOCITY 1
+#define ND_PRED_FLOW 2
+
+typedef struct nd_sampler_args {
+  int sampler;               /* ND_SAMPLER_* */
+  int prediction;            /* ND_PRED_* */
+  int64_t n;                 /* elements of one latent */
+  int branches;              /* 1, or 2: out holds [uncond][cond] */
+  const float* out;          /* the denoiser's prediction(s) [branches][n] */
+  float guidance;
+  float* sample;             /* [n], updated in place */
+  float* last_denoised;      /* DPM++: [n] previous step's denoised, read if
+                                second_order, always overwritten */
+  const float* noise;        /* EULER_A / DPMPP_2M_SDE: [n] unit noise in the
+                                generator's order */
+  float* denoised_out;       /* optional [n]: PredictedSample (the preview) */
+  float* next_input;         /* optional [n]: sample * next_input_scale, the
+                                next denoiser call's input (ScaleModelInput) */
+  float next_input_scale;
+  float sigma, sigma_next;   /* Sigmas[step], Sigmas[step + 1] */
+  /* EULER_A: up = sn * sqrt(max(s^2 - sn^2, 0)) / s, down = sqrt(max(sn^2 -
+   * up^2, 0)) and Renoise(down, sn) -> (rescale, noise_scale), in double.
+   * DPMPP: step_size = log(s / sn), shrink = sn / s, weight = step_size /
+   * (2 * last_step_size) (2M) or 0.5 * (1 - shrink^2) * step_size /
+   * last_step_size (SDE), rescale / noise_scale = Renoise(sn * shrink, sn). */
+  double up, down, rescale, noise_scale, shrink, weight;
+  int second_order;          /* DPMPP: use last_denoised this step */
+} nd_sampler_args;
+
+ND_API int nd_op_sampler_step(const nd_sampler_args* args, void* stream);
+
 /* Synchronize `stream` and report any kernel's timed-out wait (ND_ERR_TIMEOUT)
  * or CUDA fault (ND_ERR_CUDA) since the last check on this device. */
 ND_API int nd_op_sync(void* stream);

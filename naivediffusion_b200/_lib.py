@@ -22,6 +22,8 @@ ND_ERR_MISSING_WEIGHT = 7
 
 ND_F32, ND_F16, ND_BF16, ND_I8, ND_I32 = 0, 1, 2, 3, 4
 ND_BF16X2 = 5  # fp32 as a bf16 hi|lo pair: [rows, 2 * cols], hi columns then lo
+ND_SAMPLER_EULER, ND_SAMPLER_EULER_A, ND_SAMPLER_DPMPP_2M, ND_SAMPLER_DPMPP_2M_SDE = 0, 1, 2, 3
+ND_PRED_EPSILON, ND_PRED_VELOCITY, ND_PRED_FLOW = 0, 1, 2
 
 ND_EPI_STORE = 0
 ND_EPI_GELU_TANH = 1
@@ -111,6 +113,17 @@ class GemvArgs(C.Structure):
     ]
 
 
+class SamplerArgs(C.Structure):
+    _fields_ = [
+        ("sampler", C.c_int), ("prediction", C.c_int), ("n", C.c_int64), ("branches", C.c_int),
+        ("out", C.c_void_p), ("guidance", C.c_float), ("sample", C.c_void_p), ("last_denoised", C.c_void_p),
+        ("noise", C.c_void_p), ("denoised_out", C.c_void_p), ("next_input", C.c_void_p),
+        ("next_input_scale", C.c_float), ("sigma", C.c_float), ("sigma_next", C.c_float),
+        ("up", C.c_double), ("down", C.c_double), ("rescale", C.c_double), ("noise_scale", C.c_double),
+        ("shrink", C.c_double), ("weight", C.c_double), ("second_order", C.c_int),
+    ]
+
+
 _lib: C.CDLL | None = None
 
 
@@ -134,6 +147,7 @@ def lib() -> C.CDLL:
         L.nd_op_geglu.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int64, C.c_void_p]
         L.nd_op_conv2d.argtypes = [C.POINTER(ConvArgs), C.c_void_p]
         L.nd_op_attention.argtypes = [C.POINTER(AttentionArgs), C.c_void_p]
+        L.nd_op_sampler_step.argtypes = [C.POINTER(SamplerArgs), C.c_void_p]
         L.nd_op_modulate.argtypes = [C.POINTER(ModulateArgs), C.c_void_p]
         L.nd_op_rmsnorm.argtypes = [C.POINTER(RmsNormArgs), C.c_void_p]
         L.nd_op_gemv.argtypes = [C.POINTER(GemvArgs), C.c_void_p]

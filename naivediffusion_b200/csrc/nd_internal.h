@@ -55,6 +55,7 @@ int dequantize(const int8_t* q, const void* scales, int scale_dtype, int64_t qua
 int check_register_split(const void* kernel, int threads, int needed, const char* what);
 int attention(const nd_attention_args& a, cudaStream_t stream);
 int attention_f32(const nd_attention_args& a, cudaStream_t stream);
+int sampler_step(const nd_sampler_args& a, cudaStream_t stream);
 int modulate(const nd_modulate_args& a, cudaStream_t stream);
 int rmsnorm(const nd_rmsnorm_args& a, cudaStream_t stream);
 int gemv(const nd_gemv_args& a, cudaStream_t stream);

@@ -282,3 +282,25 @@ def geglu(x: torch.Tensor) -> torch.Tensor:
     y = torch.empty(rows, two_f // 2, device=x.device, dtype=x.dtype)
     check(lib().nd_op_geglu(x.data_ptr(), y.data_ptr(), _DT[x.dtype], rows, two_f // 2, C.c_void_p(_stream())))
     return y
+
+
+def sampler_step(sampler: int, prediction: int, out: torch.Tensor, sample: torch.Tensor, *,
+                 guidance: float = 1.0, last: torch.Tensor | None = None, noise: torch.Tensor | None = None,
+                 denoised_out: torch.Tensor | None = None, next_input: torch.Tensor | None = None,
+                 next_input_scale: float = 1.0, sigma: float, sigma_next: float, up: float = 0.0,
+                 down: float = 0.0, rescale: float = 1.0, noise_scale: float = 0.0, shrink: float = 0.0,
+                 weight: float = 0.0, second_order: bool = False) -> torch.Tensor:
+    """Guidance combine + one solver step in place on `sample` (fp32, device),
+    bit-identical to the reference's CPU step (Sampling/Schedulers.cs).
+    out: [n] or [2, n] (uncond then cond)."""
+    n = sample.numel()
+    branches = out.numel() // n
+    a = _lib.SamplerArgs()
+    a.sampler, a.prediction, a.n, a.branches = sampler, prediction, n, branches
+    a.out, a.guidance, a.sample = out.data_ptr(), guidance, sample.data_ptr()
+    a.last_denoised, a.noise, a.denoised_out, a.next_input = _ptr(last), _ptr(noise), _ptr(denoised_out), _ptr(next_input)
+    a.next_input_scale, a.sigma, a.sigma_next = next_input_scale, sigma, sigma_next
+    a.up, a.down, a.rescale, a.noise_scale, a.shrink, a.weight = up, down, rescale, noise_scale, shrink, weight
+    a.second_order = int(bool(second_order))
+    check(lib().nd_op_sampler_step(C.byref(a), C.c_void_p(_stream())))
+    return sample

@@ -507,3 +507,23 @@ def unet_forward(w: dict, cfg, latent, timestep, add, context):
         x = group_norm(x, 32, w["conv_norm_out.weight"], w.get("conv_norm_out.bias"), 1e-5, True)
         outs.append(conv2d(x, w["conv_out.weight"], w.get("conv_out.bias")))
     return np.stack(outs)
+
+
+def sampler_step(sampler, prediction, out, sample, guidance=1.0, last=None, noise=None, sigma=1.0,
+                 sigma_next=0.0, up=0.0, down=0.0, rescale=1.0, noise_scale=0.0, shrink=0.0, weight=0.0,
+                 second_order=False, want_denoised=False):
+    """One guidance combine + solver step in the reference's arithmetic
+    (Sampling/Schedulers.cs Step, Pipeline/GuidanceStrategy.cs Combine).
+    out [branches, n]; sample [n] is returned updated (copies), with last."""
+    out = _c(np.atleast_2d(out))
+    branches, n = out.shape
+    s = _c(sample).copy()
+    lst = _c(last).copy() if last is not None else np.zeros(n, _f)
+    nz = _c(noise) if noise is not None else None
+    den = np.empty(n, _f) if want_denoised else None
+    lib().nd_oracle_sampler_step(int(sampler), int(prediction), C.c_int64(n), int(branches), _p(out),
+                                 C.c_float(guidance), _p(s), _p(lst), _p(nz), _p(den), C.c_float(sigma),
+                                 C.c_float(sigma_next), C.c_double(up), C.c_double(down), C.c_double(rescale),
+                                 C.c_double(noise_scale), C.c_double(shrink), C.c_double(weight),
+                                 int(bool(second_order)))
+    return (s, lst, den) if want_denoised else (s, lst)

@@ -658,3 +658,84 @@ EXPORT void nd_oracle_conv2d(const float* x, int Cin, int H, int W, const float*
         }
   }
 }
+
+// ---------------------------------------------------------------- sampling
+// The guidance combine and one solver step, element by element with the
+// reference's types: float arithmetic where its arrays are float[], double
+// where it widens (Pipeline/GuidanceStrategy.cs:32-41; Sampling/Schedulers.cs
+// EulerScheduler.Step :270-280, EulerAncestralScheduler.Step :298-333,
+// DpmPlusPlus2MScheduler.Step :348-385, DpmPlusPlus2MSdeScheduler.Step
+// :404-445; Sampling/Prediction.cs Denoise / Derivative). The scalars the
+// reference derives from the sigmas in double come in as arguments.
+// sampler: 0 Euler, 1 Euler a, 2 DPM++ 2M, 3 DPM++ 2M SDE;
+// prediction: 0 epsilon, 1 velocity, 2 flow.
+namespace {
+
+float oracle_denoise(int prediction, float out, float sample, double sigma) {
+  if (prediction == 1) {  // VelocityPrediction.Denoise
+    const double variance = sigma * sigma + 1.0;
+    const double skip = 1.0 / variance;
+    const double output = sigma / std::sqrt(variance);
+    return static_cast<float>(sample * skip - out * output);
+  }
+  return static_cast<float>(sample - sigma * out);  // Epsilon / Flow
+}
+
+float oracle_derivative(int prediction, float out, float sample, double sigma) {
+  if (prediction == 1) {  // (sample - denoised) / sigma
+    const float denoised = oracle_denoise(prediction, out, sample, sigma);
+    return static_cast<float>((sample - denoised) / sigma);
+  }
+  return out;
+}
+
+}  // namespace
+
+EXPORT void nd_oracle_sampler_step(int sampler, int prediction, int64_t n, int branches, const float* out,
+                                   float guidance, float* sample, float* last_denoised, const float* noise,
+                                   float* denoised_out, float sigma_f, float sigma_next_f, double up, double down,
+                                   double rescale, double noise_scale, double shrink, double weight,
+                                   int second_order) {
+  for (int64_t i = 0; i < n; ++i) {
+    float pred = out[i];
+    if (branches == 2) {
+      const float uncond = out[i], cond = out[n + i];
+      pred = uncond + guidance * (cond - uncond);
+    }
+    const double sigma = sigma_f;
+    if (denoised_out) denoised_out[i] = oracle_denoise(prediction, pred, sample[i], sigma);
+    if (sampler == 0) {
+      const float derivative = oracle_derivative(prediction, pred, sample[i], sigma);
+      const float delta = sigma_next_f - sigma_f;
+      sample[i] += derivative * delta;
+    } else if (sampler == 1) {
+      const float derivative = oracle_derivative(prediction, pred, sample[i], sigma);
+      const float delta = static_cast<float>(down - sigma);
+      if (rescale == 1.0) {
+        const float up_scale = static_cast<float>(up);
+        sample[i] += derivative * delta + noise[i] * up_scale;
+      } else {
+        sample[i] = static_cast<float>(rescale * (sample[i] + derivative * delta) + noise[i] * noise_scale);
+      }
+    } else {
+      const float denoised = oracle_denoise(prediction, pred, sample[i], sigma);
+      if (sigma_next_f <= 0.0f) {
+        sample[i] = denoised;
+        continue;
+      }
+      if (sampler == 2) {
+        const double p = second_order ? (1.0 + weight) * denoised - weight * last_denoised[i]
+                                      : static_cast<double>(denoised);
+        sample[i] = static_cast<float>(shrink * sample[i] + (1.0 - shrink) * p);
+      } else {
+        const double keep = shrink * shrink;
+        const double take = 1.0 - keep;
+        const float noise_scale_f = static_cast<float>(noise_scale);
+        double next = keep * sample[i] + take * denoised;
+        if (second_order) next += weight * (denoised - last_denoised[i]);
+        sample[i] = static_cast<float>(rescale * next + noise[i] * noise_scale_f);
+      }
+      last_denoised[i] = denoised;
+    }
+  }
+}

@@ -42,6 +42,7 @@ def test_struct_layouts_match_the_header(tmp_path):
     if not cc:
         pytest.skip("no C compiler")
     structs = {"nd_linear_args": _lib.LinearArgs, "nd_conv_args": _lib.ConvArgs,
+               "nd_sampler_args": _lib.SamplerArgs,
                "nd_attention_args": _lib.AttentionArgs,
                "nd_modulate_args": _lib.ModulateArgs, "nd_rmsnorm_args": _lib.RmsNormArgs,
                "nd_gemv_args": _lib.GemvArgs, "nd_model_desc": D.ModelDesc,

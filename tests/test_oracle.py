@@ -261,3 +261,66 @@ def test_strided_convolution():
             for c in range(3):
                 ref[o, r, c] = (w[o] * xp[:, 2 * r:2 * r + 3, 2 * c:2 * c + 3]).sum()
     assert np.abs(y - ref).max() < 1e-4
+
+
+# ---------------------------------------------------------------- sampling
+# The reference's sampler checks, restated (SchedulersTests.cs:142-205,
+# FlowSamplingTests.cs "ASamplerRunsTheLineDownToCleanData"): given perfect
+# predictions, every sampler walks the sample down to the clean latent.
+
+def _vp_sigmas(steps, rho=7.0):
+    """SDXL's scaled-linear VP levels (beta 0.00085 .. 0.012 over 1000 steps)
+    spaced evenly in sigma^(1/rho) (Karras), then 0."""
+    import math
+    betas = np.linspace(0.00085 ** 0.5, 0.012 ** 0.5, 1000, dtype=np.float64) ** 2
+    alphas = np.cumprod(1.0 - betas)
+    levels = np.sqrt((1.0 - alphas) / alphas)
+    lo, hi = levels[0] ** (1 / rho), levels[-1] ** (1 / rho)
+    s = [(hi + i / (steps - 1) * (lo - hi)) ** rho for i in range(steps)]
+    return np.array(s + [0.0], dtype=np.float32)
+
+
+def _flow_sigmas(steps, shift=3.0):
+    t = np.linspace(1.0, 0.0, steps + 1)
+    return np.array([shift * x / (1 + (shift - 1) * x) for x in t], dtype=np.float32)
+
+
+@pytest.mark.parametrize("prediction", ["epsilon", "velocity", "flow"])
+@pytest.mark.parametrize("sampler", ["euler", "euler_a", "dpmpp_2m", "dpmpp_2m_sde"])
+def test_oracle_samplers_land_on_the_clean_latent(sampler, prediction):
+    from naivediffusion_b200.sampling import PREDICTIONS, SAMPLERS, StepScalars
+    clean = np.sin(np.arange(64) * 0.37).astype(np.float32)
+    rng = np.random.default_rng(3)
+    sigmas = _flow_sigmas(15) if prediction == "flow" else _vp_sigmas(15)
+    sch = StepScalars(sampler, prediction, sigmas)
+    sample = (clean + rng.standard_normal(64).astype(np.float32) * sigmas[0]).astype(np.float32)
+    last = np.zeros(64, np.float32)
+    for step in range(sch.steps):
+        s = float(sigmas[step])
+        if prediction == "epsilon":
+            out = (sample - clean) / np.float32(s)
+        elif prediction == "flow":
+            out = (sample - clean) / np.float32(s)   # noise - x0 on the line x = (1 - s) x0 + s noise
+        else:
+            eps = (sample - clean) / np.float32(s)
+            out = (eps - np.float32(s) * clean) / np.float32(np.sqrt(s * s + 1))
+        d = sch.at(step)
+        noise = rng.standard_normal(64).astype(np.float32) if sch.stochastic else None
+        sample, last, den = O.sampler_step(SAMPLERS[sampler], PREDICTIONS[prediction], out.astype(np.float32),
+                                           sample, last=last, noise=noise, want_denoised=True, **d)
+        assert np.abs(den - clean).max() < 2e-3, (step, np.abs(den - clean).max())
+    assert np.abs(sample - clean).max() < 2e-3
+
+
+def test_oracle_guidance_combine_and_euler_arithmetic():
+    """Combine then Euler, checked against float32 numpy arithmetic done the
+    reference's way (uncond + g * (cond - uncond); sample += d * (sn - s))."""
+    rng = np.random.default_rng(0)
+    out = rng.standard_normal((2, 1000)).astype(np.float32)
+    sample = rng.standard_normal(1000).astype(np.float32)
+    g = np.float32(4.5)
+    pred = out[0] + g * (out[1] - out[0])
+    delta = np.float32(0.25) - np.float32(1.5)
+    ref = sample + pred * delta
+    got, _ = O.sampler_step(0, 0, out, sample, guidance=float(g), sigma=1.5, sigma_next=0.25)
+    assert np.array_equal(got, ref)
