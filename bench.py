@@ -24,7 +24,9 @@ Rank 0 prints ONE JSON line.
 --config picks another BASELINE configuration for the same line (default
 cfg3, the headline): cfg1 one Anima block in fp32, cfg2 the 28-block Anima
 step (two CFG branches), cfg4 cfg3 with int8 per-channel weights, cfg5 the
-SDXL UNet (fp16, two CFG branches).
+SDXL UNet (fp16, two CFG branches), vae the SDXL VAE decoder (a 128 x 128
+latent to a 1024 x 1024 image; not a BASELINE configuration: the step after
+the denoiser).
 
 --impl reference times that CPU restatement alone (the reference is C# over
 DirectML and cannot run here or on the GPU box); rank 0 only.
@@ -113,7 +115,7 @@ class Clocks:
 def _configs():
     """BASELINE configurations: (model config, workload text, dtype, metric)."""
     from naivediffusion_b200 import _lib
-    from naivediffusion_b200.denoiser import AnimaConfig, MMDiTConfig, UNetConfig
+    from naivediffusion_b200.denoiser import AnimaConfig, MMDiTConfig, UNetConfig, VaeDecoderConfig
     return {
         "cfg3": (MMDiTConfig(), "cfg3: Qwen-Image-style MMDiT 60x3072, 24x128 heads, MLP 12288 GELU-tanh, "
                  "5376 img + 256 txt tokens, batch 1, guidance 1", "bf16", METRIC),
@@ -132,6 +134,9 @@ def _configs():
         "cfg5": (UNetConfig(), "cfg5: SDXL UNet 320/640/1280, transformer depths 0/2/10, 4x128x128 latent, "
                  "context 77x2048, add 2816, batch 2 (CFG branches of one image)", "f16",
                  "SDXL UNet s/step @1024×1024 fp16 (2 CFG branches); images/s"),
+        "vae": (VaeDecoderConfig(), "SDXL VAE decoder (AutoencoderKL 128/256/512/512, 2 layers per block): "
+                "4x128x128 latent -> 3x1024x1024 image, fp16", "f16",
+                "SDXL VAE decode s/image @1024×1024 fp16; images/s"),
     }
 
 
@@ -141,8 +146,9 @@ def _inputs(cfg, rank):
     g = torch.Generator(device="cuda").manual_seed(1000 + rank)
     b = getattr(cfg, "batch", 1)
     latent = torch.randn(b, cfg.latent_channels, cfg.latent_height, cfg.latent_width, device="cuda", generator=g)
-    context = torch.randn(b, cfg.context_rows, cfg.context_width, device="cuda", generator=g)
-    cond = {"context": context}
+    cond = {}
+    if hasattr(cfg, "context_rows"):
+        cond["context"] = torch.randn(b, cfg.context_rows, cfg.context_width, device="cuda", generator=g)
     if hasattr(cfg, "add_width"):
         cond["add"] = torch.randn(b, cfg.add_width, device="cuda", generator=g)
     return latent, cond, 500.0
@@ -223,8 +229,8 @@ def run_reference(args):
     if rank != 0:
         return 0
     cfg, workload, _dt, metric = _configs()[args.config]
-    if args.config == "cfg5":
-        print(json.dumps({"impl": "reference", "unavailable": "cfg5 has no bounded CPU sample of the UNet step"}))
+    if args.config in ("cfg5", "vae"):
+        print(json.dumps({"impl": "reference", "unavailable": f"{args.config} has no bounded CPU sample of the step"}))
         return 0
     if args.warmup > 0:
         cpu_sample(args.config, cfg, 1, 1e9)  # warm-up: one sample
@@ -272,7 +278,7 @@ def run_ours(args):
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     latent, cond, timestep = _inputs(cfg, rank)
-    out = torch.empty_like(latent)
+    out = torch.empty(den.output_shape(tuple(latent.shape)), device="cuda")
     sigma = 0.75
 
     def barrier():
@@ -307,7 +313,7 @@ def run_ours(args):
         h = torch.empty(v.shape, dtype=torch.float32, pin_memory=True)
         h.copy_(v.cpu())
         cond_h[k] = h.numpy()
-    out_h = torch.empty(latent.shape, dtype=torch.float32, pin_memory=True)
+    out_h = torch.empty(tuple(out.shape), dtype=torch.float32, pin_memory=True)
     lat_np, y = lat_h.numpy(), out_h.numpy()
     den.predict(lat_np, timestep, sigma, cond_h, out=y)
     barrier()
@@ -338,7 +344,7 @@ def run_ours(args):
     if args.config == "cfg3" and tpath.exists():
         traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
     kernel = "gemm_sm100_kernel (tcgen05, all GEMM launches of a step)"
-    if args.config == "cfg5":
+    if args.config in ("cfg5", "vae"):
         kernel = "gemm_sm100_kernel (tcgen05: conv3x3 implicit GEMMs and the linear layers)"
     elif args.config == "cfg4":
         kernel = "gemm_w8_sm100_kernel (tcgen05, int8 weights widened in the mainloop)"
@@ -395,7 +401,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["cfg3", "cfg1", "cfg2", "cfg4", "cfg5"], default="cfg3",
+    ap.add_argument("--config", choices=["cfg3", "cfg1", "cfg2", "cfg4", "cfg5", "vae"], default="cfg3",
                     help="BASELINE configuration (default cfg3, the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle sample")
     args = ap.parse_args()

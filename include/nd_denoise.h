@@ -73,6 +73,11 @@ ND_API const char* nd_version(void);
 #define ND_FAMILY_MMDIT 0   /* Qwen-Image-style dual-stream DiT (60 x 3072 at full size) */
 #define ND_FAMILY_ANIMA 1   /* Anima / Cosmos-Predict2 DiT (Models/Anima/AnimaDit.cs) */
 #define ND_FAMILY_SDXL 2    /* SDXL UNet (Models/Sdxl/UNetModel.cs) */
+#define ND_FAMILY_VAE_KL 3  /* AutoencoderKL decoder (Vae/AutoencoderKl.cs), the SDXL VAE:
+                               predict() takes the VAE latent (already divided by the
+                               scaling factor) and returns the [batch, 3, 8h, 8w] image;
+                               width = base channels, unet_mult = block_out_channels /
+                               width, unet_resnets = layers_per_block; no conditioning */
 
 typedef struct nd_device nd_device;
 typedef struct nd_denoiser nd_denoiser;

@@ -363,7 +363,7 @@ int run_predict(nd_denoiser* d, const float* latent, double timestep, double sig
     d->graph_key = in.key_limit;
   }
   ND_CUDA(cudaGraphLaunch(d->exec, st));
-  const size_t out_bytes = static_cast<size_t>(d->latent_elems()) * sizeof(float);
+  const size_t out_bytes = static_cast<size_t>(d->output_elems()) * sizeof(float);
   ND_CUDA(cudaMemcpyAsync(out, d->output(), out_bytes, device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
   if (!device) return check_device_status(st);
   return ND_OK;
@@ -417,6 +417,7 @@ int nd_denoiser_create(nd_device* dev, const nd_model_desc* desc, nd_denoiser** 
     case ND_FAMILY_MMDIT: d = nd::make_mmdit(); break;
     case ND_FAMILY_ANIMA: d = nd::make_anima(); break;
     case ND_FAMILY_SDXL: d = nd::make_unet(); break;
+    case ND_FAMILY_VAE_KL: d = nd::make_vae_decoder(); break;
     default: return nd::fail(ND_ERR_UNSUPPORTED, "nd_denoiser_create: unknown model family");
   }
   d->dev = dev;

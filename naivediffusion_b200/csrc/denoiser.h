@@ -140,6 +140,9 @@ struct nd_denoiser {
   virtual int forward(cudaStream_t s) = 0;
   virtual const float* output() const = 0;
   virtual int64_t latent_elems() const = 0;
+  // Floats predict() returns (the latent's shape for denoisers; an image for
+  // the VAE decoder).
+  virtual int64_t output_elems() const { return latent_elems(); }
   virtual int check_cond(int n, const nd_named_tensor* cond, nd::StepInputs& in) = 0;
 };
 
@@ -147,4 +150,5 @@ namespace nd {
 nd_denoiser* make_mmdit();
 nd_denoiser* make_anima();
 nd_denoiser* make_unet();
+nd_denoiser* make_vae_decoder();
 }  // namespace nd

@@ -292,7 +292,8 @@ int conv2d(const nd_conv_args& c, cudaStream_t stream) {
   if (c.in_channels % 64) return fail(ND_ERR_UNSUPPORTED, "conv2d: in_channels must be a multiple of 64");
   if (c.stride != 1 && c.stride != 2) return fail(ND_ERR_UNSUPPORTED, "conv2d: stride must be 1 or 2");
   const int ho = (c.height - 1) / c.stride + 1, wo = (c.width - 1) / c.stride + 1;
-  if (wo > 128 || 128 % wo != 0) return fail(ND_ERR_UNSUPPORTED, "conv2d: output width must divide 128");
+  if (wo <= 128 ? 128 % wo != 0 : wo % 128 != 0)
+    return fail(ND_ERR_UNSUPPORTED, "conv2d: output width must divide 128 or be a multiple of 128");
   if ((static_cast<int64_t>(ho) * wo) % 128 != 0) return fail(ND_ERR_UNSUPPORTED, "conv2d: output pixels per image must be a multiple of 128");
   const int epi = c.epilogue;
   if (epi != ND_EPI_STORE && epi != ND_EPI_ADD_STORE && epi != ND_EPI_STORE_F32 && epi != ND_EPI_SILU)
@@ -310,10 +311,12 @@ int conv2d(const nd_conv_args& c, cudaStream_t stream) {
   const int64_t cin = c.in_channels;
   const int64_t dims[4] = {cin, c.width, c.height, c.batch};
   const int64_t strides[3] = {cin * 2, cin * c.width * 2, cin * c.width * c.height * 2};
-  const int rows = 128 / wo;
-  // With a traversal stride s, TMA loads ceil(box / s) elements along a
-  // dimension, so the box spans s x the output extent.
-  const int box[4] = {64, wo * c.stride, rows * c.stride, 1};
+  // A tile is 128 output pixels: 128 / wo whole rows, or (wide images) 128
+  // pixels of one row. With a traversal stride s, TMA loads ceil(box / s)
+  // elements along a dimension, so the box spans s x the output extent.
+  const int tile_w = std::min(wo, 128);
+  const int rows = 128 / tile_w;
+  const int box[4] = {64, tile_w * c.stride, rows * c.stride, 1};
   const int es[4] = {1, c.stride, c.stride, 1};
   int rc = make_tmap_4d(&ta, c.x, c.dtype, dims, strides, box, es, 128);
   if (rc) return rc;

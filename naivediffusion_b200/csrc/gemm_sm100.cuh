@@ -420,10 +420,12 @@ __global__ void __launch_bounds__(192, 1)
         const int n0 = nt * BN;
         const int group = row_group(args, m0);
         const int brow = (args.shared_weights ? 0 : group * args.N) + n0;
-        int img = 0, y0 = 0;
+        int img = 0, y0 = 0, x0 = 0;
         if constexpr (CONV) {
           img = m0 / args.conv_hw;
-          y0 = (m0 - img * args.conv_hw) / args.conv_w_out;
+          const int rem = m0 - img * args.conv_hw;
+          y0 = rem / args.conv_w_out;
+          x0 = rem - y0 * args.conv_w_out;  // 0 unless a row holds several tiles
         }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.status,
@@ -440,7 +442,8 @@ __global__ void __launch_bounds__(192, 1)
             const int tap = kb / args.conv_kpc;
             const int c0 = (kb - tap * args.conv_kpc) * 64;
             const int dy = tap / 3, dx = tap - dy * 3;
-            tma_load_4d(a_dst, &tmA, full_bar(stage), c0, dx - 1, y0 * args.conv_stride + dy - 1, img);
+            tma_load_4d(a_dst, &tmA, full_bar(stage), c0, x0 * args.conv_stride + dx - 1,
+                        y0 * args.conv_stride + dy - 1, img);
           } else if (args.split_kb > 0) {
             // segments 0, 1, 2 = (A hi, W lo), (A lo, W hi), (A hi, W hi): the
             // two small cross terms first, into a still-small accumulator (the

@@ -19,7 +19,7 @@ import numpy as np
 from . import _lib
 from ._lib import check, lib
 
-FAMILY_MMDIT, FAMILY_ANIMA, FAMILY_SDXL = 0, 1, 2
+FAMILY_MMDIT, FAMILY_ANIMA, FAMILY_SDXL, FAMILY_VAE_KL = 0, 1, 2, 3
 
 
 class ModelDesc(C.Structure):
@@ -324,6 +324,106 @@ class UNetConfig:
         return out
 
 
+@dataclass
+class VaeDecoderConfig:
+    """The AutoencoderKL decoder (Vae/AutoencoderKl.cs). Defaults: the SDXL
+    VAE (SdxlVae.Config: block_out_channels 128 / 256 / 512 / 512, 2 layers
+    per block, 32 groups, eps 1e-6) decoding a 4 x 128 x 128 latent into a
+    1024 x 1024 image."""
+    width: int = 128
+    mult: tuple = (1, 2, 4, 4)
+    layers_per_block: int = 2
+    latent_height: int = 128
+    latent_width: int = 128
+    batch: int = 1
+    compute: int = _lib.ND_F16
+    latent_channels: int = 4
+    eps: float = 1e-6
+
+    def desc(self) -> ModelDesc:
+        d = ModelDesc()
+        d.family = FAMILY_VAE_KL
+        d.width = self.width
+        d.latent_channels, d.latent_height, d.latent_width = 4, self.latent_height, self.latent_width
+        d.batch, d.compute, d.weight_dtype, d.eps = self.batch, self.compute, self.compute, self.eps
+        d.unet_levels = len(self.mult)
+        for i, m in enumerate(self.mult):
+            d.unet_mult[i] = m
+        d.unet_resnets = self.layers_per_block
+        return d
+
+    @property
+    def image_height(self) -> int:
+        return self.latent_height << (len(self.mult) - 1)
+
+    @property
+    def image_width(self) -> int:
+        return self.latent_width << (len(self.mult) - 1)
+
+    def weight_shapes(self):
+        L = len(self.mult)
+        rev = [self.width * self.mult[L - 1 - i] for i in range(L)]
+        out = [("post_quant_conv.weight", (4, 4, 1, 1), True), ("post_quant_conv.bias", (4,), False)]
+
+        def conv(name, co, ci):
+            out.append((name + ".weight", (co, ci, 3, 3), True))
+            out.append((name + ".bias", (co,), False))
+
+        def res(p, ci, co):
+            out.extend([(p + ".norm1.weight", (ci,), True), (p + ".norm1.bias", (ci,), False)])
+            conv(p + ".conv1", co, ci)
+            out.extend([(p + ".norm2.weight", (co,), True), (p + ".norm2.bias", (co,), False)])
+            conv(p + ".conv2", co, co)
+            if ci != co:
+                out.extend([(p + ".conv_shortcut.weight", (co, ci, 1, 1), True), (p + ".conv_shortcut.bias", (co,), False)])
+
+        top = rev[0]
+        conv("decoder.conv_in", top, 4)
+        res("decoder.mid_block.resnets.0", top, top)
+        a = "decoder.mid_block.attentions.0"
+        out.extend([(a + ".group_norm.weight", (top,), True), (a + ".group_norm.bias", (top,), False)])
+        for n in ("to_q", "to_k", "to_v", "to_out.0"):
+            out.extend([(f"{a}.{n}.weight", (top, top), True), (f"{a}.{n}.bias", (top,), False)])
+        res("decoder.mid_block.resnets.1", top, top)
+        c = top
+        for i in range(L):
+            for j in range(self.layers_per_block + 1):
+                res(f"decoder.up_blocks.{i}.resnets.{j}", c, rev[i])
+                c = rev[i]
+            if i != L - 1:
+                conv(f"decoder.up_blocks.{i}.upsamplers.0.conv", c, c)
+        out.extend([("decoder.conv_norm_out.weight", (c,), True), ("decoder.conv_norm_out.bias", (c,), False)])
+        conv("decoder.conv_out", 3, c)
+        return out
+
+    def flops_per_step(self) -> float:
+        """Convolutions, 1x1 shortcuts and the mid-block attention (1 MAC = 2 FLOP)."""
+        L = len(self.mult)
+        rev = [self.width * self.mult[L - 1 - i] for i in range(L)]
+        h, w = self.latent_height, self.latent_width
+        total = 0.0
+
+        def conv(px, ci, co, k=9):
+            return 2.0 * px * ci * co * k
+
+        def res(px, ci, co):
+            return conv(px, ci, co) + conv(px, co, co) + (conv(px, ci, co, 1) if ci != co else 0.0)
+
+        px = h * w
+        top = rev[0]
+        total += conv(px, 4, top) + 2 * res(px, top, top) + 4 * 2.0 * px * top * top + 4.0 * px * px * top
+        c = top
+        for i in range(L):
+            px = (h << i) * (w << i)
+            for _ in range(self.layers_per_block + 1):
+                total += res(px, c, rev[i])
+                c = rev[i]
+            if i != L - 1:
+                total += conv(4 * px, c, c)
+        total += conv((h << (L - 1)) * (w << (L - 1)), c, 3)
+        return self.batch * total
+
+
 def _name_seed(name: str, seed: int) -> int:
     return (zlib.crc32(name.encode()) ^ (seed * 0x9E3779B1)) & 0xFFFFFFFF
 
@@ -533,15 +633,26 @@ class CudaDenoiser:
             arr[i] = NamedTensor(nm, dt, rank, shape, ptr)
         return arr, keep
 
+    def output_shape(self, latent_shape) -> tuple:
+        """What predict returns for a latent of this shape: the latent's shape,
+        or for the VAE decoder the [batch, 3, 8h, 8w] image."""
+        d = self.desc
+        if d.family == FAMILY_VAE_KL:
+            up = (d.unet_levels or 4) - 1
+            b, _, h, w = latent_shape
+            return (b, 3, h << up, w << up)
+        return tuple(latent_shape)
+
     def predict(self, latent: np.ndarray, timestep: float, sigma: float, conditioning: dict,
                 out: np.ndarray | None = None) -> np.ndarray:
         """One forward step from host memory (IDenoiser.Predict); `out` may be
-        a caller-owned (e.g. pinned) float32 array of the latent's shape."""
+        a caller-owned (e.g. pinned) float32 array of the output's shape."""
         lat = np.ascontiguousarray(latent, np.float32)
+        shape = self.output_shape(lat.shape)
         if out is None:
-            out = np.empty_like(lat)
-        elif out.shape != lat.shape or out.dtype != np.float32 or not out.flags.c_contiguous:
-            raise ValueError("out must be a contiguous float32 array shaped like the latent")
+            out = np.empty(shape, np.float32)
+        elif out.shape != shape or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise ValueError(f"out must be a contiguous float32 array of shape {shape}")
         arr, keep = self._cond(conditioning, device=False)
         check(_bind().nd_denoiser_predict(self.handle, lat.ctypes.data_as(C.c_void_p), timestep, sigma,
                                           len(conditioning), arr, out.ctypes.data_as(C.c_void_p)))

@@ -527,3 +527,47 @@ def sampler_step(sampler, prediction, out, sample, guidance=1.0, last=None, nois
                                  C.c_double(noise_scale), C.c_double(shrink), C.c_double(weight),
                                  int(bool(second_order)))
     return (s, lst, den) if want_denoised else (s, lst)
+
+
+def vae_decode(w: dict, cfg, latent):
+    """AutoencoderKl.Decoder (Vae/AutoencoderKl.cs:78-116) in fp32, one image
+    at a time: latent [B, 4, h, w] -> image [B, 3, 8h, 8w]."""
+    eps = cfg.eps
+
+    def res(x, p):
+        h = group_norm(x, 32, w[p + ".norm1.weight"], w.get(p + ".norm1.bias"), eps, True)
+        h = conv2d(h, w[p + ".conv1.weight"], w.get(p + ".conv1.bias"))
+        h = group_norm(h, 32, w[p + ".norm2.weight"], w.get(p + ".norm2.bias"), eps, True)
+        h = conv2d(h, w[p + ".conv2.weight"], w.get(p + ".conv2.bias"))
+        if p + ".conv_shortcut.weight" in w:
+            x = conv2d(x, w[p + ".conv_shortcut.weight"], w.get(p + ".conv_shortcut.bias"), 1, 0)
+        return x + h
+
+    def attn(x, p):
+        c, hh, ww = x.shape
+        t = np.ascontiguousarray(group_norm(x, 32, w[p + ".group_norm.weight"], w.get(p + ".group_norm.bias"),
+                                            eps).reshape(c, -1).T)
+        q = linear(t, w[p + ".to_q.weight"], w.get(p + ".to_q.bias"))
+        k = linear(t, w[p + ".to_k.weight"], w.get(p + ".to_k.bias"))
+        v = linear(t, w[p + ".to_v.weight"], w.get(p + ".to_v.bias"))
+        o = linear(attention(q, k, v, 1), w[p + ".to_out.0.weight"], w.get(p + ".to_out.0.bias"))
+        return np.ascontiguousarray(o.T.reshape(c, hh, ww)) + x
+
+    L = len(cfg.mult)
+    outs = []
+    for b in range(latent.shape[0]):
+        x = conv2d(np.asarray(latent[b], np.float32), w["post_quant_conv.weight"], w.get("post_quant_conv.bias"), 1, 0)
+        x = conv2d(x, w["decoder.conv_in.weight"], w.get("decoder.conv_in.bias"))
+        x = res(x, "decoder.mid_block.resnets.0")
+        x = attn(x, "decoder.mid_block.attentions.0")
+        x = res(x, "decoder.mid_block.resnets.1")
+        for i in range(L):
+            for j in range(cfg.layers_per_block + 1):
+                x = res(x, f"decoder.up_blocks.{i}.resnets.{j}")
+            if i != L - 1:
+                x = x.repeat(2, axis=1).repeat(2, axis=2)
+                x = conv2d(x, w[f"decoder.up_blocks.{i}.upsamplers.0.conv.weight"],
+                           w.get(f"decoder.up_blocks.{i}.upsamplers.0.conv.bias"))
+        x = group_norm(x, 32, w["decoder.conv_norm_out.weight"], w.get("decoder.conv_norm_out.bias"), eps, True)
+        outs.append(conv2d(x, w["decoder.conv_out.weight"], w.get("decoder.conv_out.bias")))
+    return np.stack(outs)

@@ -53,6 +53,9 @@ def _dev_weight(wt):
     (2, 8, 16, 192, 320, 1),
     (1, 64, 64, 64, 64, 2),
     (1, 128, 128, 64, 32, 1),
+    (1, 16, 256, 64, 64, 1),    # rows wider than a tile: 128-pixel pieces of a row
+    (1, 8, 512, 128, 32, 2),    # ... with stride 2 (256 output pixels per row)
+    (2, 4, 1024, 64, 64, 1),
 ])
 def test_conv3x3_matches_oracle(cuda, b, h, w, cin, cout, stride):
     x, wt, bias = _conv_case(b, h, w, cin, cout, seed=cin + cout + stride)
