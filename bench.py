@@ -115,7 +115,7 @@ class Clocks:
 def _configs():
     """BASELINE configurations: (model config, workload text, dtype, metric)."""
     from naivediffusion_b200 import _lib
-    from naivediffusion_b200.denoiser import AnimaConfig, MMDiTConfig, UNetConfig, VaeDecoderConfig
+    from naivediffusion_b200.denoiser import AnimaConfig, MMDiTConfig, QwenImageConfig, UNetConfig, VaeDecoderConfig
     return {
         "cfg3": (MMDiTConfig(), "cfg3: Qwen-Image-style MMDiT 60x3072, 24x128 heads, MLP 12288 GELU-tanh, "
                  "5376 img + 256 txt tokens, batch 1, guidance 1", "bf16", METRIC),
@@ -137,6 +137,10 @@ def _configs():
         "vae": (VaeDecoderConfig(), "SDXL VAE decoder (AutoencoderKL 128/256/512/512, 2 layers per block): "
                 "4x128x128 latent -> 3x1024x1024 image, fp16", "f16",
                 "SDXL VAE decode s/image @1024×1024 fp16; images/s"),
+        "qwen21": (QwenImageConfig(), "Qwen-Image 2.1 single-stream DiT (the reference's own QwenImageDit): "
+                   "32x4096, 32x128 heads, SwiGLU 12288, 4096 img + 256 txt tokens (1024x1024), batch 1, "
+                   "fp16 compute (the reference's half-precision option)", "f16",
+                   "Qwen-Image 2.1 DiT s/step @1024×1024 fp16; images/s"),
     }
 
 
@@ -216,7 +220,37 @@ def cpu_anima_sample(cfg, repeats: int = 1, budget_s: float = 150.0):
     return statistics.median(times) * scale, sample, O.threads()
 
 
+def cpu_qwen_image_sample(cfg, repeats: int = 1, budget_s: float = 150.0):
+    """One full-size Qwen-Image 2.1 block (with the embeddings and the final
+    layer) through the CPU oracle's step, extrapolated by FLOPs to the whole
+    step."""
+    import numpy as np
+    import oracle as O
+    from dataclasses import replace
+    from naivediffusion_b200.denoiser import synthetic_weights
+    one = replace(cfg, blocks=1)
+    w = dict(synthetic_weights(one, seed=0))
+    rng = np.random.default_rng(0)
+    lat = rng.standard_normal((1, one.latent_channels, one.latent_height, one.latent_width)).astype(np.float32)
+    ctx = rng.standard_normal((one.context_rows, one.context_width)).astype(np.float32)
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(max(1, repeats)):
+        t0 = time.perf_counter()
+        O.qwen_image_forward(w, one, lat, ctx, 0.5)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    scale = cfg.flops_per_step() / one.flops_per_step()
+    sample = (f"one full-size Qwen-Image 2.1 block ({one.tokens} tokens, width {one.width}) with the embeddings "
+              f"and final layer through the CPU oracle's step, median of {len(times)}, extrapolated x{scale:.1f} "
+              f"by FLOPs to the {cfg.blocks}-block step")
+    return statistics.median(times) * scale, sample, O.threads()
+
+
 def cpu_sample(name, cfg, repeats=1, budget_s=150.0):
+    if name == "qwen21":
+        return cpu_qwen_image_sample(cfg, repeats, budget_s)
     if name in ("cfg3", "cfg4"):
         return cpu_block_sample(cfg, repeats, budget_s)
     if name in ("cfg1", "cfg2"):
@@ -401,7 +435,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["cfg3", "cfg1", "cfg2", "cfg4", "cfg5", "vae"], default="cfg3",
+    ap.add_argument("--config", choices=["cfg3", "cfg1", "cfg2", "cfg4", "cfg5", "vae", "qwen21"], default="cfg3",
                     help="BASELINE configuration (default cfg3, the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle sample")
     args = ap.parse_args()

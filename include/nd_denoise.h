@@ -78,6 +78,12 @@ ND_API const char* nd_version(void);
                                scaling factor) and returns the [batch, 3, 8h, 8w] image;
                                width = base channels, unet_mult = block_out_channels /
                                width, unet_resnets = layers_per_block; no conditioning */
+#define ND_FAMILY_QWEN_IMAGE 4 /* Qwen-Image 2.1 single-stream DiT (Models/QwenImage/
+                               QwenImageDit.cs): image rows then text rows through
+                               shared weights, one modulation for every block (the
+                               noise level's row for image rows, time zero's for text
+                               rows), SwiGLU feed-forward, image queries over every
+                               visible key, text queries causal over the text; patch 1 */
 
 typedef struct nd_device nd_device;
 typedef struct nd_denoiser nd_denoiser;
@@ -172,6 +178,15 @@ ND_API int nd_denoiser_finalize(nd_denoiser* d);
  *          "cos", "sin" [image tokens + rows, 64] f32 (default: the
  *          reference's Qwen-Image rotary tables with text length = rows);
  *          "key_length" i32 [1] (visible keys; default all).
+ *   QWEN_IMAGE (QwenImageConditioning, Models/QwenImage/QwenImageConditioner.cs):
+ *          "context" [1, rows, context_width] f32 (required, zero-padded rows);
+ *          "key_length" i32 [1] = image tokens + real text rows (default all);
+ *          "text_mask" i32 [rows, rows] (optional; must be the causal table
+ *          closed over the padding for that real length: row i reads key j
+ *          iff j <= i and j < real; checked when given in host memory);
+ *          "cos", "sin" [image tokens + rows, 64] f32 (default: the
+ *          reference's tables with text length = the real rows).
+ *   SDXL: "context" [batch, 77, 2048], "add" [batch, 2816] f32.
  * Synchronous. */
 ND_API int nd_denoiser_predict(nd_denoiser* d, const float* latent, double timestep, double sigma,
                                int n_cond, const nd_named_tensor* cond, float* out);
@@ -212,7 +227,11 @@ ND_API int nd_denoiser_destroy(nd_denoiser* d);
  *
  * Row groups: rows >= group_split use weight rows [out, 2*out) and the
  * second half of bias / gate / qk_norm (a dual-stream block's text rows).
- * group_split must be a multiple of 128 or >= rows (one group). */
+ * group_split must be a multiple of 128 or >= rows (one group). With
+ * shared_weights = 1 every row reads weight rows [0, out) and only bias and
+ * gate differ per group, chosen per row (a single-stream block's image and
+ * text rows under their own modulation), so group_split may be any row;
+ * QK_NORM_ROPE then uses the first group's bias and norm weights. */
 #define ND_EPI_STORE 0           /* y = acc + bias                          */
 #define ND_EPI_GELU_TANH 1       /* y = gelu_tanh(acc + bias)               */
 #define ND_EPI_GELU_ERF 2        /* y = gelu(acc + bias), exact             */
@@ -222,6 +241,11 @@ ND_API int nd_denoiser_destroy(nd_denoiser* d);
 #define ND_EPI_QK_NORM_ROPE 6    /* cols < qk_cols: head RMSNorm * w, RoPE  */
 #define ND_EPI_RESIDUAL_ADD 7    /* residual(f32) += acc + bias             */
 #define ND_EPI_ADD_STORE 8       /* y = acc + bias + addend (like y)        */
+#define ND_EPI_SWIGLU 9          /* y[:, j] = silu(g_j + bias_j) * (u_j + bias_F+j),
+                                    g = x W[0:F]^T, u = x W[F:2F]^T: W is the
+                                    fused [gate; up] matrix [2F, in], out_features
+                                    = F (a multiple of 128), bias [2F] or NULL
+                                    (QwenImageDit.FeedForward) */
 
 typedef struct nd_linear_args {
   int dtype;            /* ND_BF16 or ND_F16: x, W and y. ND_BF16X2 (fp32
@@ -267,6 +291,7 @@ typedef struct nd_linear_args {
   int64_t rope_period;
   const void* addend;   /* ADD_STORE: [rows, ld_add], dtype like y */
   int64_t ld_add;
+  int shared_weights;   /* 1: one weight matrix for both row groups (see above) */
 } nd_linear_args;
 
 /* ------------------------------------------------------------ conv op

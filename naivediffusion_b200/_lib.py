@@ -34,6 +34,7 @@ ND_EPI_STORE_F32 = 5
 ND_EPI_QK_NORM_ROPE = 6
 ND_EPI_RESIDUAL_ADD = 7
 ND_EPI_ADD_STORE = 8
+ND_EPI_SWIGLU = 9
 
 
 class NdError(RuntimeError):
@@ -57,7 +58,7 @@ class LinearArgs(C.Structure):
         ("qk_cols", C.c_int64), ("eps", C.c_float),
         ("weight_dtype", C.c_int), ("scales", C.c_void_p), ("scale_dtype", C.c_int),
         ("quant_group", C.c_int64), ("norm_span", C.c_int64), ("rope_period", C.c_int64),
-        ("addend", C.c_void_p), ("ld_add", C.c_int64),
+        ("addend", C.c_void_p), ("ld_add", C.c_int64), ("shared_weights", C.c_int),
     ]
 
 

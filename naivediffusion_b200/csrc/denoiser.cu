@@ -97,11 +97,41 @@ int convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n,
   return ND_OK;
 }
 
+// dst row r = src row of the same head at feature 2f (f < half) or
+// 2(f - half) + 1 (QwenImageDit.PairsToHalves, Models/QwenImage/QwenImageDit.cs:261-279).
+__global__ void permute_head_rows_kernel(const void* __restrict__ src, void* __restrict__ dst, int64_t rows,
+                                         int64_t cols, int elem_bytes, int head) {
+  const int64_t n = rows * cols;
+  const int half = head / 2;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, c = i - r * cols;
+    const int64_t base = r - r % head;
+    const int f = static_cast<int>(r - base);
+    const int64_t from = base + (f < half ? 2 * f : 2 * (f - half) + 1);
+    if (elem_bytes == 2)
+      static_cast<uint16_t*>(dst)[i] = static_cast<const uint16_t*>(src)[from * cols + c];
+    else
+      static_cast<uint32_t*>(dst)[i] = static_cast<const uint32_t*>(src)[from * cols + c];
+  }
+}
+
 int permute_conv3x3(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t cout, int cin,
                     int cin_pad, cudaStream_t s) {
   const int64_t n = cout * 9 * cin_pad;
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, sm_count() * 8LL));
   permute_conv_kernel<<<grid, 256, 0, s>>>(src, src_dtype, dst, dst_dtype, cout, cin, cin_pad);
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+int permute_head_rows(const void* src, void* dst, int64_t rows, int64_t cols, int elem_bytes, int head,
+                      cudaStream_t s) {
+  const int64_t n = rows * cols;
+  if (n <= 0) return ND_OK;
+  if (elem_bytes != 2 && elem_bytes != 4) return fail(ND_ERR_INVALID, "permute_head_rows: element size");
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, sm_count() * 8LL));
+  permute_head_rows_kernel<<<grid, 256, 0, s>>>(src, dst, rows, cols, elem_bytes, head);
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }
@@ -140,6 +170,7 @@ nd_denoiser::~nd_denoiser() {
   for (void* p : host_allocations) cudaFreeHost(p);
   if (staged) cudaEventDestroy(staged);
   if (staging) cudaFree(staging);
+  if (staging2) cudaFree(staging2);
 }
 
 void* nd_denoiser::pinned(size_t bytes) {
@@ -200,6 +231,25 @@ void nd_denoiser::add_slot(const std::string& name, int kind, int64_t rows, int6
 
 namespace {
 
+// Grow a device buffer (kept between calls) to at least `bytes`.
+int grow(void** buf, size_t* have, size_t bytes) {
+  if (*have >= bytes) return ND_OK;
+  if (*buf) cudaFree(*buf);
+  *buf = nullptr;
+  *have = 0;
+  ND_CUDA(cudaMalloc(buf, bytes));
+  *have = bytes;
+  return ND_OK;
+}
+
+// Copy a host tensor into the denoiser's device staging buffer.
+int upload_staging(nd_denoiser* d, const void* data, size_t bytes, cudaStream_t st, const void** src) {
+  ND_TRY_RC(grow(&d->staging, &d->staging_bytes, bytes));
+  ND_CUDA(cudaMemcpyAsync(d->staging, data, bytes, cudaMemcpyHostToDevice, st));
+  *src = d->staging;
+  return ND_OK;
+}
+
 int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* shape, int rank,
                     const void* data, bool device) {
   using namespace nd;
@@ -223,6 +273,26 @@ int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* 
     return fail(ND_ERR_INVALID, std::string("set_weight: ") + name + " has the wrong shape (expected [" +
                                     std::to_string(s.rows) + ", " + std::to_string(s.src_cols > s.cols ? s.src_cols : s.cols) + "])");
   }
+  if (s.head_perm > 0) {
+    // Reorder the rows within each head (pairs -> halves) into a second
+    // device buffer, then store that copy the usual way.
+    const int64_t rows = rank >= 1 ? shape[0] : 1;
+    const int64_t cols = rows > 0 ? n / rows : 0;
+    if (rows % s.head_perm != 0 || s.head_perm % 2 != 0)
+      return fail(ND_ERR_INVALID, std::string("set_weight: ") + name + " rows do not divide into heads");
+    DeviceGuard g(d->dev->ordinal);
+    cudaStream_t st = d->dev->stream;
+    const size_t src_bytes = static_cast<size_t>(n) * elem_bytes(dtype);
+    const void* src = data;
+    if (!device) ND_TRY_RC(upload_staging(d, data, src_bytes, st, &src));
+    ND_TRY_RC(grow(&d->staging2, &d->staging2_bytes, src_bytes));
+    ND_TRY_RC(permute_head_rows(src, d->staging2, rows, cols, static_cast<int>(elem_bytes(dtype)), s.head_perm, st));
+    const int head = s.head_perm;
+    s.head_perm = 0;
+    const int rc = set_weight_impl(d, name, dtype, shape, rank, d->staging2, true);
+    s.head_perm = head;
+    return rc;
+  }
   if (s.kind == kConv3x3) {
     if (!(rank == 4 && shape[0] == s.rows && shape[1] == s.conv_cin && shape[2] == 3 && shape[3] == 3))
       return fail(ND_ERR_INVALID, std::string("set_weight: ") + name + " must be [" + std::to_string(s.rows) +
@@ -231,17 +301,7 @@ int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* 
     cudaStream_t st = d->dev->stream;
     const size_t src_bytes = static_cast<size_t>(n) * elem_bytes(dtype);
     const void* src = data;
-    if (!device) {
-      if (d->staging_bytes < src_bytes) {
-        if (d->staging) cudaFree(d->staging);
-        d->staging = nullptr;
-        d->staging_bytes = 0;
-        ND_CUDA(cudaMalloc(&d->staging, src_bytes));
-        d->staging_bytes = src_bytes;
-      }
-      ND_CUDA(cudaMemcpyAsync(d->staging, data, src_bytes, cudaMemcpyHostToDevice, st));
-      src = d->staging;
-    }
+    if (!device) ND_TRY_RC(upload_staging(d, data, src_bytes, st, &src));
     int rc = permute_conv3x3(src, dtype, s.dst, d->desc.compute, s.rows, s.conv_cin,
                              static_cast<int>(s.cols / 9), st);
     if (rc) return rc;
@@ -255,17 +315,7 @@ int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* 
     cudaStream_t st = d->dev->stream;
     const size_t src_bytes = static_cast<size_t>(n) * elem_bytes(dtype);
     const void* src = data;
-    if (!device) {
-      if (d->staging_bytes < src_bytes) {
-        if (d->staging) cudaFree(d->staging);
-        d->staging = nullptr;
-        d->staging_bytes = 0;
-        ND_CUDA(cudaMalloc(&d->staging, src_bytes));
-        d->staging_bytes = src_bytes;
-      }
-      ND_CUDA(cudaMemcpyAsync(d->staging, data, src_bytes, cudaMemcpyHostToDevice, st));
-      src = d->staging;
-    }
+    if (!device) ND_TRY_RC(upload_staging(d, data, src_bytes, st, &src));
     int rc = convert_cols(src, dtype, s.src_cols, s.dst, d->mat_dtype(), s.rows, s.cols, st);
     if (rc) return rc;
     ND_CUDA(cudaStreamSynchronize(st));
@@ -279,17 +329,7 @@ int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* 
   if (s.scales) {
     // int8 storage: quantize on the device (BlockQuantizer's rules).
     const void* src = data;
-    if (!device) {
-      if (d->staging_bytes < src_bytes) {
-        if (d->staging) cudaFree(d->staging);
-        d->staging = nullptr;
-        d->staging_bytes = 0;
-        ND_CUDA(cudaMalloc(&d->staging, src_bytes));
-        d->staging_bytes = src_bytes;
-      }
-      ND_CUDA(cudaMemcpyAsync(d->staging, data, src_bytes, cudaMemcpyHostToDevice, st));
-      src = d->staging;
-    }
+    if (!device) ND_TRY_RC(upload_staging(d, data, src_bytes, st, &src));
     int rc = quantize_weights(src, dtype, s.rows, s.cols, d->qgroup(s.cols), d->qf16() ? 1 : 0,
                               static_cast<int8_t*>(s.dst), s.scales, st);
     if (rc) return rc;
@@ -301,17 +341,7 @@ int set_weight_impl(nd_denoiser* d, const char* name, int dtype, const int64_t* 
     ND_CUDA(cudaMemcpyAsync(s.dst, data, src_bytes, device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
   } else {
     const void* src = data;
-    if (!device) {
-      if (d->staging_bytes < src_bytes) {
-        if (d->staging) cudaFree(d->staging);
-        d->staging = nullptr;
-        d->staging_bytes = 0;
-        ND_CUDA(cudaMalloc(&d->staging, src_bytes));
-        d->staging_bytes = src_bytes;
-      }
-      ND_CUDA(cudaMemcpyAsync(d->staging, data, src_bytes, cudaMemcpyHostToDevice, st));
-      src = d->staging;
-    }
+    if (!device) ND_TRY_RC(upload_staging(d, data, src_bytes, st, &src));
     int rc = dst_type == ND_BF16X2 ? convert_cols(src, dtype, s.cols, s.dst, dst_type, s.rows, s.cols, st)
                                    : convert(src, dtype, s.dst, dst_type, n, st);
     if (rc) return rc;
@@ -418,6 +448,7 @@ int nd_denoiser_create(nd_device* dev, const nd_model_desc* desc, nd_denoiser** 
     case ND_FAMILY_ANIMA: d = nd::make_anima(); break;
     case ND_FAMILY_SDXL: d = nd::make_unet(); break;
     case ND_FAMILY_VAE_KL: d = nd::make_vae_decoder(); break;
+    case ND_FAMILY_QWEN_IMAGE: d = nd::make_qwen_image(); break;
     default: return nd::fail(ND_ERR_UNSUPPORTED, "nd_denoiser_create: unknown model family");
   }
   d->dev = dev;
@@ -488,6 +519,11 @@ int nd_denoiser_finalize(nd_denoiser* d) {
     cudaFree(d->staging);
     d->staging = nullptr;
     d->staging_bytes = 0;
+  }
+  if (d->staging2) {
+    cudaFree(d->staging2);
+    d->staging2 = nullptr;
+    d->staging2_bytes = 0;
   }
   int rc = d->prepare();
   if (rc) return rc;

@@ -34,6 +34,10 @@ struct WeightSlot {
   void* scales = nullptr;  // int8 matrices: their scales (quant_group / scale type of the model)
   int64_t src_cols = 0;    // > cols: the checkpoint tensor is wider; keep its first `cols` columns
   int conv_cin = 0;        // kConv3x3: torch [rows, conv_cin, 3, 3] stored as [rows, 3, 3, cols / 9]
+  // > 0: rows are features of heads this wide, reordered on upload from
+  // adjacent pairs (2i, 2i+1) to halves (i, half + i), so the rotate-half
+  // RoPE turns the pairs the checkpoint's model turns.
+  int head_perm = 0;
   bool required = true;
   bool set = false;
 };
@@ -70,6 +74,10 @@ int convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n,
 // torch conv weights [cout, cin, 3, 3] -> [cout, 3, 3, cin_pad] (zero padded).
 int permute_conv3x3(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t cout, int cin,
                     int cin_pad, cudaStream_t s);
+// Rows of a row-major [rows, cols] src (elem_bytes each) reordered within
+// every `head` rows from pairs to halves (QwenImageDit.PairsToHalves).
+int permute_head_rows(const void* src, void* dst, int64_t rows, int64_t cols, int elem_bytes, int head,
+                      cudaStream_t s);
 // Rows x cols of a row-major src (leading dimension src_ld) into a packed dst.
 int convert_cols(const void* src, int src_dtype, int64_t src_ld, void* dst, int dst_dtype, int64_t rows,
                  int64_t cols, cudaStream_t s);
@@ -89,6 +97,8 @@ struct nd_denoiser {
   bool finalized = false;
   void* staging = nullptr;
   size_t staging_bytes = 0;
+  void* staging2 = nullptr;  // the permuted copy of a head_perm slot's tensor
+  size_t staging2_bytes = 0;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   int graph_key = -1;  // key_limit the captured graph was built for
@@ -151,4 +161,5 @@ nd_denoiser* make_mmdit();
 nd_denoiser* make_anima();
 nd_denoiser* make_unet();
 nd_denoiser* make_vae_decoder();
+nd_denoiser* make_qwen_image();
 }  // namespace nd

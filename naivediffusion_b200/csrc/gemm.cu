@@ -74,10 +74,15 @@ int linear_split(const nd_linear_args& a, cudaStream_t stream) {
   if (!a.x || !a.weight) return fail(ND_ERR_INVALID, "linear: null operand");
   if (a.ldx < 2 * a.in_features || a.ldx % 8) return fail(ND_ERR_INVALID, "linear: bf16x2 x needs ldx >= 2 * in_features, ldx % 8 == 0");
   const bool split = a.group_split < a.rows;
-  if (split && (a.group_split % 128 != 0 || a.group_split <= 0))
-    return fail(ND_ERR_INVALID, "linear: group_split must be a positive multiple of 128");
+  const bool shared = a.shared_weights != 0;
+  if (split && a.group_split <= 0) return fail(ND_ERR_INVALID, "linear: group_split must be positive");
+  if (split && !shared && a.group_split % 128 != 0)
+    return fail(ND_ERR_INVALID, "linear: group_split must be a multiple of 128 (or give shared_weights)");
   const int epi = a.epilogue;
-  if (epi < 0 || epi > ND_EPI_RESIDUAL_ADD) return fail(ND_ERR_INVALID, "linear: unknown epilogue (ADD_STORE is not offered for bf16x2)");
+  if (epi < 0 || epi > ND_EPI_SWIGLU || epi == ND_EPI_ADD_STORE)
+    return fail(ND_ERR_INVALID, "linear: unknown epilogue (ADD_STORE is not offered for bf16x2)");
+  const bool swiglu = epi == ND_EPI_SWIGLU;
+  if (swiglu && a.out_features % 128) return fail(ND_ERR_INVALID, "linear: SWIGLU needs out_features % 128 == 0");
   const bool resid = epi == ND_EPI_RESIDUAL_GATE || epi == ND_EPI_RESIDUAL_ADD || epi == ND_EPI_STORE_F32;
   const bool qk = epi == ND_EPI_QK_NORM_ROPE;
   if (resid && (!a.residual || a.ldr < a.out_features || a.ldr % 4 != 0 || (reinterpret_cast<uintptr_t>(a.residual) & 15u)))
@@ -107,7 +112,7 @@ int linear_split(const nd_linear_args& a, cudaStream_t stream) {
   if (a.out_features % 4 != 0 && (a.bias || a.gate))
     return fail(ND_ERR_INVALID, "linear: bias/gate need out_features % 4 == 0");
 
-  const int groups = split ? 2 : 1;
+  const int groups = split && !shared ? 2 : 1;
   const int64_t K2 = 2 * a.in_features;
   CUtensorMap ta, tb, tc;
   int rc = make_tmap_2d(&ta, a.x, 2, a.rows, K2, a.ldx, 128, 64, true);
@@ -119,8 +124,11 @@ int linear_split(const nd_linear_args& a, cudaStream_t stream) {
 
   GemmArgs g{};
   g.M = static_cast<int>(a.rows);
-  g.N = static_cast<int>(a.out_features);
+  g.N = static_cast<int>(swiglu ? 2 * a.out_features : a.out_features);
   g.K = static_cast<int>(a.in_features);
+  g.swiglu_half = swiglu ? static_cast<int>(a.out_features) : 0;
+  g.shared_weights = shared ? 1 : 0;
+  g.row_groups = shared && split ? 1 : 0;
   g.split_kb = static_cast<int>(a.in_features / 64);
   g.split_koff = static_cast<int>(a.in_features);
   g.out_kind = resid ? 0 : (qk ? 2 : 1);
@@ -131,7 +139,7 @@ int linear_split(const nd_linear_args& a, cudaStream_t stream) {
   g.resid = a.residual;
   g.ldr = a.ldr;
   g.bias = a.bias;
-  g.bias_stride = static_cast<int>(a.out_features);
+  g.bias_stride = static_cast<int>(swiglu ? 2 * a.out_features : a.out_features);
   g.gate = a.gate;
   g.gate_stride = static_cast<int>(a.gate_stride > 0 ? a.gate_stride : a.out_features);
   if (a.gate && (g.gate_stride % 4 != 0 || (reinterpret_cast<uintptr_t>(a.gate) & 15u)))
@@ -149,10 +157,11 @@ int linear_split(const nd_linear_args& a, cudaStream_t stream) {
   if (!g.status) return fail(ND_ERR_CUDA, "linear: no device status word");
 
   const int sms = sm_count();
-  const int64_t tiles256 = ((a.rows + 127) / 128) * ((a.out_features + 255) / 256);
-  const int bn = (qk || (a.out_features >= 256 && tiles256 >= sms)) ? 256 : 128;
+  const int64_t n_all = g.N;
+  const int64_t tiles256 = ((a.rows + 127) / 128) * ((n_all + 255) / 256);
+  const int bn = (qk || (n_all >= 256 && tiles256 >= sms)) ? 256 : 128;
   g.idesc = make_idesc_f16(128, bn, true);
-  rc = make_tmap_2d(&tb, a.weight, 2, groups * a.out_features, K2, K2, bn, 64, true);
+  rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, K2, K2, swiglu ? bn / 2 : bn, 64, true);
   if (rc) return rc;
   if (bn == 256) return launch_gemm<256, 4>(ta, tb, tc, g, stream);
   return launch_gemm<128, 6>(ta, tb, tc, g, stream);
@@ -182,11 +191,15 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
   if (a.ldx < a.in_features || a.ldx % 8 != 0) return fail(ND_ERR_INVALID, "linear: ldx must be >= in_features and a multiple of 8");
   if (!a.x || !a.weight) return fail(ND_ERR_INVALID, "linear: null operand");
   const bool split = a.group_split < a.rows;
-  if (split && (a.group_split % 128 != 0 || a.group_split <= 0))
-    return fail(ND_ERR_INVALID, "linear: group_split must be a positive multiple of 128");
+  const bool shared = a.shared_weights != 0;
+  if (split && a.group_split <= 0) return fail(ND_ERR_INVALID, "linear: group_split must be positive");
+  if (split && !shared && a.group_split % 128 != 0)
+    return fail(ND_ERR_INVALID, "linear: group_split must be a multiple of 128 (or give shared_weights)");
   const int epi = a.epilogue;
   const bool resid = epi == ND_EPI_RESIDUAL_GATE || epi == ND_EPI_RESIDUAL_ADD || epi == ND_EPI_STORE_F32;
-  if (epi < 0 || epi > ND_EPI_ADD_STORE) return fail(ND_ERR_INVALID, "linear: unknown epilogue");
+  if (epi < 0 || epi > ND_EPI_SWIGLU) return fail(ND_ERR_INVALID, "linear: unknown epilogue");
+  const bool swiglu = epi == ND_EPI_SWIGLU;
+  if (swiglu && a.out_features % 128) return fail(ND_ERR_INVALID, "linear: SWIGLU needs out_features % 128 == 0");
   if (epi == ND_EPI_ADD_STORE && (!a.addend || a.ld_add < a.out_features || a.ld_add % 8 != 0))
     return fail(ND_ERR_INVALID, "linear: ADD_STORE needs addend with ld_add >= out_features, ld_add % 8 == 0");
   if (resid && (!a.residual || a.ldr < a.out_features || a.ldr % 4 != 0))
@@ -211,7 +224,7 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
   if (a.out_features % 4 != 0 && (a.bias || a.gate))
     return fail(ND_ERR_INVALID, "linear: bias/gate need out_features % 4 == 0");
 
-  const int groups = split ? 2 : 1;
+  const int groups = split && !shared ? 2 : 1;
   CUtensorMap ta, tb, tc;
   int rc = make_tmap_2d(&ta, a.x, 2, a.rows, a.in_features, a.ldx, 128, 64, true);
   if (rc) return rc;
@@ -228,8 +241,11 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
 
   GemmArgs g{};
   g.M = static_cast<int>(a.rows);
-  g.N = static_cast<int>(a.out_features);
+  g.N = static_cast<int>(swiglu ? 2 * a.out_features : a.out_features);
   g.K = static_cast<int>(a.in_features);
+  g.swiglu_half = swiglu ? static_cast<int>(a.out_features) : 0;
+  g.shared_weights = shared ? 1 : 0;
+  g.row_groups = shared && split ? 1 : 0;
   g.group_split = split ? static_cast<int>(a.group_split) : INT_MAX;
   g.epi = epi;
   g.out_f16 = a.dtype == ND_F16;
@@ -238,7 +254,7 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
   g.resid = a.residual;
   g.ldr = a.ldr;
   g.bias = a.bias;
-  g.bias_stride = static_cast<int>(a.out_features);
+  g.bias_stride = static_cast<int>(swiglu ? 2 * a.out_features : a.out_features);
   g.gate = a.gate;
   g.gate_stride = static_cast<int>(a.gate_stride > 0 ? a.gate_stride : a.out_features);
   if (a.gate && (g.gate_stride % 4 != 0 || (reinterpret_cast<uintptr_t>(a.gate) & 15u)))
@@ -268,18 +284,20 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
   // (narrow outputs, few rows); then 128. (A 192-wide variant filled the last
   // wave better at N = 3072 but measured slower per tile on B200.)
   const int sms = sm_count();
-  const int64_t tiles256 = ((a.rows + 127) / 128) * ((a.out_features + 255) / 256);
-  const int bn = (epi == ND_EPI_QK_NORM_ROPE || (a.out_features >= 256 && tiles256 >= sms)) ? 256 : 128;
+  const int64_t n_all = g.N;
+  const int64_t tiles256 = ((a.rows + 127) / 128) * ((n_all + 255) / 256);
+  const int bn = (epi == ND_EPI_QK_NORM_ROPE || (n_all >= 256 && tiles256 >= sms)) ? 256 : 128;
   g.idesc = make_idesc_f16(128, bn, a.dtype == ND_BF16);
   if (w8) {
     // Raw int8 tiles [bn rows x 64 bytes], unswizzled (the converters swizzle).
-    rc = make_tmap_2d_typed(&tb, a.weight, ND_I8, groups * a.out_features, a.in_features, a.in_features,
-                            bn, 64, 0);
+    rc = make_tmap_2d_typed(&tb, a.weight, ND_I8, groups * n_all, a.in_features, a.in_features,
+                            swiglu ? bn / 2 : bn, 64, 0);
     if (rc) return rc;
     if (bn == 256) return launch_gemm_w8<256, 4>(ta, tb, tc, g, stream);
     return launch_gemm_w8<128, 6>(ta, tb, tc, g, stream);
   }
-  rc = make_tmap_2d(&tb, a.weight, 2, groups * a.out_features, a.in_features, a.in_features, bn, 64, true);
+  rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, a.in_features, a.in_features, swiglu ? bn / 2 : bn, 64,
+                    true);
   if (rc) return rc;
   if (bn == 256) return launch_gemm<256, 4>(ta, tb, tc, g, stream);
   return launch_gemm<128, 6>(ta, tb, tc, g, stream);

@@ -34,6 +34,7 @@ enum GemmEpilogue : int {
   kEpiQkNormRope = 6,     // columns < qk_cols: per-head RMSNorm * w, then RoPE
   kEpiResidualAdd = 7,    // resid(f32) += acc + bias
   kEpiAddStore = 8,       // out = acc + bias + addend[row, col]     (bf16/f16)
+  kEpiSwiGlu = 9,         // out[:, j] = silu(gate_j) * up_j  (W = [gate rows; up rows])
 };
 
 struct GemmArgs {
@@ -84,6 +85,16 @@ struct GemmArgs {
   int split_kb;     // 0: plain operands
   int split_koff;
   int out_kind;     // 0: bf16/f16 out, 1: hi|lo pair out (lo at column + N), 2: fp32 out
+  // kEpiSwiGlu: W is [gate rows; up rows] with the up rows starting at row
+  // swiglu_half (= the output width F; N = 2F). Tile nt loads gate rows
+  // [nt*BN/2, +BN/2) into the first half of its B tile and the matching up
+  // rows into the second, so the epilogue finds both operands of output
+  // column j in one accumulator.
+  int swiglu_half;
+  // Bias / gate group chosen per row (rows >= group_split take the second
+  // vectors) with one weight matrix for every row: a single-stream block
+  // whose image and text rows differ only in their modulation.
+  int row_groups;
 };
 
 // Tile order of the persistent loop: bands of kTileBandM row tiles, each
@@ -226,6 +237,7 @@ __device__ __forceinline__ void emit_chunk(const CUtensorMap* tm, int kind, uint
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, const CUtensorMap* tmC, int group,
                                                int row0, int col, const uint32_t (&r)[32],
                                                uint32_t buf0, int& sb, int lane) {
+  if (a.row_groups) group = (row0 + lane) >= a.group_split ? 1 : 0;
   float v[32];
   float b[32];
   load_vec32(a.bias ? a.bias + group * a.bias_stride : nullptr, col, a.N, b);
@@ -291,6 +303,36 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, const CUtensor
       break;
   }
   emit_chunk(tmC, kind, buf0, sb, lane, row0, a.M, col, v, a.N);
+}
+
+// SwiGLU over one tile: output columns [ocol0, ocol0 + half) from the gate
+// accumulator columns [0, half) and the up columns [half, 2 * half), biases
+// at bias[j] (gate) and bias[F + j] (up) -- QwenImageDit.FeedForward's
+// Silu(gate) * up (Models/QwenImage/QwenImageDit.cs:386-403) where the two
+// products already sit.
+template <int HALF>
+__device__ __forceinline__ void epilogue_swiglu(const GemmArgs& a, const CUtensorMap* tmC, int group,
+                                                int row0, int ocol0, uint32_t tbase, uint32_t buf0,
+                                                int& sb, int lane) {
+  const int F = a.swiglu_half;
+  if (a.row_groups) group = (row0 + lane) >= a.group_split ? 1 : 0;
+  const float* bias = a.bias ? a.bias + group * a.bias_stride : nullptr;
+#pragma unroll 1
+  for (int c = 0; c < HALF / 32; ++c) {
+    const int ocol = ocol0 + c * 32;
+    if (ocol >= F) break;
+    uint32_t rg[32], ru[32];
+    tmem_ld32(tbase + c * 32, rg);
+    tmem_ld32(tbase + HALF + c * 32, ru);
+    tmem_ld_wait();
+    float bg[32], bu[32], v[32];
+    load_vec32(bias, ocol, F, bg);
+    load_vec32(bias ? bias + F : nullptr, ocol, F, bu);
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      v[i] = silu(__uint_as_float(rg[i]) + bg[i]) * (__uint_as_float(ru[i]) + bu[i]);
+    emit_chunk(tmC, out_emit_kind(a), buf0, sb, lane, row0, a.M, ocol, v, F);
+  }
 }
 
 // The Q/K projection epilogue for one 128-wide head: RMSNorm over the head's
@@ -420,6 +462,16 @@ __global__ void __launch_bounds__(192, 1)
         const int n0 = nt * BN;
         const int group = row_group(args, m0);
         const int brow = (args.shared_weights ? 0 : group * args.N) + n0;
+        // The tile's W rows: one box of BN rows, or (SwiGLU) BN/2 gate rows
+        // and the BN/2 matching up rows, each box BN/2 rows high.
+        auto load_b = [&](uint32_t dst, int kcol, uint32_t bar) {
+          if (!CONV && args.swiglu_half > 0) {
+            tma_load_2d(dst, &tmB, bar, kcol, nt * (BN / 2));
+            tma_load_2d(dst + (BN / 2) * 128, &tmB, bar, kcol, args.swiglu_half + nt * (BN / 2));
+          } else {
+            tma_load_2d(dst, &tmB, bar, kcol, brow);
+          }
+        };
         int img = 0, y0 = 0, x0 = 0;
         if constexpr (CONV) {
           img = m0 / args.conv_hw;
@@ -453,11 +505,11 @@ __global__ void __launch_bounds__(192, 1)
             const int seg = kb / args.split_kb;
             const int kc = (kb - seg * args.split_kb) * 64;
             tma_load_2d(a_dst, &tmA, full_bar(stage), kc + (seg == 1 ? args.split_koff : 0), m0);
-            tma_load_2d(b_dst, &tmB, full_bar(stage), kc + (seg == 0 ? args.split_koff : 0), brow);
+            load_b(b_dst, kc + (seg == 0 ? args.split_koff : 0), full_bar(stage));
           } else {
             tma_load_2d(a_dst, &tmA, full_bar(stage), kb * 64, m0);
           }
-          if (CONV || args.split_kb == 0) tma_load_2d(b_dst, &tmB, full_bar(stage), kb * 64, brow);
+          if (CONV || args.split_kb == 0) load_b(b_dst, kb * 64, full_bar(stage));
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -541,13 +593,17 @@ __global__ void __launch_bounds__(192, 1)
       tile_coords(t, num_m, num_n, mt, nt);
       const int m0 = mt * 128;
       const int n0 = nt * BN;
-      const int group = row_group(args, m0);
+      // row_groups: the plain and SwiGLU epilogues pick the vectors per row;
+      // the head norm uses the one shared set.
+      const int group = args.row_groups ? 0 : row_group(args, m0);
       const int row0 = m0 + ew * 32;
       const int row = m0 + row_in_tile;
       const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
 
-      if (args.epi == kEpiQkNormRope) {
+      if (args.epi == kEpiSwiGlu) {
+        epilogue_swiglu<BN / 2>(args, &tmC, group, row0, nt * (BN / 2), tbase, buf0, sb, lane);
+      } else if (args.epi == kEpiQkNormRope) {
 #pragma unroll 1
         for (int h = 0; h < BN / 128; ++h) {
           const int col0 = n0 + h * 128;

@@ -149,7 +149,14 @@ __global__ void __launch_bounds__(kW8Threads, 1)
           }
           mbar_arrive_expect_tx(full_bar(stage), L::kABytes + L::kRawBytes);
           tma_load_2d(a_buf(stage), &tmA, full_bar(stage), kb * 64, m0);
-          tma_load_2d(raw_buf(stage), &tmW, full_bar(stage), kb * 64, brow);
+          if (args.swiglu_half > 0) {
+            // BN/2 gate rows, then the matching BN/2 up rows (boxes BN/2 high)
+            tma_load_2d(raw_buf(stage), &tmW, full_bar(stage), kb * 64, nt * (BN / 2));
+            tma_load_2d(raw_buf(stage) + (BN / 2) * 64, &tmW, full_bar(stage), kb * 64,
+                        args.swiglu_half + nt * (BN / 2));
+          } else {
+            tma_load_2d(raw_buf(stage), &tmW, full_bar(stage), kb * 64, brow);
+          }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -237,6 +244,13 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       const int n0 = nt * BN;
       const int group = row_group(args, m0);
       const long long wrow0 = (args.shared_weights ? 0LL : static_cast<long long>(group) * args.N) + n0;
+      // W row of tile row r (SwiGLU: gate rows, then the matching up rows)
+      auto wrow_of = [&](int r) -> long long {
+        if (args.swiglu_half > 0)
+          return (r < BN / 2 ? 0LL : static_cast<long long>(args.swiglu_half) - BN / 2) +
+                 static_cast<long long>(nt) * (BN / 2) + r;
+        return wrow0 + r;
+      };
       auto load_scale = [&](long long wrow, int kcol) {
         if (wrow >= w_rows || kcol >= args.K) return 0.f;
         const long long si = wrow * args.w8_scale_cols + (per_channel ? 0 : kcol / args.w8_group);
@@ -246,14 +260,14 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       float sc[kPer];
       if (per_channel) {
 #pragma unroll
-        for (int j = 0; j < kPer; ++j) sc[j] = load_scale(wrow0 + ((ct + j * 256) >> 2), 0);
+        for (int j = 0; j < kPer; ++j) sc[j] = load_scale(wrow_of((ct + j * 256) >> 2), 0);
       }
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!per_channel) {
 #pragma unroll
           for (int j = 0; j < kPer; ++j) {
             const int u = ct + j * 256;
-            sc[j] = load_scale(wrow0 + (u >> 2), kb * 64 + (u & 3) * 16);
+            sc[j] = load_scale(wrow_of(u >> 2), kb * 64 + (u & 3) * 16);
           }
         }
         if (!mbar_wait(full_bar(stage), phase, abort_flag, args.status, kStatusTimeoutProducer)) {
@@ -326,12 +340,14 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       tile_coords(t, num_m, num_n, mt, nt);
       const int m0 = mt * 128;
       const int n0 = nt * BN;
-      const int group = row_group(args, m0);
+      const int group = args.row_groups ? 0 : row_group(args, m0);
       const int row0 = m0 + ew * 32;
       const int row = m0 + row_in_tile;
       const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
-      if (args.epi == kEpiQkNormRope) {
+      if (args.epi == kEpiSwiGlu) {
+        epilogue_swiglu<BN / 2>(args, &tmC, group, row0, nt * (BN / 2), tbase, buf0, sb, lane);
+      } else if (args.epi == kEpiQkNormRope) {
 #pragma unroll 1
         for (int h = 0; h < BN / 128; ++h) {
           const int col0 = n0 + h * 128;

@@ -19,7 +19,7 @@ import numpy as np
 from . import _lib
 from ._lib import check, lib
 
-FAMILY_MMDIT, FAMILY_ANIMA, FAMILY_SDXL, FAMILY_VAE_KL = 0, 1, 2, 3
+FAMILY_MMDIT, FAMILY_ANIMA, FAMILY_SDXL, FAMILY_VAE_KL, FAMILY_QWEN_IMAGE = 0, 1, 2, 3, 4
 
 
 class ModelDesc(C.Structure):
@@ -134,6 +134,93 @@ class MMDiTConfig:
         cin = self.latent_channels * self.patch ** 2
         emb = ni * cin * D + self.context_rows * self.context_width * D + ni * D * cin
         return 2.0 * (self.blocks * per_block + emb)
+
+
+@dataclass
+class QwenImageConfig:
+    """Qwen-Image 2.1's single-stream DiT (Models/QwenImage/QwenImageDit.cs).
+    Defaults: the released model's shape (32 blocks x 4096, 32 x 128 heads,
+    SwiGLU 12288, 64-channel latent at patch 1, 4096-wide text rows; shapes
+    from the reference's fixture FakeSafetensors.QwenImageDit) at 1024 x 1024
+    (64 x 64 latent cells = 4096 image tokens) with 256 text rows, computing
+    at fp16 (the reference's half-precision option)."""
+    width: int = 4096
+    heads: int = 32
+    blocks: int = 32
+    mlp_width: int = 12288
+    context_rows: int = 256
+    context_width: int = 4096
+    latent_channels: int = 64
+    latent_height: int = 64
+    latent_width: int = 64
+    time_width: int = 256
+    compute: int = _lib.ND_F16
+    eps: float = 1e-6
+    weight_dtype: int = 0
+    quant_group: int = 32
+    quant_scale_dtype: int = _lib.ND_F16
+    fused_gate_up: bool = True      # img_mlp.gate_up (Comfy-Org's layout) or gate_layer + proj
+
+    @property
+    def image_tokens(self) -> int:
+        return self.latent_height * self.latent_width
+
+    @property
+    def tokens(self) -> int:
+        return self.image_tokens + self.context_rows
+
+    def desc(self) -> ModelDesc:
+        d = ModelDesc()
+        d.family = FAMILY_QWEN_IMAGE
+        d.width, d.heads, d.head_dim = self.width, self.heads, 128
+        d.blocks, d.mlp_width = self.blocks, self.mlp_width
+        d.context_rows, d.context_width = self.context_rows, self.context_width
+        d.latent_channels, d.latent_height, d.latent_width = (
+            self.latent_channels, self.latent_height, self.latent_width)
+        d.patch, d.time_width, d.batch = 1, self.time_width, 1
+        d.compute = self.compute
+        d.weight_dtype = self.weight_dtype or self.compute
+        d.quant_group = self.quant_group
+        d.quant_scale_dtype = self.quant_scale_dtype
+        d.eps = self.eps
+        return d
+
+    def quantized(self, rows: int, cols: int) -> bool:
+        g = self.quant_group or cols
+        return self.weight_dtype == _lib.ND_I8 and rows * cols >= 65536 and cols % g == 0 and cols % 16 == 0
+
+    def weight_shapes(self):
+        """(name, shape, required) of every tensor the family reads. No biases."""
+        D, F, cw, tw, C_ = self.width, self.mlp_width, self.context_width, self.time_width, self.latent_channels
+        t = [("img_in.weight", (D, C_), True), ("txt_in.text_norm.weight", (cw,), True),
+             ("txt_in.in_layer.weight", (D, cw), True), ("txt_in.out_layer.weight", (D, D), True),
+             ("time_text_embed.timestep_embedder.linear_1.weight", (D, tw), True),
+             ("time_text_embed.timestep_embedder.linear_2.weight", (D, D), True),
+             ("modulation.1.weight", (4 * D, D), True), ("norm_out.linear.weight", (D, D), True),
+             ("proj_out.weight", (C_, D), True)]
+        for b in range(self.blocks):
+            p = f"transformer_blocks.{b}."
+            t += [(p + "attn.to_q.weight", (D, D), True), (p + "attn.to_k.weight", (D, D), True),
+                  (p + "attn.to_v.weight", (D, D), True), (p + "attn.norm_q.weight", (128,), True),
+                  (p + "attn.norm_k.weight", (128,), True), (p + "attn.to_out.0.weight", (D, D), True)]
+            if self.fused_gate_up:
+                t += [(p + "img_mlp.gate_up.weight", (2 * F, D), True)]
+            else:
+                t += [(p + "img_mlp.gate_layer.weight", (F, D), True), (p + "img_mlp.proj.weight", (F, D), True)]
+            t += [(p + "img_mlp.out.weight", (D, F), True)]
+        return t
+
+    def flops_per_step(self, real_rows: int | None = None) -> float:
+        """Algorithmic FLOPs of one step (1 MAC = 2 FLOP): block GEMMs (QKV,
+        out, gate+up, down), the image rows' attention over every visible key
+        and the text rows' causal attention, embeddings and the final layer."""
+        D, F, ni, R = self.width, self.mlp_width, self.image_tokens, self.context_rows
+        real = R if real_rows is None else real_rows
+        M = ni + R
+        gemm = M * (4 * D * D + 3 * D * F)
+        attn = 2 * ni * (ni + real) * D + R * real * D
+        emb = ni * self.latent_channels * D * 2 + R * self.context_width * D + R * D * D
+        return 2.0 * (self.blocks * (gemm + attn) + emb)
 
 
 @dataclass

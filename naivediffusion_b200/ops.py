@@ -52,7 +52,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
            rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
            qk_cols: int = 0, eps: float = 1e-6, scales: torch.Tensor | None = None,
            quant_group: int = 32, norm_span: int = 0, rope_period: int = 0,
-           gate_stride: int = 0, pairs: bool = False) -> torch.Tensor:
+           gate_stride: int = 0, pairs: bool = False, shared_weights: bool = False) -> torch.Tensor:
     """y = x . W^T + bias with a fused epilogue (Layers.Linear, Graph/Layers.cs:131-160).
 
     weight is [groups * out, in]; rows >= group_split use the second group.
@@ -62,12 +62,17 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     pairs=True: fp32 compute on ND_BF16X2 operands (x [rows, 2 * in], weight
     [groups * out, 2 * in]); the output is a pair [rows, 2 * out], or fp32
     [rows, out] for QK_NORM_ROPE.
+    ND_EPI_SWIGLU: weight is the fused [gate; up] matrix [2F, in]; the output
+    is [rows, F]. shared_weights=True: one weight matrix for every row, the
+    bias / gate vectors chosen per row by group_split (any row).
     """
     rows, k = x.shape
     if pairs:
         k //= 2
-    groups = 1 if group_split is None or group_split >= rows else 2
+    groups = 1 if shared_weights or group_split is None or group_split >= rows else 2
     n = weight.shape[0] // groups
+    if epilogue == _lib.ND_EPI_SWIGLU:
+        n //= 2
     resid_epi = epilogue in (_lib.ND_EPI_RESIDUAL_GATE, _lib.ND_EPI_RESIDUAL_ADD, _lib.ND_EPI_STORE_F32)
     if resid_epi:
         if residual is None:
@@ -100,6 +105,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     a.norm_span = norm_span
     a.rope_period = rope_period
     a.gate_stride = gate_stride
+    a.shared_weights = 1 if shared_weights else 0
     if weight.dtype == torch.int8:
         a.weight_dtype = _lib.ND_I8
         a.scales = scales.data_ptr()

@@ -390,6 +390,97 @@ def anima_forward(w: dict, cfg, latent, context, sigma, cos=None, sin=None):
     return np.stack(outs)
 
 
+def rope_pairs(x, heads, cos, sin) -> np.ndarray:
+    """The rotation Qwen-Image's own model applies: adjacent feature pairs
+    (2i, 2i+1) of every head turned by angle i. The reference's graph runs
+    rotate-half on weights permuted pairs -> halves (QwenImageDit.PairsToHalves,
+    Models/QwenImage/QwenImageDit.cs:261-279), which is this rotation with the
+    features reordered; the oracle turns the pairs directly on the file's own
+    weight order, so the device's permutation is checked, not repeated."""
+    x = _c(x)
+    rows = x.shape[0]
+    h = x.reshape(rows, heads, -1)
+    c = _c(cos)[:, None, :]
+    s = _c(sin)[:, None, :]
+    a, b = h[:, :, 0::2], h[:, :, 1::2]
+    y = np.empty_like(h)
+    y[:, :, 0::2] = a * c - b * s
+    y[:, :, 1::2] = b * c + a * s
+    return y.reshape(x.shape)
+
+
+def qwen_image_forward(w: dict, cfg, latent, context, sigma, cos=None, sin=None, key_len=0):
+    """Qwen-Image 2.1's single-stream step in fp32, composed in the order of
+    QwenImageDit.Build / .Block / .Attention / .FeedForward
+    (Models/QwenImage/QwenImageDit.cs:306-505): image rows then text rows,
+    one modulation [2, 4D] (time sigma and time zero) shared by every block
+    with tanh'd gates, image queries over the visible keys, text queries
+    under QwenImageConditioning.CausalTable (causal, closed over the padding,
+    Models/QwenImage/QwenImageConditioner.cs:66-78). latent [1, 64, H, W];
+    context [rows, width]; key_len = image tokens + real text rows (0: all)."""
+    D, H, F, eps = cfg.width, cfg.heads, cfg.mlp_width, cfg.eps
+    C_, Hl, Wl, R = cfg.latent_channels, cfg.latent_height, cfg.latent_width, cfg.context_rows
+    n_img = Hl * Wl
+    real = key_len - n_img if key_len else R
+    if cos is None:
+        cos, sin = qwen_rope_tables(Hl, Wl, real, R)
+    x_img = linear(patchify(np.asarray(latent, np.float32)[0], 1), w["img_in.weight"])
+    ctx = np.asarray(context, np.float32).reshape(R, cfg.context_width)
+    t = rmsnorm(ctx, np.asarray(w["txt_in.text_norm.weight"], np.float32) + np.float32(1), eps)
+    t = linear(gelu_tanh(linear(t, w["txt_in.in_layer.weight"])), w["txt_in.out_layer.weight"])
+    x = np.concatenate([x_img, t])
+    tsin = np.stack([sinusoid(np.float32(sigma * 1000.0), cfg.time_width), sinusoid(np.float32(0), cfg.time_width)])
+    pre = "time_text_embed.timestep_embedder."
+    temb = linear(silu(linear(tsin, w[pre + "linear_1.weight"])), w[pre + "linear_2.weight"])
+    mod = linear(silu(temb), w["modulation.1.weight"])
+    scale_a, gate_a = mod[:, :D], np.tanh(mod[:, D:2 * D])
+    scale_m, gate_m = mod[:, 2 * D:3 * D], np.tanh(mod[:, 3 * D:])
+
+    def rows(v):  # the noise level's row over the image rows, time zero's over the text
+        return np.concatenate([np.broadcast_to(v[0], (n_img, D)), np.broadcast_to(v[1], (R, D))])
+
+    def mod_rows(x, scale):
+        return np.concatenate([modulate(x[:n_img], None, scale[0], eps), modulate(x[n_img:], None, scale[1], eps)])
+
+    img_keys = n_img + real if real < R else 0
+    txt_keys = real if real < R else 0
+    for b in range(cfg.blocks):
+        p = f"transformer_blocks.{b}."
+        n = mod_rows(x, scale_a)
+        M = n.shape[0]
+
+        def qk(name, norm):
+            y = linear(n, w[p + name])
+            y = rmsnorm(y.reshape(M * H, 128), w[p + norm], eps).reshape(M, D)
+            return rope_pairs(y, H, cos, sin)
+        q, k = qk("attn.to_q.weight", "attn.norm_q.weight"), qk("attn.to_k.weight", "attn.norm_k.weight")
+        v = linear(n, w[p + "attn.to_v.weight"])
+        a_img = attention(q[:n_img], k, v, H, key_len=img_keys)
+        a_txt = attention(q[n_img:], k[n_img:], v[n_img:], H, causal=True, key_len=txt_keys)
+        o = linear(np.concatenate([a_img, a_txt]), w[p + "attn.to_out.0.weight"])
+        x = x + rows(gate_a) * o
+        n = mod_rows(x, scale_m)
+        if p + "img_mlp.gate_up.weight" in w:
+            gu = linear(n, w[p + "img_mlp.gate_up.weight"])
+        else:
+            gu = np.concatenate([linear(n, w[p + "img_mlp.gate_layer.weight"]),
+                                 linear(n, w[p + "img_mlp.proj.weight"])], axis=1)
+        h = silu(np.ascontiguousarray(gu[:, :F])) * gu[:, F:]
+        x = x + rows(gate_m) * linear(h, w[p + "img_mlp.out.weight"])
+    scale = linear(silu(temb[:1]), w["norm_out.linear.weight"])[0]
+    y = modulate(x[:n_img], None, scale, eps)
+    out = linear(y, w["proj_out.weight"])
+    return unpatchify(out, C_, Hl, Wl, 1)[None]
+
+
+def causal_table(real: int, rows: int) -> np.ndarray:
+    """QwenImageConditioning.CausalTable (Models/QwenImage/QwenImageConditioner.cs:66-78):
+    row i may read key j when j <= i and j < real."""
+    i = np.arange(rows)[:, None]
+    j = np.arange(rows)[None, :]
+    return ((j <= i) & (j < real)).astype(np.int32)
+
+
 def group_norm(x, groups, weight=None, bias=None, eps=1e-5, silu=False):
     """GroupNorm over one image x [C, H, W] (or [C, HW])."""
     x = _c(x)

@@ -324,3 +324,46 @@ def test_oracle_guidance_combine_and_euler_arithmetic():
     ref = sample + pred * delta
     got, _ = O.sampler_step(0, 0, out, sample, guidance=float(g), sigma=1.5, sigma_next=0.25)
     assert np.array_equal(got, ref)
+
+
+def test_causal_table_golden():
+    # TransformerInputsTests.TheCausalTableIsATriangleClosedOverThePadding and
+    # QwenImagesBranchesArePaddedAndMaskedToTheirOwnLength.
+    assert O.causal_table(1, 1).ravel().tolist() == [1]
+    assert O.causal_table(2, 4).ravel().tolist() == [1, 0, 0, 0, 1, 1, 0, 0, 1, 1, 0, 0, 1, 1, 0, 0]
+    assert O.causal_table(2, 3).ravel().tolist() == [1, 0, 0, 1, 1, 0, 1, 1, 0]
+    assert O.causal_table(3, 3).ravel().tolist() == [1, 0, 0, 1, 1, 0, 1, 1, 1]
+
+
+@pytest.mark.parametrize("real,rows", [(3, 7), (7, 7), (1, 5)])
+def test_causal_plus_key_count_is_the_causal_table(real, rows):
+    """The text rows' attention under QwenImageConditioning.CausalTable is the
+    causal mask with the keys past the real text left out."""
+    rng = np.random.default_rng(real * 10 + rows)
+    heads, d = 2, 16
+    q, k, v = (rng.standard_normal((rows, heads * d)).astype(np.float32) for _ in range(3))
+    y = O.attention(q, k, v, heads, causal=True, key_len=real if real < rows else 0)
+    mask = O.causal_table(real, rows) > 0
+    ref = np.zeros((rows, heads * d))
+    for h in range(heads):
+        sl = slice(h * d, (h + 1) * d)
+        s = q[:, sl].astype(np.float64) @ k[:, sl].astype(np.float64).T / math.sqrt(d)
+        s = np.where(mask, s, -np.inf)
+        p = np.exp(s - s.max(1, keepdims=True))
+        ref[:, sl] = (p / p.sum(1, keepdims=True)) @ v[:, sl]
+    assert np.abs(y - ref).max() < 1e-5
+
+
+def test_pair_rotation_is_rotate_half_on_permuted_features():
+    """QwenImageDit.PairsToHalves: rotating adjacent pairs equals rotating
+    halves after reordering each head's features (2i, 2i+1) -> (i, 64+i)."""
+    rng = np.random.default_rng(9)
+    rows, heads, dim = 6, 3, 128
+    x = rng.standard_normal((rows, heads * dim)).astype(np.float32)
+    ang = rng.random((rows, dim // 2)).astype(np.float32) * 6
+    c, s = np.cos(ang), np.sin(ang)
+    perm = np.concatenate([np.arange(0, dim, 2), np.arange(1, dim, 2)])  # halves order -> pair source
+    xp = x.reshape(rows, heads, dim)[:, :, perm].reshape(rows, heads * dim)
+    y_half = O.rope(xp, heads, c, s).reshape(rows, heads, dim)
+    y_pair = O.rope_pairs(x, heads, c, s).reshape(rows, heads, dim)
+    assert np.array_equal(y_half, y_pair[:, :, perm])
