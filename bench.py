@@ -115,7 +115,8 @@ class Clocks:
 def _configs():
     """BASELINE configurations: (model config, workload text, dtype, metric)."""
     from naivediffusion_b200 import _lib
-    from naivediffusion_b200.denoiser import AnimaConfig, MMDiTConfig, QwenImageConfig, UNetConfig, VaeDecoderConfig
+    from naivediffusion_b200.denoiser import (AnimaConfig, MMDiTConfig, QwenImageConfig, UNetConfig,
+                                              VaeDecoderConfig, WanVaeConfig)
     return {
         "cfg3": (MMDiTConfig(), "cfg3: Qwen-Image-style MMDiT 60x3072, 24x128 heads, MLP 12288 GELU-tanh, "
                  "5376 img + 256 txt tokens, batch 1, guidance 1", "bf16", METRIC),
@@ -141,6 +142,13 @@ def _configs():
                    "32x4096, 32x128 heads, SwiGLU 12288, 4096 img + 256 txt tokens (1024x1024), batch 1, "
                    "fp16 compute (the reference's half-precision option)", "f16",
                    "Qwen-Image 2.1 DiT s/step @1024×1024 fp16; images/s"),
+        "wan21": (WanVaeConfig(), "Wan 2.1 VAE decoder on one frame (Anima's): widths 384/192/96, "
+                  "16x128x128 latent -> 3x1024x1024 image, fp16", "f16",
+                  "Wan 2.1 VAE decode s/image @1024×1024 fp16; images/s"),
+        "wan22": (WanVaeConfig(version=22, width=144, latent_channels=64, latent_height=64, latent_width=64),
+                  "Qwen-Image 2.1's Wan 2.2-layout VAE decoder on one frame: widths 1152/576/288/144, "
+                  "64x64x64 latent -> 3x1024x1024 image, fp16", "f16",
+                  "Qwen-Image 2.1 VAE decode s/image @1024×1024 fp16; images/s"),
     }
 
 
@@ -263,7 +271,7 @@ def run_reference(args):
     if rank != 0:
         return 0
     cfg, workload, _dt, metric = _configs()[args.config]
-    if args.config in ("cfg5", "vae"):
+    if args.config in ("cfg5", "vae", "wan21", "wan22"):
         print(json.dumps({"impl": "reference", "unavailable": f"{args.config} has no bounded CPU sample of the step"}))
         return 0
     if args.warmup > 0:
@@ -378,7 +386,7 @@ def run_ours(args):
     if args.config == "cfg3" and tpath.exists():
         traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
     kernel = "gemm_sm100_kernel (tcgen05, all GEMM launches of a step)"
-    if args.config in ("cfg5", "vae"):
+    if args.config in ("cfg5", "vae", "wan21", "wan22"):
         kernel = "gemm_sm100_kernel (tcgen05: conv3x3 implicit GEMMs and the linear layers)"
     elif args.config == "cfg4":
         kernel = "gemm_w8_sm100_kernel (tcgen05, int8 weights widened in the mainloop)"
@@ -435,7 +443,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["cfg3", "cfg1", "cfg2", "cfg4", "cfg5", "vae", "qwen21"], default="cfg3",
+    ap.add_argument("--config", choices=["cfg3", "cfg1", "cfg2", "cfg4", "cfg5", "vae", "qwen21", "wan21", "wan22"], default="cfg3",
                     help="BASELINE configuration (default cfg3, the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle sample")
     args = ap.parse_args()

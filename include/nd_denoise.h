@@ -84,6 +84,15 @@ ND_API const char* nd_version(void);
                                noise level's row for image rows, time zero's for text
                                rows), SwiGLU feed-forward, image queries over every
                                visible key, text queries causal over the text; patch 1 */
+#define ND_FAMILY_VAE_WAN21 5  /* Wan 2.1 VAE decoder on one frame (Vae/WanVae.cs), Anima's:
+                               width = base dim (96), latent_channels 16, 8x upsampling;
+                               unet_resnets = resblocks per level - 1 (2); weights as
+                               WanVae.SingleFrame leaves them (3-D kernels cut to their
+                               last temporal tap); output [batch, 3, 8h, 8w] */
+#define ND_FAMILY_VAE_WAN22 6  /* Wan 2.2-layout VAE decoder of Qwen-Image 2.1
+                               (Vae/Wan22Vae.cs): width 144, latent_channels 64, five
+                               levels, 16x upsampling, the up shortcuts; the RGB of
+                               its RGBA output, [batch, 3, 16h, 16w] */
 
 typedef struct nd_device nd_device;
 typedef struct nd_denoiser nd_denoiser;
@@ -300,14 +309,15 @@ typedef struct nd_linear_args {
  * nine taps x input channels, each tap's patch loaded by TMA straight from the
  * input (borders zero-filled). Replaces Layers.Conv2d
  * (src/NaiveDiffusion/Graph/Layers.cs:115-128) -> DmlOps.Convolution
- * (src/NaiveDiffusion/Dml/DmlOps.cs:265). Limits: in_channels % 64 == 0;
- * output width divides 128; output pixels per image a multiple of 128. */
+ * (src/NaiveDiffusion/Dml/DmlOps.cs:265). Limits: in_channels a multiple of
+ * 8, at least 64; output width divides 128 or is a multiple of 128; output
+ * pixels per image a multiple of 128. */
 typedef struct nd_conv_args {
   int dtype;            /* ND_F16 or ND_BF16 */
   int epilogue;         /* ND_EPI_STORE, ND_EPI_ADD_STORE, ND_EPI_STORE_F32, ND_EPI_SILU */
   int batch, height, width, in_channels, out_channels, stride;
   const void* x;        /* [batch, height, width, in_channels] */
-  const void* weight;   /* [out_channels, 3, 3, in_channels] */
+  const void* weight;   /* [out_channels, 3, 3, in_channels rounded up to 64], the pad zero */
   const float* bias;    /* [out_channels], or [batch][out_channels] with per_batch_bias */
   int per_batch_bias;   /* the ResBlock's time-embedding projection folded into the bias */
   int64_t bias_stride;  /* per_batch_bias: floats between batch items' bias vectors (0: out_channels) */
@@ -379,6 +389,7 @@ typedef struct nd_rmsnorm_args {
   const float* weight;
   int plus_one;         /* zero-centred stored weight (QwenImageDit txt_in norm) */
   float eps;
+  int silu;             /* 1: y = silu(y) after the norm (WanVae's norm + SiLU pairs) */
 } nd_rmsnorm_args;
 
 ND_API int nd_op_rmsnorm(const nd_rmsnorm_args* args, void* stream);

@@ -100,7 +100,7 @@ class RmsNormArgs(C.Structure):
         ("x", C.c_void_p), ("ldx", C.c_int64), ("in_dtype", C.c_int),
         ("y", C.c_void_p), ("ldy", C.c_int64), ("out_dtype", C.c_int),
         ("rows", C.c_int64), ("width", C.c_int64),
-        ("weight", C.c_void_p), ("plus_one", C.c_int), ("eps", C.c_float),
+        ("weight", C.c_void_p), ("plus_one", C.c_int), ("eps", C.c_float), ("silu", C.c_int),
     ]
 
 

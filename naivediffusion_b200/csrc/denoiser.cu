@@ -449,6 +449,8 @@ int nd_denoiser_create(nd_device* dev, const nd_model_desc* desc, nd_denoiser** 
     case ND_FAMILY_SDXL: d = nd::make_unet(); break;
     case ND_FAMILY_VAE_KL: d = nd::make_vae_decoder(); break;
     case ND_FAMILY_QWEN_IMAGE: d = nd::make_qwen_image(); break;
+    case ND_FAMILY_VAE_WAN21:
+    case ND_FAMILY_VAE_WAN22: d = nd::make_wan_decoder(); break;
     default: return nd::fail(ND_ERR_UNSUPPORTED, "nd_denoiser_create: unknown model family");
   }
   d->dev = dev;

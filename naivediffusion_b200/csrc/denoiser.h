@@ -162,4 +162,5 @@ nd_denoiser* make_anima();
 nd_denoiser* make_unet();
 nd_denoiser* make_vae_decoder();
 nd_denoiser* make_qwen_image();
+nd_denoiser* make_wan_decoder();
 }  // namespace nd

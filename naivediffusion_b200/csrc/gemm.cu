@@ -307,7 +307,8 @@ int conv2d(const nd_conv_args& c, cudaStream_t stream) {
   if (c.dtype != ND_F16 && c.dtype != ND_BF16) return fail(ND_ERR_INVALID, "conv2d: dtype must be f16 or bf16");
   if (c.batch <= 0 || c.height <= 0 || c.width <= 0 || c.in_channels <= 0 || c.out_channels <= 0)
     return fail(ND_ERR_INVALID, "conv2d: empty shape");
-  if (c.in_channels % 64) return fail(ND_ERR_UNSUPPORTED, "conv2d: in_channels must be a multiple of 64");
+  if (c.in_channels % 8 || c.in_channels < 64)
+    return fail(ND_ERR_UNSUPPORTED, "conv2d: in_channels must be a multiple of 8, at least 64");
   if (c.stride != 1 && c.stride != 2) return fail(ND_ERR_UNSUPPORTED, "conv2d: stride must be 1 or 2");
   const int ho = (c.height - 1) / c.stride + 1, wo = (c.width - 1) / c.stride + 1;
   if (wo <= 128 ? 128 % wo != 0 : wo % 128 != 0)
@@ -322,7 +323,11 @@ int conv2d(const nd_conv_args& c, cudaStream_t stream) {
   if (epi != ND_EPI_STORE_F32 && c.out_channels % 8) return fail(ND_ERR_INVALID, "conv2d: out_channels % 8 for a 16-bit output");
   if (c.out_channels % 4) return fail(ND_ERR_INVALID, "conv2d: out_channels must be a multiple of 4");
   const int64_t M = static_cast<int64_t>(c.batch) * ho * wo;
-  const int64_t K = 9LL * c.in_channels;
+  // Each tap's channels in chunks of 64; a last partial chunk reads past the
+  // tensor's channel extent, which TMA fills with zeros, against zero rows of
+  // the weight (stored with the channels padded to a multiple of 64).
+  const int kpc = (c.in_channels + 63) / 64;
+  const int64_t K = 9LL * kpc * 64;
   if (M > INT_MAX || K > INT_MAX) return fail(ND_ERR_INVALID, "conv2d: shape too large");
 
   CUtensorMap ta, tb, tc;
@@ -362,7 +367,7 @@ int conv2d(const nd_conv_args& c, cudaStream_t stream) {
   g.shared_weights = 1;
   g.addend = c.addend;
   g.ld_add = c.out_channels;
-  g.conv_kpc = c.in_channels / 64;
+  g.conv_kpc = kpc;
   g.conv_hw = ho * wo;
   g.conv_w_out = wo;
   g.conv_stride = c.stride;

@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const void* __restrict__ x
                                                       long long ldx, void* __restrict__ y,
                                                       long long ldy, int out_type, int rows,
                                                       int width, const float* __restrict__ w,
-                                                      float plus_one, float eps) {
+                                                      float plus_one, float eps, int silu_after) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -158,6 +158,12 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const void* __restrict__ x
       o.y = v[i].y * r * (k.y + plus_one);
       o.z = v[i].z * r * (k.z + plus_one);
       o.w = v[i].w * r * (k.w + plus_one);
+      if (silu_after) {
+        o.x = silu(o.x);
+        o.y = silu(o.y);
+        o.z = silu(o.z);
+        o.w = silu(o.w);
+      }
       store4(y, static_cast<long long>(warp) * ldy + 4 * c, o, out_type, width);
     }
   }
@@ -354,7 +360,7 @@ int rmsnorm(const nd_rmsnorm_args& a, cudaStream_t stream) {
   if (!bucket) return fail(ND_ERR_UNSUPPORTED, "rmsnorm: width above 4096");
   const int rows = static_cast<int>(a.rows);
   const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
-#define ND_RMS(V) rmsnorm_kernel<V><<<grid, 256, 0, stream>>>(a.x, a.in_dtype, a.ldx, a.y, a.ldy, a.out_dtype, rows, static_cast<int>(a.width), a.weight, a.plus_one ? 1.f : 0.f, a.eps)
+#define ND_RMS(V) rmsnorm_kernel<V><<<grid, 256, 0, stream>>>(a.x, a.in_dtype, a.ldx, a.y, a.ldy, a.out_dtype, rows, static_cast<int>(a.width), a.weight, a.plus_one ? 1.f : 0.f, a.eps, a.silu)
   switch (bucket) {
     case 2: ND_RMS(2); break;
     case 4: ND_RMS(4); break;

@@ -492,8 +492,449 @@ struct VaeDecoder final : nd_denoiser {
 #undef ND_OP
 };
 
+// ------------------------------------------------------------ Wan decoders
+// WanVae.Decoder (Vae/WanVae.cs:170-207, the Wan 2.1 VAE Anima decodes with)
+// and Wan22Vae.Decoder (Vae/Wan22Vae.cs:161-206, Qwen-Image 2.1's), on one
+// frame: every causal 3-D convolution cut to its last temporal tap (the host
+// passes WanVae.SingleFrame's tensors), an RMS norm over each pixel's channels
+// instead of GroupNorm, SiLU, a single-head attention in the middle. The
+// level channel plan follows the checkpoints: dims = width x [m_last, m
+// reversed]; Wan 2.1 halves the width in each upsample convolution (the next
+// level's resblocks start from half), Wan 2.2 keeps it and adds a shortcut of
+// the level's input beside every upsampling level.
+
+// NCHW fp32 latent [B, C, HW] -> conv2 (1x1: y = W x + b) -> NHWC 16-bit
+// [B, HW, Cp] with channels C..Cp-1 zero (the 3x3 conv reads whole 64-channel chunks).
+__global__ void wan_latent_in_kernel(const float* __restrict__ in, const float* __restrict__ w,
+                                     const float* __restrict__ b, void* __restrict__ out, int f16, int B, int HW,
+                                     int C, int Cp) {
+  const long long n = static_cast<long long>(B) * HW * Cp;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int o = static_cast<int>(i % Cp);
+    const long long pix = i / Cp;
+    const int bi = static_cast<int>(pix / HW);
+    const int p = static_cast<int>(pix - static_cast<long long>(bi) * HW);
+    float acc = 0.f;
+    if (o < C) {
+      acc = b[o];
+      for (int c = 0; c < C; ++c) acc = fmaf(w[o * C + c], in[(static_cast<long long>(bi) * C + c) * HW + p], acc);
+    }
+    uint16_t* dst = static_cast<uint16_t*>(out) + i;
+    if (f16) {
+      const __half h = __float2half_rn(acc);
+      *dst = *reinterpret_cast<const uint16_t*>(&h);
+    } else {
+      const __nv_bfloat16 h = __float2bfloat16_rn(acc);
+      *dst = *reinterpret_cast<const uint16_t*>(&h);
+    }
+  }
+}
+
+__device__ __forceinline__ float ld16(const uint16_t* p, int f16) {
+  const uint16_t v = *p;
+  return f16 ? __half2float(*reinterpret_cast<const __half*>(&v))
+             : __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(&v));
+}
+
+// h [B, 2H, 2W, Co] += Wan22Vae.UpShortcut(x [B, H, W, Ci]) (Vae/Wan22Vae.cs:121-155):
+// mode 0 (Ci == Co) nearest upsample; mode 1 (a level that doubled time,
+// Ci == 2 Co) the odd input channels, nearest; mode 2 (Ci == 2 Co) output
+// channel c takes input channel 2c on even rows and 2c + 1 on odd rows.
+__global__ void wan_up_shortcut_kernel(void* __restrict__ h, const void* __restrict__ x, int f16, int B, int H,
+                                       int W, int Ci, int Co, int mode) {
+  const long long n = static_cast<long long>(B) * 4 * H * W * Co;
+  uint16_t* hp = static_cast<uint16_t*>(h);
+  const uint16_t* xp = static_cast<const uint16_t*>(x);
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % Co);
+    long long q = i / Co;
+    const int X = static_cast<int>(q % (2 * W));
+    q /= 2 * W;
+    const int Y = static_cast<int>(q % (2 * H));
+    const long long b = q / (2 * H);
+    const int sc = mode == 0 ? c : (mode == 1 ? 2 * c + 1 : 2 * c + (Y & 1));
+    const long long src = ((b * H + (Y >> 1)) * W + (X >> 1)) * Ci + sc;
+    const float v = ld16(hp + i, f16) + ld16(xp + src, f16);
+    if (f16) {
+      const __half r = __float2half_rn(v);
+      hp[i] = *reinterpret_cast<const uint16_t*>(&r);
+    } else {
+      const __nv_bfloat16 r = __float2bfloat16_rn(v);
+      hp[i] = *reinterpret_cast<const uint16_t*>(&r);
+    }
+  }
+}
+
+struct WanRes {
+  int cin = 0, cout = 0;
+  float *g1 = nullptr, *g2 = nullptr, *c1b = nullptr, *c2b = nullptr, *scb = nullptr;
+  void *c1w = nullptr, *c2w = nullptr, *scw = nullptr;
+};
+
+struct WanLevel {
+  int cin = 0, cout = 0, up_out = 0;  // up_out 0: no upsample
+  int sc_mode = -1;                   // Wan 2.2 shortcut mode (-1: none)
+  std::vector<WanRes> res;
+  void* upw = nullptr;
+  float* upb = nullptr;
+};
+
+int round64(int c) { return (c + 63) / 64 * 64; }
+
+struct WanDecoder final : nd_denoiser {
+  bool v22 = false;
+  int B = 1, h0 = 0, w0 = 0, Cl = 16, Clp = 64, W0 = 96, R = 2, L = 4, top = 0, img_c = 3;
+  int dt = ND_F16;
+  size_t e = 2;
+  float *cv2_w = nullptr, *cv2_b = nullptr, *c1_b = nullptr, *head_g = nullptr, *head_b = nullptr;
+  void *c1_w = nullptr, *head_w = nullptr;
+  WanRes mid0, mid1;
+  float *ag = nullptr, *aqkv_b = nullptr, *ap_b = nullptr;
+  void *aqkv = nullptr, *ap = nullptr;
+  std::vector<WanLevel> lv;
+  float *in_latent = nullptr, *out_nhwc = nullptr, *out_image = nullptr, *scores = nullptr;
+  void *xin = nullptr, *X[3] = {nullptr, nullptr, nullptr}, *H1 = nullptr, *H2 = nullptr, *SC = nullptr,
+       *UPB = nullptr, *Q = nullptr, *K = nullptr, *Vb = nullptr, *VT = nullptr, *P = nullptr, *ATT = nullptr,
+       *A16 = nullptr;
+
+  int res_h(int i) const { return h0 << i; }
+  int res_w(int i) const { return w0 << i; }
+  float* V(int64_t n) { return static_cast<float*>(alloc(static_cast<size_t>(n) * 4, true)); }
+  void* Wt(int64_t n) { return alloc(static_cast<size_t>(n) * e, true); }
+
+  void conv_slot(const std::string& name, int cout, int cin, void*& w, float*& b, int cout_pad = 0) {
+    const int cp = round64(cin);
+    const int co = cout_pad ? cout_pad : cout;
+    w = Wt(static_cast<int64_t>(co) * 9 * cp);
+    b = V(co);
+    add_slot(name + ".weight", kConv3x3, cout, 9LL * cp, w);
+    slots.back().conv_cin = cin;
+    add_slot(name + ".bias", kVector, cout, 1, b, false);
+  }
+
+  WanRes make_res(const std::string& p, int cin, int cout) {
+    WanRes r;
+    r.cin = cin;
+    r.cout = cout;
+    r.g1 = V(cin);
+    add_slot(p + ".residual.0.gamma", kVector, cin, 1, r.g1);
+    conv_slot(p + ".residual.2", cout, cin, r.c1w, r.c1b);
+    r.g2 = V(cout);
+    add_slot(p + ".residual.3.gamma", kVector, cout, 1, r.g2);
+    conv_slot(p + ".residual.6", cout, cout, r.c2w, r.c2b);
+    if (cin != cout) {
+      r.scw = Wt(static_cast<int64_t>(cout) * cin);
+      r.scb = V(cout);
+      add_slot(p + ".shortcut.weight", kMatrix, cout, cin, r.scw);
+      add_slot(p + ".shortcut.bias", kVector, cout, 1, r.scb, false);
+    }
+    return r;
+  }
+
+  int build() override {
+    const nd_model_desc& d = desc;
+    v22 = d.family == ND_FAMILY_VAE_WAN22;
+    if (d.compute != ND_F16 && d.compute != ND_BF16) return fail(ND_ERR_UNSUPPORTED, "wan vae: compute must be fp16 or bf16");
+    if (d.weight_dtype != d.compute) return fail(ND_ERR_UNSUPPORTED, "wan vae: weights must be stored in the compute dtype");
+    if (d.batch < 1 || d.batch > 4) return fail(ND_ERR_INVALID, "wan vae: batch must be 1..4");
+    dt = d.compute;
+    B = d.batch;
+    Cl = d.latent_channels > 0 ? d.latent_channels : (v22 ? 64 : 16);
+    if (Cl > 64) return fail(ND_ERR_INVALID, "wan vae: at most 64 latent channels");
+    Clp = 64;
+    W0 = d.width > 0 ? d.width : (v22 ? 144 : 96);
+    R = d.unet_resnets > 0 ? d.unet_resnets : 2;
+    h0 = d.latent_height;
+    w0 = d.latent_width;
+    img_c = v22 ? 4 : 3;
+    static const int m21[4] = {1, 2, 4, 4};
+    static const int m22[5] = {1, 2, 4, 8, 8};
+    const int* m = v22 ? m22 : m21;
+    L = v22 ? 5 : 4;
+    // dims = width x [m_last, m reversed] (the checkpoints' Decoder3d layout)
+    std::vector<int> dims(L + 1);
+    dims[0] = W0 * m[L - 1];
+    for (int i = 0; i < L; ++i) dims[i + 1] = W0 * m[L - 1 - i];
+    top = dims[0];
+    for (int c : dims)
+      if (c % 8 || c < 64) return fail(ND_ERR_INVALID, "wan vae: every level's width must be a multiple of 8, at least 64");
+    for (int i = 0; i < L; ++i) {
+      const int w = res_w(i), h = res_h(i);
+      if ((w <= 128 ? 128 % w != 0 : w % 128 != 0) || (static_cast<int64_t>(h) * w) % 128 != 0)
+        return fail(ND_ERR_UNSUPPORTED, "wan vae: every level's width must divide 128 or be a multiple of 128");
+    }
+    // ---- weights
+    cv2_w = V(static_cast<int64_t>(Cl) * Cl);
+    cv2_b = V(Cl);
+    add_slot("conv2.weight", kVector, static_cast<int64_t>(Cl) * Cl, 1, cv2_w);
+    add_slot("conv2.bias", kVector, Cl, 1, cv2_b, false);
+    conv_slot("decoder.conv1", top, Cl, c1_w, c1_b);
+    mid0 = make_res("decoder.middle.0", top, top);
+    ag = V(top);
+    add_slot("decoder.middle.1.norm.gamma", kVector, top, 1, ag);
+    aqkv = Wt(3LL * top * top);
+    aqkv_b = V(3LL * top);
+    add_slot("decoder.middle.1.to_qkv.weight", kMatrix, 3LL * top, top, aqkv);
+    add_slot("decoder.middle.1.to_qkv.bias", kVector, 3LL * top, 1, aqkv_b, false);
+    ap = Wt(static_cast<int64_t>(top) * top);
+    ap_b = V(top);
+    add_slot("decoder.middle.1.proj.weight", kMatrix, top, top, ap);
+    add_slot("decoder.middle.1.proj.bias", kVector, top, 1, ap_b, false);
+    mid1 = make_res("decoder.middle.2", top, top);
+    lv.resize(L);
+    int idx = 0;  // Wan 2.1 numbers its upsamples straight through
+    static const bool temporal22[4] = {false, true, true, true};
+    for (int i = 0; i < L; ++i) {
+      WanLevel& v = lv[i];
+      v.cin = (!v22 && i > 0) ? dims[i] / 2 : dims[i];
+      v.cout = dims[i + 1];
+      const bool up = i != L - 1;
+      v.up_out = up ? (v22 ? v.cout : v.cout / 2) : 0;
+      const std::string pre = v22 ? "decoder.upsamples." + std::to_string(i) + ".upsamples." : "decoder.upsamples.";
+      if (v22) idx = 0;
+      int c = v.cin;
+      for (int j = 0; j < R + 1; ++j) {
+        v.res.push_back(make_res(pre + std::to_string(idx++), c, v.cout));
+        c = v.cout;
+      }
+      if (up) {
+        conv_slot(pre + std::to_string(idx++) + ".resample.1", v.up_out, v.cout, v.upw, v.upb);
+        if (v22) {
+          if (v.cin == v.up_out) v.sc_mode = 0;
+          else if (v.cin == 2 * v.up_out) v.sc_mode = temporal22[L - 2 - i] ? 1 : 2;
+          else return fail(ND_ERR_INVALID, "wan vae: an up level halves its channels at most");
+        }
+      }
+      if (!v22 && i > 0 && lv[i - 1].up_out != v.cin)
+        return fail(ND_ERR_INVALID, "wan vae: level widths do not chain");
+    }
+    const int last = lv[L - 1].cout;
+    head_g = V(last);
+    add_slot("decoder.head.0.gamma", kVector, last, 1, head_g);
+    conv_slot("decoder.head.2", img_c, last, head_w, head_b, 4);
+    // ---- buffers
+    auto S = [&](size_t bytes) { return alloc(bytes, false); };
+    const int64_t hw0 = static_cast<int64_t>(h0) * w0;
+    const int64_t lat_px = B * hw0;
+    int64_t max_act = lat_px * top;
+    for (int i = 0; i < L; ++i) {
+      const int64_t px = static_cast<int64_t>(B) * res_h(i) * res_w(i);
+      max_act = std::max<int64_t>(max_act, px * std::max(lv[i].cin, lv[i].cout));
+      if (lv[i].up_out) max_act = std::max<int64_t>(max_act, 4 * px * std::max(lv[i].cout, lv[i].up_out));
+    }
+    const int64_t img_px = static_cast<int64_t>(B) * res_h(L - 1) * res_w(L - 1);
+    in_latent = static_cast<float*>(S(static_cast<size_t>(lat_px) * Cl * 4));
+    xin = S(static_cast<size_t>(lat_px) * Clp * e);
+    for (auto& x : X) x = S(max_act * e);
+    H1 = S(max_act * e);
+    H2 = S(max_act * e);
+    SC = S(max_act * e);
+    UPB = S(max_act * e);
+    Q = S(hw0 * top * e);
+    K = S(hw0 * top * e);
+    Vb = S(hw0 * top * e);
+    VT = S(hw0 * top * e);
+    ATT = S(hw0 * top * e);
+    A16 = S(lat_px * top * e);
+    scores = static_cast<float*>(S(static_cast<size_t>(hw0) * hw0 * 4));
+    P = S(static_cast<size_t>(hw0) * hw0 * e);
+    out_nhwc = static_cast<float*>(S(static_cast<size_t>(img_px) * 4 * 4));
+    out_image = static_cast<float*>(S(static_cast<size_t>(img_px) * 3 * 4));
+    if (alloc_failed) return fail(ND_ERR_OOM, "wan vae: device allocation failed");
+    ND_CUDA(cudaEventCreateWithFlags(&staged, cudaEventDisableTiming));
+    return ND_OK;
+  }
+
+  int64_t latent_elems() const override { return static_cast<int64_t>(B) * Cl * h0 * w0; }
+  int64_t output_elems() const override { return static_cast<int64_t>(B) * 3 * res_h(L - 1) * res_w(L - 1); }
+  const float* output() const override { return out_image; }
+
+  int check_cond(int n, const nd_named_tensor*, StepInputs&) override {
+    if (n != 0) return fail(ND_ERR_INVALID, "wan vae decode takes no conditioning");
+    return ND_OK;
+  }
+
+  int stage(const StepInputs& in, cudaStream_t s) override {
+    const cudaMemcpyKind k = in.device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    ND_CUDA(cudaMemcpyAsync(in_latent, in.latent, static_cast<size_t>(latent_elems()) * 4, k, s));
+    return ND_OK;
+  }
+
+#define ND_OP(cls, flops, expr)     \
+  do {                              \
+    prof_begin(s);                  \
+    int rc_ = (expr);               \
+    if (rc_) return rc_;            \
+    prof_end(s, cls, flops, 0.0);   \
+  } while (0)
+
+  // WanVae.ChannelRmsNorm (Vae/WanVae.cs:111-121): each pixel's channels over
+  // sqrt(mean(x^2) + 1e-24 / C), times gamma; SiLU after where the block has it.
+  int rms(cudaStream_t s, const void* x, void* y, int64_t px, int C, const float* g, bool silu_after) {
+    nd_rmsnorm_args a{};
+    a.x = x;
+    a.ldx = C;
+    a.in_dtype = dt;
+    a.y = y;
+    a.ldy = C;
+    a.out_dtype = dt;
+    a.rows = px;
+    a.width = C;
+    a.weight = g;
+    a.plus_one = 0;
+    a.eps = 1e-24f / static_cast<float>(C);
+    a.silu = silu_after ? 1 : 0;
+    return rmsnorm(a, s);
+  }
+
+  int conv(cudaStream_t s, const void* x, int hh, int ww, int cin, const void* w, const float* b, int cout, int epi,
+           void* y, const void* addend, float* y32 = nullptr) {
+    nd_conv_args c{};
+    c.dtype = dt;
+    c.epilogue = epi;
+    c.batch = B;
+    c.height = hh;
+    c.width = ww;
+    c.in_channels = cin;
+    c.out_channels = cout;
+    c.stride = 1;
+    c.x = x;
+    c.weight = w;
+    c.bias = b;
+    c.y = y;
+    c.y_f32 = y32;
+    c.addend = addend;
+    return conv2d(c, s);
+  }
+
+  int lin(cudaStream_t s, const void* x, int64_t rows, int64_t k, const void* w, const float* b, int64_t n, int epi,
+          void* y, float* resid = nullptr, const void* addend = nullptr) {
+    nd_linear_args a{};
+    a.dtype = dt;
+    a.epilogue = epi;
+    a.rows = rows;
+    a.in_features = k;
+    a.out_features = n;
+    a.x = x;
+    a.ldx = k;
+    a.weight = w;
+    a.bias = b;
+    a.group_split = rows;
+    a.y = y;
+    a.ldy = n;
+    a.residual = resid;
+    a.ldr = n;
+    a.addend = addend;
+    a.ld_add = n;
+    return linear(a, s);
+  }
+
+  double conv_flops(int hh, int ww, int cin, int cout) const { return 2.0 * B * hh * ww * 9.0 * cin * cout; }
+
+  // WanVae.ResidualBlock (Vae/WanVae.cs:132-146).
+  int res(cudaStream_t s, const WanRes& r, int hh, int ww, const void* x, void* y) {
+    const int64_t px = static_cast<int64_t>(B) * hh * ww;
+    ND_OP("rmsnorm", 0.0, rms(s, x, H1, px, r.cin, r.g1, true));
+    ND_OP("conv3x3", conv_flops(hh, ww, r.cin, r.cout), conv(s, H1, hh, ww, r.cin, r.c1w, r.c1b, r.cout, ND_EPI_STORE, H2, nullptr));
+    ND_OP("rmsnorm", 0.0, rms(s, H2, H1, px, r.cout, r.g2, true));
+    const void* sc = x;
+    if (r.scw) {
+      ND_OP("gemm.shortcut", 2.0 * px * r.cin * r.cout, lin(s, x, px, r.cin, r.scw, r.scb, r.cout, ND_EPI_STORE, SC));
+      sc = SC;
+    }
+    ND_OP("conv3x3", conv_flops(hh, ww, r.cout, r.cout),
+          conv(s, H1, hh, ww, r.cout, r.c2w, r.c2b, r.cout, ND_EPI_ADD_STORE, y, sc));
+    return ND_OK;
+  }
+
+  // WanVae.AttentionBlock (Vae/WanVae.cs:150-168): one head over every pixel.
+  int attn(cudaStream_t s, const void* x, void* y) {
+    const int C = top;
+    const int64_t hw = static_cast<int64_t>(h0) * w0;
+    ND_OP("rmsnorm", 0.0, rms(s, x, A16, B * hw, C, ag, false));
+    const float scale = 1.0f / std::sqrt(static_cast<float>(C));
+    const size_t wrow = static_cast<size_t>(C) * C * e;
+    for (int b = 0; b < B; ++b) {
+      const uint8_t* xb = static_cast<const uint8_t*>(A16) + b * hw * C * e;
+      const uint8_t* w = static_cast<const uint8_t*>(aqkv);
+      ND_OP("gemm.qkv", 2.0 * hw * C * C, lin(s, xb, hw, C, w, aqkv_b, C, ND_EPI_STORE, Q));
+      ND_OP("gemm.qkv", 2.0 * hw * C * C, lin(s, xb, hw, C, w + wrow, aqkv_b + C, C, ND_EPI_STORE, K));
+      ND_OP("gemm.qkv", 2.0 * hw * C * C, lin(s, xb, hw, C, w + 2 * wrow, aqkv_b + 2 * C, C, ND_EPI_STORE, Vb));
+      ND_OP("attention", 2.0 * hw * hw * C, lin(s, Q, hw, C, K, nullptr, hw, ND_EPI_STORE_F32, nullptr, scores));
+      if (hw > INT_MAX) return fail(ND_ERR_INVALID, "wan vae: too many pixels for the attention");
+      prof_begin(s);
+      vae_softmax_kernel<<<static_cast<unsigned>(hw), 256, 0, s>>>(scores, P, dt == ND_F16, static_cast<int>(hw), scale);
+      ND_CUDA(cudaGetLastError());
+      dim3 grid(static_cast<unsigned>((C + 31) / 32), static_cast<unsigned>((hw + 31) / 32));
+      transpose16_kernel<<<grid, dim3(32, 8), 0, s>>>(static_cast<const uint16_t*>(Vb), static_cast<uint16_t*>(VT),
+                                                     static_cast<int>(hw), C);
+      ND_CUDA(cudaGetLastError());
+      prof_end(s, "attention", 0.0, 0.0);
+      ND_OP("attention", 2.0 * hw * hw * C, lin(s, P, hw, hw, VT, nullptr, C, ND_EPI_STORE, ATT));
+      const uint8_t* xres = static_cast<const uint8_t*>(x) + b * hw * C * e;
+      uint8_t* yb = static_cast<uint8_t*>(y) + b * hw * C * e;
+      ND_OP("gemm.out", 2.0 * hw * C * C, lin(s, ATT, hw, C, ap, ap_b, C, ND_EPI_ADD_STORE, yb, nullptr, xres));
+    }
+    return ND_OK;
+  }
+
+  int forward(cudaStream_t s) override {
+    const int64_t lat_px = static_cast<int64_t>(B) * h0 * w0;
+    prof_begin(s);
+    wan_latent_in_kernel<<<grid_of(lat_px * Clp), 256, 0, s>>>(in_latent, cv2_w, cv2_b, xin, dt == ND_F16, B, h0 * w0,
+                                                                Cl, Clp);
+    ND_CUDA(cudaGetLastError());
+    prof_end(s, "layout", 0.0, 0.0);
+    ND_OP("conv3x3", conv_flops(h0, w0, Clp, top), conv(s, xin, h0, w0, Clp, c1_w, c1_b, top, ND_EPI_STORE, X[0], nullptr));
+    ND_TRY_RC(res(s, mid0, h0, w0, X[0], X[1]));
+    ND_TRY_RC(attn(s, X[1], X[0]));
+    ND_TRY_RC(res(s, mid1, h0, w0, X[0], X[1]));
+    int cur = 1;  // index into X of the running activation
+    for (int i = 0; i < L; ++i) {
+      const WanLevel& v = lv[i];
+      const int hh = res_h(i), ww = res_w(i);
+      const int in = cur;  // the level's input stays put for the Wan 2.2 shortcut
+      const int o1 = (in + 1) % 3, o2 = (in + 2) % 3;
+      for (int j = 0; j < R + 1; ++j) {
+        const int dst = (j % 2 == 0) ? o1 : o2;
+        ND_TRY_RC(res(s, v.res[j], hh, ww, X[cur], X[dst]));
+        cur = dst;
+      }
+      if (v.up_out) {
+        const int dst = cur == o1 ? o2 : o1;
+        ND_OP("upsample", 0.0, upsample2x(X[cur], UPB, B, hh, ww, v.cout, s));
+        ND_OP("conv3x3", conv_flops(2 * hh, 2 * ww, v.cout, v.up_out),
+              conv(s, UPB, 2 * hh, 2 * ww, v.cout, v.upw, v.upb, v.up_out, ND_EPI_STORE, X[dst], nullptr));
+        cur = dst;
+        if (v.sc_mode >= 0) {
+          const int64_t n = static_cast<int64_t>(B) * 4 * hh * ww * v.up_out;
+          prof_begin(s);
+          wan_up_shortcut_kernel<<<grid_of(n), 256, 0, s>>>(X[cur], X[in], dt == ND_F16, B, hh, ww, v.cin, v.up_out,
+                                                            v.sc_mode);
+          ND_CUDA(cudaGetLastError());
+          prof_end(s, "upsample", 0.0, 0.0);
+        }
+      }
+    }
+    const int hh = res_h(L - 1), ww = res_w(L - 1), c = lv[L - 1].cout;
+    const int64_t img_px = static_cast<int64_t>(B) * hh * ww;
+    ND_OP("rmsnorm", 0.0, rms(s, X[cur], H1, img_px, c, head_g, true));
+    ND_OP("conv3x3", conv_flops(hh, ww, c, img_c),
+          conv(s, H1, hh, ww, c, head_w, head_b, 4, ND_EPI_STORE_F32, nullptr, nullptr, out_nhwc));
+    prof_begin(s);
+    vae_image_out_kernel<<<grid_of(img_px * 3), 256, 0, s>>>(out_nhwc, out_image, B, hh * ww);
+    ND_CUDA(cudaGetLastError());
+    prof_end(s, "layout", 0.0, 0.0);
+    return ND_OK;
+  }
+#undef ND_OP
+};
+
 }  // namespace
 
 nd_denoiser* make_vae_decoder() { return new VaeDecoder(); }
+nd_denoiser* make_wan_decoder() { return new WanDecoder(); }
 
 }  // namespace nd

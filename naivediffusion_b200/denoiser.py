@@ -20,6 +20,7 @@ from . import _lib
 from ._lib import check, lib
 
 FAMILY_MMDIT, FAMILY_ANIMA, FAMILY_SDXL, FAMILY_VAE_KL, FAMILY_QWEN_IMAGE = 0, 1, 2, 3, 4
+FAMILY_VAE_WAN21, FAMILY_VAE_WAN22 = 5, 6
 
 
 class ModelDesc(C.Structure):
@@ -511,6 +512,127 @@ class VaeDecoderConfig:
         return self.batch * total
 
 
+@dataclass
+class WanVaeConfig:
+    """The Wan VAE decoders on one frame: version 21 (Vae/WanVae.cs, Anima's:
+    base width 96, 16 latent channels, 8x) or 22 (Vae/Wan22Vae.cs, Qwen-Image
+    2.1's: base width 144, 64 latent channels, five levels, 16x, the up
+    shortcuts). Defaults: Wan 2.1 decoding a 16 x 128 x 128 latent into a
+    1024 x 1024 image at fp16."""
+    version: int = 21
+    width: int = 96
+    latent_channels: int = 16
+    latent_height: int = 128
+    latent_width: int = 128
+    batch: int = 1
+    resnets: int = 2                  # resblocks per level - 1 (the reference's ResnetsPerLevel)
+    compute: int = _lib.ND_F16
+
+    @property
+    def scale(self) -> int:
+        return 16 if self.version == 22 else 8
+
+    @property
+    def image_height(self) -> int:
+        return self.latent_height * self.scale
+
+    @property
+    def image_width(self) -> int:
+        return self.latent_width * self.scale
+
+    def desc(self) -> ModelDesc:
+        d = ModelDesc()
+        d.family = FAMILY_VAE_WAN22 if self.version == 22 else FAMILY_VAE_WAN21
+        d.width = self.width
+        d.latent_channels, d.latent_height, d.latent_width = self.latent_channels, self.latent_height, self.latent_width
+        d.batch, d.compute, d.weight_dtype = self.batch, self.compute, self.compute
+        d.unet_resnets = self.resnets
+        return d
+
+    def levels(self):
+        """(in, out, upsample-conv out or 0, shortcut mode or -1) per level:
+        dims = width x [m_last, m reversed]; Wan 2.1's upsample convolution
+        halves the width, Wan 2.2's keeps it and adds the up shortcut."""
+        v22 = self.version == 22
+        m = (1, 2, 4, 8, 8) if v22 else (1, 2, 4, 4)
+        L = len(m)
+        dims = [self.width * m[-1]] + [self.width * u for u in reversed(m)]
+        temporal = (False, True, True, True)
+        out = []
+        for i in range(L):
+            cin = dims[i] // 2 if (not v22 and i > 0) else dims[i]
+            cout = dims[i + 1]
+            up = 0 if i == L - 1 else (cout if v22 else cout // 2)
+            mode = -1
+            if v22 and up:
+                mode = 0 if cin == up else (1 if temporal[L - 2 - i] else 2)
+            out.append((cin, cout, up, mode))
+        return out
+
+    def weight_shapes(self):
+        C, R = self.latent_channels, self.resnets
+        lv = self.levels()
+        top = lv[0][0]
+        t = [("conv2.weight", (C, C, 1, 1), True), ("conv2.bias", (C,), False),
+             ("decoder.conv1.weight", (top, C, 3, 3), True), ("decoder.conv1.bias", (top,), False)]
+
+        def res(p, ci, co):
+            r = [(p + ".residual.0.gamma", (ci,), True), (p + ".residual.2.weight", (co, ci, 3, 3), True),
+                 (p + ".residual.2.bias", (co,), False), (p + ".residual.3.gamma", (co,), True),
+                 (p + ".residual.6.weight", (co, co, 3, 3), True), (p + ".residual.6.bias", (co,), False)]
+            if ci != co:
+                r += [(p + ".shortcut.weight", (co, ci, 1, 1), True), (p + ".shortcut.bias", (co,), False)]
+            return r
+        t += res("decoder.middle.0", top, top)
+        t += [("decoder.middle.1.norm.gamma", (top,), True), ("decoder.middle.1.to_qkv.weight", (3 * top, top, 1, 1), True),
+              ("decoder.middle.1.to_qkv.bias", (3 * top,), False), ("decoder.middle.1.proj.weight", (top, top, 1, 1), True),
+              ("decoder.middle.1.proj.bias", (top,), False)]
+        t += res("decoder.middle.2", top, top)
+        idx = 0
+        for i, (ci, co, up, _mode) in enumerate(lv):
+            pre = f"decoder.upsamples.{i}.upsamples." if self.version == 22 else "decoder.upsamples."
+            if self.version == 22:
+                idx = 0
+            c = ci
+            for _ in range(R + 1):
+                t += res(f"{pre}{idx}", c, co)
+                idx += 1
+                c = co
+            if up:
+                t += [(f"{pre}{idx}.resample.1.weight", (up, co, 3, 3), True), (f"{pre}{idx}.resample.1.bias", (up,), False)]
+                idx += 1
+        last = lv[-1][1]
+        img = 4 if self.version == 22 else 3
+        t += [("decoder.head.0.gamma", (last,), True), ("decoder.head.2.weight", (img, last, 3, 3), True),
+              ("decoder.head.2.bias", (img,), False)]
+        return t
+
+    def flops_per_step(self) -> float:
+        """Convolutions, 1x1 shortcuts and the mid-block attention (1 MAC = 2 FLOP)."""
+        h, w = self.latent_height, self.latent_width
+        lv = self.levels()
+        top = lv[0][0]
+
+        def conv(px, ci, co, k=9):
+            return 2.0 * px * ci * co * k
+
+        def res(px, ci, co):
+            return conv(px, ci, co) + conv(px, co, co) + (conv(px, ci, co, 1) if ci != co else 0.0)
+        px = h * w
+        total = conv(px, self.latent_channels, top) + 2 * res(px, top, top) + 4 * 2.0 * px * top * top + 4.0 * px * px * top
+        for i, (ci, co, up, _m) in enumerate(lv):
+            px = (h << i) * (w << i)
+            c = ci
+            for _ in range(self.resnets + 1):
+                total += res(px, c, co)
+                c = co
+            if up:
+                total += conv(4 * px, co, up)
+        px = (h << (len(lv) - 1)) * (w << (len(lv) - 1))
+        total += conv(px, lv[-1][1], 4 if self.version == 22 else 3)
+        return self.batch * total
+
+
 def _name_seed(name: str, seed: int) -> int:
     return (zlib.crc32(name.encode()) ^ (seed * 0x9E3779B1)) & 0xFFFFFFFF
 
@@ -527,7 +649,7 @@ def synthetic_weights(cfg, seed: int = 0):
         for name, shape, _req in cfg.weight_shapes():
             rng = np.random.default_rng(_name_seed(name, seed))
             a = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
-            if len(shape) == 1 and "norm" in name and name.endswith(".weight"):
+            if len(shape) == 1 and (("norm" in name and name.endswith(".weight")) or name.endswith(".gamma")):
                 a += np.float32(1.0)
             if len(shape) > 1:
                 a = _round(a, cfg.compute)
@@ -556,7 +678,7 @@ def synthetic_weights_device(cfg, seed: int = 0, device="cuda"):
         for name, shape, _req in cfg.weight_shapes():
             g.manual_seed(_name_seed(name, seed))
             t = torch.randn(*shape, device=device, generator=g) * 0.02
-            if len(shape) == 1 and "norm" in name and name.endswith(".weight"):
+            if len(shape) == 1 and (("norm" in name and name.endswith(".weight")) or name.endswith(".gamma")):
                 t += 1.0
             yield name, (t.to(dt) if len(shape) > 1 else t)
         return
@@ -722,12 +844,15 @@ class CudaDenoiser:
 
     def output_shape(self, latent_shape) -> tuple:
         """What predict returns for a latent of this shape: the latent's shape,
-        or for the VAE decoder the [batch, 3, 8h, 8w] image."""
+        or for a VAE decoder the [batch, 3, s h, s w] image."""
         d = self.desc
+        b, _, h, w = latent_shape
         if d.family == FAMILY_VAE_KL:
             up = (d.unet_levels or 4) - 1
-            b, _, h, w = latent_shape
             return (b, 3, h << up, w << up)
+        if d.family in (FAMILY_VAE_WAN21, FAMILY_VAE_WAN22):
+            s = 16 if d.family == FAMILY_VAE_WAN22 else 8
+            return (b, 3, h * s, w * s)
         return tuple(latent_shape)
 
     def predict(self, latent: np.ndarray, timestep: float, sigma: float, conditioning: dict,

@@ -170,8 +170,9 @@ def modulate(x: torch.Tensor, shift: torch.Tensor | None, scale: torch.Tensor, *
 
 
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor | None, *, out_dtype=None, plus_one=False,
-            eps: float = 1e-6) -> torch.Tensor:
-    """x * rsqrt(mean(x^2) + eps) * (weight [+ 1]) over rows (CpuMath.RmsNorm)."""
+            eps: float = 1e-6, silu: bool = False) -> torch.Tensor:
+    """x * rsqrt(mean(x^2) + eps) * (weight [+ 1]) over rows (CpuMath.RmsNorm),
+    then SiLU when silu=True."""
     rows, width = x.shape
     out = torch.empty(rows, width, device=x.device, dtype=out_dtype or x.dtype)
     a = RmsNormArgs()
@@ -181,6 +182,7 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor | None, *, out_dtype=None, plu
     a.weight = _ptr(weight)
     a.plus_one = int(plus_one)
     a.eps = eps
+    a.silu = int(silu)
     check(lib().nd_op_rmsnorm(C.byref(a), C.c_void_p(_stream())))
     return out
 
@@ -248,7 +250,8 @@ def conv2d(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
            epilogue: str = "store", addend: torch.Tensor | None = None,
            per_batch_bias: bool = False) -> torch.Tensor:
     """3x3 convolution, padding 1, over NHWC activations x [B, H, W, Cin] with
-    weight [Cout, 3, 3, Cin] (Layers.Conv2d, Graph/Layers.cs:115-128).
+    weight [Cout, 3, 3, Cin rounded up to 64, the pad zero] (Layers.Conv2d,
+    Graph/Layers.cs:115-128).
     bias: [Cout] fp32, or [B, Cout] with per_batch_bias."""
     b, h, w, cin = x.shape
     cout = weight.shape[0]

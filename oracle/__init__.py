@@ -662,3 +662,81 @@ def vae_decode(w: dict, cfg, latent):
         x = group_norm(x, 32, w["decoder.conv_norm_out.weight"], w.get("decoder.conv_norm_out.bias"), eps, True)
         outs.append(conv2d(x, w["decoder.conv_out.weight"], w.get("decoder.conv_out.bias")))
     return np.stack(outs)
+
+
+def wan_channel_rms(x, gamma, silu_after=False):
+    """WanVae.ChannelRmsNorm (Vae/WanVae.cs:111-121) over one image x [C, H, W]:
+    each pixel's channels over sqrt(mean(x^2) + 1e-24 / C), times gamma."""
+    c = x.shape[0]
+    t = np.ascontiguousarray(np.asarray(x, np.float32).reshape(c, -1).T)
+    y = rmsnorm(t, gamma, 1e-24 / c)
+    if silu_after:
+        y = silu(y)
+    return np.ascontiguousarray(y.T.reshape(x.shape))
+
+
+def wan22_up_shortcut(x, out_c, temporal):
+    """Wan22Vae.UpShortcut (Vae/Wan22Vae.cs:121-155) for one image x [C, H, W]."""
+    c = x.shape[0]
+    if c == out_c:
+        return x.repeat(2, axis=1).repeat(2, axis=2)
+    if c != 2 * out_c:
+        raise ValueError("an up level halves its channels at most")
+    if temporal:
+        return x[1::2].repeat(2, axis=1).repeat(2, axis=2)
+    _, h, w = x.shape
+    y = np.empty((out_c, 2 * h, 2 * w), np.float32)
+    y[:, 0::2, :] = x[0::2].repeat(2, axis=2)
+    y[:, 1::2, :] = x[1::2].repeat(2, axis=2)
+    return y
+
+
+def wan_vae_decode(w: dict, cfg, latent):
+    """WanVae.Decoder / Wan22Vae.Decoder (Vae/WanVae.cs:170-207,
+    Vae/Wan22Vae.cs:161-206) in fp32 on one frame, one image at a time:
+    latent [B, C, h, w] -> image [B, 3, s h, s w] (Wan 2.2's RGB of RGBA)."""
+    v22 = cfg.version == 22
+
+    def res(x, p):
+        h = conv2d(wan_channel_rms(x, w[p + ".residual.0.gamma"], True), w[p + ".residual.2.weight"],
+                   w.get(p + ".residual.2.bias"))
+        h = conv2d(wan_channel_rms(h, w[p + ".residual.3.gamma"], True), w[p + ".residual.6.weight"],
+                   w.get(p + ".residual.6.bias"))
+        if p + ".shortcut.weight" in w:
+            x = conv2d(x, w[p + ".shortcut.weight"], w.get(p + ".shortcut.bias"), 1, 0)
+        return x + h
+
+    def attn(x, p):
+        c, hh, ww = x.shape
+        qkv = conv2d(wan_channel_rms(x, w[p + ".norm.gamma"]), w[p + ".to_qkv.weight"], w.get(p + ".to_qkv.bias"), 1, 0)
+        part = lambda i: np.ascontiguousarray(qkv[i * c:(i + 1) * c].reshape(c, -1).T)  # noqa: E731
+        o = np.ascontiguousarray(attention(part(0), part(1), part(2), 1).T.reshape(c, hh, ww))
+        return conv2d(o, w[p + ".proj.weight"], w.get(p + ".proj.bias"), 1, 0) + x
+
+    L = 5 if v22 else 4
+    temporal = (False, True, True, True)
+    outs = []
+    for b in range(latent.shape[0]):
+        x = conv2d(np.asarray(latent[b], np.float32), w["conv2.weight"], w.get("conv2.bias"), 1, 0)
+        x = conv2d(x, w["decoder.conv1.weight"], w.get("decoder.conv1.bias"))
+        x = res(x, "decoder.middle.0")
+        x = attn(x, "decoder.middle.1")
+        x = res(x, "decoder.middle.2")
+        idx = 0
+        for level in range(L):
+            pre = f"decoder.upsamples.{level}.upsamples." if v22 else "decoder.upsamples."
+            if v22:
+                idx = 0
+            inp = x
+            for _ in range(cfg.resnets + 1):
+                x = res(x, f"{pre}{idx}")
+                idx += 1
+            if level != L - 1:
+                x = x.repeat(2, axis=1).repeat(2, axis=2)
+                x = conv2d(x, w[f"{pre}{idx}.resample.1.weight"], w.get(f"{pre}{idx}.resample.1.bias"))
+                idx += 1
+                if v22:
+                    x = x + wan22_up_shortcut(inp, x.shape[0], temporal[L - 2 - level])
+        x = wan_channel_rms(x, w["decoder.head.0.gamma"], True)
+        outs.append(conv2d(x, w["decoder.head.2.weight"], w.get("decoder.head.2.bias"))[:3])
+    return np.stack(outs)

@@ -43,8 +43,13 @@ def _conv_ref(x, wt, bias, stride):
 
 
 def _dev_weight(wt):
-    """[Cout, Cin, 3, 3] -> the kernel's [Cout, 3, 3, Cin] on the device."""
-    return wt.permute(0, 2, 3, 1).contiguous().cuda()
+    """[Cout, Cin, 3, 3] -> the kernel's [Cout, 3, 3, Cin rounded up to 64] on the device."""
+    w = wt.permute(0, 2, 3, 1)
+    cin = w.shape[3]
+    pad = (cin + 63) // 64 * 64 - cin
+    if pad:
+        w = torch.nn.functional.pad(w, (0, pad))
+    return w.contiguous().cuda()
 
 
 @pytest.mark.parametrize("b,h,w,cin,cout,stride", [
@@ -56,6 +61,9 @@ def _dev_weight(wt):
     (1, 16, 256, 64, 64, 1),    # rows wider than a tile: 128-pixel pieces of a row
     (1, 8, 512, 128, 32, 2),    # ... with stride 2 (256 output pixels per row)
     (2, 4, 1024, 64, 64, 1),
+    (1, 16, 16, 96, 64, 1),     # channels not a multiple of 64: the last chunk is zero-filled
+    (1, 32, 32, 144, 96, 1),
+    (1, 16, 32, 288, 144, 2),
 ])
 def test_conv3x3_matches_oracle(cuda, b, h, w, cin, cout, stride):
     x, wt, bias = _conv_case(b, h, w, cin, cout, seed=cin + cout + stride)
@@ -89,8 +97,8 @@ def test_conv3x3_epilogues(cuda):
 
 
 def test_conv3x3_rejects_unsupported(cuda):
-    x = torch.zeros(1, 16, 16, 48, dtype=torch.float16, device="cuda")
-    wt = torch.zeros(64, 3, 3, 48, dtype=torch.float16, device="cuda")
+    x = torch.zeros(1, 16, 16, 60, dtype=torch.float16, device="cuda")
+    wt = torch.zeros(64, 3, 3, 64, dtype=torch.float16, device="cuda")
     with pytest.raises(Exception, match="in_channels"):
         ops.conv2d(x, wt)
     x = torch.zeros(1, 12, 12, 64, dtype=torch.float16, device="cuda")
