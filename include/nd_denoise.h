@@ -93,6 +93,14 @@ ND_API const char* nd_version(void);
                                (Vae/Wan22Vae.cs): width 144, latent_channels 64, five
                                levels, 16x upsampling, the up shortcuts; the RGB of
                                its RGBA output, [batch, 3, 16h, 16w] */
+#define ND_FAMILY_QWEN3_TEXT 7 /* Qwen3 decoder as a text encoder (Text/Qwen/Qwen3TextModel.cs):
+                               width, heads x head_dim 128, kv_heads, blocks = layers,
+                               mlp_width, vocab, rope_theta; context_rows = most tokens
+                               per call; run with nd_text_encode */
+#define ND_FAMILY_LLM_ADAPTER 8 /* Anima's LLM adapter (Models/Anima/LlmAdapter.cs): width
+                               1024, heads 16 x 64, blocks 6, mlp_width 4096, vocab (T5),
+                               rope_theta 1e4; context_rows = most T5 ids per call,
+                               source_rows = most Qwen3 rows; run with nd_text_encode */
 
 typedef struct nd_device nd_device;
 typedef struct nd_denoiser nd_denoiser;
@@ -120,6 +128,11 @@ typedef struct nd_model_desc {
   int unet_depth[4];
   int unet_resnets;
   int add_width;              /* SDXL: width of the "add" conditioning (2816) */
+  /* text towers (ND_FAMILY_QWEN3_TEXT, ND_FAMILY_LLM_ADAPTER) */
+  int kv_heads;               /* key / value heads (grouped-query attention; 0 = heads) */
+  int vocab;                  /* rows of the token embedding table */
+  int source_rows;            /* LLM adapter: most Qwen3 rows one call cross-attends to */
+  double rope_theta;          /* rotary base (Qwen3-0.6B 1e6, Qwen3-VL-8B 5e6, adapter 1e4) */
 } nd_model_desc;
 
 typedef struct nd_named_tensor {
@@ -205,6 +218,28 @@ ND_API int nd_denoiser_predict(nd_denoiser* d, const float* latent, double times
 ND_API int nd_denoiser_predict_device(nd_denoiser* d, const float* latent, double timestep,
                                       double sigma, int n_cond, const nd_named_tensor* cond,
                                       float* out, void* stream);
+
+/* The text towers, the step before the path: Qwen3TextModel.Forward
+ * (Text/Qwen/Qwen3TextModel.cs:47-104) for ND_FAMILY_QWEN3_TEXT and
+ * LlmAdapter.Forward (Models/Anima/LlmAdapter.cs:29-78) for
+ * ND_FAMILY_LLM_ADAPTER, on a denoiser handle of that family (weights set
+ * and finalized as for the denoisers). ids: `rows` token ids in host memory
+ * (rows <= desc.context_rows, every id < desc.vocab); source: the adapter's
+ * Qwen3 hidden states [source_rows, width] fp32 host (NULL, 0 for Qwen3);
+ * final_norm: Qwen3 only, 1 = through model.norm (what Anima's adapter reads),
+ * 0 = the last block's output (what Qwen-Image 2.1 reads). out: [rows, width]
+ * fp32 host. Synchronous. */
+ND_API int nd_text_encode(nd_denoiser* d, const int32_t* ids, int rows, const float* source, int source_rows,
+                          int final_norm, float* out);
+
+/* Per-head RMSNorm then rotate-half RoPE, in place (Transformer.HeadNorm +
+ * Transformer.Rotate, Graph/Transformer.cs:37-64; CpuMath.RmsNorm + Rope):
+ * x [rows, ld] bf16 / f16 / f32, heads of head_dim (64 or 128) from column 0;
+ * each head's features times rsqrt(mean(x^2) + eps) * weight[head_dim], then
+ * rotated by row r's angles cos / sin [rows, head_dim / 2] (NULL: no rotation). */
+ND_API int nd_op_head_norm_rope(void* x, int dtype, int64_t ld, int64_t rows, int heads, int head_dim,
+                                const float* weight, const float* cos, const float* sin, float eps,
+                                void* stream);
 
 /* Per-kernel-class timing: run the step `steps` times eagerly on the last
  * staged inputs with a CUDA event pair around every launch, and return per
@@ -355,6 +390,11 @@ typedef struct nd_attention_args {
   int out_dtype;        /* 0: dtype. With dtype ND_F32 also ND_BF16X2: out is a
                            hi|lo pair [rows, 2 * heads * head_dim] (ldo counts
                            bf16 elements) */
+  int kv_heads;         /* 0: heads. Fewer (dividing heads) is grouped-query
+                           attention: query head h reads key / value head
+                           h / (heads / kv_heads) (CpuMath.Attention,
+                           Tensors/CpuMath.cs:196-248); k and v are then
+                           [rows, kv_heads * head_dim] */
 } nd_attention_args;
 
 ND_API int nd_op_attention(const nd_attention_args* args, void* stream);

@@ -80,7 +80,7 @@ class AttentionArgs(C.Structure):
         ("causal", C.c_int),
         ("q", C.c_void_p), ("ldq", C.c_int64), ("k", C.c_void_p), ("ldk", C.c_int64),
         ("v", C.c_void_p), ("ldv", C.c_int64), ("out", C.c_void_p), ("ldo", C.c_int64),
-        ("scale", C.c_float), ("out_dtype", C.c_int),
+        ("scale", C.c_float), ("out_dtype", C.c_int), ("kv_heads", C.c_int),
     ]
 
 
@@ -151,6 +151,8 @@ def lib() -> C.CDLL:
         L.nd_op_sampler_step.argtypes = [C.POINTER(SamplerArgs), C.c_void_p]
         L.nd_op_modulate.argtypes = [C.POINTER(ModulateArgs), C.c_void_p]
         L.nd_op_rmsnorm.argtypes = [C.POINTER(RmsNormArgs), C.c_void_p]
+        L.nd_op_head_norm_rope.argtypes = [C.c_void_p, C.c_int, C.c_int64, C.c_int64, C.c_int, C.c_int, C.c_void_p,
+                                           C.c_void_p, C.c_void_p, C.c_float, C.c_void_p]
         L.nd_op_gemv.argtypes = [C.POINTER(GemvArgs), C.c_void_p]
         L.nd_op_patchify.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                      C.c_int, C.c_int, C.c_int64, C.c_void_p]

@@ -21,17 +21,20 @@ int attention(const nd_attention_args& a, cudaStream_t stream) {
     return fail(ND_ERR_INVALID, "attention: shape too large");
   const int64_t limit = a.key_limit <= 0 || a.key_limit > a.kv_rows ? a.kv_rows : a.key_limit;
   if (!a.q || !a.k || !a.v || !a.out) return fail(ND_ERR_INVALID, "attention: null operand");
+  const int kvh = a.kv_heads > 0 ? a.kv_heads : a.heads;
+  if (a.heads % kvh) return fail(ND_ERR_INVALID, "attention: kv_heads must divide heads");
   const int64_t width = static_cast<int64_t>(a.heads) * hd;
-  if (a.ldq < width || a.ldk < width || a.ldv < width || a.ldo < width)
-    return fail(ND_ERR_INVALID, "attention: leading dimensions must cover heads * head_dim");
+  const int64_t kv_width = static_cast<int64_t>(kvh) * hd;
+  if (a.ldq < width || a.ldk < kv_width || a.ldv < kv_width || a.ldo < width)
+    return fail(ND_ERR_INVALID, "attention: leading dimensions must cover heads (kv_heads) * head_dim");
   if ((a.ldo % 8) || (reinterpret_cast<uintptr_t>(a.out) & 15u))
     return fail(ND_ERR_INVALID, "attention: out must be 16-byte aligned with ldo % 8 == 0");
   if (a.causal && a.q_rows != a.kv_rows) return fail(ND_ERR_INVALID, "attention: causal needs q_rows == kv_rows");
 
   CUtensorMap tq, tk, tv;
   int rc = make_tmap_2d(&tq, a.q, 2, a.batch * a.q_rows, width, a.ldq, 128, 64, true);
-  if (!rc) rc = make_tmap_2d(&tk, a.k, 2, a.batch * a.kv_rows, width, a.ldk, 128, 64, true);
-  if (!rc) rc = make_tmap_2d(&tv, a.v, 2, a.batch * a.kv_rows, width, a.ldv, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&tk, a.k, 2, a.batch * a.kv_rows, kv_width, a.ldk, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&tv, a.v, 2, a.batch * a.kv_rows, kv_width, a.ldv, 128, 64, true);
   if (rc) return rc;
 
   AttnArgs g{};
@@ -39,6 +42,7 @@ int attention(const nd_attention_args& a, cudaStream_t stream) {
   g.kv_rows = static_cast<int>(a.kv_rows);
   g.key_limit = static_cast<int>(limit);
   g.causal = a.causal ? 1 : 0;
+  g.kv_group = a.heads / kvh;
   const float scale = a.scale > 0.f ? a.scale : 1.0f / std::sqrt(static_cast<float>(hd));
   g.scale_log2 = scale * 1.4426950408889634f;
   g.out = a.out;

@@ -32,6 +32,7 @@ struct AttnF32Args {
   int out_split;     // 0: fp32 out; 1: bf16 hi|lo pair, lo lo_off elements along
   long long lo_off;
   int q_rows, kv_rows, key_limit, causal;
+  int kv_group;      // query heads per key / value head
   float scale;
 };
 
@@ -62,6 +63,7 @@ __global__ void __launch_bounds__(128) attention_f32_kernel(const AttnF32Args g)
   const long long qbase = static_cast<long long>(b) * g.q_rows;
   const long long kbase = static_cast<long long>(b) * g.kv_rows;
   const int col0 = head * HD;
+  const int kv_col0 = (head / g.kv_group) * HD;
 
   // Q^T, pre-multiplied by nothing: the scale is applied to the scores.
   for (int idx = tid; idx < kBQ * HD / 4; idx += 128) {
@@ -95,7 +97,7 @@ __global__ void __launch_bounds__(128) attention_f32_kernel(const AttnF32Args g)
       const int c = idx % kBK, d4 = idx / kBK;
       float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
       if (k0 + c < g.kv_rows)
-        t = __ldg(reinterpret_cast<const float4*>(g.k + (kbase + k0 + c) * g.ldk + col0) + d4);
+        t = __ldg(reinterpret_cast<const float4*>(g.k + (kbase + k0 + c) * g.ldk + kv_col0) + d4);
       kt[(4 * d4 + 0) * kBK + c] = t.x;
       kt[(4 * d4 + 1) * kBK + c] = t.y;
       kt[(4 * d4 + 2) * kBK + c] = t.z;
@@ -105,7 +107,7 @@ __global__ void __launch_bounds__(128) attention_f32_kernel(const AttnF32Args g)
       const int j = idx / (HD / 4), d4 = idx % (HD / 4);
       float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
       if (k0 + j < g.kv_rows)
-        t = __ldg(reinterpret_cast<const float4*>(g.v + (kbase + k0 + j) * g.ldv + col0) + d4);
+        t = __ldg(reinterpret_cast<const float4*>(g.v + (kbase + k0 + j) * g.ldv + kv_col0) + d4);
       reinterpret_cast<float4*>(vs)[idx] = t;
     }
     __syncthreads();
@@ -254,9 +256,12 @@ int attention_f32(const nd_attention_args& a, cudaStream_t stream) {
   const int out_dtype = a.out_dtype ? a.out_dtype : ND_F32;
   if (out_dtype != ND_F32 && out_dtype != ND_BF16X2)
     return fail(ND_ERR_INVALID, "attention: fp32 attention writes f32 or bf16x2");
+  const int kvh = a.kv_heads > 0 ? a.kv_heads : a.heads;
+  if (a.heads % kvh) return fail(ND_ERR_INVALID, "attention: kv_heads must divide heads");
   const int64_t width = static_cast<int64_t>(a.heads) * hd;
-  if (a.ldq < width || a.ldk < width || a.ldv < width || a.ldq % 4 || a.ldk % 4 || a.ldv % 4)
-    return fail(ND_ERR_INVALID, "attention: fp32 q/k/v need ld >= heads * head_dim, ld % 4 == 0");
+  const int64_t kv_width = static_cast<int64_t>(kvh) * hd;
+  if (a.ldq < width || a.ldk < kv_width || a.ldv < kv_width || a.ldq % 4 || a.ldk % 4 || a.ldv % 4)
+    return fail(ND_ERR_INVALID, "attention: fp32 q/k/v need ld >= heads (kv_heads) * head_dim, ld % 4 == 0");
   const auto mis16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; };
   if (mis16(a.q) || mis16(a.k) || mis16(a.v) || mis16(a.out))
     return fail(ND_ERR_INVALID, "attention: operands must be 16-byte aligned");
@@ -281,6 +286,7 @@ int attention_f32(const nd_attention_args& a, cudaStream_t stream) {
   g.kv_rows = static_cast<int>(a.kv_rows);
   g.key_limit = static_cast<int>(a.key_limit <= 0 || a.key_limit > a.kv_rows ? a.kv_rows : a.key_limit);
   g.causal = a.causal ? 1 : 0;
+  g.kv_group = a.heads / kvh;
   g.scale = a.scale > 0.f ? a.scale : 1.0f / std::sqrt(static_cast<float>(hd));
   return hd == 128 ? launch_f32<128>(g, a.heads, a.batch, stream) : launch_f32<64>(g, a.heads, a.batch, stream);
 }

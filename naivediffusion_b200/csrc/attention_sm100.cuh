@@ -32,6 +32,7 @@ struct AttnArgs {
   int kv_rows;      // key rows per batch item
   int key_limit;    // keys visible per batch item (<= kv_rows)
   int causal;       // row i sees keys [0, i]
+  int kv_group;     // query heads per key / value head (grouped-query attention)
   float scale_log2; // softmax scale * log2(e)
   void* out;        // [batch * q_rows, ldo], head h at columns [h*128, h*128+128)
   long long ldo;
@@ -112,6 +113,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (a.causal) limit = min(limit, q_tile0 + 256);
   const int n_kv = (limit + 127) / 128;
   const int col0 = head * HD;
+  const int kv_col0 = (head / a.kv_group) * HD;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -168,11 +170,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_arrive_expect_tx(k_full(st), L::kTile);
         for (int c = 0; c < L::kChunks; ++c)
           tma_load_2d(sbase + L::kK + st * L::kTile + c * 16384, &tmK, k_full(st),
-                      col0 + c * 64, krow);
+                      kv_col0 + c * 64, krow);
         mbar_arrive_expect_tx(v_full(st), L::kTile);
         for (int c = 0; c < L::kChunks; ++c)
           tma_load_2d(sbase + L::kV + st * L::kTile + c * 16384, &tmV, v_full(st),
-                      col0 + c * 64, krow);
+                      kv_col0 + c * 64, krow);
         issued |= 1u << st;
         issued_parity = (issued_parity & ~(1u << st)) | (ph << st);
       }

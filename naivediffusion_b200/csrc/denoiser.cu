@@ -451,6 +451,8 @@ int nd_denoiser_create(nd_device* dev, const nd_model_desc* desc, nd_denoiser** 
     case ND_FAMILY_QWEN_IMAGE: d = nd::make_qwen_image(); break;
     case ND_FAMILY_VAE_WAN21:
     case ND_FAMILY_VAE_WAN22: d = nd::make_wan_decoder(); break;
+    case ND_FAMILY_QWEN3_TEXT: d = nd::make_qwen3_text(); break;
+    case ND_FAMILY_LLM_ADAPTER: d = nd::make_llm_adapter(); break;
     default: return nd::fail(ND_ERR_UNSUPPORTED, "nd_denoiser_create: unknown model family");
   }
   d->dev = dev;
@@ -537,6 +539,18 @@ int nd_denoiser_finalize(nd_denoiser* d) {
   if (rc) return rc;
   d->finalized = true;
   return ND_OK;
+}
+
+int nd_denoiser::encode(const int32_t*, int, const float*, int, int, float*) {
+  return nd::fail(ND_ERR_INVALID, "text_encode: this family is not a text tower");
+}
+
+int nd_text_encode(nd_denoiser* d, const int32_t* ids, int rows, const float* source, int source_rows,
+                   int final_norm, float* out) {
+  if (!d || !ids || !out) return nd::fail(ND_ERR_INVALID, "text_encode: null argument");
+  if (!d->finalized) return nd::fail(ND_ERR_STATE, "text_encode: call nd_denoiser_finalize first");
+  nd::DeviceGuard g(d->dev->ordinal);
+  return d->encode(ids, rows, source, source_rows, final_norm, out);
 }
 
 int nd_denoiser_predict(nd_denoiser* d, const float* latent, double timestep, double sigma, int n_cond,

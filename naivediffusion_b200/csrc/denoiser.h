@@ -154,6 +154,9 @@ struct nd_denoiser {
   // the VAE decoder).
   virtual int64_t output_elems() const { return latent_elems(); }
   virtual int check_cond(int n, const nd_named_tensor* cond, nd::StepInputs& in) = 0;
+  // Text towers (nd_text_encode): one call over `rows` token ids.
+  virtual int encode(const int32_t* ids, int rows, const float* source, int source_rows, int final_norm,
+                     float* out);
 };
 
 namespace nd {
@@ -163,4 +166,8 @@ nd_denoiser* make_unet();
 nd_denoiser* make_vae_decoder();
 nd_denoiser* make_qwen_image();
 nd_denoiser* make_wan_decoder();
+nd_denoiser* make_qwen3_text();
+nd_denoiser* make_llm_adapter();
+int head_norm_rope(void* x, int dtype, int64_t ld, int64_t rows, int heads, int head_dim, const float* weight,
+                   const float* cos, const float* sin, float eps, cudaStream_t s);
 }  // namespace nd

@@ -21,6 +21,7 @@ from ._lib import check, lib
 
 FAMILY_MMDIT, FAMILY_ANIMA, FAMILY_SDXL, FAMILY_VAE_KL, FAMILY_QWEN_IMAGE = 0, 1, 2, 3, 4
 FAMILY_VAE_WAN21, FAMILY_VAE_WAN22 = 5, 6
+FAMILY_QWEN3_TEXT, FAMILY_LLM_ADAPTER = 7, 8
 
 
 class ModelDesc(C.Structure):
@@ -30,7 +31,8 @@ class ModelDesc(C.Structure):
         "patch", "time_width", "batch", "compute", "weight_dtype", "quant_group",
         "quant_scale_dtype", "adaln_rank")] + [("eps", C.c_float), ("unet_levels", C.c_int),
         ("unet_mult", C.c_int * 4), ("unet_depth", C.c_int * 4), ("unet_resnets", C.c_int),
-        ("add_width", C.c_int)]
+        ("add_width", C.c_int), ("kv_heads", C.c_int), ("vocab", C.c_int), ("source_rows", C.c_int),
+        ("rope_theta", C.c_double)]
 
 
 class NamedTensor(C.Structure):
@@ -68,6 +70,7 @@ def _bind() -> C.CDLL:
     L.nd_denoiser_memory.argtypes = [P, C.POINTER(Memory)]
     L.nd_denoiser_profile.argtypes = [P, C.c_int, C.POINTER(KernelTime), C.c_int, C.POINTER(C.c_int)]
     L.nd_denoiser_destroy.argtypes = [P]
+    L.nd_text_encode.argtypes = [P, P, C.c_int, P, C.c_int, C.c_int, P]
     L._nd_denoiser_bound = True
     return L
 
@@ -222,6 +225,99 @@ class QwenImageConfig:
         attn = 2 * ni * (ni + real) * D + R * real * D
         emb = ni * self.latent_channels * D * 2 + R * self.context_width * D + R * D * D
         return 2.0 * (self.blocks * (gemm + attn) + emb)
+
+
+@dataclass
+class Qwen3TextConfig:
+    """A Qwen3 decoder read as a text encoder (Text/Qwen/Qwen3TextModel.cs).
+    Defaults: Qwen3-0.6B (Anima's: 1024 wide, 28 layers, 16 x 128 query heads,
+    8 key/value heads, SwiGLU 3072, rotary base 1e6); Qwen3-VL-8B's language
+    model is qwen3_vl_8b(). context_rows = most tokens per call."""
+    width: int = 1024
+    blocks: int = 28
+    heads: int = 16
+    kv_heads: int = 8
+    mlp_width: int = 3072
+    vocab: int = 151936
+    rope_theta: float = 1e6
+    context_rows: int = 512
+    compute: int = _lib.ND_BF16
+    eps: float = 1e-6
+
+    @staticmethod
+    def qwen3_vl_8b(**kw):
+        return Qwen3TextConfig(width=4096, blocks=36, heads=32, kv_heads=8, mlp_width=12288, rope_theta=5e6, **kw)
+
+    def desc(self) -> ModelDesc:
+        d = ModelDesc()
+        d.family = FAMILY_QWEN3_TEXT
+        d.width, d.heads, d.head_dim, d.kv_heads = self.width, self.heads, 128, self.kv_heads
+        d.blocks, d.mlp_width, d.vocab, d.rope_theta = self.blocks, self.mlp_width, self.vocab, self.rope_theta
+        d.context_rows, d.batch = self.context_rows, 1
+        d.compute = d.weight_dtype = self.compute
+        d.eps = self.eps
+        return d
+
+    def weight_shapes(self):
+        W, F, QW, KW = self.width, self.mlp_width, self.heads * 128, self.kv_heads * 128
+        t = [("model.embed_tokens.weight", (self.vocab, W), True), ("model.norm.weight", (W,), True)]
+        for l in range(self.blocks):
+            p = f"model.layers.{l}."
+            t += [(p + "input_layernorm.weight", (W,), True), (p + "self_attn.q_proj.weight", (QW, W), True),
+                  (p + "self_attn.k_proj.weight", (KW, W), True), (p + "self_attn.v_proj.weight", (KW, W), True),
+                  (p + "self_attn.q_norm.weight", (128,), True), (p + "self_attn.k_norm.weight", (128,), True),
+                  (p + "self_attn.o_proj.weight", (W, QW), True), (p + "post_attention_layernorm.weight", (W,), True),
+                  (p + "mlp.gate_proj.weight", (F, W), True), (p + "mlp.up_proj.weight", (F, W), True),
+                  (p + "mlp.down_proj.weight", (W, F), True)]
+        return t
+
+    def flops(self, rows: int) -> float:
+        W, F, QW, KW = self.width, self.mlp_width, self.heads * 128, self.kv_heads * 128
+        per = rows * (W * (QW + 2 * KW) + QW * W + 3 * W * F) + rows * rows * QW
+        return 2.0 * self.blocks * per
+
+
+@dataclass
+class LlmAdapterConfig:
+    """Anima's LLM adapter (Models/Anima/LlmAdapter.cs): 6 blocks 1024 wide,
+    16 x 64 heads, GELU MLP 4096, rotary base 1e4, T5's 32128-id table.
+    context_rows = most T5 ids per call, source_rows = most Qwen3 rows."""
+    width: int = 1024
+    blocks: int = 6
+    heads: int = 16
+    head_dim: int = 64
+    mlp_width: int = 4096
+    vocab: int = 32128
+    rope_theta: float = 1e4
+    context_rows: int = 512
+    source_rows: int = 512
+    compute: int = _lib.ND_BF16
+    eps: float = 1e-6
+
+    def desc(self) -> ModelDesc:
+        d = ModelDesc()
+        d.family = FAMILY_LLM_ADAPTER
+        d.width, d.heads, d.head_dim = self.width, self.heads, self.head_dim
+        d.blocks, d.mlp_width, d.vocab, d.rope_theta = self.blocks, self.mlp_width, self.vocab, self.rope_theta
+        d.context_rows, d.source_rows, d.batch = self.context_rows, self.source_rows, 1
+        d.compute = d.weight_dtype = self.compute
+        d.eps = self.eps
+        return d
+
+    def weight_shapes(self):
+        W, F, hd = self.width, self.mlp_width, self.head_dim
+        t = [("embed.weight", (self.vocab, W), True), ("out_proj.weight", (W, W), True), ("out_proj.bias", (W,), False),
+             ("norm.weight", (W,), True)]
+        for b in range(self.blocks):
+            p = f"blocks.{b}."
+            t += [(p + "norm_self_attn.weight", (W,), True), (p + "norm_cross_attn.weight", (W,), True),
+                  (p + "norm_mlp.weight", (W,), True)]
+            for a in ("self_attn", "cross_attn"):
+                t += [(p + f"{a}.{n}_proj.weight", (W, W), True) for n in ("q", "k", "v", "o")]
+                t += [(p + f"{a}.q_norm.weight", (hd,), True), (p + f"{a}.k_norm.weight", (hd,), True)]
+            t += [(p + "mlp.0.weight", (F, W), True), (p + "mlp.0.bias", (F,), False),
+                  (p + "mlp.2.weight", (W, F), True), (p + "mlp.2.bias", (W,), False)]
+        return t
 
 
 @dataclass
@@ -869,6 +965,19 @@ class CudaDenoiser:
         check(_bind().nd_denoiser_predict(self.handle, lat.ctypes.data_as(C.c_void_p), timestep, sigma,
                                           len(conditioning), arr, out.ctypes.data_as(C.c_void_p)))
         del keep
+        return out
+
+    def text_encode(self, ids, source: np.ndarray | None = None, final_norm: bool = True) -> np.ndarray:
+        """A text tower over token ids (nd_text_encode): Qwen3TextModel.Forward
+        or LlmAdapter.Forward (source = the Qwen3 hidden states). Returns
+        [len(ids), width] float32."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty((ids.size, self.desc.width), np.float32)
+        src = None if source is None else np.ascontiguousarray(source, np.float32)
+        check(_bind().nd_text_encode(self.handle, ids.ctypes.data_as(C.c_void_p), ids.size,
+                                     None if src is None else src.ctypes.data_as(C.c_void_p),
+                                     0 if src is None else src.shape[0], 1 if final_norm else 0,
+                                     out.ctypes.data_as(C.c_void_p)))
         return out
 
     def predict_device(self, latent, timestep: float, sigma: float, conditioning: dict, out, stream=None):

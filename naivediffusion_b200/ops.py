@@ -118,12 +118,13 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *,
               out: torch.Tensor | None = None, batch: int = 1, key_limit: int = 0,
               causal: bool = False, scale: float = 0.0, head_dim: int = 128,
-              out_pairs: bool = False) -> torch.Tensor:
+              out_pairs: bool = False, kv_heads: int = 0) -> torch.Tensor:
     """Flash attention over packed heads (Layers.Attend, Graph/Layers.cs:260-279).
 
     q: [batch * q_rows, >= heads*128] (row stride q.stride(0)); k, v likewise
     with kv_rows per item. Returns out [batch * q_rows, heads * 128].
     fp32 q/k/v run the fp32 attention; out_pairs then writes an ND_BF16X2 pair.
+    kv_heads < heads: grouped-query attention (k, v [rows, kv_heads * head_dim]).
     """
     q_rows = q.shape[0] // batch
     kv_rows = k.shape[0] // batch
@@ -142,6 +143,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *,
     a.v, a.ldv = v.data_ptr(), v.stride(0)
     a.out, a.ldo = out.data_ptr(), out.stride(0)
     a.scale = scale
+    a.kv_heads = kv_heads
     check(lib().nd_op_attention(C.byref(a), C.c_void_p(_stream())))
     return out
 
@@ -185,6 +187,16 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor | None, *, out_dtype=None, plu
     a.silu = int(silu)
     check(lib().nd_op_rmsnorm(C.byref(a), C.c_void_p(_stream())))
     return out
+
+
+def head_norm_rope(x: torch.Tensor, heads: int, head_dim: int, weight: torch.Tensor,
+                   cos: torch.Tensor | None = None, sin: torch.Tensor | None = None, eps: float = 1e-6) -> torch.Tensor:
+    """In place: per-head RMSNorm * weight then rotate-half RoPE with row r's
+    angles (Transformer.HeadNorm + Transformer.Rotate) over x [rows, >= heads * head_dim]."""
+    check(lib().nd_op_head_norm_rope(C.c_void_p(x.data_ptr()), _DT[x.dtype], x.stride(0), x.shape[0], heads, head_dim,
+                                     C.c_void_p(weight.data_ptr()), _ptr(cos), _ptr(sin), C.c_float(eps),
+                                     C.c_void_p(_stream())))
+    return x
 
 
 def gemv(w: torch.Tensor, x: torch.Tensor, bias: torch.Tensor | None = None, *,

@@ -740,3 +740,71 @@ def wan_vae_decode(w: dict, cfg, latent):
         x = wan_channel_rms(x, w["decoder.head.0.gamma"], True)
         outs.append(conv2d(x, w["decoder.head.2.weight"], w.get("decoder.head.2.bias"))[:3])
     return np.stack(outs)
+
+
+# ------------------------------------------------------------------ text towers
+
+def rope_tables_1d(rows, dim, theta):
+    """CpuMath.RopeTables (Tensors/CpuMath.cs:177-194): inverse frequencies in
+    float32, angle = position * frequency, [rows, dim / 2] cos and sin."""
+    half = dim // 2
+    i = np.arange(half, dtype=np.float32)
+    freq = np.float32(1) / np.power(np.float32(theta), np.float32(2) * i / np.float32(dim))
+    ang = np.arange(rows, dtype=np.float32)[:, None] * freq[None, :]
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def qwen3_text_forward(w: dict, cfg, ids, final_norm=True):
+    """Qwen3TextModel.Forward (Text/Qwen/Qwen3TextModel.cs:47-104) in fp32:
+    ids [rows] -> hidden states [rows, width]."""
+    ids = np.asarray(ids, np.int64)
+    n, W, H, KV, eps = ids.size, cfg.width, cfg.heads, cfg.kv_heads, cfg.eps
+    x = np.ascontiguousarray(np.asarray(w["model.embed_tokens.weight"], np.float32)[ids])
+    cos, sin = rope_tables_1d(n, 128, cfg.rope_theta)
+    for l in range(cfg.blocks):
+        p = f"model.layers.{l}."
+        t = rmsnorm(x, w[p + "input_layernorm.weight"], eps)
+        q = linear(t, w[p + "self_attn.q_proj.weight"])
+        k = linear(t, w[p + "self_attn.k_proj.weight"])
+        v = linear(t, w[p + "self_attn.v_proj.weight"])
+        q = rmsnorm(q.reshape(n * H, 128), w[p + "self_attn.q_norm.weight"], eps).reshape(n, H * 128)
+        k = rmsnorm(k.reshape(n * KV, 128), w[p + "self_attn.k_norm.weight"], eps).reshape(n, KV * 128)
+        q = rope(q, H, cos, sin)
+        k = rope(k, KV, cos, sin)
+        a = attention(q, k, v, H, kv_heads=KV, causal=True)
+        x = x + linear(a, w[p + "self_attn.o_proj.weight"])
+        t = rmsnorm(x, w[p + "post_attention_layernorm.weight"], eps)
+        g = silu(linear(t, w[p + "mlp.gate_proj.weight"]))
+        x = x + linear(g * linear(t, w[p + "mlp.up_proj.weight"]), w[p + "mlp.down_proj.weight"])
+    return rmsnorm(x, w["model.norm.weight"], eps) if final_norm else x
+
+
+def llm_adapter_forward(w: dict, cfg, ids, context):
+    """LlmAdapter.Forward (Models/Anima/LlmAdapter.cs:29-102) in fp32: T5 ids
+    [rows] and Qwen3 hidden states [context_rows, width] -> [rows, width]."""
+    ids = np.asarray(ids, np.int64)
+    ctx = np.ascontiguousarray(context, np.float32)
+    n, S, W, H, hd, eps = ids.size, ctx.shape[0], cfg.width, cfg.heads, cfg.head_dim, cfg.eps
+    x = np.ascontiguousarray(np.asarray(w["embed.weight"], np.float32)[ids])
+    cos, sin = rope_tables_1d(n, hd, cfg.rope_theta)
+    ccos, csin = rope_tables_1d(S, hd, cfg.rope_theta)
+
+    def attend(p, queries, source, qc, qs, kc, ks):
+        q = linear(queries, w[p + ".q_proj.weight"])
+        k = linear(source, w[p + ".k_proj.weight"])
+        v = linear(source, w[p + ".v_proj.weight"])
+        q = rmsnorm(q.reshape(-1, hd), w[p + ".q_norm.weight"], eps).reshape(q.shape)
+        k = rmsnorm(k.reshape(-1, hd), w[p + ".k_norm.weight"], eps).reshape(k.shape)
+        return attention(rope(q, H, qc, qs), rope(k, H, kc, ks), v, H)
+
+    for b in range(cfg.blocks):
+        p = f"blocks.{b}."
+        t = rmsnorm(x, w[p + "norm_self_attn.weight"], eps)
+        x = x + linear(attend(p + "self_attn", t, t, cos, sin, cos, sin), w[p + "self_attn.o_proj.weight"])
+        t = rmsnorm(x, w[p + "norm_cross_attn.weight"], eps)
+        x = x + linear(attend(p + "cross_attn", t, ctx, cos, sin, ccos, csin), w[p + "cross_attn.o_proj.weight"])
+        t = rmsnorm(x, w[p + "norm_mlp.weight"], eps)
+        h = gelu(linear(t, w[p + "mlp.0.weight"], w.get(p + "mlp.0.bias")))
+        x = x + linear(h, w[p + "mlp.2.weight"], w.get(p + "mlp.2.bias"))
+    y = linear(x, w["out_proj.weight"], w.get("out_proj.bias"))
+    return rmsnorm(y, w["norm.weight"], eps)

@@ -183,3 +183,25 @@ def test_attention_head_dim_64_fp16(cuda, rows, kv_rows, heads, batch):
         sq, sk = slice(b * rows, (b + 1) * rows), slice(b * kv_rows, (b + 1) * kv_rows)
         ref = O.attention(f(h(q))[sq], f(h(k))[sk], f(h(v))[sk], heads)
         assert rel(out[sq], ref) < 2e-2 and cos(out[sq], ref) > 0.999
+
+
+@pytest.mark.parametrize("rows,heads,kv_heads,hd,causal", [(300, 16, 8, 128, True), (77, 32, 8, 128, True),
+                                                            (512, 16, 4, 64, False), (200, 4, 1, 128, False)])
+def test_attention_grouped_query(cuda, rows, heads, kv_heads, hd, causal):
+    """Grouped-query attention (Qwen3): query head h reads key / value head
+    h / (heads / kv_heads), as CpuMath.Attention does."""
+    from naivediffusion_b200 import ops
+    rng = np.random.default_rng(rows + heads)
+    q = rng.standard_normal((rows, heads * hd)).astype(np.float32)
+    k = rng.standard_normal((rows, kv_heads * hd)).astype(np.float32)
+    v = rng.standard_normal((rows, kv_heads * hd)).astype(np.float32)
+    qb, kb, vb = bf(q), bf(k), bf(v)
+    y = ops.attention(qb, kb, vb, heads, kv_heads=kv_heads, causal=causal, head_dim=hd)
+    y32 = ops.attention(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), heads,
+                        kv_heads=kv_heads, causal=causal, head_dim=hd)
+    ops.sync()
+    ref = O.attention(f32(qb), f32(kb), f32(vb), heads, kv_heads=kv_heads, causal=causal)
+    out = f32(y)
+    assert rel(out, ref) < 2e-2 and cos(out, ref) > 0.999
+    ref32 = O.attention(q, k, v, heads, kv_heads=kv_heads, causal=causal)
+    assert rel(y32.cpu().numpy(), ref32) < 1e-5
