@@ -293,6 +293,89 @@ def run_reference(args):
     return 0
 
 
+TEXT_CONFIGS = ("qwen3vl8b", "qwen3", "adapter")
+
+
+def _text_config(name):
+    """The text towers (the step before the path): Qwen3-VL-8B's language
+    model as Qwen-Image 2.1 reads it, Qwen3-0.6B as Anima reads it, Anima's
+    LLM adapter. A step is one prompt of PROMPT_ROWS tokens."""
+    from naivediffusion_b200.denoiser import LlmAdapterConfig, Qwen3TextConfig
+    if name == "qwen3vl8b":
+        return (Qwen3TextConfig.qwen3_vl_8b(context_rows=512), "Qwen3-VL-8B language model as Qwen-Image 2.1's "
+                "text encoder (36 x 4096, 32 x 128 query heads over 8 key heads, SwiGLU 12288), one 300-token "
+                "prompt, bf16", "Qwen-Image 2.1 text encode s/prompt (300 tokens); prompts/s")
+    if name == "qwen3":
+        return (Qwen3TextConfig(context_rows=512), "Qwen3-0.6B as Anima's text encoder (28 x 1024, 16 x 128 "
+                "query heads over 8 key heads, SwiGLU 3072), one 300-token prompt, bf16",
+                "Anima Qwen3 text encode s/prompt (300 tokens); prompts/s")
+    return (LlmAdapterConfig(context_rows=512, source_rows=512), "Anima's LLM adapter (6 x 1024, 16 x 64 "
+            "heads, GELU 4096): 300 T5 ids cross-attending to 300 Qwen3 rows, bf16",
+            "Anima LLM adapter s/prompt (300 ids); prompts/s")
+
+
+PROMPT_ROWS = 300
+
+
+def run_text(args):
+    """Text towers: e2e = nd_text_encode from host ids to host hidden states;
+    value = the device time of the same forward (event pairs per launch)."""
+    import numpy as np
+    import torch
+    from naivediffusion_b200.denoiser import CudaDenoiser, Device, synthetic_weights_device
+
+    rank, world, local = env_rank()
+    if rank != 0:
+        return 0  # one prompt per call: replicas only, rank 0 reports
+    torch.cuda.set_device(local)
+    cfg, workload, metric = _text_config(args.config)
+    dev = Device(local)
+    den = CudaDenoiser(dev, cfg.desc())
+    for name, t in synthetic_weights_device(cfg, seed=0):
+        den.set_weight(name, t)
+    den.finalize()
+    rng = np.random.default_rng(0)
+    ids = rng.integers(0, cfg.vocab, PROMPT_ROWS).astype(np.int32)
+    src = rng.standard_normal((PROMPT_ROWS, cfg.width)).astype(np.float32) if args.config == "adapter" else None
+    for _ in range(max(3, args.warmup)):
+        y = den.text_encode(ids, source=src)
+    clocks = Clocks(local)
+    clocks.start()
+    step_s = []
+    for _ in range(args.steps):
+        t1 = time.perf_counter()
+        y = den.text_encode(ids, source=src)
+        step_s.append(time.perf_counter() - t1)
+    clk = clocks.stop()
+    prof = den.profile(steps=max(1, args.steps))
+    dev_ms = sum(p["ms"] for p in prof)
+    gemm = [p for p in prof if p["name"].startswith("gemm")]
+    g_ms, g_fl = sum(p["ms"] for p in gemm), sum(p["flops"] for p in gemm)
+    peaks = measured_peaks()
+    e2e_ms = statistics.median(step_s) * 1e3
+    line = {
+        "metric": metric, "value": 1e3 / dev_ms, "unit": "prompts/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights on device, random ids)",
+        "config": {"workload": workload, "global_batch": 1, "prompt_rows": PROMPT_ROWS},
+        "e2e": {"value": 1e3 / e2e_ms, "unit": "prompts/s", "ms_per_step_median": e2e_ms,
+                "h2d_bytes_per_step": int(ids.nbytes + (src.nbytes if src is not None else 0)),
+                "d2h_bytes_per_step": int(y.nbytes)},
+        "gpu_launches": sum(p["launches"] for p in prof),
+        "roofline": {"bound": "tensor", "kernel": "gemm_sm100_kernel (tcgen05, all GEMM launches of a prompt)",
+                     "achieved": g_fl / (g_ms / 1e3) / 1e12, "peak": peaks["bf16"], "unit": "TFLOP/s",
+                     "frac": g_fl / (g_ms / 1e3) / 1e12 / peaks["bf16"], "traffic": None,
+                     "peak_source": f"{peaks['source']} bf16 burst",
+                     "note": "300 rows per GEMM: weight-streaming (HBM) territory, see gemm_bytes"},
+        "kernels": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in p.items()} for p in prof],
+        "clocks": clk, "output_finite": bool(np.isfinite(y).all()),
+    }
+    print(json.dumps(line), flush=True)
+    den.close()
+    dev.close()
+    return 0
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -443,12 +526,18 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["cfg3", "cfg1", "cfg2", "cfg4", "cfg5", "vae", "qwen21", "wan21", "wan22"], default="cfg3",
+    ap.add_argument("--config", choices=["cfg3", "cfg1", "cfg2", "cfg4", "cfg5", "vae", "qwen21", "wan21", "wan22", *TEXT_CONFIGS], default="cfg3",
                     help="BASELINE configuration (default cfg3, the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle sample")
     args = ap.parse_args()
     if args.impl == "reference":
+        if args.config in TEXT_CONFIGS:
+            print(json.dumps({"impl": "reference", "unavailable": f"{args.config}: the text towers are not a "
+                              "BASELINE configuration; no bounded CPU sample is timed"}))
+            return 0
         return run_reference(args)
+    if args.config in TEXT_CONFIGS:
+        return run_text(args)
     return run_ours(args)
 
 
