@@ -290,6 +290,8 @@ ND_API int nd_denoiser_destroy(nd_denoiser* d);
                                     fused [gate; up] matrix [2F, in], out_features
                                     = F (a multiple of 128), bias [2F] or NULL
                                     (QwenImageDit.FeedForward) */
+#define ND_EPI_GEGLU 10          /* y[:, j] = (h_j + bias_j) * gelu(g_j + bias_F+j), exact
+                                    GELU, W = [h; g] [2F, in] (UNetLayers.Geglu) */
 
 typedef struct nd_linear_args {
   int dtype;            /* ND_BF16 or ND_F16: x, W and y. ND_BF16X2 (fp32

@@ -35,6 +35,7 @@ ND_EPI_QK_NORM_ROPE = 6
 ND_EPI_RESIDUAL_ADD = 7
 ND_EPI_ADD_STORE = 8
 ND_EPI_SWIGLU = 9
+ND_EPI_GEGLU = 10
 
 
 class NdError(RuntimeError):

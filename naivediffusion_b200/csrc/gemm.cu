@@ -79,10 +79,10 @@ int linear_split(const nd_linear_args& a, cudaStream_t stream) {
   if (split && !shared && a.group_split % 128 != 0)
     return fail(ND_ERR_INVALID, "linear: group_split must be a multiple of 128 (or give shared_weights)");
   const int epi = a.epilogue;
-  if (epi < 0 || epi > ND_EPI_SWIGLU || epi == ND_EPI_ADD_STORE)
+  if (epi < 0 || epi > ND_EPI_GEGLU || epi == ND_EPI_ADD_STORE)
     return fail(ND_ERR_INVALID, "linear: unknown epilogue (ADD_STORE is not offered for bf16x2)");
-  const bool swiglu = epi == ND_EPI_SWIGLU;
-  if (swiglu && a.out_features % 128) return fail(ND_ERR_INVALID, "linear: SWIGLU needs out_features % 128 == 0");
+  const bool swiglu = epi == ND_EPI_SWIGLU || epi == ND_EPI_GEGLU;
+  if (swiglu && a.out_features % 128) return fail(ND_ERR_INVALID, "linear: SWIGLU / GEGLU need out_features % 128 == 0");
   const bool resid = epi == ND_EPI_RESIDUAL_GATE || epi == ND_EPI_RESIDUAL_ADD || epi == ND_EPI_STORE_F32;
   const bool qk = epi == ND_EPI_QK_NORM_ROPE;
   if (resid && (!a.residual || a.ldr < a.out_features || a.ldr % 4 != 0 || (reinterpret_cast<uintptr_t>(a.residual) & 15u)))
@@ -197,9 +197,9 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
     return fail(ND_ERR_INVALID, "linear: group_split must be a multiple of 128 (or give shared_weights)");
   const int epi = a.epilogue;
   const bool resid = epi == ND_EPI_RESIDUAL_GATE || epi == ND_EPI_RESIDUAL_ADD || epi == ND_EPI_STORE_F32;
-  if (epi < 0 || epi > ND_EPI_SWIGLU) return fail(ND_ERR_INVALID, "linear: unknown epilogue");
-  const bool swiglu = epi == ND_EPI_SWIGLU;
-  if (swiglu && a.out_features % 128) return fail(ND_ERR_INVALID, "linear: SWIGLU needs out_features % 128 == 0");
+  if (epi < 0 || epi > ND_EPI_GEGLU) return fail(ND_ERR_INVALID, "linear: unknown epilogue");
+  const bool swiglu = epi == ND_EPI_SWIGLU || epi == ND_EPI_GEGLU;
+  if (swiglu && a.out_features % 128) return fail(ND_ERR_INVALID, "linear: SWIGLU / GEGLU need out_features % 128 == 0");
   if (epi == ND_EPI_ADD_STORE && (!a.addend || a.ld_add < a.out_features || a.ld_add % 8 != 0))
     return fail(ND_ERR_INVALID, "linear: ADD_STORE needs addend with ld_add >= out_features, ld_add % 8 == 0");
   if (resid && (!a.residual || a.ldr < a.out_features || a.ldr % 4 != 0))

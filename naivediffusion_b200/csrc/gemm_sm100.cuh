@@ -35,6 +35,7 @@ enum GemmEpilogue : int {
   kEpiResidualAdd = 7,    // resid(f32) += acc + bias
   kEpiAddStore = 8,       // out = acc + bias + addend[row, col]     (bf16/f16)
   kEpiSwiGlu = 9,         // out[:, j] = silu(gate_j) * up_j  (W = [gate rows; up rows])
+  kEpiGeGlu = 10,         // out[:, j] = h_j * gelu(g_j)      (W = [h rows; g rows])
 };
 
 struct GemmArgs {
@@ -305,11 +306,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, const CUtensor
   emit_chunk(tmC, kind, buf0, sb, lane, row0, a.M, col, v, a.N);
 }
 
-// SwiGLU over one tile: output columns [ocol0, ocol0 + half) from the gate
-// accumulator columns [0, half) and the up columns [half, 2 * half), biases
-// at bias[j] (gate) and bias[F + j] (up) -- QwenImageDit.FeedForward's
-// Silu(gate) * up (Models/QwenImage/QwenImageDit.cs:386-403) where the two
-// products already sit.
+// SwiGLU / GEGLU over one tile: output columns [ocol0, ocol0 + half) from
+// the first half's accumulator columns [0, half) and the second half's
+// [half, 2 * half), biases at bias[j] and bias[F + j] -- QwenImageDit.
+// FeedForward's Silu(gate) * up (Models/QwenImage/QwenImageDit.cs:386-403), or
+// UNetLayers.Geglu's h * gelu(g) (Models/Sdxl/UNetLayers.cs:30-46), where the
+// two products already sit.
 template <int HALF>
 __device__ __forceinline__ void epilogue_swiglu(const GemmArgs& a, const CUtensorMap* tmC, int group,
                                                 int row0, int ocol0, uint32_t tbase, uint32_t buf0,
@@ -328,9 +330,15 @@ __device__ __forceinline__ void epilogue_swiglu(const GemmArgs& a, const CUtenso
     float bg[32], bu[32], v[32];
     load_vec32(bias, ocol, F, bg);
     load_vec32(bias ? bias + F : nullptr, ocol, F, bu);
+    if (a.epi == kEpiGeGlu) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      v[i] = silu(__uint_as_float(rg[i]) + bg[i]) * (__uint_as_float(ru[i]) + bu[i]);
+      for (int i = 0; i < 32; ++i)
+        v[i] = (__uint_as_float(rg[i]) + bg[i]) * gelu_erf(__uint_as_float(ru[i]) + bu[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        v[i] = silu(__uint_as_float(rg[i]) + bg[i]) * (__uint_as_float(ru[i]) + bu[i]);
+    }
     emit_chunk(tmC, out_emit_kind(a), buf0, sb, lane, row0, a.M, ocol, v, F);
   }
 }
@@ -601,7 +609,7 @@ __global__ void __launch_bounds__(192, 1)
       const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
 
-      if (args.epi == kEpiSwiGlu) {
+      if (args.epi == kEpiSwiGlu || args.epi == kEpiGeGlu) {
         epilogue_swiglu<BN / 2>(args, &tmC, group, row0, nt * (BN / 2), tbase, buf0, sb, lane);
       } else if (args.epi == kEpiQkNormRope) {
 #pragma unroll 1

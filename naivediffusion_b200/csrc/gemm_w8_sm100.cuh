@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       const int row = m0 + row_in_tile;
       const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
-      if (args.epi == kEpiSwiGlu) {
+      if (args.epi == kEpiSwiGlu || args.epi == kEpiGeGlu) {
         epilogue_swiglu<BN / 2>(args, &tmC, group, row0, nt * (BN / 2), tbase, buf0, sb, lane);
       } else if (args.epi == kEpiQkNormRope) {
 #pragma unroll 1

@@ -273,6 +273,87 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint16_t* __restrict__ 
   }
 }
 
+// The GEMV for 16-bit weights: one warp per output row, U 16-byte loads per
+// lane issued before any arithmetic (no pair registers), so that enough bytes
+// are in flight per SM to cover HBM latency at the occupancy the registers allow.
+template <int F16, int U>
+__global__ void __launch_bounds__(256) gemv16_kernel(const uint16_t* __restrict__ W, long long N, int K,
+                                                     const float* __restrict__ x, int B, int pre,
+                                                     const float* __restrict__ bias, int act,
+                                                     float* __restrict__ y, long long xrows, int nvec,
+                                                     long long bias_period) {
+  extern __shared__ float xs[];
+  for (int i = threadIdx.x; i < nvec * K; i += blockDim.x) {
+    float v = x[i];
+    if (pre == 1) v = v / (1.0f + __expf(-v));
+    xs[i] = v;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const int k8 = K >> 3;
+  for (long long n = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; n < N;
+       n += warps) {
+    const uint4* wr = reinterpret_cast<const uint4*>(W + n * K);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c0 = lane; c0 < k8; c0 += 32 * U) {
+      uint4 p[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + 32 * u;
+        p[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (c < k8)
+          asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(p[u].x), "=r"(p[u].y), "=r"(p[u].z), "=r"(p[u].w)
+                       : "l"(wr + c));
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + 32 * u;
+        if (c >= k8) break;
+        float wv[8];
+        const uint32_t uh[4] = {p[u].x, p[u].y, p[u].z, p[u].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = F16 ? __half22float2(*reinterpret_cast<const __half2*>(&uh[i]))
+                               : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uh[i]));
+          wv[2 * i] = f.x;
+          wv[2 * i + 1] = f.y;
+        }
+#pragma unroll 4
+        for (int b = 0; b < 4; ++b) {
+          if (b < B) {
+            const float* xb = xs + (xrows > 0 ? (n / xrows) : b) * K + 8 * c;
+            const float4 x0 = *reinterpret_cast<const float4*>(xb);
+            const float4 x1 = *reinterpret_cast<const float4*>(xb + 4);
+            float s0 = wv[0] * x0.x;
+            s0 = fmaf(wv[1], x0.y, s0);
+            s0 = fmaf(wv[2], x0.z, s0);
+            s0 = fmaf(wv[3], x0.w, s0);
+            float s1 = wv[4] * x1.x;
+            s1 = fmaf(wv[5], x1.y, s1);
+            s1 = fmaf(wv[6], x1.z, s1);
+            s1 = fmaf(wv[7], x1.w, s1);
+            acc[b] += s0 + s1;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      if (b < B) {
+        float v = warp_sum(acc[b]);
+        if (lane == 0) {
+          if (bias) v += bias[bias_period > 0 ? n % bias_period : n];
+          if (act == 1) v = v / (1.0f + __expf(-v));
+          else if (act == 2) v = tanhf(v);
+          y[static_cast<long long>(b) * N + n] = v;
+        }
+      }
+    }
+  }
+}
+
 // latent [B][C][H][W] fp32 -> tokens [B][(H/p)(W/p)][C p p] (bf16/f16/fp32);
 // feature c*p*p + m*p + n of patch (i, j) is channel c at (p*i + m, p*j + n)
 // (AnimaDit.Patchify, Models/Anima/AnimaDit.cs:193-247).
@@ -392,6 +473,21 @@ int gemv(const nd_gemv_args& a, cudaStream_t stream) {
   long long blocks = (a.n + 7) / 8;
   const long long cap = static_cast<long long>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
+  if (a.w_dtype != ND_BF16X2) {
+    const unsigned g = static_cast<unsigned>(blocks);
+    const uint16_t* w = static_cast<const uint16_t*>(a.w);
+    const int k = static_cast<int>(a.k);
+    const int pre = a.pre_silu ? 1 : 0;
+    const int nv = static_cast<int>(nvec);
+    if (a.w_dtype == ND_F16)
+      gemv16_kernel<1, 8><<<g, 256, shmem, stream>>>(w, a.n, k, a.x, a.batch, pre, a.bias, a.act, a.y,
+                                                     a.x_rows_per_vec, nv, a.bias_period);
+    else
+      gemv16_kernel<0, 8><<<g, 256, shmem, stream>>>(w, a.n, k, a.x, a.batch, pre, a.bias, a.act, a.y,
+                                                     a.x_rows_per_vec, nv, a.bias_period);
+    ND_CUDA(cudaGetLastError());
+    return ND_OK;
+  }
   gemv_kernel<<<static_cast<unsigned>(blocks), 256, shmem, stream>>>(
       static_cast<const uint16_t*>(a.w), a.w_dtype == ND_BF16X2 ? 2 : (a.w_dtype == ND_F16 ? 1 : 0), a.n, static_cast<int>(a.k), a.x,
       a.batch, a.pre_silu ? 1 : 0, a.bias, a.act, a.y, a.x_rows_per_vec, static_cast<int>(nvec),

@@ -44,6 +44,7 @@ struct ResUnit {
 struct TBlock {
   float *n1w, *n1b, *n2w, *n2b, *n3w, *n3b, *o1b, *o2b, *f1b, *f2b;
   void *qkv, *o1, *q2, *kv2, *o2, *f1, *f2;
+  int64_t kv_col;  // this block's K columns in the step's merged context K/V (V follows at + C)
 };
 
 struct T2d {
@@ -88,8 +89,10 @@ struct Unet final : nd_denoiser {
   std::vector<void*> skips;
   std::vector<int> skip_c;
   void *xin = nullptr, *X0 = nullptr, *X1 = nullptr, *H1 = nullptr, *H2 = nullptr, *SC = nullptr, *CAT = nullptr,
-       *UPB = nullptr, *A16 = nullptr, *QKV = nullptr, *ATT = nullptr, *Q2 = nullptr, *KV2 = nullptr, *FFH = nullptr,
+       *UPB = nullptr, *A16 = nullptr, *QKV = nullptr, *ATT = nullptr, *Q2 = nullptr, *KV2 = nullptr,
        *FFG = nullptr, *CTX16 = nullptr;
+  void* kv_all = nullptr;    // [kv_rows, cw]: every block's attn2 to_k then to_v rows
+  int64_t kv_rows = 0, kv_next = 0;
   float *TOK = nullptr, *te1 = nullptr, *te = nullptr, *ae1 = nullptr, *ae = nullptr, *temb = nullptr,
         *rbias = nullptr, *out_nhwc = nullptr, *out_latent = nullptr;
   void* gn_scratch = nullptr;
@@ -168,7 +171,10 @@ struct Unet final : nd_denoiser {
       add_slot(q + ".attn1.to_out.0.bias", kVector, C, 1, b.o1b, false);
       b.q2 = Wt(CC);
       add_slot(q + ".attn2.to_q.weight", kMatrix, C, C, b.q2);
-      b.kv2 = Wt(2LL * C * cw);
+      // every block's context K/V weights in one matrix: one GEMM per step
+      b.kv_col = kv_next;
+      b.kv2 = static_cast<uint8_t*>(kv_all) + kv_next * cw * e;
+      kv_next += 2LL * C;
       add_slot(q + ".attn2.to_k.weight", kMatrix, C, cw, b.kv2);
       add_slot(q + ".attn2.to_v.weight", kMatrix, C, cw, static_cast<uint8_t*>(b.kv2) + static_cast<int64_t>(C) * cw * e);
       b.o2 = Wt(CC);
@@ -245,6 +251,16 @@ struct Unet final : nd_denoiser {
     add_slot("add_embedding.linear_1.bias", kVector, kTembWidth, 1, a1b, false);
     add_slot("add_embedding.linear_2.weight", kMatrix, kTembWidth, kTembWidth, a2w);
     add_slot("add_embedding.linear_2.bias", kVector, kTembWidth, 1, a2b, false);
+
+    // the context K/V rows of every transformer block (2C each), in build order
+    kv_rows = 0;
+    for (int l = 0; l < L; ++l)
+      if (depth[l] > 0) kv_rows += static_cast<int64_t>(R) * depth[l] * 2 * level_c(l);
+    kv_rows += static_cast<int64_t>(depth[L - 1] > 0 ? depth[L - 1] : 1) * 2 * level_c(L - 1);
+    for (int l = 0; l < L; ++l)
+      if (depth[l] > 0) kv_rows += static_cast<int64_t>(R + 1) * depth[l] * 2 * level_c(l);
+    kv_all = Wt(kv_rows * cw);
+    kv_next = 0;
 
     std::vector<int> chans, levels;  // channels and level of every skip, in push order
     chans.push_back(C0);
@@ -356,9 +372,9 @@ struct Unet final : nd_denoiser {
     QKV = S(max_qkv * e);
     ATT = S(max_tok * e);
     Q2 = S(max_tok * e);
-    KV2 = S(static_cast<size_t>(B) * ctx * 2 * level_c(L - 1) * e);
-    FFH = S(max_ff * e);
-    FFG = S(max_ff / 2 * e);
+    if (kv_next != kv_rows) return fail(ND_ERR_INVALID, "sdxl: context K/V row count mismatch");
+    KV2 = S(static_cast<size_t>(B) * ctx * kv_rows * e);
+    FFG = S(max_ff / 2 * e);  // the GEGLU GEMM writes h * gelu(g) directly
     CTX16 = S(static_cast<size_t>(B) * ctx * cw * e);
     te1 = static_cast<float*>(S(static_cast<size_t>(B) * kTembWidth * 4));
     te = static_cast<float*>(S(static_cast<size_t>(B) * kTembWidth * 4));
@@ -532,15 +548,13 @@ struct Unet final : nd_denoiser {
       // cross-attention to the text rows
       ND_OP("layernorm", 0.0, ln(s, M, C, b.n2w, b.n2b));
       ND_OP("gemm.cross_q", 2.0 * M * C * C, lin(s, A16, M, C, b.q2, nullptr, C, ND_EPI_STORE, Q2));
-      ND_OP("gemm.cross_kv", 4.0 * B * ctx * static_cast<double>(C) * cw,
-            lin(s, CTX16, static_cast<int64_t>(B) * ctx, cw, b.kv2, nullptr, 2LL * C, ND_EPI_STORE, KV2));
       ND_OP("attention", 4.0 * B * static_cast<double>(hw) * ctx * C,
-            attend(s, Q2, C, KV2, static_cast<uint8_t*>(KV2) + C * e, 2LL * C, heads, hw, ctx));
+            attend(s, Q2, C, static_cast<uint8_t*>(KV2) + b.kv_col * e, static_cast<uint8_t*>(KV2) + (b.kv_col + C) * e,
+                   kv_rows, heads, hw, ctx));
       ND_OP("gemm.out", 2.0 * M * C * C, lin(s, ATT, M, C, b.o2, b.o2b, C, ND_EPI_RESIDUAL_ADD, nullptr, TOK));
       // GEGLU feed-forward
       ND_OP("layernorm", 0.0, ln(s, M, C, b.n3w, b.n3b));
-      ND_OP("gemm.up", 16.0 * M * C * C, lin(s, A16, M, C, b.f1, b.f1b, 8LL * C, ND_EPI_STORE, FFH));
-      ND_OP("geglu", 0.0, geglu(FFH, FFG, dt, M, 4LL * C, s));
+      ND_OP("gemm.up", 16.0 * M * C * C, lin(s, A16, M, C, b.f1, b.f1b, 4LL * C, ND_EPI_GEGLU, FFG));
       ND_OP("gemm.down", 8.0 * M * C * C, lin(s, FFG, M, 4LL * C, b.f2, b.f2b, C, ND_EPI_RESIDUAL_ADD, nullptr, TOK));
     }
     ND_OP("convert", 0.0, convert(TOK, ND_F32, A16, dt, M * C, s));
@@ -591,6 +605,9 @@ struct Unet final : nd_denoiser {
     // embeddings
     ND_OP("layout", 0.0, nchw_to_nhwc(in_latent, xin, dt, B, 4, H0 * W0, cinp, s));
     ND_OP("layout", 0.0, convert(in_ctx, ND_F32, CTX16, dt, static_cast<int64_t>(B) * ctx * cw, s));
+    // every block's cross-attention K and V of the (step-constant) context
+    ND_OP("gemm.cross_kv", 2.0 * B * ctx * static_cast<double>(kv_rows) * cw,
+          lin(s, CTX16, static_cast<int64_t>(B) * ctx, cw, kv_all, nullptr, kv_rows, ND_EPI_STORE, KV2));
     ND_OP("gemv", 0.0, gv(s, t1w, kTembWidth, tw, in_tsin, t1b, false, 1, te1));
     ND_OP("gemv", 0.0, gv(s, t2w, kTembWidth, kTembWidth, te1, t2b, false, 0, te));
     ND_OP("gemv", 0.0, gv(s, a1w, kTembWidth, aw, in_add, a1b, false, 1, ae1));

@@ -71,7 +71,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
         k //= 2
     groups = 1 if shared_weights or group_split is None or group_split >= rows else 2
     n = weight.shape[0] // groups
-    if epilogue == _lib.ND_EPI_SWIGLU:
+    if epilogue in (_lib.ND_EPI_SWIGLU, _lib.ND_EPI_GEGLU):
         n //= 2
     resid_epi = epilogue in (_lib.ND_EPI_RESIDUAL_GATE, _lib.ND_EPI_RESIDUAL_ADD, _lib.ND_EPI_STORE_F32)
     if resid_epi:

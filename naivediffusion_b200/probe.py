@@ -80,7 +80,7 @@ def probe_quant(a) -> None:
 
 
 _EPI = {"store": _lib.ND_EPI_STORE, "gelu_tanh": _lib.ND_EPI_GELU_TANH, "residual_gate": _lib.ND_EPI_RESIDUAL_GATE,
-        "qk": _lib.ND_EPI_QK_NORM_ROPE}
+        "qk": _lib.ND_EPI_QK_NORM_ROPE, "swiglu": _lib.ND_EPI_SWIGLU, "geglu": _lib.ND_EPI_GEGLU}
 
 
 def probe_gemm(a) -> None:
@@ -107,7 +107,7 @@ def probe_gemm(a) -> None:
 def probe_conv(a) -> None:
     g = torch.Generator(device="cuda").manual_seed(0)
     x = torch.randn(a.batch, a.size, a.size, a.cin, device="cuda", generator=g).half()
-    w = (torch.randn(a.cout, 3, 3, a.cin, device="cuda", generator=g) * 0.02).half()
+    w = (torch.randn(a.cout, 3, 3, (a.cin + 63) // 64 * 64, device="cuda", generator=g) * 0.02).half()
     b = torch.randn(a.cout, device="cuda", generator=g) * 0.1
     ho = (a.size - 1) // a.stride + 1
     ms = _time(lambda: ops.conv2d(x, w, b, stride=a.stride), a.warmup, a.iters)

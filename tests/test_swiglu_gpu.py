@@ -120,3 +120,20 @@ def test_shared_weights_qk_norm_uses_one_set(cuda):
     b = ops.linear(x, w, None, group_split=137, shared_weights=True, **kw)
     ops.sync()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("m,f,k", [(8192, 2560, 640), (300, 384, 256)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_geglu_epilogue_matches_torch(cuda, m, f, k, dtype):
+    """ND_EPI_GEGLU: h * gelu(g) (exact GELU) from the fused [h; g] projection,
+    SDXL's feed-forward (UNetLayers.Geglu)."""
+    g = torch.Generator().manual_seed(m + f)
+    x = torch.randn(m, k, generator=g).to(dtype).cuda()
+    w = (torch.randn(2 * f, k, generator=g) * 0.05).to(dtype).cuda()
+    b = (torch.randn(2 * f, generator=g) * 0.1).cuda()
+    y = ops.linear(x, w, b, epilogue=_lib.ND_EPI_GEGLU)
+    ops.sync()
+    h = x.float() @ w.float().t() + b
+    ref = h[:, :f] * torch.nn.functional.gelu(h[:, f:])
+    assert y.shape == (m, f)
+    assert _rel(y, ref) < 2e-2 and _cos(y, ref) > 0.999
