@@ -67,7 +67,7 @@ int attention(const nd_attention_args& a, cudaStream_t stream) {
                                    AttnSmem<128>::kLaunchBytes));
       configured[dev & 63] = true;
     }
-    attention_sm100_kernel<128><<<grid, kAttnThreads, AttnSmem<128>::kLaunchBytes, stream>>>(tq, tk, tv, g);
+    ND_CUDA(launch_pdl(attention_sm100_kernel<128>, grid, dim3(kAttnThreads), AttnSmem<128>::kLaunchBytes, stream, tq, tk, tv, g));
   } else {
     static bool configured[64] = {};
     if (!configured[dev & 63]) {
@@ -78,7 +78,7 @@ int attention(const nd_attention_args& a, cudaStream_t stream) {
                                    AttnSmem<64>::kLaunchBytes));
       configured[dev & 63] = true;
     }
-    attention_sm100_kernel<64><<<grid, kAttnThreads, AttnSmem<64>::kLaunchBytes, stream>>>(tq, tk, tv, g);
+    ND_CUDA(launch_pdl(attention_sm100_kernel<64>, grid, dim3(kAttnThreads), AttnSmem<64>::kLaunchBytes, stream, tq, tk, tv, g));
   }
   ND_CUDA(cudaGetLastError());
   return ND_OK;

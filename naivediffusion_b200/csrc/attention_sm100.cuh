@@ -142,6 +142,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_launch();
+  griddep_wait();
 
   // Each role's code sits inside its warpgroup's setmaxnreg branch, so the
   // compiler budgets each region with that branch's register count.

@@ -30,7 +30,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   const int num_n = (g.N + BN - 1) / BN;
   const int tiles = num_m * num_n;
   const int grid = std::min(tiles, sm_count());
-  gemm_sm100_kernel<BN, STAGES, CONV><<<grid, 192, L::kLaunchBytes, stream>>>(ta, tb, tc, g);
+  ND_CUDA(launch_pdl(gemm_sm100_kernel<BN, STAGES, CONV>, dim3(grid), dim3(192), L::kLaunchBytes, stream, ta, tb, tc, g));
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }
@@ -52,7 +52,7 @@ int launch_gemm_w8(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorM
   }
   const int tiles = ((g.M + 127) / 128) * ((g.N + BN - 1) / BN);
   const int grid = std::min(tiles, sm_count());
-  gemm_w8_sm100_kernel<BN, STAGES><<<grid, kW8Threads, L::kLaunchBytes, stream>>>(ta, tw, tc, g);
+  ND_CUDA(launch_pdl(gemm_w8_sm100_kernel<BN, STAGES>, dim3(grid), dim3(kW8Threads), L::kLaunchBytes, stream, ta, tw, tc, g));
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }

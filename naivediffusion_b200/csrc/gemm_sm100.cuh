@@ -455,6 +455,8 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_launch();
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer

@@ -123,6 +123,8 @@ __global__ void __launch_bounds__(kW8Threads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_launch();
+  griddep_wait();
 
   // Each role's code sits inside its warpgroup's setmaxnreg branch so the
   // compiler budgets each region with that branch's register count.

@@ -358,6 +358,15 @@ __device__ __forceinline__ float poly_exp2(float x) {
   return x < -126.0f ? 0.0f : r;
 }
 
+// Programmatic dependent launch: let the next kernel in the stream be
+// scheduled now (its CTAs fill SMs this grid no longer needs and run their
+// prologue), and wait until the previous kernel's grid has completed and its
+// memory is visible. Every kernel launched with launch_pdl() calls
+// griddep_wait() before touching global memory the stream's earlier work
+// reads or writes; launched without the attribute both are no-ops.
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }

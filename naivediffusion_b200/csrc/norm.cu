@@ -53,6 +53,8 @@ __global__ void __launch_bounds__(256) modulate_kernel(const float* __restrict__
                                                        const float* __restrict__ scale,
                                                        int vec_stride, int split, float eps,
                                                        int affine) {
+  griddep_launch();
+  griddep_wait();
   __shared__ float red[2][2][4];
   const int half = threadIdx.x >> 7;        // which of the block's two rows
   const int t = threadIdx.x & 127;
@@ -117,6 +119,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const void* __restrict__ x
                                                       long long ldy, int out_type, int rows,
                                                       int width, const float* __restrict__ w,
                                                       float plus_one, float eps, int silu_after) {
+  griddep_launch();
+  griddep_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -190,6 +194,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint16_t* __restrict__ 
                                                    int B, int pre, const float* __restrict__ bias,
                                                    int act, float* __restrict__ y, long long xrows,
                                                    int nvec, long long bias_period) {
+  griddep_launch();
+  griddep_wait();
   extern __shared__ float xs[];
   for (int i = threadIdx.x; i < nvec * K; i += blockDim.x) {
     float v = x[i];
@@ -282,6 +288,8 @@ __global__ void __launch_bounds__(256) gemv16_kernel(const uint16_t* __restrict_
                                                      const float* __restrict__ bias, int act,
                                                      float* __restrict__ y, long long xrows, int nvec,
                                                      long long bias_period) {
+  griddep_launch();
+  griddep_wait();
   extern __shared__ float xs[];
   for (int i = threadIdx.x; i < nvec * K; i += blockDim.x) {
     float v = x[i];
@@ -354,6 +362,65 @@ __global__ void __launch_bounds__(256) gemv16_kernel(const uint16_t* __restrict_
   }
 }
 
+// RMSNorm over short 16-bit rows (an image's pixels x channels, the Wan VAE's
+// channel norm): L lanes per row (L = 8, 16 or 32), each holding up to V
+// 16-byte vectors, so one warp keeps 32 / L rows' bytes in flight instead of
+// one row's. Same arithmetic as rmsnorm_kernel.
+template <int V>
+__global__ void __launch_bounds__(256) rms_rows16_kernel(const uint4* __restrict__ x, uint4* __restrict__ y,
+                                                         int f16, long long rows, int c8, int L,
+                                                         const float* __restrict__ w, float plus_one,
+                                                         float eps, int silu_after, int width) {
+  griddep_launch();
+  griddep_wait();
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % L;  // lane within the row's segment
+  const long long warp = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 5;
+  const long long row = warp * (32 / L) + lane / L;
+  const bool live = row < rows;
+  uint4 v[V];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int c = sub + k * L;
+    v[k] = make_uint4(0u, 0u, 0u, 0u);
+    if (live && c < c8) v[k] = __ldg(x + row * c8 + c);
+    const uint32_t u[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = f16 ? __half22float2(*reinterpret_cast<const __half2*>(&u[i]))
+                           : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[i]));
+      ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+    }
+  }
+  for (int o = L / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / width + eps);
+  if (!live) return;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int c = sub + k * L;
+    if (c >= c8) break;
+    const uint32_t u[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+    uint32_t o4[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = f16 ? __half22float2(*reinterpret_cast<const __half2*>(&u[i]))
+                     : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[i]));
+      const int ch = c * 8 + 2 * i;
+      const float w0 = (w ? __ldg(w + ch) : 0.f) + (w ? plus_one : 1.f);
+      const float w1 = (w ? __ldg(w + ch + 1) : 0.f) + (w ? plus_one : 1.f);
+      f.x = f.x * r * w0;
+      f.y = f.y * r * w1;
+      if (silu_after) {
+        f.x = silu(f.x);
+        f.y = silu(f.y);
+      }
+      o4[i] = f16 ? pack_f16(f.x, f.y) : pack_bf16(f.x, f.y);
+    }
+    y[row * c8 + c] = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+  }
+}
+
 // latent [B][C][H][W] fp32 -> tokens [B][(H/p)(W/p)][C p p] (bf16/f16/fp32);
 // feature c*p*p + m*p + n of patch (i, j) is channel c at (p*i + m, p*j + n)
 // (AnimaDit.Patchify, Models/Anima/AnimaDit.cs:193-247).
@@ -416,7 +483,7 @@ int modulate(const nd_modulate_args& a, cudaStream_t stream) {
   const int vs = a.vec_stride ? static_cast<int>(a.vec_stride) : static_cast<int>(a.width);
   const unsigned grid = static_cast<unsigned>((rows + 1) / 2);
   const int per_thread = (static_cast<int>(a.width) / 4 + 127) / 128;
-#define ND_MOD(V) modulate_kernel<V><<<grid, 256, 0, stream>>>(a.x, a.ldx, a.y, a.ldy, a.out_dtype, rows, static_cast<int>(a.width), a.shift, a.scale, vs, split, a.eps, a.affine)
+#define ND_MOD(V) ND_CUDA(launch_pdl(modulate_kernel<V>, dim3(grid), dim3(256), 0, stream, a.x, a.ldx, a.y, a.ldy, a.out_dtype, rows, static_cast<int>(a.width), a.shift, a.scale, vs, split, a.eps, a.affine))
   if (per_thread <= 1) ND_MOD(1);
   else if (per_thread <= 2) ND_MOD(2);
   else if (per_thread <= 4) ND_MOD(4);
@@ -437,11 +504,37 @@ int rmsnorm(const nd_rmsnorm_args& a, cudaStream_t stream) {
   if (a.ldy < (a.out_dtype == ND_BF16X2 ? 2 : 1) * a.width)
     return fail(ND_ERR_INVALID, "rmsnorm: ldy too small (a bf16x2 output needs 2 * width)");
   if (!a.x || !a.y) return fail(ND_ERR_INVALID, "rmsnorm: null operand");
+  // Short contiguous 16-bit rows: several rows per warp.
+  const bool narrow16 = (a.in_dtype == ND_F16 || a.in_dtype == ND_BF16) && a.out_dtype == a.in_dtype &&
+                        a.width % 8 == 0 && a.width <= 1280 && a.ldx == a.width && a.ldy == a.width &&
+                        (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15u) == 0;
+  if (narrow16) {
+    const int c8 = static_cast<int>(a.width / 8);
+    const int L = c8 >= 64 ? 32 : (c8 >= 24 ? 16 : 8);
+    const int per = (c8 + L - 1) / L;  // vectors per lane, <= 5
+    const long long warps = (a.rows + 32 / L - 1) / (32 / L);
+    const unsigned grid = static_cast<unsigned>((warps * 32 + 255) / 256);
+    const int f16 = a.in_dtype == ND_F16 ? 1 : 0;
+    const float po = a.plus_one ? 1.f : 0.f;
+#define ND_RR(V)                                                                                               \
+  ND_CUDA(launch_pdl(rms_rows16_kernel<V>, dim3(grid), dim3(256), 0, stream, static_cast<const uint4*>(a.x),    \
+                     static_cast<uint4*>(a.y), f16, static_cast<long long>(a.rows), c8, L, a.weight, po, a.eps, \
+                     a.silu, static_cast<int>(a.width)))
+    switch (per) {
+      case 1: ND_RR(1); break;
+      case 2: ND_RR(2); break;
+      case 3: ND_RR(3); break;
+      case 4: ND_RR(4); break;
+      default: ND_RR(5); break;
+    }
+#undef ND_RR
+    return ND_OK;
+  }
   const int bucket = pick_bucket(static_cast<int>(a.width));
   if (!bucket) return fail(ND_ERR_UNSUPPORTED, "rmsnorm: width above 4096");
   const int rows = static_cast<int>(a.rows);
   const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
-#define ND_RMS(V) rmsnorm_kernel<V><<<grid, 256, 0, stream>>>(a.x, a.in_dtype, a.ldx, a.y, a.ldy, a.out_dtype, rows, static_cast<int>(a.width), a.weight, a.plus_one ? 1.f : 0.f, a.eps, a.silu)
+#define ND_RMS(V) ND_CUDA(launch_pdl(rmsnorm_kernel<V>, dim3(grid), dim3(256), 0, stream, a.x, a.in_dtype, a.ldx, a.y, a.ldy, a.out_dtype, rows, static_cast<int>(a.width), a.weight, a.plus_one ? 1.f : 0.f, a.eps, a.silu))
   switch (bucket) {
     case 2: ND_RMS(2); break;
     case 4: ND_RMS(4); break;
@@ -480,12 +573,11 @@ int gemv(const nd_gemv_args& a, cudaStream_t stream) {
     const int pre = a.pre_silu ? 1 : 0;
     const int nv = static_cast<int>(nvec);
     if (a.w_dtype == ND_F16)
-      gemv16_kernel<1, 8><<<g, 256, shmem, stream>>>(w, a.n, k, a.x, a.batch, pre, a.bias, a.act, a.y,
-                                                     a.x_rows_per_vec, nv, a.bias_period);
+      ND_CUDA(launch_pdl(gemv16_kernel<1, 8>, dim3(g), dim3(256), shmem, stream, w, a.n, k, a.x, a.batch, pre,
+                         a.bias, a.act, a.y, a.x_rows_per_vec, nv, a.bias_period));
     else
-      gemv16_kernel<0, 8><<<g, 256, shmem, stream>>>(w, a.n, k, a.x, a.batch, pre, a.bias, a.act, a.y,
-                                                     a.x_rows_per_vec, nv, a.bias_period);
-    ND_CUDA(cudaGetLastError());
+      ND_CUDA(launch_pdl(gemv16_kernel<0, 8>, dim3(g), dim3(256), shmem, stream, w, a.n, k, a.x, a.batch, pre,
+                         a.bias, a.act, a.y, a.x_rows_per_vec, nv, a.bias_period));
     return ND_OK;
   }
   gemv_kernel<<<static_cast<unsigned>(blocks), 256, shmem, stream>>>(

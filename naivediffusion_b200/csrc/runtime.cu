@@ -106,6 +106,14 @@ int op_scratch(size_t need, void** ptr, size_t* bytes) {
   return ND_OK;
 }
 
+namespace {
+thread_local bool t_pdl = false;
+}  // namespace
+
+bool pdl_enabled() { return t_pdl; }
+PdlScope::PdlScope(bool on) : prev(t_pdl) { t_pdl = on; }
+PdlScope::~PdlScope() { t_pdl = prev; }
+
 int check_device_status(cudaStream_t stream) {
   ND_CUDA(cudaStreamSynchronize(stream));
   unsigned* st = device_status();

@@ -601,6 +601,7 @@ struct Unet final : nd_denoiser {
   }
 
   int forward(cudaStream_t s) override {
+    PdlScope pdl(true);  // over a thousand short launches: overlap each one's launch with the previous
     const int64_t px0 = static_cast<int64_t>(B) * H0 * W0;
     // embeddings
     ND_OP("layout", 0.0, nchw_to_nhwc(in_latent, xin, dt, B, 4, H0 * W0, cinp, s));

@@ -41,7 +41,7 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8], int f16) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// Per (image, chunk of kGnChunk pixels, group): sum and sum of squares.
+// Per (image, chunk of pixels, group): sum and sum of squares.
 // Threads read 16-byte vectors (8 channels), consecutive threads on
 // consecutive vectors of a pixel row and several rows per pass, so every load
 // is coalesced; each thread sums its 8 channels in fp32, the block adds the
@@ -54,12 +54,15 @@ constexpr int kGnMaxSlab = 2048;  // channels per block (static shared memory: 1
 // grid (pixel chunks, channel slabs, images): a slab is a run of whole groups
 // and whole 8-channel vectors, [slab * slab_c, ...) clipped to C.
 __global__ void __launch_bounds__(256) gn_partial_kernel(const void* __restrict__ x, int f16, int hw,
-                                                         int C, int G, int slab_c, float2* __restrict__ part) {
+                                                         int C, int G, int slab_c, int chunk,
+                                                         float2* __restrict__ part) {
+  griddep_launch();
+  griddep_wait();
   __shared__ float red[256][17];
   __shared__ float chs[2][kGnMaxSlab];
   const int ck = blockIdx.x, b = blockIdx.z;
   const int c_lo = blockIdx.y * slab_c, c_hi = min(C, c_lo + slab_c);
-  const int p0 = ck * kGnChunk, p1 = min(hw, p0 + kGnChunk);
+  const int p0 = ck * chunk, p1 = min(hw, p0 + chunk);
   const int nchunks = gridDim.x;
   const int c8 = C / 8;
   const int v_lo = c_lo / 8, nv = (c_hi - c_lo) / 8;  // this slab's vectors
@@ -74,6 +77,7 @@ __global__ void __launch_bounds__(256) gn_partial_kernel(const void* __restrict_
 #pragma unroll
     for (int k = 0; k < 8; ++k) s1[k] = s2[k] = 0.f;
     if (pr < rows && j < nv) {
+#pragma unroll 4
       for (int p = p0 + pr; p < p1; p += rows) {
         float v[8];
         unpack8(__ldg(xv + static_cast<long long>(p) * c8 + v_lo + j), f16, v);
@@ -120,6 +124,8 @@ __global__ void __launch_bounds__(256) gn_partial_kernel(const void* __restrict_
 // chunks' partial sums added in fp64.
 __global__ void gn_finalize_kernel(const float2* __restrict__ part, int nchunks, int C, int G, int hw,
                                    float eps, float2* __restrict__ stats) {
+  griddep_launch();
+  griddep_wait();
   const int b = blockIdx.x / G, g = blockIdx.x % G;
   __shared__ double red[2][8];
   double s1 = 0.0, s2 = 0.0;
@@ -164,6 +170,8 @@ __global__ void __launch_bounds__(256) gn_apply_kernel(const void* __restrict__ 
                                                        const float2* __restrict__ stats,
                                                        const float* __restrict__ w,
                                                        const float* __restrict__ bias, int silu_after) {
+  griddep_launch();
+  griddep_wait();
   const int b = blockIdx.y;
   const int p0 = blockIdx.x * pix_per_block, p1 = min(hw, p0 + pix_per_block);
   const int c8 = C / 8;
@@ -203,6 +211,8 @@ __global__ void __launch_bounds__(256) gn_apply_kernel(const void* __restrict__ 
 // first half times the exact GELU of its second half.
 __global__ void geglu_kernel(const void* __restrict__ in, void* __restrict__ out, int f16, long long rows,
                              int F) {
+  griddep_launch();
+  griddep_wait();
   const int f8 = F / 8;
   const long long n = rows * f8;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
@@ -221,6 +231,8 @@ __global__ void geglu_kernel(const void* __restrict__ in, void* __restrict__ out
 
 __global__ void upsample2x_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, int B, int H, int W,
                                   int c8) {
+  griddep_launch();
+  griddep_wait();
   const long long n = static_cast<long long>(B) * 2 * H * 2 * W * c8;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -235,6 +247,8 @@ __global__ void upsample2x_kernel(const uint4* __restrict__ in, uint4* __restric
 
 __global__ void concat_kernel(const uint4* __restrict__ a, int ca8, const uint4* __restrict__ b, int cb8,
                               uint4* __restrict__ out, long long pixels) {
+  griddep_launch();
+  griddep_wait();
   const int c8 = ca8 + cb8;
   const long long n = pixels * c8;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
@@ -293,7 +307,12 @@ int group_norm(const void* x, void* y, int dtype, int B, int HW, int C, int G, c
   if (dtype != ND_F16 && dtype != ND_BF16) return fail(ND_ERR_INVALID, "group_norm: dtype must be f16 or bf16");
   if (B <= 0 || HW <= 0 || C <= 0 || G <= 0 || C % G || C % 8) return fail(ND_ERR_INVALID, "group_norm: bad shape");
   if (!x || !y) return fail(ND_ERR_INVALID, "group_norm: null operand");
-  const int nchunks = (HW + kGnChunk - 1) / kGnChunk;
+  // Pixel chunks of kGnChunk, or longer when that would make far more blocks
+  // than the SMs can hold at once (large images: fewer partials to combine).
+  const long long min_chunks = (HW + kGnChunk - 1) / kGnChunk;
+  const long long cap_blocks = 8LL * sm_count();
+  const int chunk = kGnChunk * static_cast<int>(std::max<long long>(1, (min_chunks * B + cap_blocks - 1) / cap_blocks));
+  const int nchunks = (HW + chunk - 1) / chunk;
   // Channel slabs: whole groups and whole vectors (multiples of lcm(C/G, 8)),
   // as many as it takes for ~4 blocks per SM, at most kGnMaxSlab channels.
   const int cg = C / G;
@@ -313,17 +332,15 @@ int group_norm(const void* x, void* y, int dtype, int B, int HW, int C, int G, c
   float2* part = static_cast<float2*>(scratch);
   float2* stats = reinterpret_cast<float2*>(static_cast<uint8_t*>(scratch) + ((part_bytes + 255) & ~size_t{255}));
   const int f16 = dtype == ND_F16;
-  gn_partial_kernel<<<dim3(nchunks, static_cast<unsigned>(slabs), B), 256, 0, s>>>(x, f16, HW, C, G, slab_c, part);
-  ND_CUDA(cudaGetLastError());
-  gn_finalize_kernel<<<B * G, 256, 0, s>>>(part, nchunks, C, G, HW, eps, stats);
-  ND_CUDA(cudaGetLastError());
+  ND_CUDA(launch_pdl(gn_partial_kernel, dim3(nchunks, static_cast<unsigned>(slabs), B), dim3(256), 0, s, x, f16, HW,
+                     C, G, slab_c, chunk, part));
+  ND_CUDA(launch_pdl(gn_finalize_kernel, dim3(B * G), dim3(256), 0, s, part, nchunks, C, G, HW, eps, stats));
   const long long vectors = static_cast<long long>(B) * HW * (C / 8);
   const int rows = 256 / std::min(C / 8, 256);  // pixel rows a block covers per pass
   const int ppb = static_cast<int>(std::max<long long>(
       rows, std::min<long long>(kGnApplyPixels, vectors / (want * 256 * 2))));
-  gn_apply_kernel<<<dim3((HW + ppb - 1) / ppb, B), 256, 0, s>>>(x, y, f16, HW, C, G, ppb, stats, w, bias,
-                                                                silu_after);
-  ND_CUDA(cudaGetLastError());
+  ND_CUDA(launch_pdl(gn_apply_kernel, dim3((HW + ppb - 1) / ppb, B), dim3(256), 0, s, x, y, f16, HW, C, G, ppb,
+                     stats, w, bias, silu_after));
   return ND_OK;
 }
 
@@ -336,7 +353,8 @@ size_t group_norm_scratch(int B, int HW, int C, int G) {
 
 int geglu(const void* in, void* out, int dtype, int64_t rows, int64_t F, cudaStream_t s) {
   if (F % 8 || rows <= 0) return fail(ND_ERR_INVALID, "geglu: bad shape");
-  geglu_kernel<<<grid_for(rows * (F / 8)), 256, 0, s>>>(in, out, dtype == ND_F16, rows, static_cast<int>(F));
+  ND_CUDA(launch_pdl(geglu_kernel, dim3(grid_for(rows * (F / 8))), dim3(256), 0, s, in, out, dtype == ND_F16 ? 1 : 0,
+                     rows, static_cast<int>(F)));
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }
@@ -344,7 +362,8 @@ int geglu(const void* in, void* out, int dtype, int64_t rows, int64_t F, cudaStr
 int upsample2x(const void* in, void* out, int B, int H, int W, int C, cudaStream_t s) {
   if (C % 8) return fail(ND_ERR_INVALID, "upsample2x: channels must be a multiple of 8");
   const long long n = static_cast<long long>(B) * 4 * H * W * (C / 8);
-  upsample2x_kernel<<<grid_for(n), 256, 0, s>>>(static_cast<const uint4*>(in), static_cast<uint4*>(out), B, H, W, C / 8);
+  ND_CUDA(launch_pdl(upsample2x_kernel, dim3(grid_for(n)), dim3(256), 0, s, static_cast<const uint4*>(in),
+                     static_cast<uint4*>(out), B, H, W, C / 8));
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }

@@ -531,6 +531,24 @@ __global__ void wan_latent_in_kernel(const float* __restrict__ in, const float* 
   }
 }
 
+__device__ __forceinline__ void unpack8v(const uint4& u, int f16, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = f16 ? __half22float2(*reinterpret_cast<const __half2*>(&w[i]))
+                         : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8v(const float (&v)[8], int f16) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = f16 ? pack_f16(v[2 * i], v[2 * i + 1]) : pack_bf16(v[2 * i], v[2 * i + 1]);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 __device__ __forceinline__ float ld16(const uint16_t* p, int f16) {
   const uint16_t v = *p;
   return f16 ? __half2float(*reinterpret_cast<const __half*>(&v))
@@ -564,6 +582,42 @@ __global__ void wan_up_shortcut_kernel(void* __restrict__ h, const void* __restr
       const __nv_bfloat16 r = __float2bfloat16_rn(v);
       hp[i] = *reinterpret_cast<const uint16_t*>(&r);
     }
+  }
+}
+
+// The same, 8 output channels per thread (Co % 8 == 0): one 16-byte load of
+// h, one (mode 0) or two (modes 1, 2: the 16 input channels 2c .. 2c+15) of x.
+__global__ void wan_up_shortcut8_kernel(uint4* __restrict__ h, const uint4* __restrict__ x, int f16, int B, int H,
+                                        int W, int Ci, int Co, int mode) {
+  const int co8 = Co / 8, ci8 = Ci / 8;
+  const long long n = static_cast<long long>(B) * 4 * H * W * co8;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % co8);
+    long long q = i / co8;
+    const int X = static_cast<int>(q % (2 * W));
+    q /= 2 * W;
+    const int Y = static_cast<int>(q % (2 * H));
+    const long long b = q / (2 * H);
+    const long long src = ((b * H + (Y >> 1)) * W + (X >> 1)) * ci8;
+    float hv[8], xv[8];
+    unpack8v(h[i], f16, hv);
+    if (mode == 0) {
+      unpack8v(__ldg(x + src + c), f16, xv);
+    } else {
+      float lo[8], hi[8];
+      unpack8v(__ldg(x + src + 2 * c), f16, lo);
+      unpack8v(__ldg(x + src + 2 * c + 1), f16, hi);
+      const int odd = mode == 1 ? 1 : (Y & 1);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        xv[k] = lo[2 * k + odd];
+        xv[4 + k] = hi[2 * k + odd];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) hv[k] += xv[k];
+    h[i] = pack8v(hv, f16);
   }
 }
 
@@ -911,8 +965,13 @@ struct WanDecoder final : nd_denoiser {
         if (v.sc_mode >= 0) {
           const int64_t n = static_cast<int64_t>(B) * 4 * hh * ww * v.up_out;
           prof_begin(s);
-          wan_up_shortcut_kernel<<<grid_of(n), 256, 0, s>>>(X[cur], X[in], dt == ND_F16, B, hh, ww, v.cin, v.up_out,
-                                                            v.sc_mode);
+          if (v.up_out % 8 == 0)
+            wan_up_shortcut8_kernel<<<grid_of(n / 8), 256, 0, s>>>(static_cast<uint4*>(X[cur]),
+                                                                   static_cast<const uint4*>(X[in]), dt == ND_F16, B,
+                                                                   hh, ww, v.cin, v.up_out, v.sc_mode);
+          else
+            wan_up_shortcut_kernel<<<grid_of(n), 256, 0, s>>>(X[cur], X[in], dt == ND_F16, B, hh, ww, v.cin, v.up_out,
+                                                              v.sc_mode);
           ND_CUDA(cudaGetLastError());
           prof_end(s, "upsample", 0.0, 0.0);
         }
