@@ -49,8 +49,8 @@ struct AttnSmem {
   static constexpr int kK = 2 * kTile;          // K stages
   static constexpr int kV = 4 * kTile;          // V stages
   static constexpr int kBar = 6 * kTile;        // 192 KB at HD 128
-  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], drain
-  static constexpr int kNumBars = 14;
+  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2][2 halves], o_full[2], drain
+  static constexpr int kNumBars = 16;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kTotal = kMisc + 16;
   static constexpr int kLaunchBytes = kTotal + 1024;
@@ -95,9 +95,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   auto v_full = [&](int s) { return bars + 8u * (3 + s); };
   auto kv_empty = [&](int s) { return bars + 8u * (5 + s); };
   auto s_full = [&](int t) { return bars + 8u * (7 + t); };
-  auto p_full = [&](int t) { return bars + 8u * (9 + t); };
-  auto o_full = [&](int t) { return bars + 8u * (11 + t); };
-  const uint32_t drain_bar = bars + 8u * 13;
+  // P of keys [0, 64) and [64, 128) of tile t's current key block
+  auto p_full = [&](int t, int h) { return bars + 8u * (9 + 2 * t + h); };
+  auto o_full = [&](int t) { return bars + 8u * (13 + t); };
+  const uint32_t drain_bar = bars + 8u * 15;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
 
@@ -122,7 +123,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(v_full(s), 1);
       mbar_init(kv_empty(s), 1);
       mbar_init(s_full(s), 1);
-      mbar_init(p_full(s), 4);
+      mbar_init(p_full(s, 0), 4);
+      mbar_init(p_full(s, 1), 4);
       mbar_init(o_full(s), 1);
     }
     mbar_init(drain_bar, 1);
@@ -208,10 +210,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         umma_commit(s_full(t));
       };
-      auto issue_pv = [&](int t, int st, bool acc) {
+      auto issue_pv = [&](int t, int st, bool acc, int kk0) {  // keys [16 kk0, 16 kk0 + 64)
         const uint32_t v_addr = sbase + L::kV + st * L::kTile;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int kk = kk0; kk < kk0 + 4; ++kk) {
           // V as the B operand [N = d, K = keys], d contiguous: MN-major,
           // 64-wide d chunks 16 KB apart (LBO), 8-key groups 1 KB apart (SBO).
           umma_ts(tmem + 256 + t * HD, tmem + t * 128 + kk * 8,
@@ -235,12 +237,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t nph = ((j + 1) >> 1) & 1;
         if (!mbar_wait(v_full(st), ph, abort_flag, a.status, kStatusTimeoutMma)) break;
         for (int t = 0; t < 2; ++t) {
-          if (!mbar_wait(p_full(t), j & 1, abort_flag, a.status, kStatusTimeoutMma)) {
+          // PV over the first 64 keys as soon as their P is in TMEM, while
+          // the softmax still works on the other 64
+          if (!mbar_wait(p_full(t, 0), j & 1, abort_flag, a.status, kStatusTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(t, st, j > 0);
+          issue_pv(t, st, j > 0, 0);
+          if (!mbar_wait(p_full(t, 1), j & 1, abort_flag, a.status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(t, st, true, 4);
           if (t == 1) umma_commit(kv_empty(st));
           if (more) {
             if (t == 0 && !mbar_wait(k_full(nst), nph, abort_flag, a.status, kStatusTimeoutMma)) {
@@ -341,13 +351,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           pk[i] = a.out_f16 ? pack_f16(p.x, p.y) : pack_bf16(p.x, p.y);
         }
         tmem_st16(s_tm + c * 16, pk);
+        if (c == 1 || c == 3) {  // one half of the row's P is in TMEM: hand it to the tensor core
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(p_full(t, c >> 1));
+        }
       }
       const float rowsum = ((s4[0].x + s4[0].y) + (s4[1].x + s4[1].y)) + ((s4[2].x + s4[2].y) + (s4[3].x + s4[3].y));
       l = l * factor + rowsum;
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full(t));
     }
     if (ok && n_kv > 0 && mbar_wait(o_full(t), 0, abort_flag, a.status, kStatusTimeoutEpilogue)) {
       __syncwarp();
