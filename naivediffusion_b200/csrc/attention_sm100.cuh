@@ -20,7 +20,9 @@
 //               grows by more than 2^8), final 1/l scaling and store.
 // TMEM columns: S_A [0,128) S_B [128,256) O_A [256, 256+HD) O_B [256+HD, 256+2HD).
 // While tile A's softmax runs, the tensor core does PV_B and S_B of the
-// next step, and the other way round.
+// next step, and the other way round. The softmax hands P over in parts (32
+// keys at d = 128, 64 at d = 64), each with its own barrier, so PV over the
+// first keys runs while the exponentials of the last are still computed.
 #pragma once
 
 #include "nd_common.cuh"
@@ -49,8 +51,8 @@ struct AttnSmem {
   static constexpr int kK = 2 * kTile;          // K stages
   static constexpr int kV = 4 * kTile;          // V stages
   static constexpr int kBar = 6 * kTile;        // 192 KB at HD 128
-  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2][2 halves], o_full[2], drain
-  static constexpr int kNumBars = 16;
+  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2][4 parts], o_full[2], drain
+  static constexpr int kNumBars = 20;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kTotal = kMisc + 16;
   static constexpr int kLaunchBytes = kTotal + 1024;
@@ -95,10 +97,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   auto v_full = [&](int s) { return bars + 8u * (3 + s); };
   auto kv_empty = [&](int s) { return bars + 8u * (5 + s); };
   auto s_full = [&](int t) { return bars + 8u * (7 + t); };
-  // P of keys [0, 64) and [64, 128) of tile t's current key block
-  auto p_full = [&](int t, int h) { return bars + 8u * (9 + 2 * t + h); };
-  auto o_full = [&](int t) { return bars + 8u * (13 + t); };
-  const uint32_t drain_bar = bars + 8u * 15;
+  // P of part h (128 / kParts keys) of tile t's current key block
+  constexpr int kParts = HD == 128 ? 4 : 2;  // measured: quarters at d = 128, halves at d = 64
+  auto p_full = [&](int t, int h) { return bars + 8u * (9 + 4 * t + h); };
+  auto o_full = [&](int t) { return bars + 8u * (17 + t); };
+  const uint32_t drain_bar = bars + 8u * 19;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
 
@@ -123,8 +126,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(v_full(s), 1);
       mbar_init(kv_empty(s), 1);
       mbar_init(s_full(s), 1);
-      mbar_init(p_full(s, 0), 4);
-      mbar_init(p_full(s, 1), 4);
+      for (int h = 0; h < kParts; ++h) mbar_init(p_full(s, h), 4);
       mbar_init(o_full(s), 1);
     }
     mbar_init(drain_bar, 1);
@@ -210,10 +212,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         umma_commit(s_full(t));
       };
-      auto issue_pv = [&](int t, int st, bool acc, int kk0) {  // keys [16 kk0, 16 kk0 + 64)
+      auto issue_pv = [&](int t, int st, bool acc, int kk0) {  // keys [16 kk0, 16 kk0 + 128 / kParts)
         const uint32_t v_addr = sbase + L::kV + st * L::kTile;
 #pragma unroll
-        for (int kk = kk0; kk < kk0 + 4; ++kk) {
+        for (int kk = kk0; kk < kk0 + 8 / kParts; ++kk) {
           // V as the B operand [N = d, K = keys], d contiguous: MN-major,
           // 64-wide d chunks 16 KB apart (LBO), 8-key groups 1 KB apart (SBO).
           umma_ts(tmem + 256 + t * HD, tmem + t * 128 + kk * 8,
@@ -237,20 +239,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t nph = ((j + 1) >> 1) & 1;
         if (!mbar_wait(v_full(st), ph, abort_flag, a.status, kStatusTimeoutMma)) break;
         for (int t = 0; t < 2; ++t) {
-          // PV over the first 64 keys as soon as their P is in TMEM, while
-          // the softmax still works on the other 64
-          if (!mbar_wait(p_full(t, 0), j & 1, abort_flag, a.status, kStatusTimeoutMma)) {
-            ok = false;
-            break;
+          // PV over each part of the keys as soon as its P is in TMEM, while
+          // the softmax still works on the rest
+          for (int h = 0; h < kParts && ok; ++h) {
+            if (!mbar_wait(p_full(t, h), j & 1, abort_flag, a.status, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(t, st, j > 0 || h > 0, h * (8 / kParts));
           }
-          tc_fence_after();
-          issue_pv(t, st, j > 0, 0);
-          if (!mbar_wait(p_full(t, 1), j & 1, abort_flag, a.status, kStatusTimeoutMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_pv(t, st, true, 4);
+          if (!ok) break;
           if (t == 1) umma_commit(kv_empty(st));
           if (more) {
             if (t == 0 && !mbar_wait(k_full(nst), nph, abort_flag, a.status, kStatusTimeoutMma)) {
@@ -351,11 +350,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           pk[i] = a.out_f16 ? pack_f16(p.x, p.y) : pack_bf16(p.x, p.y);
         }
         tmem_st16(s_tm + c * 16, pk);
-        if (c == 1 || c == 3) {  // one half of the row's P is in TMEM: hand it to the tensor core
+        if ((c + 1) % (4 / kParts) == 0) {  // a part of the row's P is in TMEM: hand it over
           tmem_st_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(p_full(t, c >> 1));
+          if (lane == 0) mbar_arrive(p_full(t, c / (4 / kParts)));
         }
       }
       const float rowsum = ((s4[0].x + s4[0].y) + (s4[1].x + s4[1].y)) + ((s4[2].x + s4[2].y) + (s4[3].x + s4[3].y));
