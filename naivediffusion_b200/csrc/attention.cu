@@ -49,6 +49,7 @@ int attention(const nd_attention_args& a, cudaStream_t stream) {
   g.ldo = a.ldo;
   g.out_f16 = a.dtype == ND_F16;
   g.idesc_s = make_idesc_f16(128, 128, a.dtype == ND_BF16);
+  g.idesc_s64 = make_idesc_f16(128, 64, a.dtype == ND_BF16);
   g.idesc_pv = make_idesc_f16(128, hd, a.dtype == ND_BF16, false, true);
   g.status = device_status();
   if (!g.status) return fail(ND_ERR_CUDA, "attention: no device status word");

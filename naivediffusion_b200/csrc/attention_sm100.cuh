@@ -39,7 +39,7 @@ struct AttnArgs {
   void* out;        // [batch * q_rows, ldo], head h at columns [h*128, h*128+128)
   long long ldo;
   int out_f16;
-  uint32_t idesc_s, idesc_pv;
+  uint32_t idesc_s, idesc_pv, idesc_s64;
   unsigned* status;
 };
 
@@ -51,8 +51,8 @@ struct AttnSmem {
   static constexpr int kK = 2 * kTile;          // K stages
   static constexpr int kV = 4 * kTile;          // V stages
   static constexpr int kBar = 6 * kTile;        // 192 KB at HD 128
-  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2][4 parts], o_full[2], drain
-  static constexpr int kNumBars = 20;
+  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2][4 parts], o_full[2], drain, s_loaded[2]
+  static constexpr int kNumBars = 22;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kTotal = kMisc + 16;
   static constexpr int kLaunchBytes = kTotal + 1024;
@@ -99,9 +99,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   auto s_full = [&](int t) { return bars + 8u * (7 + t); };
   // P of part h (128 / kParts keys) of tile t's current key block
   constexpr int kParts = HD == 128 ? 4 : 2;  // measured: quarters at d = 128, halves at d = 64
+  // At d = 64 the next key block's upper-half scores are computed before
+  // this block's PV (+6 % measured); at d = 128 that delays PV (-18 %).
+  constexpr bool kEarlyS = HD == 64;
   auto p_full = [&](int t, int h) { return bars + 8u * (9 + 4 * t + h); };
   auto o_full = [&](int t) { return bars + 8u * (17 + t); };
   const uint32_t drain_bar = bars + 8u * 19;
+  // the softmax has read tile t's scores into registers: S columns [64, 128)
+  // may take the next key block's scores
+  auto s_loaded = [&](int t) { return bars + 8u * (20 + t); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
 
@@ -128,6 +134,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(s_full(s), 1);
       for (int h = 0; h < kParts; ++h) mbar_init(p_full(s, h), 4);
       mbar_init(o_full(s), 1);
+      mbar_init(s_loaded(s), 4);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -212,6 +219,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         umma_commit(s_full(t));
       };
+      // S of one half of the key block (keys [64 hi, 64 hi + 64)) into the
+      // matching half of the tile's S columns
+      auto issue_s_half = [&](int t, int st, int hi) {
+        const uint32_t q_addr = sbase + L::kQ + t * L::kTile;
+        const uint32_t k_addr = sbase + L::kK + st * L::kTile + hi * 64 * 128;
+#pragma unroll
+        for (int c = 0; c < L::kChunks; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t off = c * 16384 + kk * 32;
+            umma_ss(tmem + t * 128 + hi * 64, make_sdesc_sw128(q_addr + off, 16, 1024),
+                    make_sdesc_sw128(k_addr + off, 16, 1024), a.idesc_s64, (c | kk) != 0 ? 1u : 0u);
+          }
+      };
       auto issue_pv = [&](int t, int st, bool acc, int kk0) {  // keys [16 kk0, 16 kk0 + 128 / kParts)
         const uint32_t v_addr = sbase + L::kV + st * L::kTile;
 #pragma unroll
@@ -239,6 +260,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t nph = ((j + 1) >> 1) & 1;
         if (!mbar_wait(v_full(st), ph, abort_flag, a.status, kStatusTimeoutMma)) break;
         for (int t = 0; t < 2; ++t) {
+          if (kEarlyS && more) {
+            // the next key block's scores for keys 64..127 go to S columns the
+            // softmax has already read, before this block's PV
+            if (t == 0 && !mbar_wait(k_full(nst), nph, abort_flag, a.status, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            if (!mbar_wait(s_loaded(t), j & 1, abort_flag, a.status, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s_half(t, nst, 1);
+          }
           // PV over each part of the keys as soon as its P is in TMEM, while
           // the softmax still works on the rest
           for (int h = 0; h < kParts && ok; ++h) {
@@ -252,12 +287,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (!ok) break;
           if (t == 1) umma_commit(kv_empty(st));
           if (more) {
-            if (t == 0 && !mbar_wait(k_full(nst), nph, abort_flag, a.status, kStatusTimeoutMma)) {
-              ok = false;
-              break;
+            if (kEarlyS) {
+              issue_s_half(t, nst, 0);  // keys 0..63: over P, after the PVs that read it
+              umma_commit(s_full(t));
+            } else {
+              if (t == 0 && !mbar_wait(k_full(nst), nph, abort_flag, a.status, kStatusTimeoutMma)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_s(t, nst);  // the whole block's scores (commits s_full)
             }
-            tc_fence_after();
-            issue_s(t, nst);
           } else {
             umma_commit(o_full(t));
           }
@@ -292,6 +332,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(s_tm + c * 32, sr[c]);
       tmem_ld_wait();
+      if (kEarlyS) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_loaded(t));
+      }
       // Masks: keys past the visible count (and past the end), causal.
       int vis = limit - j * 128;
       if (a.causal) vis = min(vis, q_in_batch + 1 - j * 128);
