@@ -562,6 +562,8 @@ int gemv(const nd_gemv_args& a, cudaStream_t stream) {
   if (a.w_dtype != ND_BF16 && a.w_dtype != ND_F16 && a.w_dtype != ND_BF16X2)
     return fail(ND_ERR_INVALID, "gemv: weight must be bf16, f16, bf16x2 or int8");
   if (!a.w || !a.x || !a.y) return fail(ND_ERR_INVALID, "gemv: null operand");
+  // The kernels read W in 16-byte vectors.
+  if (reinterpret_cast<uintptr_t>(a.w) & 15u) return fail(ND_ERR_INVALID, "gemv: weight must be 16-byte aligned");
   const size_t shmem = static_cast<size_t>(a.k) * nvec * sizeof(float);
   long long blocks = (a.n + 7) / 8;
   const long long cap = static_cast<long long>(sm_count()) * 8;

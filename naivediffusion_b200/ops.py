@@ -200,18 +200,22 @@ def head_norm_rope(x: torch.Tensor, heads: int, head_dim: int, weight: torch.Ten
 
 
 def gemv(w: torch.Tensor, x: torch.Tensor, bias: torch.Tensor | None = None, *,
-         pre_silu: bool = False, act: int = 0, w_pairs: bool = False) -> torch.Tensor:
+         pre_silu: bool = False, act: int = 0, w_pairs: bool = False, x_rows_per_vec: int = 0,
+         bias_period: int = 0) -> torch.Tensor:
     """y[b] = act(W . pre(x[b]) + bias) for 1-4 fp32 rows x; W bf16/f16 [n, k]
-    (w_pairs: an ND_BF16X2 pair [n, 2k])."""
+    (w_pairs: an ND_BF16X2 pair [n, 2k]). x_rows_per_vec > 0: output row j
+    reads input vector j // x_rows_per_vec (x holds ceil(n / x_rows_per_vec)
+    vectors; y is [1, n]); bias_period > 0: bias index j % bias_period."""
     n, k = w.shape
     if w_pairs:
         k //= 2
     x = x.reshape(-1, k).contiguous()
-    y = torch.empty(x.shape[0], n, device=w.device, dtype=torch.float32)
+    y = torch.empty(1 if x_rows_per_vec else x.shape[0], n, device=w.device, dtype=torch.float32)
     a = GemvArgs()
     a.w, a.w_dtype, a.n, a.k = w.data_ptr(), (_lib.ND_BF16X2 if w_pairs else _DT[w.dtype]), n, k
-    a.x, a.batch, a.pre_silu = x.data_ptr(), x.shape[0], int(pre_silu)
+    a.x, a.batch, a.pre_silu = x.data_ptr(), 1 if x_rows_per_vec else x.shape[0], int(pre_silu)
     a.bias, a.act, a.y = _ptr(bias), act, y.data_ptr()
+    a.x_rows_per_vec, a.bias_period = x_rows_per_vec, bias_period
     check(lib().nd_op_gemv(C.byref(a), C.c_void_p(_stream())))
     return y
 

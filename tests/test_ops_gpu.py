@@ -151,6 +151,43 @@ def test_gemv(cuda):
     assert rel(f32(y2), np.tanh(O.linear(x[:1], f32(wb)))) < 1e-4
 
 
+@pytest.mark.parametrize("n,k,batch,f16", [(1003, 3072, 1, False), (77, 256, 4, True), (4099, 1280, 3, False),
+                                            (50, 8192, 1, False)])
+def test_gemv_shapes(cuda, n, k, batch, f16):
+    """Row counts off a multiple of 8, short and long rows, batch 1-4, fp16."""
+    from naivediffusion_b200 import ops
+    rng = np.random.default_rng(n + k)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((batch, k)).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    wd = torch.from_numpy(w).cuda().half() if f16 else bf(w)
+    y = ops.gemv(wd, torch.from_numpy(x).cuda(), torch.from_numpy(b).cuda(), act=1)
+    ops.sync()
+    ref = O.linear(x, f32(wd), b)
+    ref = ref / (1 + np.exp(-ref))
+    assert rel(f32(y), ref) < 1e-4
+
+
+def test_gemv_per_row_vectors(cuda):
+    """Output row j reads input vector j // rows_per_vec, bias j % period (the
+    batched modulation of every block: one vector per block)."""
+    from naivediffusion_b200 import ops
+    rng = np.random.default_rng(5)
+    per, vecs, k = 6 * 512, 5, 512
+    n = per * vecs - 40
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((vecs, k)).astype(np.float32)
+    b = rng.standard_normal(per).astype(np.float32)
+    wb = bf(w)
+    y = ops.gemv(wb, torch.from_numpy(x).cuda(), torch.from_numpy(b).cuda(), pre_silu=True, x_rows_per_vec=per,
+                 bias_period=per)
+    ops.sync()
+    wf = f32(wb)
+    xs = O.silu(x)
+    ref = np.array([wf[j] @ xs[j // per] + b[j % per] for j in range(n)], np.float64)
+    assert rel(f32(y)[0], ref) < 1e-4
+
+
 def test_patchify_round_trip(cuda):
     from naivediffusion_b200 import ops
     rng = np.random.default_rng(3)
