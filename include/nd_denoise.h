@@ -112,7 +112,8 @@ typedef struct nd_model_desc {
   int context_rows, context_width; /* text rows per predict and their width */
   int latent_channels, latent_height, latent_width, patch;
   int time_width;             /* sinusoid width of the timestep embedder */
-  int batch;                  /* latents per predict (stacked CFG branches) */
+  int batch;                  /* latents per predict (stacked CFG branches): 1..4; the VAE
+                                 decoders 1..64 (a tiled decode's tiles) */
   int compute;                /* ND_BF16 (DiTs), ND_F16 (SDXL), or ND_F32 (the DiTs' fp32
                                  mode: bf16 hi|lo operand pairs on the tensor cores) */
   int weight_dtype;           /* storage: the compute dtype, or ND_I8 (weight-only, 16-bit compute) */
@@ -500,6 +501,33 @@ ND_API int nd_op_patchify(const float* latent, void* tokens, int out_dtype, int 
                           void* stream);
 ND_API int nd_op_unpatchify(const float* tokens, int64_t ldt, float* latent, int batch,
                             int channels, int height, int width, int patch, void* stream);
+
+/* ------------------------------------------------------------ tiled VAE
+ * The reference decodes in overlapping square tiles by default
+ * (GenerationOptions.TileVae, src/NaiveDiffusion/Pipeline/GenerationOptions.cs:79;
+ * TiledVaeDecoder.Run, src/NaiveDiffusion/Vae/TiledVae.cs:136-159). Here every
+ * tile goes through the decoder in ONE batch: a VAE decoder created for the
+ * tile's size with batch = the tile count (each batch item is normalised on
+ * its own, as a tile run alone is).
+ *   nd_op_tile_gather: latent [channels, height, width] fp32 -> tiles
+ *     [n_rows * n_cols, channels, tile, tile], tile (i, j) starting at
+ *     (rows[i], cols[j]) (CopyTile, TiledVae.cs:67-82).
+ *   nd_op_tile_blend: decoded tiles [n_rows * n_cols, channels, side, side]
+ *     -> out [channels, height, width]: each tile weighted by
+ *     vertical[y] * horizontal[x] (VaeTiling.Window), summed over the tiles in
+ *     row-then-column order together with the weights, then multiplied by the
+ *     reciprocal of the weight sum (BlendTile / DivideByWeights,
+ *     TiledVae.cs:84-121), one rounding per float operation as there: for the
+ *     same tiles the result is bit-identical to the reference's.
+ * rows / cols: HOST arrays of 1..256 tile origins (latent cells for the
+ * gather, pixels for the blend), each tile inside the image (ND_ERR_INVALID
+ * otherwise); vertical / horizontal: DEVICE arrays of `side` floats
+ * (VaeTiling.Crossfade); channels <= 16 for the blend. */
+ND_API int nd_op_tile_gather(const float* latent, int channels, int height, int width, const int32_t* rows,
+                             int n_rows, const int32_t* cols, int n_cols, int tile, float* tiles, void* stream);
+ND_API int nd_op_tile_blend(const float* tiles, int channels, int side, const int32_t* rows, int n_rows,
+                            const int32_t* cols, int n_cols, const float* vertical, const float* horizontal,
+                            float* out, int height, int width, void* stream);
 
 /* Widen int8 weights: out[r, c] = round(q[r, c] * scale(r, c)) in out_dtype
  * (ND_BF16 or ND_F16), scale as in nd_linear_args (quant_group 32 or 0). The

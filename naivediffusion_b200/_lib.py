@@ -159,6 +159,10 @@ def lib() -> C.CDLL:
                                      C.c_int, C.c_int, C.c_int64, C.c_void_p]
         L.nd_op_unpatchify.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                        C.c_int, C.c_int, C.c_void_p]
+        L.nd_op_tile_gather.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                        C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        L.nd_op_tile_blend.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                                       C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         _lib = L
     return _lib
 

@@ -208,7 +208,7 @@ struct VaeDecoder final : nd_denoiser {
     if (d.compute != ND_F16 && d.compute != ND_BF16) return fail(ND_ERR_UNSUPPORTED, "vae: compute must be fp16 or bf16");
     if (d.weight_dtype != d.compute) return fail(ND_ERR_UNSUPPORTED, "vae: weights must be stored in the compute dtype");
     if (d.latent_channels != 4) return fail(ND_ERR_INVALID, "vae: the latent has 4 channels");
-    if (d.batch < 1 || d.batch > 4) return fail(ND_ERR_INVALID, "vae: batch must be 1..4");
+    if (d.batch < 1 || d.batch > 64) return fail(ND_ERR_INVALID, "vae: batch must be 1..64");
     dt = d.compute;
     B = d.batch;
     C0 = d.width > 0 ? d.width : 128;
@@ -692,7 +692,7 @@ struct WanDecoder final : nd_denoiser {
     v22 = d.family == ND_FAMILY_VAE_WAN22;
     if (d.compute != ND_F16 && d.compute != ND_BF16) return fail(ND_ERR_UNSUPPORTED, "wan vae: compute must be fp16 or bf16");
     if (d.weight_dtype != d.compute) return fail(ND_ERR_UNSUPPORTED, "wan vae: weights must be stored in the compute dtype");
-    if (d.batch < 1 || d.batch > 4) return fail(ND_ERR_INVALID, "wan vae: batch must be 1..4");
+    if (d.batch < 1 || d.batch > 64) return fail(ND_ERR_INVALID, "wan vae: batch must be 1..64");
     dt = d.compute;
     B = d.batch;
     Cl = d.latent_channels > 0 ? d.latent_channels : (v22 ? 64 : 16);

@@ -238,6 +238,33 @@ def unpatchify(tokens: torch.Tensor, shape, patch: int) -> torch.Tensor:
     return lat
 
 
+def tile_gather(latent: torch.Tensor, rows, cols, tile: int) -> torch.Tensor:
+    """latent [C, H, W] fp32 -> tiles [len(rows) * len(cols), C, tile, tile],
+    tile (i, j) starting at (rows[i], cols[j]) (TiledVae.CopyTile)."""
+    c, h, w = latent.shape
+    r = (C.c_int32 * len(rows))(*rows)
+    q = (C.c_int32 * len(cols))(*cols)
+    tiles = torch.empty(len(rows) * len(cols), c, tile, tile, device=latent.device, dtype=torch.float32)
+    check(lib().nd_op_tile_gather(latent.data_ptr(), c, h, w, r, len(rows), q, len(cols), tile, tiles.data_ptr(),
+                                  C.c_void_p(_stream())))
+    return tiles
+
+
+def tile_blend(tiles: torch.Tensor, rows, cols, vertical: torch.Tensor, horizontal: torch.Tensor, height: int,
+               width: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Decoded tiles [len(rows) * len(cols), C, side, side] crossfaded into
+    out [C, height, width] (TiledVae.BlendTile + DivideByWeights); rows / cols
+    in the tiles' own units, vertical / horizontal the two axes' ramps."""
+    t, c, side, _ = tiles.shape
+    if out is None:
+        out = torch.empty(c, height, width, device=tiles.device, dtype=torch.float32)
+    r = (C.c_int32 * len(rows))(*rows)
+    q = (C.c_int32 * len(cols))(*cols)
+    check(lib().nd_op_tile_blend(tiles.data_ptr(), c, side, r, len(rows), q, len(cols), vertical.data_ptr(),
+                                 horizontal.data_ptr(), out.data_ptr(), height, width, C.c_void_p(_stream())))
+    return out
+
+
 def dequantize(q: torch.Tensor, scales: torch.Tensor, quant_group: int = 32,
                out_dtype=torch.bfloat16) -> torch.Tensor:
     """w = round(q * scale) in out_dtype (DmlOps.Dequantize, Dml/DmlOps.cs:208-228)."""

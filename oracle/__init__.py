@@ -664,6 +664,73 @@ def vae_decode(w: dict, cfg, latent):
     return np.stack(outs)
 
 
+def vae_tile_starts(extent: int, tile: int, overlap: int) -> list:
+    """VaeTiling.TileStarts (Vae/VaeTiling.cs:12-25): equal tiles, enough of
+    them to keep every overlap at least `overlap` wide, origins spread evenly
+    (Math.Round: half to even)."""
+    if extent <= tile:
+        return [0]
+    count = ((extent - overlap) + (tile - overlap) - 1) // (tile - overlap)
+    span = extent - tile
+    return [int(round(float(i) * span / (count - 1))) for i in range(count)]
+
+
+def vae_crossfade(starts, tile: int) -> np.ndarray:
+    """VaeTiling.Crossfade (Vae/VaeTiling.cs:29-49), float32 as there."""
+    weight = np.ones(tile, np.float32)
+    if len(starts) > 1:
+        step = min(starts[i] - starts[i - 1] for i in range(1, len(starts)))
+        overlap = tile - step
+        for i in range(overlap):
+            ramp = _f(i + 1) / _f(overlap + 1)
+            weight[i] = ramp
+            weight[tile - 1 - i] = ramp
+    return weight
+
+
+def vae_window(rows, cols, side: int) -> np.ndarray:
+    """VaeTiling.Window (Vae/VaeTiling.cs:55-68): window[y, x] = vertical[y] * horizontal[x]."""
+    v, h = vae_crossfade(rows, side), vae_crossfade(cols, side)
+    out = np.empty((side, side), np.float32)
+    for y in range(side):
+        out[y] = v[y] * h
+    return out
+
+
+def vae_tile_blend(tiles, rows, cols, height: int, width: int) -> np.ndarray:
+    """BlendTile over the tiles in row-then-column order, then DivideByWeights
+    (Vae/TiledVae.cs:84-121), in float32 one operation at a time: tiles
+    [len(rows) * len(cols), C, side, side] -> [C, height, width]."""
+    tiles = np.asarray(tiles, np.float32)
+    side = tiles.shape[-1]
+    win = vae_window(rows, cols, side)
+    target = np.zeros((tiles.shape[1], height, width), np.float32)
+    weight = np.zeros((height, width), np.float32)
+    t = 0
+    for top in rows:
+        for left in cols:
+            target[:, top:top + side, left:left + side] += tiles[t] * win
+            weight[top:top + side, left:left + side] += win
+            t += 1
+    target *= _f(1.0) / weight
+    return target
+
+
+def vae_tiled_decode(decode, latent, scale: int, tile: int = 64, overlap: int = 8) -> np.ndarray:
+    """TiledVaeDecoder.Run (Vae/TiledVae.cs:136-159) with the tile geometry of
+    the TiledVae constructor (:43-55): `decode` maps one latent tile
+    [C, t, t] to its image [3, t * scale, t * scale]; latent [1, C, h, w] ->
+    image [1, 3, h * scale, w * scale]."""
+    lat = np.asarray(latent, np.float32)[0]
+    h, w = lat.shape[1] * scale, lat.shape[2] * scale
+    t = min(tile, min(h, w) // scale)
+    overlap = min(overlap, t // 2)
+    rows = vae_tile_starts(h // scale, t, overlap)
+    cols = vae_tile_starts(w // scale, t, overlap)
+    tiles = np.stack([decode(np.ascontiguousarray(lat[:, r:r + t, c:c + t])) for r in rows for c in cols])
+    return vae_tile_blend(tiles, [r * scale for r in rows], [c * scale for c in cols], h, w)[None]
+
+
 def wan_channel_rms(x, gamma, silu_after=False):
     """WanVae.ChannelRmsNorm (Vae/WanVae.cs:111-121) over one image x [C, H, W]:
     each pixel's channels over sqrt(mean(x^2) + 1e-24 / C), times gamma."""
