@@ -376,6 +376,80 @@ def run_text(args):
     return 0
 
 
+def run_vae_tiled(args):
+    """The SDXL VAE's tiled decode of a 1024 x 1024 image, the reference's
+    default decode (64-cell tiles overlapping by 8: 3 x 3 tiles of 512 x 512
+    pixels, decoded as one batch of 9, then crossfaded). value: device time of
+    one decode on device-resident latents; e2e: TiledVaeDecoder.run from a
+    host latent to a host image."""
+    import numpy as np
+    import torch
+    from naivediffusion_b200.denoiser import Device, VaeDecoderConfig, synthetic_weights_device
+    from naivediffusion_b200.tiled_vae import open_tiled_decoder
+
+    rank, world, local = env_rank()
+    if rank != 0:
+        return 0  # one image per call: replicas only, rank 0 reports
+    torch.cuda.set_device(local)
+    cfg = VaeDecoderConfig()
+    dev = Device(local)
+    weights = dict(synthetic_weights_device(cfg, seed=0))
+    dec = open_tiled_decoder(dev, cfg, weights, 1024, 1024)
+    del weights
+    g = torch.Generator(device="cuda").manual_seed(1000)
+    latent = torch.randn(1, 4, 128, 128, device="cuda", generator=g)
+    for _ in range(max(3, args.warmup)):
+        img = dec.run_device(latent)
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        img = dec.run_device(latent)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    lat_h = latent.cpu().numpy()
+    y = dec.run(lat_h)
+    step_s = []
+    for _ in range(args.steps):
+        t1 = time.perf_counter()
+        y = dec.run(lat_h)
+        step_s.append(time.perf_counter() - t1)
+    same = bool(np.array_equal(y, img.cpu().numpy()))
+    prof = dec.model.profile(steps=3)
+    conv = [p for p in prof if p["name"].startswith("gemm") or p["name"] == "conv3x3"]
+    c_ms, c_fl = sum(p["ms"] for p in conv), sum(p["flops"] for p in conv)
+    peaks = measured_peaks()
+    e2e_ms = statistics.median(step_s) * 1e3
+    line = {
+        "metric": "SDXL VAE tiled decode s/image @1024×1024 fp16 (the reference's default decode); images/s",
+        "value": 1e3 / ms, "unit": "images/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,0.02) weights on device, N(0,1) latent)",
+        "config": {"workload": f"SDXL VAE decoder, 4x128x128 latent -> 3x1024x1024 image in {dec.tile_count} tiles "
+                   f"of {dec.tile_side}x{dec.tile_side} (rows {dec.rows}, columns {dec.cols} in latent cells), "
+                   "one batch", "global_batch": 1, "tiles": dec.tile_count},
+        "e2e": {"value": 1e3 / e2e_ms, "unit": "images/s", "ms_per_step_median": e2e_ms,
+                "h2d_bytes_per_step": int(lat_h.nbytes), "d2h_bytes_per_step": int(y.nbytes)},
+        "e2e_matches_device_path": same,
+        "gpu_launches": sum(p["launches"] for p in prof) + 2,
+        "roofline": {"bound": "tensor", "kernel": "gemm_sm100_kernel (conv3x3 implicit GEMM + 1x1 / attention GEMMs)",
+                     "achieved": c_fl / (c_ms / 1e3) / 1e12, "peak": peaks["bf16"], "unit": "TFLOP/s",
+                     "frac": c_fl / (c_ms / 1e3) / 1e12 / peaks["bf16"], "traffic": None,
+                     "peak_source": f"{peaks['source']} bf16 burst (fp16 dense taken as equal)"},
+        "kernels": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in p.items()} for p in prof],
+        "clocks": clk, "output_finite": bool(np.isfinite(y).all()),
+    }
+    print(json.dumps(line), flush=True)
+    dec.close()
+    dev.close()
+    return 0
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -526,7 +600,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["cfg3", "cfg1", "cfg2", "cfg4", "cfg5", "vae", "qwen21", "wan21", "wan22", *TEXT_CONFIGS], default="cfg3",
+    ap.add_argument("--config", choices=["cfg3", "cfg1", "cfg2", "cfg4", "cfg5", "vae", "vae_tiled", "qwen21", "wan21",
+                                         "wan22", *TEXT_CONFIGS], default="cfg3",
                     help="BASELINE configuration (default cfg3, the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle sample")
     args = ap.parse_args()
@@ -535,9 +610,14 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": f"{args.config}: the text towers are not a "
                               "BASELINE configuration; no bounded CPU sample is timed"}))
             return 0
+        if args.config == "vae_tiled":
+            print(json.dumps({"impl": "reference", "unavailable": "vae_tiled has no bounded CPU sample of the decode"}))
+            return 0
         return run_reference(args)
     if args.config in TEXT_CONFIGS:
         return run_text(args)
+    if args.config == "vae_tiled":
+        return run_vae_tiled(args)
     return run_ours(args)
 
 
