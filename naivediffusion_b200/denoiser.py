@@ -863,6 +863,7 @@ class CudaDenoiser:
         self.handle = h
         self.device = device
         self.desc = desc
+        self._side = None  # predict_device's stream when the caller names none
 
     # --- construction (IModelFamily.BuildDenoiser) ---------------------------
     def weight_info(self):
@@ -981,11 +982,26 @@ class CudaDenoiser:
         return out
 
     def predict_device(self, latent, timestep: float, sigma: float, conditioning: dict, out, stream=None):
-        """The same over torch CUDA tensors, enqueued on `stream` (cudaStream_t int or None)."""
+        """The same over torch CUDA tensors, enqueued on `stream` (a cudaStream_t
+        handle). stream=None: ordered with torch's current stream, as a torch op
+        is -- the step runs on a stream of this object's own, after the current
+        stream's work so far and before its work from here on. (The C ABI's
+        null stream means the library's device stream, which is not ordered
+        with torch's default stream.)"""
+        import torch
         arr, keep = self._cond(conditioning, device=True)
+        cur = None
+        if stream is None:
+            cur = torch.cuda.current_stream(latent.device)
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=latent.device)
+            self._side.wait_stream(cur)
+            stream = self._side.cuda_stream
         check(_bind().nd_denoiser_predict_device(
             self.handle, C.c_void_p(latent.data_ptr()), timestep, sigma, len(conditioning), arr,
-            C.c_void_p(out.data_ptr()), C.c_void_p(stream or 0)))
+            C.c_void_p(out.data_ptr()), C.c_void_p(stream)))
+        if cur is not None:
+            cur.wait_stream(self._side)
         del keep
         return out
 
