@@ -135,6 +135,26 @@ def test_gemm_known_product():
     np.testing.assert_array_equal(y, a @ b)
 
 
+def test_linear_reads_every_float_width_alike():
+    """CpuMathTests.LinearReadsEveryFloatWidthAlike (tests/NaiveDiffusion.Tests/
+    CpuMathTests.cs:40-67): a 5 x 8 matrix of values exact at every width,
+    (i % 7 - 3) * 0.25, read from fp32, fp16 and bf16 storage (widened as
+    HostTensor does), gives the same product as the float loop."""
+    w = np.array([(i % 7 - 3) * 0.25 for i in range(40)], np.float32).reshape(5, 8)
+    x = np.sin(np.arange(24, dtype=np.float32)).reshape(3, 8)
+    bias = np.array([1, 2, 3, 4, 5], np.float32)
+    expected = np.empty((3, 5), np.float32)
+    for m in range(3):
+        for o in range(5):
+            acc = np.float32(bias[o])
+            for i in range(8):
+                acc = np.float32(acc + x[m, i] * w[o, i])
+            expected[m, o] = acc
+    for widened in (w, O.from_f16_bits(O.to_f16_bits(w)), O.from_bf16_bits(O.to_bf16_bits(w))):
+        assert np.array_equal(widened, w)
+        assert np.abs(O.linear(x, widened, bias) - expected).max() <= 1e-5
+
+
 def test_linear_matches_float64():
     rng = np.random.default_rng(0)
     x = rng.standard_normal((37, 200)).astype(np.float32)

@@ -133,3 +133,28 @@ def test_head_norm_rope_op(cuda, hd, dtype):
     got = t.float().cpu().numpy()
     assert rel(got[:, :heads * hd], ref) < (1e-5 if dtype == torch.float32 else 1e-2)
     assert np.array_equal(got[:, heads * hd:], xin[:, heads * hd:])  # columns past the heads untouched
+
+
+def test_weights_mean_the_same_at_every_float_width(device):
+    """CpuMathTests' point on the device (tests/NaiveDiffusion.Tests/CpuMathTests.cs:
+    a matrix has to mean the same numbers at every width a checkpoint stores it
+    at): the same tower uploaded from fp32 and fp16 host arrays and from bf16
+    device tensors -- every value exact at all three widths -- encodes a prompt
+    bit-identically (the embedding row gather and every GEMM read the same numbers)."""
+    cfg = Qwen3TextConfig(**SMALL_Q)
+    w = {}
+    for name, a in synthetic_weights(cfg, seed=5):
+        v = O.round_bf16(a)
+        v[np.abs(v) < 2.0 ** -14] = 0.0   # below fp16's normal range: keep every value exact in fp16
+        assert np.array_equal(v.astype(np.float16).astype(np.float32), v)
+        w[name] = v
+    ids = np.random.default_rng(5).integers(0, cfg.vocab, 29)
+    uploads = [w, {k: v.astype(np.float16) for k, v in w.items()},
+               {k: torch.from_numpy(v).cuda().bfloat16() for k, v in w.items()}]
+    outs = []
+    for weights in uploads:
+        with build_denoiser(device, cfg, weights) as d:
+            outs.append(d.text_encode(ids))
+    assert np.isfinite(outs[0]).all()
+    assert np.array_equal(outs[0], outs[1])
+    assert np.array_equal(outs[0], outs[2])
