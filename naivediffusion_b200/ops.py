@@ -241,6 +241,9 @@ def unpatchify(tokens: torch.Tensor, shape, patch: int) -> torch.Tensor:
 def tile_gather(latent: torch.Tensor, rows, cols, tile: int) -> torch.Tensor:
     """latent [C, H, W] fp32 -> tiles [len(rows) * len(cols), C, tile, tile],
     tile (i, j) starting at (rows[i], cols[j]) (TiledVae.CopyTile)."""
+    if latent.dim() != 3 or latent.dtype != torch.float32:
+        raise ValueError("tile_gather: latent must be a float32 [C, H, W] tensor")
+    latent = latent.contiguous()
     c, h, w = latent.shape
     r = (C.c_int32 * len(rows))(*rows)
     q = (C.c_int32 * len(cols))(*cols)
@@ -255,9 +258,19 @@ def tile_blend(tiles: torch.Tensor, rows, cols, vertical: torch.Tensor, horizont
     """Decoded tiles [len(rows) * len(cols), C, side, side] crossfaded into
     out [C, height, width] (TiledVae.BlendTile + DivideByWeights); rows / cols
     in the tiles' own units, vertical / horizontal the two axes' ramps."""
+    if tiles.dim() != 4 or tiles.dtype != torch.float32 or not tiles.is_contiguous():
+        raise ValueError("tile_blend: tiles must be a contiguous float32 [tiles, C, side, side] tensor")
     t, c, side, _ = tiles.shape
+    if t != len(rows) * len(cols) or tiles.shape[3] != side:
+        raise ValueError(f"tile_blend: {len(rows)} x {len(cols)} square tiles expected, got {tuple(tiles.shape)}")
+    for ramp in (vertical, horizontal):
+        if ramp.dtype != torch.float32 or ramp.numel() != side or ramp.device != tiles.device:
+            raise ValueError(f"tile_blend: the ramps must be float32 vectors of {side} on the tiles' device")
     if out is None:
         out = torch.empty(c, height, width, device=tiles.device, dtype=torch.float32)
+    elif (tuple(out.shape) != (c, height, width) or out.dtype != torch.float32 or not out.is_contiguous()
+          or out.device != tiles.device):
+        raise ValueError(f"tile_blend: out must be a contiguous float32 [{c}, {height}, {width}] tensor")
     r = (C.c_int32 * len(rows))(*rows)
     q = (C.c_int32 * len(cols))(*cols)
     check(lib().nd_op_tile_blend(tiles.data_ptr(), c, side, r, len(rows), q, len(cols), vertical.data_ptr(),

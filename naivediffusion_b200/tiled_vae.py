@@ -136,6 +136,9 @@ class TiledVaeDecoder:
         if tuple(latent.shape) != (1, self.latent_channels, self.height // self.scale, self.width // self.scale):
             raise ValueError(f"latent must be [1, {self.latent_channels}, {self.height // self.scale}, "
                              f"{self.width // self.scale}], got {tuple(latent.shape)}")
+        if out is not None and (tuple(out.shape) != (1, 3, self.height, self.width) or out.dtype != torch.float32
+                                or not out.is_contiguous()):
+            raise ValueError(f"out must be a contiguous float32 [1, 3, {self.height}, {self.width}] tensor")
         caller = torch.cuda.current_stream(self._device)
         self._stream.wait_stream(caller)
         with torch.cuda.stream(self._stream):

@@ -74,3 +74,20 @@ def test_blend_of_constant_tiles_is_constant():
     tiles = np.full((len(rows) * len(cols), 3, 64, 64), 0.75, np.float32)
     img = O.vae_tile_blend(tiles, rows, cols, 96, 160)
     assert np.allclose(img, 0.75, rtol=0, atol=1e-6)
+
+
+def test_tile_ops_check_their_tensors_before_any_launch():
+    """The C ABI sees plain pointers: the wrappers refuse a tile count, a ramp
+    or an output that does not match the grid (CPU tensors; nothing launches)."""
+    import torch
+    from naivediffusion_b200 import ops
+    ramp = torch.ones(16)
+    with pytest.raises(ValueError, match="square tiles"):
+        ops.tile_blend(torch.zeros(5, 3, 16, 16), [0, 8], [0, 12, 24], ramp, ramp, 24, 40)
+    with pytest.raises(ValueError, match="ramps"):
+        ops.tile_blend(torch.zeros(6, 3, 16, 16), [0, 8], [0, 12, 24], torch.ones(8), ramp, 24, 40)
+    with pytest.raises(ValueError, match="out must be"):
+        ops.tile_blend(torch.zeros(6, 3, 16, 16), [0, 8], [0, 12, 24], ramp, ramp, 24, 40,
+                       out=torch.zeros(3, 24, 39))
+    with pytest.raises(ValueError, match="float32"):
+        ops.tile_gather(torch.zeros(4, 24, 40, dtype=torch.float16), [0, 8], [0, 12, 24], 16)
