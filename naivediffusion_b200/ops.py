@@ -22,6 +22,20 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def _check_out(what: str, t: torch.Tensor, rows: int, cols: int, dtypes, device) -> None:
+    """A caller's output tensor must hold what the op writes: the C ABI sees
+    only its pointer and row stride."""
+    if (t.dim() != 2 or t.shape[0] < rows or t.shape[1] < cols or t.stride(1) != 1 or t.dtype not in dtypes
+            or t.device != device):
+        raise ValueError(f"{what} must be a 2-D {'/'.join(str(d) for d in dtypes)} tensor of at least "
+                         f"[{rows}, {cols}] with unit column stride on {device}, got {tuple(t.shape)} {t.dtype}")
+
+
+def _check_vec(what: str, t: torch.Tensor | None, n: int, device) -> None:
+    if t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < n or t.device != device):
+        raise ValueError(f"{what} must be a contiguous float32 tensor of at least {n} values on {device}")
+
+
 def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
@@ -77,7 +91,16 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     if resid_epi:
         if residual is None:
             residual = torch.empty(rows, n, device=x.device, dtype=torch.float32)
-    elif out is None:
+        else:
+            _check_out("linear: residual", residual, rows, n, (torch.float32,), x.device)
+    elif out is not None:
+        if pairs and epilogue == _lib.ND_EPI_QK_NORM_ROPE:
+            _check_out("linear: out", out, rows, n, (torch.float32,), x.device)
+        elif pairs:
+            _check_out("linear: out", out, rows, 2 * n, (torch.bfloat16,), x.device)
+        else:
+            _check_out("linear: out", out, rows, n, (torch.float16, torch.bfloat16), x.device)
+    if out is None and not resid_epi:
         if pairs and epilogue == _lib.ND_EPI_QK_NORM_ROPE:
             out = torch.empty(rows, n, device=x.device, dtype=torch.float32)
         elif pairs:
@@ -128,6 +151,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *,
     """
     q_rows = q.shape[0] // batch
     kv_rows = k.shape[0] // batch
+    if out is not None:
+        _check_out("attention: out", out, q.shape[0], (2 if out_pairs else 1) * heads * head_dim,
+                   (torch.bfloat16,) if out_pairs else (q.dtype,), q.device)
     if out is None:
         if out_pairs:
             out = torch.empty(q.shape[0], 2 * heads * head_dim, device=q.device, dtype=torch.bfloat16)
@@ -155,9 +181,15 @@ def modulate(x: torch.Tensor, shift: torch.Tensor | None, scale: torch.Tensor, *
     scale/shift: [width] or [2, width] (second row for rows >= group_split)."""
     rows, width = x.shape
     pairs = out_dtype == "pairs"
+    groups = 2 if group_split is not None and group_split < rows else 1
+    _check_vec("modulate: scale", scale, groups * width, x.device)
+    _check_vec("modulate: shift", shift, groups * width, x.device)
     if out is None:
         out = torch.empty(rows, 2 * width if pairs else width, device=x.device,
                           dtype=torch.bfloat16 if pairs else out_dtype)
+    else:
+        _check_out("modulate: out", out, rows, 2 * width if pairs else width,
+                   (torch.bfloat16,) if pairs else (torch.float32, torch.float16, torch.bfloat16), x.device)
     a = ModulateArgs()
     a.x, a.ldx = x.data_ptr(), x.stride(0)
     a.y, a.ldy, a.out_dtype = out.data_ptr(), out.stride(0), (_lib.ND_BF16X2 if pairs else _DT[out.dtype])
@@ -360,6 +392,11 @@ def sampler_step(sampler: int, prediction: int, out: torch.Tensor, sample: torch
     out: [n] or [2, n] (uncond then cond)."""
     n = sample.numel()
     branches = out.numel() // n
+    if branches not in (1, 2) or out.numel() != branches * n:
+        raise ValueError(f"sampler_step: out must hold 1 or 2 branches of {n} values")
+    for what, t in (("out", out), ("sample", sample), ("last", last), ("noise", noise),
+                    ("denoised_out", denoised_out), ("next_input", next_input)):
+        _check_vec(f"sampler_step: {what}", t, branches * n if what == "out" else n, sample.device)
     a = _lib.SamplerArgs()
     a.sampler, a.prediction, a.n, a.branches = sampler, prediction, n, branches
     a.out, a.guidance, a.sample = out.data_ptr(), guidance, sample.data_ptr()
