@@ -94,6 +94,32 @@ def test_f16_and_bf16_conversions_round_to_nearest_even():
 
 # ---------------------------------------------------------------- TransformerInputs
 
+def _bf16_truncated(values):
+    """NarrowingLossTests.BFloat16 (tests/NaiveDiffusion.Tests/NarrowingLossTests.cs:15-24):
+    the top 16 bits of each float32."""
+    bits = (np.array(values, np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    return O.from_bf16_bits(bits)
+
+
+def test_bfloat16_inside_the_normal_range_narrows_to_float16_exactly():
+    """NarrowingLossTests.BFloat16InsideTheNormalRangeNarrowsExactly (:26-35):
+    what the fp16 (SDXL) upload does to a bf16 checkpoint's values."""
+    v = _bf16_truncated([1.0, -0.5, 0.0, 1024.0, 1e-3, -60000.0])
+    assert np.array_equal(O.round_f16(v), v)
+
+
+def test_each_way_out_of_the_float16_range():
+    """NarrowingLossTests.EachWayOutOfTheRangeIsCountedWithItsEnergy (:37-49):
+    1e5 overflows, 1e-5 lands in the subnormal range, 1e-9 flushes to zero, NaN stays NaN."""
+    v = _bf16_truncated([1e5, 1e-5, 1e-9, 1.0, float("nan")])
+    h = O.round_f16(v)
+    assert np.isinf(h[0])
+    assert 0 < abs(float(h[1])) < 6.103515625e-05   # below fp16's smallest normal, 2^-14
+    assert h[2] == 0.0
+    assert h[3] == 1.0
+    assert np.isnan(h[4])
+
+
 def test_sinusoid_is_half_cosines_then_half_sines():
     assert list(O.sinusoid(0.0, 8)) == [1, 1, 1, 1, 0, 0, 0, 0]
     a = O.sinusoid(1.0, 8)
