@@ -41,3 +41,49 @@ def max_over_ranks(value: float, device: torch.device | str = "cpu") -> float:
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+# ------------------------------------------------------------ CFG-parallel pairs
+#
+# The alternative partitioning for the two-branch (classifier-free guidance)
+# configurations: two ranks per image, one branch each. Both hold the full
+# weights in a batch-1 denoiser; per step each predicts its own branch, one
+# all_gather inside the pair stacks the two predictions as [uncond, cond]
+# (GuidanceStrategy.Combine, Pipeline/GuidanceStrategy.cs:34-47, needs both),
+# and both ranks take the same sampler step on the same inputs, so their
+# latents stay bit-identical without a second exchange. At cfg2's latent that
+# is 1 MB per step over NVLink against a step of tens of milliseconds: the
+# image's latency halves where the replicas layout keeps one image per GPU.
+
+
+class CfgPair:
+    """This rank's place in a CFG-parallel pair: ranks (2i, 2i + 1) denoise
+    image i, the even one the unconditional branch (0), the odd one the
+    conditional branch (1). Every rank must construct it (the pair groups are
+    created collectively, in the same order on every rank)."""
+
+    def __init__(self, rank: int, world: int):
+        if world < 2 or world % 2:
+            raise ValueError("CfgPair: an even number of ranks, two per image")
+        if not 0 <= rank < world:
+            raise ValueError("CfgPair: rank outside the job")
+        self.rank = rank
+        self.image = rank // 2
+        self.branch = rank % 2
+        self.group = None  # two ranks: the default group is the pair
+        if world > 2:
+            groups = [dist.new_group([2 * i, 2 * i + 1]) for i in range(world // 2)]
+            self.group = groups[self.image]
+
+    def exchange(self, mine: torch.Tensor, both: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's prediction [1, ...] -> both branches' [2, ...] (uncond,
+        cond), identical on the two ranks of the pair."""
+        if mine.shape[0] != 1:
+            raise ValueError("CfgPair.exchange: one branch per rank ([1, ...])")
+        if both is None:
+            both = torch.empty((2,) + tuple(mine.shape[1:]), dtype=mine.dtype, device=mine.device)
+        elif tuple(both.shape) != (2,) + tuple(mine.shape[1:]) or both.dtype != mine.dtype:
+            raise ValueError("CfgPair.exchange: `both` must be [2, ...] of the prediction's dtype")
+        # into the two contiguous halves of `both`, in pair order: uncond, cond
+        dist.all_gather([both[0], both[1]], mine[0].contiguous(), group=self.group)
+        return both

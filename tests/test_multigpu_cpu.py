@@ -11,7 +11,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from naivediffusion_b200.multigpu import gather_latents, image_shard, max_over_ranks
+from naivediffusion_b200.multigpu import CfgPair, gather_latents, image_shard, max_over_ranks
 
 
 def _free_port() -> int:
@@ -108,3 +108,82 @@ def test_a_lost_rank_ends_the_collective_with_an_error(mode):
                 p.kill()
     assert all(r[0] == "error" for r in results), results
     assert any(r[1].startswith("rank 0") for r in results), results
+
+
+# ---------------------------------------------------------------- CFG-parallel pairs
+#
+# A stand-in denoiser and solver step (deterministic torch float ops) replace
+# the GPU ones: what is tested is the pairing, the order of the exchanged
+# branches and that the two ranks of a pair stay bit-identical.
+
+SIGMAS = [1.0, 0.7, 0.4, 0.0]
+GUIDANCE = 4.0
+
+
+def _start(image):
+    return torch.randn(1, 4, 8, 8, generator=torch.Generator().manual_seed(100 + image))
+
+
+def _context(image, branch):
+    return torch.randn(1, 4, 8, 8, generator=torch.Generator().manual_seed(200 + 10 * image + branch))
+
+
+def _predict(model_in, context):
+    return torch.tanh(model_in * 0.5 + context)
+
+
+def _solver_step(both, sample, step):
+    uncond, cond = both[0:1], both[1:2]
+    denoised = uncond + GUIDANCE * (cond - uncond)
+    return sample + (SIGMAS[step + 1] - SIGMAS[step]) * denoised
+
+
+def _one_image_on_one_rank(image):
+    sample = _start(image)
+    ctx = torch.cat([_context(image, 0), _context(image, 1)])
+    for step in range(len(SIGMAS) - 1):
+        both = _predict(sample.expand(2, -1, -1, -1), ctx)
+        sample = _solver_step(both, sample, step)
+    return sample
+
+
+def _cfg_pair_worker(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        pair = CfgPair(rank, world)
+        sample = _start(pair.image)
+        ctx = _context(pair.image, pair.branch)
+        both = torch.empty(2, 4, 8, 8)
+        for step in range(len(SIGMAS) - 1):
+            mine = _predict(sample, ctx)                 # this rank's branch only
+            pair.exchange(mine, both)                    # [uncond, cond] on both ranks
+            sample = _solver_step(both, sample, step)
+        q.put(("ok", rank, pair.image, pair.branch, sample))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        q.put(("error", rank, traceback.format_exc(), None, None))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_cfg_parallel_pairs_match_one_rank_per_image(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_cfg_pair_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(r[0] == "ok" for r in results), [r[2] for r in results if r[0] != "ok"]
+    for _, rank, image, branch, sample in results:
+        assert (image, branch) == (rank // 2, rank % 2)
+        assert torch.equal(sample, _one_image_on_one_rank(image)), (rank, image)
+
+
+def test_cfg_pair_needs_an_even_job():
+    with pytest.raises(ValueError):
+        CfgPair(0, 3)
+    with pytest.raises(ValueError):
+        CfgPair(4, 4)
