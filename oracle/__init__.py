@@ -511,6 +511,54 @@ def conv2d(x, w, b=None, stride=1, pad=1):
     return y
 
 
+def unet_resblock(w: dict, p: str, x, temb):
+    """UNetModel.ResnetBlock (Models/Sdxl/UNetModel.cs:230-254) on one image
+    x [C, H, W]: GN+SiLU, conv3x3, + the time projection, GN+SiLU, conv3x3,
+    plus the (1x1-projected when the width changes) input."""
+    h = group_norm(x, 32, w[p + ".norm1.weight"], w.get(p + ".norm1.bias"), 1e-5, True)
+    h = conv2d(h, w[p + ".conv1.weight"], w.get(p + ".conv1.bias"))
+    proj = linear(silu(temb)[None], w[p + ".time_emb_proj.weight"], w.get(p + ".time_emb_proj.bias"))[0]
+    h = h + proj[:, None, None]
+    h = group_norm(h, 32, w[p + ".norm2.weight"], w.get(p + ".norm2.bias"), 1e-5, True)
+    h = conv2d(h, w[p + ".conv2.weight"], w.get(p + ".conv2.bias"))
+    if p + ".conv_shortcut.weight" in w:
+        sc = w[p + ".conv_shortcut.weight"]
+        x = conv2d(x, sc.reshape(sc.shape[0], sc.shape[1], 1, 1), w.get(p + ".conv_shortcut.bias"), 1, 0)
+    return x + h
+
+
+def _unet_attn(w: dict, x, src, p, heads):
+    q = linear(x, w[p + ".to_q.weight"])
+    k = linear(src, w[p + ".to_k.weight"])
+    v = linear(src, w[p + ".to_v.weight"])
+    return linear(attention(q, k, v, heads), w[p + ".to_out.0.weight"], w.get(p + ".to_out.0.bias"))
+
+
+def unet_transformer2d(w: dict, p: str, x, ctx):
+    """UNetModel.Transformer2d (Models/Sdxl/UNetModel.cs:279-301) on one image
+    x [C, H, W] with its context rows: GN (eps 1e-6), proj_in, the blocks
+    (self-attention, cross-attention, GEGLU feed-forward, each after an
+    LN with eps 1e-5), proj_out, plus the input."""
+    c, h_, w_ = x.shape
+    t = group_norm(x, 32, w[p + ".norm.weight"], w.get(p + ".norm.bias"), 1e-6).reshape(c, -1).T
+    t = linear(np.ascontiguousarray(t), w[p + ".proj_in.weight"], w.get(p + ".proj_in.bias"))
+    j = 0
+    while f"{p}.transformer_blocks.{j}.norm1.weight" in w:
+        q = f"{p}.transformer_blocks.{j}"
+        heads = c // 64
+        n = layernorm(t, 1e-5, w[q + ".norm1.weight"], w.get(q + ".norm1.bias"))
+        t = t + _unet_attn(w, n, n, q + ".attn1", heads)
+        n = layernorm(t, 1e-5, w[q + ".norm2.weight"], w.get(q + ".norm2.bias"))
+        t = t + _unet_attn(w, n, ctx, q + ".attn2", heads)
+        n = layernorm(t, 1e-5, w[q + ".norm3.weight"], w.get(q + ".norm3.bias"))
+        hh = linear(n, w[q + ".ff.net.0.proj.weight"], w.get(q + ".ff.net.0.proj.bias"))
+        inner = hh.shape[1] // 2
+        t = t + linear(hh[:, :inner] * gelu(hh[:, inner:]), w[q + ".ff.net.2.weight"], w.get(q + ".ff.net.2.bias"))
+        j += 1
+    t = linear(t, w[p + ".proj_out.weight"], w.get(p + ".proj_out.bias"))
+    return np.ascontiguousarray(t.T.reshape(c, h_, w_)) + x
+
+
 def unet_forward(w: dict, cfg, latent, timestep, add, context):
     """The SDXL UNet step in fp32, one image at a time (UNetModel.Build,
     Models/Sdxl/UNetModel.cs:333-437). latent [B, 4, H, W]; add [B, aw];
@@ -527,42 +575,10 @@ def unet_forward(w: dict, cfg, latent, timestep, add, context):
                       w[p + ".linear_2.weight"], w.get(p + ".linear_2.bias"))
 
     def res(x, p, temb):
-        h = group_norm(x, 32, w[p + ".norm1.weight"], w.get(p + ".norm1.bias"), 1e-5, True)
-        h = conv2d(h, w[p + ".conv1.weight"], w.get(p + ".conv1.bias"))
-        proj = linear(silu(temb)[None], w[p + ".time_emb_proj.weight"], w.get(p + ".time_emb_proj.bias"))[0]
-        h = h + proj[:, None, None]
-        h = group_norm(h, 32, w[p + ".norm2.weight"], w.get(p + ".norm2.bias"), 1e-5, True)
-        h = conv2d(h, w[p + ".conv2.weight"], w.get(p + ".conv2.bias"))
-        if p + ".conv_shortcut.weight" in w:
-            sc = w[p + ".conv_shortcut.weight"]
-            x = conv2d(x, sc.reshape(sc.shape[0], sc.shape[1], 1, 1), w.get(p + ".conv_shortcut.bias"), 1, 0)
-        return x + h
-
-    def attn(x, src, p, heads):
-        q = linear(x, w[p + ".to_q.weight"])
-        k = linear(src, w[p + ".to_k.weight"])
-        v = linear(src, w[p + ".to_v.weight"])
-        return linear(attention(q, k, v, heads), w[p + ".to_out.0.weight"], w.get(p + ".to_out.0.bias"))
+        return unet_resblock(w, p, x, temb)
 
     def t2d(x, p, ctx):
-        c, h_, w_ = x.shape
-        t = group_norm(x, 32, w[p + ".norm.weight"], w.get(p + ".norm.bias"), 1e-6).reshape(c, -1).T
-        t = linear(np.ascontiguousarray(t), w[p + ".proj_in.weight"], w.get(p + ".proj_in.bias"))
-        j = 0
-        while f"{p}.transformer_blocks.{j}.norm1.weight" in w:
-            q = f"{p}.transformer_blocks.{j}"
-            heads = c // 64
-            n = layernorm(t, 1e-5, w[q + ".norm1.weight"], w.get(q + ".norm1.bias"))
-            t = t + attn(n, n, q + ".attn1", heads)
-            n = layernorm(t, 1e-5, w[q + ".norm2.weight"], w.get(q + ".norm2.bias"))
-            t = t + attn(n, ctx, q + ".attn2", heads)
-            n = layernorm(t, 1e-5, w[q + ".norm3.weight"], w.get(q + ".norm3.bias"))
-            hh = linear(n, w[q + ".ff.net.0.proj.weight"], w.get(q + ".ff.net.0.proj.bias"))
-            inner = hh.shape[1] // 2
-            t = t + linear(hh[:, :inner] * gelu(hh[:, inner:]), w[q + ".ff.net.2.weight"], w.get(q + ".ff.net.2.bias"))
-            j += 1
-        t = linear(t, w[p + ".proj_out.weight"], w.get(p + ".proj_out.bias"))
-        return np.ascontiguousarray(t.T.reshape(c, h_, w_)) + x
+        return unet_transformer2d(w, p, x, ctx)
 
     L = len(cfg.mult)
     outs = []

@@ -13,6 +13,7 @@
 //
 // Conventions: row-major float32 arrays; nn.Linear weights are [out, in].
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -152,18 +153,27 @@ EXPORT int nd_oracle_threads(void) {
 
 // ------------------------------------------------------------------ layers
 
-// CpuMath.Linear (Tensors/CpuMath.cs:34-64): y[m, o] = dot(x[m], w[o]) + b[o],
-// one task per output column, as Parallel.For over `outer`.
+// CpuMath.Linear (Tensors/CpuMath.cs:34-64): y[m, o] = dot(x[m], w[o]) + b[o].
+// The reference runs one task per output column (Parallel.For over `outer`);
+// here the (row, column) pairs are visited in cache tiles of 64 rows x 16
+// columns. Every element is still one dot() over the whole inner length plus
+// the bias, so the result is the same bit for bit; only the visiting order
+// (which the arithmetic does not depend on) changes.
 EXPORT void nd_oracle_linear(const float* x, int rows, int inner, const float* w,
                              const float* bias, float* y, int outer) {
-#pragma omp parallel for schedule(static)
-  for (int o = 0; o < outer; ++o) {
-    const float* col = w + static_cast<int64_t>(o) * inner;
-    const float shift = bias ? bias[o] : 0.f;
-    for (int m = 0; m < rows; ++m) {
-      y[static_cast<int64_t>(m) * outer + o] = dot(x + static_cast<int64_t>(m) * inner, col, inner) + shift;
+  constexpr int kRows = 64, kCols = 16;
+  const int rblocks = (rows + kRows - 1) / kRows, cblocks = (outer + kCols - 1) / kCols;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int cb = 0; cb < cblocks; ++cb)
+    for (int rb = 0; rb < rblocks; ++rb) {
+      const int m1 = std::min(rows, (rb + 1) * kRows), o1 = std::min(outer, (cb + 1) * kCols);
+      for (int m = rb * kRows; m < m1; ++m) {
+        const float* xm = x + static_cast<int64_t>(m) * inner;
+        for (int o = cb * kCols; o < o1; ++o)
+          y[static_cast<int64_t>(m) * outer + o] =
+              dot(xm, w + static_cast<int64_t>(o) * inner, inner) + (bias ? bias[o] : 0.f);
+      }
     }
-  }
 }
 
 // CpuMath.LayerNorm (Tensors/CpuMath.cs:92-122): two passes in double.
@@ -637,26 +647,39 @@ EXPORT void nd_oracle_group_norm(const float* x, int C, int HW, int groups, cons
 EXPORT void nd_oracle_conv2d(const float* x, int Cin, int H, int W, const float* w, const float* b,
                              int Cout, int k, int stride, int pad, float* y) {
   const int Ho = (H + 2 * pad - k) / stride + 1, Wo = (W + 2 * pad - k) / stride + 1;
-#pragma omp parallel for schedule(static)
-  for (int o = 0; o < Cout; ++o) {
-    float* yo = y + static_cast<int64_t>(o) * Ho * Wo;
-    for (int p = 0; p < Ho * Wo; ++p) yo[p] = b ? b[o] : 0.f;
-    for (int i = 0; i < Cin; ++i)
-      for (int dy = 0; dy < k; ++dy)
-        for (int dx = 0; dx < k; ++dx) {
-          const float wv = w[((static_cast<int64_t>(o) * Cin + i) * k + dy) * k + dx];
-          const float* xi = x + static_cast<int64_t>(i) * H * W;
-          for (int r = 0; r < Ho; ++r) {
-            const int yy = r * stride + dy - pad;
-            if (yy < 0 || yy >= H) continue;
-            for (int c = 0; c < Wo; ++c) {
-              const int xx = c * stride + dx - pad;
-              if (xx < 0 || xx >= W) continue;
-              yo[r * Wo + c] += wv * xi[yy * W + xx];
+  // Output rows in bands of ~2048 values so a band's sums stay in L1 while
+  // every (i, dy, dx) term is added in; each element still receives its terms
+  // in the order (i, dy, dx), so the band split does not change any sum.
+  const int band = std::max(1, 2048 / std::max(1, Wo));
+  const int bands = (Ho + band - 1) / band;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int o = 0; o < Cout; ++o)
+    for (int rb = 0; rb < bands; ++rb) {
+      float* yo = y + static_cast<int64_t>(o) * Ho * Wo;
+      const int r0 = rb * band, r1 = std::min(Ho, r0 + band);
+      for (int p = r0 * Wo; p < r1 * Wo; ++p) yo[p] = b ? b[o] : 0.f;
+      for (int i = 0; i < Cin; ++i)
+        for (int dy = 0; dy < k; ++dy)
+          for (int dx = 0; dx < k; ++dx) {
+            const float wv = w[((static_cast<int64_t>(o) * Cin + i) * k + dy) * k + dx];
+            const float* xi = x + static_cast<int64_t>(i) * H * W;
+            // columns c with 0 <= c*stride + dx - pad < W
+            const int c0 = std::max(0, (pad - dx + stride - 1) / stride);
+            const int last = W - 1 + pad - dx;  // c*stride <= last
+            const int c1 = last < 0 ? 0 : std::min(Wo, last / stride + 1);
+            for (int r = r0; r < r1; ++r) {
+              const int yy = r * stride + dy - pad;
+              if (yy < 0 || yy >= H) continue;
+              float* yr = yo + static_cast<int64_t>(r) * Wo;
+              const float* xr = xi + static_cast<int64_t>(yy) * W + dx - pad;
+              if (stride == 1) {
+                for (int c = c0; c < c1; ++c) yr[c] += wv * xr[c];
+              } else {
+                for (int c = c0; c < c1; ++c) yr[c] += wv * xr[c * stride];
+              }
             }
           }
-        }
-  }
+    }
 }
 
 // ---------------------------------------------------------------- sampling
