@@ -591,6 +591,18 @@ ND_API int nd_op_sampler_step(const nd_sampler_args* args, void* stream);
  * or CUDA fault (ND_ERR_CUDA) since the last check on this device. */
 ND_API int nd_op_sync(void* stream);
 
+/* The device-timeout path on demand (DeviceRemovedException,
+ * src/NaiveDiffusion/Dml/DeviceExceptions.cs:13-21, which the reference
+ * raises after a dispatch's fence wait, Dml/DmlDevice.cs:920-948). Launches
+ * `ctas` CTAs that wait on an mbarrier through the library's bounded wait,
+ * giving up after `limit_ns` (1 ns .. 10 s). armed = 0: nothing arrives on
+ * the barrier, the wait runs out, the kernel records a timeout in the
+ * device's status word and returns; the next nd_op_sync on the device
+ * reports ND_ERR_TIMEOUT and clears the word. armed = 1: the barrier is
+ * arrived on first and the wait completes at once. Either way the CUDA
+ * context stays usable. */
+ND_API int nd_op_wait_probe(uint64_t limit_ns, int ctas, int armed, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -140,6 +140,7 @@ def lib() -> C.CDLL:
         L.nd_version.restype = C.c_char_p
         L.nd_op_linear.argtypes = [C.POINTER(LinearArgs), C.c_void_p]
         L.nd_op_sync.argtypes = [C.c_void_p]
+        L.nd_op_wait_probe.argtypes = [C.c_uint64, C.c_int, C.c_int, C.c_void_p]
         L.nd_op_quantize.argtypes = [C.c_void_p, C.c_int, C.c_int64, C.c_int64, C.c_int64, C.c_int,
                                      C.c_void_p, C.c_void_p, C.c_void_p]
         L.nd_op_dequantize.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int64,

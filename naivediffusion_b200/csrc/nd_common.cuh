@@ -28,6 +28,7 @@ enum DeviceStatus : unsigned {
   kStatusTimeoutEpilogue = 0x300,
   kStatusTimeoutDrain = 0x400,
   kStatusBadShape = 0x500,
+  kStatusTimeoutProbe = 0x600,
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -88,18 +89,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase of `bar` with parity `parity` to complete. Gives up
-// after ND_WAIT_LIMIT_NS, or as soon as another role of the CTA has set
-// *abort; on giving up it records `where` in *status (first writer wins)
-// and sets *abort so the CTA's other roles stop too.
+// after `limit_ns` (ND_WAIT_LIMIT_NS unless a caller passes its own), or as
+// soon as another role of the CTA has set *abort; on giving up it records
+// `where` in *status (first writer wins) and sets *abort so the CTA's other
+// roles stop too.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          unsigned* status, unsigned where) {
+                                          unsigned* status, unsigned where,
+                                          uint64_t limit_ns = ND_WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (*abort) return false;
-      if (globaltimer() - t0 > ND_WAIT_LIMIT_NS) {
+      if (globaltimer() - t0 > limit_ns) {
         if (status) atomicCAS(status, 0u, where);
         *abort = 1;
         return false;

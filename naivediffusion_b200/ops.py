@@ -45,6 +45,13 @@ def sync() -> None:
     check(lib().nd_op_sync(C.c_void_p(_stream())))
 
 
+def wait_probe(limit_ns: int, ctas: int = 1, armed: bool = False) -> None:
+    """Launch the bounded-wait probe (nd_op_wait_probe) on the current stream.
+    Unarmed, its wait runs out after limit_ns and the next sync() raises
+    NdError with ND_ERR_TIMEOUT; armed, it completes at once."""
+    check(lib().nd_op_wait_probe(C.c_uint64(limit_ns), ctas, int(armed), C.c_void_p(_stream())))
+
+
 def to_pairs(t: torch.Tensor) -> torch.Tensor:
     """fp32 [rows, cols] -> the ND_BF16X2 pair [rows, 2 * cols] (hi = bf16(t),
     lo = bf16(t - hi)), the operand format of fp32-compute GEMMs."""
