@@ -51,7 +51,11 @@ def max_over_ranks(value: float, device: torch.device | str = "cpu") -> float:
 # all_gather inside the pair stacks the two predictions as [uncond, cond]
 # (GuidanceStrategy.Combine, Pipeline/GuidanceStrategy.cs:34-47, needs both),
 # and both ranks take the same sampler step on the same inputs, so their
-# latents stay bit-identical without a second exchange. At cfg2's latent that
+# latents stay bit-identical without a second exchange. For the stochastic
+# samplers (Euler a, DPM++ 2M SDE) "the same inputs" includes the noise: both
+# ranks of a pair must draw it from the image's seed (the image index and
+# step), never from a per-rank one, or the two copies of the latent drift
+# apart after the first noisy step. At cfg2's latent that
 # is 1 MB per step over NVLink against a step of tens of milliseconds: the
 # image's latency halves where the replicas layout keeps one image per GPU.
 
@@ -82,8 +86,10 @@ class CfgPair:
             raise ValueError("CfgPair.exchange: one branch per rank ([1, ...])")
         if both is None:
             both = torch.empty((2,) + tuple(mine.shape[1:]), dtype=mine.dtype, device=mine.device)
-        elif tuple(both.shape) != (2,) + tuple(mine.shape[1:]) or both.dtype != mine.dtype:
-            raise ValueError("CfgPair.exchange: `both` must be [2, ...] of the prediction's dtype")
+        elif (tuple(both.shape) != (2,) + tuple(mine.shape[1:]) or both.dtype != mine.dtype
+              or not both.is_contiguous() or both.device != mine.device):
+            raise ValueError("CfgPair.exchange: `both` must be a contiguous [2, ...] tensor of the prediction's "
+                             "dtype on its device")
         # into the two contiguous halves of `both`, in pair order: uncond, cond
         dist.all_gather([both[0], both[1]], mine[0].contiguous(), group=self.group)
         return both

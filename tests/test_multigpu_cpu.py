@@ -132,22 +132,35 @@ def _predict(model_in, context):
     return torch.tanh(model_in * 0.5 + context)
 
 
-def _solver_step(both, sample, step):
+def _noise(seed, step):
+    return torch.randn(1, 4, 8, 8, generator=torch.Generator().manual_seed(300 + 10 * seed + step))
+
+
+def _solver_step(both, sample, step, noise=None):
+    """A deterministic Euler-like step, or with `noise` an ancestral one (the
+    shape of Euler a: a deterministic move plus fresh noise scaled by the
+    step)."""
     uncond, cond = both[0:1], both[1:2]
     denoised = uncond + GUIDANCE * (cond - uncond)
-    return sample + (SIGMAS[step + 1] - SIGMAS[step]) * denoised
+    out = sample + (SIGMAS[step + 1] - SIGMAS[step]) * denoised
+    if noise is not None:
+        out = out + 0.3 * SIGMAS[step + 1] * noise
+    return out
 
 
-def _one_image_on_one_rank(image):
+def _one_image_on_one_rank(image, stochastic=False):
     sample = _start(image)
     ctx = torch.cat([_context(image, 0), _context(image, 1)])
     for step in range(len(SIGMAS) - 1):
         both = _predict(sample.expand(2, -1, -1, -1), ctx)
-        sample = _solver_step(both, sample, step)
+        sample = _solver_step(both, sample, step, _noise(image, step) if stochastic else None)
     return sample
 
 
-def _cfg_pair_worker(rank, world, port, q):
+def _cfg_pair_worker(rank, world, port, q, noise_seed):
+    """noise_seed: None (deterministic step), "image" (both ranks of a pair
+    draw the noise from the image's seed, as CfgPair requires) or "rank" (a
+    per-rank seed: the mistake the requirement guards against)."""
     try:
         _init(rank, world, port)
         pair = CfgPair(rank, world)
@@ -157,7 +170,12 @@ def _cfg_pair_worker(rank, world, port, q):
         for step in range(len(SIGMAS) - 1):
             mine = _predict(sample, ctx)                 # this rank's branch only
             pair.exchange(mine, both)                    # [uncond, cond] on both ranks
-            sample = _solver_step(both, sample, step)
+            noise = None
+            if noise_seed == "image":
+                noise = _noise(pair.image, step)
+            elif noise_seed == "rank":
+                noise = _noise(100 + rank, step)
+            sample = _solver_step(both, sample, step, noise)
         q.put(("ok", rank, pair.image, pair.branch, sample))
         dist.barrier()
         dist.destroy_process_group()
@@ -165,21 +183,71 @@ def _cfg_pair_worker(rank, world, port, q):
         q.put(("error", rank, traceback.format_exc(), None, None))
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_cfg_parallel_pairs_match_one_rank_per_image(world):
+def _run_pairs(world, noise_seed):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_cfg_pair_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_cfg_pair_worker, args=(r, world, port, q, noise_seed)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in range(world)]
     for p in procs:
         p.join(timeout=60)
     assert all(r[0] == "ok" for r in results), [r[2] for r in results if r[0] != "ok"]
-    for _, rank, image, branch, sample in results:
+    return sorted(results, key=lambda r: r[1])
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_cfg_parallel_pairs_match_one_rank_per_image(world):
+    for _, rank, image, branch, sample in _run_pairs(world, None):
         assert (image, branch) == (rank // 2, rank % 2)
         assert torch.equal(sample, _one_image_on_one_rank(image)), (rank, image)
+
+
+def test_cfg_pairs_with_a_stochastic_step_need_the_image_seed():
+    """With an ancestral (noisy) step the two ranks of a pair stay
+    bit-identical, and equal to one rank per image, when both draw the noise
+    from the image's seed; with per-rank seeds they drift apart."""
+    for _, rank, image, _, sample in _run_pairs(2, "image"):
+        assert torch.equal(sample, _one_image_on_one_rank(image, stochastic=True)), rank
+    r = _run_pairs(2, "rank")
+    assert not torch.equal(r[0][4], r[1][4])
+
+
+def _exchange_checks_worker(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        pair = CfgPair(rank, world)
+        mine = torch.ones(1, 4, 8, 8) * rank
+        errors = 0
+        for bad in (torch.empty(2, 8, 8, 4).permute(0, 3, 1, 2),   # right shape, not contiguous
+                    torch.empty(2, 4, 8, 8, dtype=torch.float64),    # wrong dtype
+                    torch.empty(3, 4, 8, 8)):                        # wrong shape
+            try:
+                pair.exchange(mine, bad)
+            except ValueError:
+                errors += 1
+        both = pair.exchange(mine)
+        q.put(("ok", rank, errors, both[:, 0, 0, 0].tolist()))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        q.put(("error", rank, traceback.format_exc(), None))
+
+
+def test_cfg_pair_exchange_rejects_unusable_outputs():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_checks_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(r[0] == "ok" for r in results), [r[2] for r in results if r[0] != "ok"]
+    for _, _, errors, got in results:
+        assert errors == 3 and got == [0.0, 1.0]
 
 
 def test_cfg_pair_needs_an_even_job():
