@@ -166,14 +166,40 @@ def _inputs(cfg, rank):
     return latent, cond, 500.0
 
 
+def host_cpu() -> dict:
+    """The host the CPU baseline ran on: CPU model, logical CPUs, and the
+    oracle's OpenMP thread count."""
+    import oracle as O
+    model = "unknown"
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"cpu_model": model, "nproc": os.cpu_count(), "omp_threads": O.threads()}
+
+
+def _timed(fn, repeats: int, budget_s: float) -> list:
+    """Time fn() up to `repeats` times, stopping early once `budget_s` is spent."""
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(max(1, repeats)):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    return times
+
+
 def cpu_block_sample(cfg, repeats: int = 1, budget_s: float = 150.0):
     """Time one full-size dual-stream block on the CPU oracle (the reference's
-    CPU layer arithmetic, all host threads) and extrapolate to a whole step:
-    blocks x per-block + the embeddings' share of the FLOPs. Returns
-    (seconds per step, sample description, threads)."""
-    import numpy as np
-    import torch
+    CPU layer arithmetic, all host threads). Returns (per-sample seconds,
+    step / sample FLOP ratio, description)."""
     import oracle as O
+    import torch
     D, F, N, ni = cfg.width, cfg.mlp_width, cfg.tokens, cfg.image_tokens
     torch.manual_seed(0)
     g = lambda *s: (torch.randn(*s) * 0.02).numpy()  # noqa: E731
@@ -185,20 +211,11 @@ def cpu_block_sample(cfg, repeats: int = 1, budget_s: float = 150.0):
     x = torch.randn(N, D).numpy()
     temb = torch.randn(D).numpy()
     cs, sn = O.qwen_rope_tables(cfg.latent_height // 2, cfg.latent_width // 2, cfg.context_rows, cfg.context_rows)
-    times = []
-    t_start = time.perf_counter()
-    for _ in range(max(1, repeats)):
-        t0 = time.perf_counter()
-        O.mmdit_block(streams[0], streams[1], x, ni, temb, cs, sn, cfg.heads)
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() - t_start > budget_s:
-            break
-    per_block = statistics.median(times)
+    times = _timed(lambda: O.mmdit_block(streams[0], streams[1], x, ni, temb, cs, sn, cfg.heads), repeats, budget_s)
     block_flops = 2.0 * (N * (4 * D * D + 2 * D * F) + 2 * N * N * D + 2 * 6 * D * D)
-    per_step = per_block * cfg.flops_per_step() / block_flops
-    sample = (f"one full-size dual-stream block ({N} tokens, width {D}) on the CPU oracle, "
-              f"median of {len(times)}, extrapolated x{cfg.flops_per_step() / block_flops:.2f} by FLOPs to a 60-block step")
-    return per_step, sample, O.threads()
+    scale = cfg.flops_per_step() / block_flops
+    return times, scale, (f"one full-size dual-stream block ({N} tokens, width {D}) on the CPU oracle, "
+                          f"{len(times)} sample(s), extrapolated x{scale:.2f} by FLOPs to a {cfg.blocks}-block step")
 
 
 def cpu_anima_sample(cfg, repeats: int = 1, budget_s: float = 150.0):
@@ -214,18 +231,11 @@ def cpu_anima_sample(cfg, repeats: int = 1, budget_s: float = 150.0):
     rng = np.random.default_rng(0)
     lat = rng.standard_normal((1, 16, one.latent_height, one.latent_width)).astype(np.float32)
     ctx = rng.standard_normal((1, one.context_rows, one.context_width)).astype(np.float32)
-    times = []
-    t_start = time.perf_counter()
-    for _ in range(max(1, repeats)):
-        t0 = time.perf_counter()
-        O.anima_forward(w, one, lat, ctx, 0.5)
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() - t_start > budget_s:
-            break
+    times = _timed(lambda: O.anima_forward(w, one, lat, ctx, 0.5), repeats, budget_s)
     scale = cfg.flops_per_step() / one.flops_per_step()
-    sample = (f"one full-size Anima block ({one.tokens} tokens, width {one.width}, batch 1) through the CPU "
-              f"oracle's step, median of {len(times)}" + (f", extrapolated x{scale:.0f} by FLOPs" if scale > 1 else ""))
-    return statistics.median(times) * scale, sample, O.threads()
+    return times, scale, (f"one full-size Anima block ({one.tokens} tokens, width {one.width}, batch 1) through the "
+                          f"CPU oracle's step, {len(times)} sample(s)"
+                          + (f", extrapolated x{scale:.0f} by FLOPs" if scale > 1 else ""))
 
 
 def cpu_qwen_image_sample(cfg, repeats: int = 1, budget_s: float = 150.0):
@@ -241,53 +251,92 @@ def cpu_qwen_image_sample(cfg, repeats: int = 1, budget_s: float = 150.0):
     rng = np.random.default_rng(0)
     lat = rng.standard_normal((1, one.latent_channels, one.latent_height, one.latent_width)).astype(np.float32)
     ctx = rng.standard_normal((one.context_rows, one.context_width)).astype(np.float32)
-    times = []
-    t_start = time.perf_counter()
-    for _ in range(max(1, repeats)):
-        t0 = time.perf_counter()
-        O.qwen_image_forward(w, one, lat, ctx, 0.5)
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() - t_start > budget_s:
-            break
+    times = _timed(lambda: O.qwen_image_forward(w, one, lat, ctx, 0.5), repeats, budget_s)
     scale = cfg.flops_per_step() / one.flops_per_step()
-    sample = (f"one full-size Qwen-Image 2.1 block ({one.tokens} tokens, width {one.width}) with the embeddings "
-              f"and final layer through the CPU oracle's step, median of {len(times)}, extrapolated x{scale:.1f} "
-              f"by FLOPs to the {cfg.blocks}-block step")
-    return statistics.median(times) * scale, sample, O.threads()
+    return times, scale, (f"one full-size Qwen-Image 2.1 block ({one.tokens} tokens, width {one.width}) with the "
+                          f"embeddings and final layer through the CPU oracle's step, {len(times)} sample(s), "
+                          f"extrapolated x{scale:.1f} by FLOPs to the {cfg.blocks}-block step")
+
+
+def cpu_unet_sample(cfg, repeats: int = 1, budget_s: float = 150.0):
+    """The SDXL UNet's two dominant units at full size and batch 1 through the
+    CPU oracle: a level-0 ResBlock (320 -> 320 channels over 128 x 128) and a
+    level-1 Transformer2d with one block (640 wide over 64 x 64, 10 heads,
+    cross-attention to 77 x 2048), extrapolated by FLOPs to the step."""
+    import numpy as np
+    import oracle as O
+    from dataclasses import replace
+    from naivediffusion_b200.denoiser import synthetic_weights
+    one = replace(cfg, depth=(0, 1, 1), batch=1)
+    res, t2d = "down_blocks.0.resnets.0", "down_blocks.1.attentions.0"
+    w = dict(synthetic_weights(one, seed=0, only=(res + ".", t2d + ".")))
+    rng = np.random.default_rng(0)
+    c0, c1 = cfg.width * cfg.mult[0], cfg.width * cfg.mult[1]
+    h, wd = cfg.latent_height, cfg.latent_width
+    x0 = rng.standard_normal((c0, h, wd)).astype(np.float32)
+    x1 = rng.standard_normal((c1, h // 2, wd // 2)).astype(np.float32)
+    temb = rng.standard_normal(1280).astype(np.float32)
+    ctx = rng.standard_normal((cfg.context_rows, cfg.context_width)).astype(np.float32)
+
+    def run():
+        O.unet_resblock(w, res, x0, temb)
+        O.unet_transformer2d(w, t2d, x1, ctx)
+
+    times = _timed(run, repeats, budget_s)
+    sample_flops = one.resblock_flops(c0, c0, h * wd) + one.transformer2d_flops(c1, h * wd // 4, 1)
+    scale = cfg.flops_per_step() / sample_flops
+    return times, scale, (f"a level-0 ResBlock ({c0} ch, {h}x{wd}) and a level-1 Transformer2d block ({c1} ch, "
+                          f"{h // 2}x{wd // 2}, 77 context rows) at batch 1 on the CPU oracle, {len(times)} sample(s), "
+                          f"extrapolated x{scale:.1f} by FLOPs to the batch-{cfg.batch} UNet step")
 
 
 def cpu_sample(name, cfg, repeats=1, budget_s=150.0):
+    """(per-sample seconds, step / sample ratio, description) or None."""
     if name == "qwen21":
         return cpu_qwen_image_sample(cfg, repeats, budget_s)
     if name in ("cfg3", "cfg4"):
         return cpu_block_sample(cfg, repeats, budget_s)
     if name in ("cfg1", "cfg2"):
         return cpu_anima_sample(cfg, repeats, budget_s)
-    return None  # cfg5: no bounded full-size sample of the UNet on the oracle
+    if name == "cfg5":
+        return cpu_unet_sample(cfg, repeats, budget_s)
+    return None  # the VAE decoders: no bounded sample is timed
 
 
 def run_reference(args):
+    """The reference's CPU layer path (the oracle port) on the host cores.
+    Each timed step is one bounded sample of the workload (one full-size
+    block, or the UNet's two dominant units); `value` extrapolates the median
+    sample by FLOPs to one whole denoiser step per image."""
     rank, world, _ = env_rank()
     if rank != 0:
         return 0
     cfg, workload, _dt, metric = _configs()[args.config]
-    if args.config in ("cfg5", "vae", "wan21", "wan22"):
+    if args.config in ("vae", "wan21", "wan22"):
         print(json.dumps({"impl": "reference", "unavailable": f"{args.config} has no bounded CPU sample of the step"}))
         return 0
-    if args.warmup > 0:
-        cpu_sample(args.config, cfg, 1, 1e9)  # warm-up: one sample
-    per_step, sample, threads = cpu_sample(args.config, cfg, args.steps, 150.0)
+    for _ in range(args.warmup):
+        cpu_sample(args.config, cfg, 1, 1e9)
+    times, scale, sample = cpu_sample(args.config, cfg, args.steps, 120.0)
+    per_sample = statistics.median(times)
+    per_step = per_sample * scale
     value = 1.0 / per_step
+    host = host_cpu()
     line = {
         "impl": "reference", "metric": metric, "value": value, "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+        "steps": len(times), "steps_requested": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_sample * 1e3,
+        "ms_per_image_extrapolated": per_step * 1e3, "sample_fraction_of_step": 1.0 / scale,
+        "timed_s": sum(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-        "config": {"workload": workload, "sample": "one block, extrapolated"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "config": {"workload": workload, "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": host["omp_threads"], "kind": "port",
+                         "sample": sample, **host},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "the reference is C# over DirectML/D3D12 (Windows); its CPU layer arithmetic is timed "
-                "through the C++ restatement in oracle/ on this box's host cores",
+        "note": "each step is one bounded sample (ms_per_step is what one sample took); value extrapolates the "
+                "median sample by FLOPs to one denoiser step per image. The reference is C# over DirectML/D3D12 "
+                "(Windows); its CPU layer arithmetic is timed through the C++ restatement in oracle/",
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -456,14 +505,25 @@ def run_ours(args):
     import torch.distributed as dist
     from datetime import timedelta
 
+    from dataclasses import replace
+
     from naivediffusion_b200.denoiser import CudaDenoiser, Device, synthetic_weights_device
-    from naivediffusion_b200.multigpu import gather_latents, max_over_ranks
+    from naivediffusion_b200.multigpu import CfgPair, gather_latents, max_over_ranks
 
     rank, world, local = env_rank()
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
     cfg, workload, dtype, metric = _configs()[args.config]
+    pair = None
+    if args.cfg_pairs:
+        # Two ranks per image, one CFG branch each (batch-1 denoisers), one
+        # exchange of the predictions per step inside the pair.
+        if getattr(cfg, "batch", 1) != 2 or world < 2 or world % 2:
+            raise SystemExit("--cfg-pairs needs a two-branch configuration (cfg2, cfg5) and an even rank count")
+        pair = CfgPair(rank, world)
+        cfg = replace(cfg, batch=1)
+    images = world // 2 if pair else world
     dev = Device(local)
     den = CudaDenoiser(dev, cfg.desc())
     for name, t in synthetic_weights_device(cfg, seed=0):
@@ -476,9 +536,23 @@ def run_ours(args):
     # stream, which the events below would not be ordered with).
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
-    latent, cond, timestep = _inputs(cfg, rank)
+    if pair:
+        # both ranks of a pair draw the image's two-branch inputs from the
+        # image's seed and keep their own branch
+        full, _, _, _ = _configs()[args.config]
+        latent, cond, timestep = _inputs(full, pair.image)
+        latent = latent[pair.branch:pair.branch + 1].contiguous()
+        cond = {k: v[pair.branch:pair.branch + 1].contiguous() for k, v in cond.items()}
+    else:
+        latent, cond, timestep = _inputs(cfg, rank)
     out = torch.empty(den.output_shape(tuple(latent.shape)), device="cuda")
+    both = torch.empty((2,) + tuple(out.shape[1:]), device="cuda") if pair else None
     sigma = 0.75
+
+    def step_device():
+        den.predict_device(latent, timestep, sigma, cond, out, stream=stream.cuda_stream)
+        if pair:
+            pair.exchange(out, both)  # [uncond, cond] on both ranks of the pair
 
     def barrier():
         torch.cuda.synchronize()
@@ -487,22 +561,34 @@ def run_ours(args):
 
     # ---- device-resident step (the kernels' number)
     for _ in range(max(3, args.warmup)):
-        den.predict_device(latent, timestep, sigma, cond, out, stream=stream.cuda_stream)
+        step_device()
     barrier()
     clocks = Clocks(local)
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        den.predict_device(latent, timestep, sigma, cond, out, stream=stream.cuda_stream)
-    gathered = gather_latents(out, world)  # the run's one collective (world > 1)
+        step_device()
+    gathered = gather_latents(out, world)  # the replicas' one collective (world > 1)
     e1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
     total_ms = max_over_ranks(e0.elapsed_time(e1), device="cuda")
     ms_per_step = total_ms / args.steps
-    value = world * args.steps / (total_ms / 1e3)
+    value = images * args.steps / (total_ms / 1e3)
     finite = bool(all(torch.isfinite(g).all().item() for g in gathered))
+    pair_same = None
+    if pair:
+        # the two ranks of a pair hold the same [uncond, cond] stack
+        stacks = gather_latents(both, world)
+        pair_same = all(torch.equal(stacks[2 * i], stacks[2 * i + 1]) for i in range(world // 2))
+    # which GPUs the ranks drove (by UUID), as NCCL saw the job
+    uuid = str(torch.cuda.get_device_properties(local).uuid)
+    if world > 1:
+        uuids = [None] * world
+        dist.all_gather_object(uuids, uuid)
+    else:
+        uuids = [uuid]
 
     # ---- end to end through the host C ABI (pinned host buffers)
     lat_h = torch.empty(latent.shape, dtype=torch.float32, pin_memory=True)
@@ -514,17 +600,34 @@ def run_ours(args):
         cond_h[k] = h.numpy()
     out_h = torch.empty(tuple(out.shape), dtype=torch.float32, pin_memory=True)
     lat_np, y = lat_h.numpy(), out_h.numpy()
-    den.predict(lat_np, timestep, sigma, cond_h, out=y)
+    pair_io = None
+    if pair:
+        # the exchange needs the prediction on the device: pinned host -> device,
+        # exchange, both branches back to pinned host memory
+        pair_io = (torch.empty(tuple(out.shape), device="cuda"),
+                   torch.empty(tuple(both.shape), dtype=torch.float32, pin_memory=True))
+
+    def step_host():
+        den.predict(lat_np, timestep, sigma, cond_h, out=y)
+        if pair:
+            dev_y, both_h = pair_io
+            dev_y.copy_(out_h, non_blocking=True)
+            pair.exchange(dev_y, both)
+            both_h.copy_(both)
+
+    step_host()
     barrier()
     step_s = []
     t0 = time.perf_counter()
     for _ in range(args.steps):
         t1 = time.perf_counter()
-        den.predict(lat_np, timestep, sigma, cond_h, out=y)
+        step_host()
         step_s.append(time.perf_counter() - t1)
     e2e_s = max_over_ranks(time.perf_counter() - t0, device="cuda")
-    e2e_value = world * args.steps / e2e_s
+    e2e_value = images * args.steps / e2e_s
     same = bool(np.allclose(y, out.cpu().numpy(), rtol=0, atol=0))
+    h2d = int(lat_np.nbytes + sum(v.nbytes for v in cond_h.values())) + (int(y.nbytes) if pair else 0)
+    d2h = int(y.nbytes) + (int(pair_io[1].numpy().nbytes) if pair else 0)
 
     # ---- per-kernel-class profile (a captured step with an event pair around every launch)
     prof = den.profile(steps=3)
@@ -556,13 +659,16 @@ def run_ours(args):
         "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": dtype,
         "data": "synthetic (seeded N(0,0.02) weights generated on device, N(0,1) latent and conditioning)",
-        "config": {"workload": workload, "global_batch": world * getattr(cfg, "batch", 1),
-                   "parallelism": f"replicas x{world} (one image per GPU)",
+        "config": {"workload": workload, "global_batch": images * (2 if pair else getattr(cfg, "batch", 1)),
+                   "parallelism": (f"CFG pairs x{images} (two GPUs per image, one branch each, one exchange of "
+                                   "the predictions per step)" if pair else
+                                   f"replicas x{world} (one image per GPU)"),
                    "l2": "no flush: each step streams its weights and activations, far above the 126 MB L2"},
+        "ranks": {"world": world, "backend": dist.get_backend() if world > 1 else None,
+                  "gpus_active": len(set(uuids))},
         "e2e": {"value": e2e_value, "unit": UNIT,
                 "ms_per_step_median": statistics.median(step_s) * 1e3,
-                "h2d_bytes_per_step": int(lat_np.nbytes + sum(v.nbytes for v in cond_h.values())),
-                "d2h_bytes_per_step": int(y.nbytes)},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches * args.steps,
         "roofline": {"bound": "tensor", "kernel": kernel,
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -578,12 +684,17 @@ def run_ours(args):
     }
     if args.config in ("cfg3", "cfg4"):
         line["config"]["seq_len"] = cfg.tokens
+    if pair:
+        line["image_latency_ms"] = ms_per_step
+        line["pairs_bit_identical"] = pair_same
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        got = cpu_sample(args.config, cfg, 1)
+        got = cpu_sample(args.config, cfg, 3, 60.0)
         if got is not None:
-            per_step, sample, threads = got
-            line["cpu_baseline"] = {"value": 1.0 / per_step, "unit": UNIT, "cores": threads, "kind": "port",
-                                    "sample": sample}
+            times, scale, sample = got
+            host = host_cpu()
+            line["cpu_baseline"] = {"value": 1.0 / (statistics.median(times) * scale), "unit": UNIT,
+                                    "cores": host["omp_threads"], "kind": "port", "sample": sample,
+                                    "samples_s": [round(t, 3) for t in times], **host}
     if rank == 0:
         print(json.dumps(line), flush=True)
     den.close()
@@ -604,6 +715,8 @@ def main():
                                          "wan22", *TEXT_CONFIGS], default="cfg3",
                     help="BASELINE configuration (default cfg3, the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle sample")
+    ap.add_argument("--cfg-pairs", action="store_true",
+                    help="two-branch configurations (cfg2, cfg5): two ranks per image, one CFG branch each")
     args = ap.parse_args()
     if args.impl == "reference":
         if args.config in TEXT_CONFIGS:

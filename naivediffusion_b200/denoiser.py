@@ -507,6 +507,53 @@ class UNetConfig:
             out.extend([(name + ".time_emb_proj.weight", (co, 1280), True), (name + ".time_emb_proj.bias", (co,), False)])
         return out
 
+    # Algorithmic FLOPs per image (1 MAC = 2 FLOP), walking UNetModel.Build's
+    # layout (Models/Sdxl/UNetModel.cs:333-437): convolutions 2 Ho Wo Cout
+    # Cin k^2, linear layers 2 rows in out, attention 4 Nq Nk C (QK^T and PV).
+    def resblock_flops(self, ci: int, co: int, pixels: int) -> float:
+        f = 2.0 * pixels * co * ci * 9 + 2.0 * pixels * co * co * 9 + 2.0 * 1280 * co
+        return f + (2.0 * pixels * co * ci if ci != co else 0.0)
+
+    def transformer2d_flops(self, c: int, pixels: int, depth: int) -> float:
+        ctx, cw = self.context_rows, self.context_width
+        per_block = (2.0 * pixels * c * c * 4 + 4.0 * pixels * pixels * c      # self-attention
+                     + 2.0 * pixels * c * c * 2 + 2.0 * ctx * cw * c * 2       # cross q, out; k, v
+                     + 4.0 * pixels * ctx * c                                   # cross attention
+                     + 2.0 * pixels * c * 8 * c + 2.0 * pixels * 4 * c * c)     # GEGLU feed-forward
+        return 2.0 * 2.0 * pixels * c * c + depth * per_block                  # proj_in / proj_out
+
+    def flops_per_step(self) -> float:
+        C0, L = self.width, len(self.mult)
+        px = self.latent_height * self.latent_width
+        f = 2.0 * px * C0 * self.latent_channels * 9 * 2                       # conv_in, conv_out
+        f += 2.0 * (self.time_width * 1280 + 1280 * 1280 + self.add_width * 1280 + 1280 * 1280)
+        chans, c = [C0], C0
+        for lvl in range(L):
+            co = C0 * self.mult[lvl]
+            for _ in range(self.resnets):
+                f += self.resblock_flops(c, co, px)
+                c = co
+                if self.depth[lvl]:
+                    f += self.transformer2d_flops(co, px, self.depth[lvl])
+                chans.append(co)
+            if lvl != L - 1:
+                px //= 4
+                f += 2.0 * px * co * co * 9                                     # stride-2 conv
+                chans.append(co)
+        f += 2 * self.resblock_flops(c, c, px) + self.transformer2d_flops(c, px, self.depth[L - 1] or 1)
+        for i in range(L):
+            lvl = L - 1 - i
+            co = C0 * self.mult[lvl]
+            for _ in range(self.resnets + 1):
+                f += self.resblock_flops(c + chans.pop(), co, px)
+                c = co
+                if self.depth[lvl]:
+                    f += self.transformer2d_flops(co, px, self.depth[lvl])
+            if i != L - 1:
+                px *= 4
+                f += 2.0 * px * co * co * 9                                     # conv after the upsample
+        return self.batch * f
+
 
 @dataclass
 class VaeDecoderConfig:
@@ -737,12 +784,16 @@ def _table(cfg):
     return cfg.weight_table() if hasattr(cfg, "weight_table") else weight_table(cfg)
 
 
-def synthetic_weights(cfg, seed: int = 0):
+def synthetic_weights(cfg, seed: int = 0, only: tuple | None = None):
     """Seeded synthetic weights in the storage precision, one generator per
     tensor name: matrices and biases N(0, 0.02), norm weights 1 + N(0, 0.02).
-    Yields (name, float32 array already rounded to bf16/fp16)."""
+    Yields (name, float32 array already rounded to bf16/fp16). `only`: name
+    prefixes to generate (the others are skipped; each tensor's values do
+    not depend on which others are drawn)."""
     if hasattr(cfg, "weight_shapes"):
         for name, shape, _req in cfg.weight_shapes():
+            if only is not None and not name.startswith(only):
+                continue
             rng = np.random.default_rng(_name_seed(name, seed))
             a = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
             if len(shape) == 1 and (("norm" in name and name.endswith(".weight")) or name.endswith(".gamma")):
@@ -752,6 +803,8 @@ def synthetic_weights(cfg, seed: int = 0):
             yield name, a
         return
     for name, rows, cols, _req in _table(cfg):
+        if only is not None and not name.startswith(only):
+            continue
         rng = np.random.default_rng(_name_seed(name, seed))
         a = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02)
         if "norm" in name and name.endswith(".weight") and cols == 1:
