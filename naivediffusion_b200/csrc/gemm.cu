@@ -5,6 +5,7 @@
 #include <cmath>
 #include <string>
 
+#include "gemm2_sm100.cuh"
 #include "gemm_sm100.cuh"
 #include "gemm_w8_sm100.cuh"
 #include "nd_internal.h"
@@ -33,6 +34,55 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   ND_CUDA(launch_pdl(gemm_sm100_kernel<BN, STAGES, CONV>, dim3(grid), dim3(192), L::kLaunchBytes, stream, ta, tb, tc, g));
   ND_CUDA(cudaGetLastError());
   return ND_OK;
+}
+
+// The pair kernel (gemm2_sm100.cuh): clusters of two CTAs, as many pairs as
+// fit on the GPU at once (cudaOccupancyMaxActiveClusters, looked up once per
+// device), each looping over 256-row tiles.
+template <int BN, int STAGES, bool CONV = false>
+int launch_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& g,
+                 cudaStream_t stream) {
+  using L = Gemm2Smem<BN, STAGES>;
+  auto kernel = gemm2_sm100_kernel<BN, STAGES, CONV>;
+  static int max_pairs[64] = {};
+  int dev = 0;
+  ND_CUDA(cudaGetDevice(&dev));
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = L::kLaunchBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  if (!max_pairs[dev & 63]) {
+    ND_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kLaunchBytes));
+    cfg.gridDim = dim3(2 * sm_count());
+    cfg.numAttrs = 1;
+    int n = 0;
+    ND_CUDA(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
+    if (n <= 0) return fail(ND_ERR_UNSUPPORTED, "linear: no CTA pair fits on this GPU");
+    max_pairs[dev & 63] = n;
+  }
+  const int tiles = ((g.M + 255) / 256) * ((g.N + BN - 1) / BN);
+  cfg.gridDim = dim3(2 * std::min(tiles, max_pairs[dev & 63]));
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  ND_CUDA(cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, g));
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+// Whether a 256-wide GEMM runs on CTA pairs: enough rows for the 256-row
+// tiles to fill the GPU, and no pair straddling two weight groups (the two
+// CTAs of a pair multiply by one W tile).
+bool use_pairs(const GemmArgs& g, int bn) {
+  if (bn != 256 || g.M < 1024) return false;
+  if (g.group_split >= g.M || g.shared_weights || g.row_groups) return true;
+  return g.group_split % 256 == 0;
 }
 
 template <int BN, int STAGES>
@@ -160,6 +210,12 @@ int linear_split(const nd_linear_args& a, cudaStream_t stream) {
   const int64_t n_all = g.N;
   const int64_t tiles256 = ((a.rows + 127) / 128) * ((n_all + 255) / 256);
   const int bn = (qk || (n_all >= 256 && tiles256 >= sms)) ? 256 : 128;
+  if (use_pairs(g, bn)) {
+    g.idesc = make_idesc_f16(256, bn, true);
+    rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, K2, K2, bn / 2, 64, true);
+    if (rc) return rc;
+    return launch_gemm2<256, 6>(ta, tb, tc, g, stream);
+  }
   g.idesc = make_idesc_f16(128, bn, true);
   rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, K2, K2, swiglu ? bn / 2 : bn, 64, true);
   if (rc) return rc;
@@ -296,6 +352,12 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
     if (bn == 256) return launch_gemm_w8<256, 4>(ta, tb, tc, g, stream);
     return launch_gemm_w8<128, 6>(ta, tb, tc, g, stream);
   }
+  if (use_pairs(g, bn)) {
+    g.idesc = make_idesc_f16(256, bn, a.dtype == ND_BF16);
+    rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, a.in_features, a.in_features, bn / 2, 64, true);
+    if (rc) return rc;
+    return launch_gemm2<256, 6>(ta, tb, tc, g, stream);
+  }
   rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, a.in_features, a.in_features, swiglu ? bn / 2 : bn, 64,
                     true);
   if (rc) return rc;
@@ -377,6 +439,12 @@ int conv2d(const nd_conv_args& c, cudaStream_t stream) {
   const int sms = sm_count();
   const int64_t tiles256 = ((M + 127) / 128) * ((c.out_channels + 255) / 256);
   const int bn = (c.out_channels >= 256 && tiles256 >= sms) ? 256 : 128;
+  if (use_pairs(g, bn)) {
+    g.idesc = make_idesc_f16(256, bn, c.dtype == ND_BF16);
+    rc = make_tmap_2d(&tb, c.weight, 2, c.out_channels, K, K, bn / 2, 64, true);
+    if (rc) return rc;
+    return launch_gemm2<256, 6, true>(ta, tb, tc, g, stream);
+  }
   g.idesc = make_idesc_f16(128, bn, c.dtype == ND_BF16);
   rc = make_tmap_2d(&tb, c.weight, 2, c.out_channels, K, K, bn, 64, true);
   if (rc) return rc;

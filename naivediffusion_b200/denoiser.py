@@ -5,8 +5,8 @@ IDenoiser.cs:10-32) becomes over libnd_denoise: `predict(latent, timestep,
 sigma, conditioning)` plus the memory figures, disposable. `build_denoiser`
 plays `IModelFamily.BuildDenoiser` (Pipeline/IModelFamily.cs:142-143): it
 creates the native model, copies every (LoRA-folded) weight into HBM once and
-finalizes. The C# binding a maintainer would add is in INTEGRATION.md; this
-module calls the same C entry points through ctypes.
+finalizes. A C# host would bind the same C entry points (include/nd_denoise.h)
+through P/Invoke; this module calls them through ctypes.
 """
 from __future__ import annotations
 

@@ -44,6 +44,7 @@ def cos(a, b):
 
 def check(y, ref, what):
     r, c = rel(y, ref), cos(y, ref)
+    print(f"{what}: max rel {r:.3e}, cosine {c:.7f}")
     assert y.shape == ref.shape, (what, y.shape, ref.shape)
     assert np.isfinite(y).all(), what
     assert r <= REL and c >= COS, f"{what}: max rel {r:.3e}, cosine {c:.6f}"
