@@ -479,7 +479,10 @@ ND_API int nd_op_group_norm(const void* x, void* y, int dtype, int batch, int pi
  *  - Nothing needs to start at zero: every partial sum and group statistic
  *    is written before it is read within the same call.
  *  - The first call on each device looks up the array's address (with that
- *    device current); make that first call before any stream capture.
+ *    device current); make that first call before any stream capture. The
+ *    address stays valid for the life of the device's CUDA context: a process
+ *    that calls cudaDeviceReset must not call this entry point afterwards
+ *    (the cached address would point into the destroyed context).
  *  - One array per device: calls in flight at the same time on one device
  *    (different streams or host threads) race on it. Calls on one stream,
  *    or otherwise ordered, are fine. */

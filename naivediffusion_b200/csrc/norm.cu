@@ -111,6 +111,92 @@ __global__ void __launch_bounds__(256) modulate_kernel(const float* __restrict__
   }
 }
 
+// The same modulation for a 16-bit output (bf16 / fp16: the operand of the
+// next GEMM), as a persistent loop: each block keeps one pair of rows (128
+// threads per row) in registers while the next pair's loads are already in
+// flight, so the grid is one wave of resident blocks with no tail and no
+// block launches per row pair. Same arithmetic as modulate_kernel: the mean,
+// then the centred second moment over the registers, then
+// (x - mean) * rstd * (1 + scale) + shift. The two block-wide reductions of
+// an iteration use a parity-indexed slot so the next iteration's writes
+// never race this one's reads.
+template <int V, int F16OUT>
+__global__ void __launch_bounds__(256) modulate16_kernel(const float* __restrict__ x, long long ldx,
+                                                         uint16_t* __restrict__ y, long long ldy, int rows,
+                                                         int width, const float* __restrict__ shift,
+                                                         const float* __restrict__ scale, int vec_stride,
+                                                         int split, float eps, int affine) {
+  griddep_launch();
+  griddep_wait();
+  __shared__ float red[2][2][2][4];  // [parity][row of the pair][mean / second moment][warp]
+  const int half = threadIdx.x >> 7;
+  const int t = threadIdx.x & 127;
+  const int w = t >> 5;
+  const int lane = threadIdx.x & 31;
+  const int w4 = width >> 2;
+  const int pairs = (rows + 1) >> 1;
+  const float one = affine ? 0.f : 1.f;
+  auto load_row = [&](int row, float4 (&v)[V]) {
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(row < rows ? row : 0) * ldx);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = t + 128 * i;
+      v[i] = (row < rows && c < w4) ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  float4 v[V], nv[V];
+  int pair = blockIdx.x;
+  if (pair < pairs) load_row(2 * pair + half, v);
+  for (int it = 0; pair < pairs; ++it) {
+    const int next = pair + gridDim.x;
+    if (next < pairs) load_row(2 * next + half, nv);
+    const int row = 2 * pair + half;
+    const int par = it & 1;
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    s = warp_sum(s);
+    if (lane == 0) red[par][half][0][w] = s;
+    __syncthreads();
+    const float mean = (red[par][half][0][0] + red[par][half][0][1] + red[par][half][0][2] + red[par][half][0][3]) / width;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      if (t + 128 * i < w4) {
+        const float a = v[i].x - mean, b = v[i].y - mean, cc = v[i].z - mean, d = v[i].w - mean;
+        q += (a * a + b * b) + (cc * cc + d * d);
+      }
+    }
+    q = warp_sum(q);
+    if (lane == 0) red[par][half][1][w] = q;
+    __syncthreads();
+    if (row < rows) {
+      const float var = (red[par][half][1][0] + red[par][half][1][1] + red[par][half][1][2] + red[par][half][1][3]) / width;
+      const float rstd = rsqrtf(var + eps);
+      const int g = row >= split ? 1 : 0;
+      const float4* sc = reinterpret_cast<const float4*>(scale + g * vec_stride);
+      const float4* sh = shift ? reinterpret_cast<const float4*>(shift + g * vec_stride) : nullptr;
+      uint2* yr = reinterpret_cast<uint2*>(y + static_cast<long long>(row) * ldy);
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const int c = t + 128 * i;
+        if (c < w4) {
+          const float4 k = __ldg(sc + c);
+          const float4 b = sh ? __ldg(sh + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float ox = (v[i].x - mean) * rstd * (one + k.x) + b.x;
+          const float oy = (v[i].y - mean) * rstd * (one + k.y) + b.y;
+          const float oz = (v[i].z - mean) * rstd * (one + k.z) + b.z;
+          const float ow = (v[i].w - mean) * rstd * (one + k.w) + b.w;
+          yr[c] = F16OUT ? make_uint2(pack_f16(ox, oy), pack_f16(oz, ow)) : make_uint2(pack_bf16(ox, oy), pack_bf16(oz, ow));
+        }
+      }
+    }
+    pair = next;
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = nv[i];
+  }
+}
+
 // RMSNorm over rows (CpuMath.RmsNorm, Tensors/CpuMath.cs:128-146):
 // y = x * rsqrt(mean(x^2) + eps) * (w + plus_one). x fp32 or bf16/f16.
 template <int V>
@@ -362,6 +448,93 @@ __global__ void __launch_bounds__(256) gemv16_kernel(const uint16_t* __restrict_
   }
 }
 
+// The GEMV for one input vector and K = 256 * KC (the modulation GEMVs:
+// every block's adaLN vectors from one timestep embedding, cfg3 13.6 GB of
+// bf16 weights per step). Lane l of a warp always covers the same 8-column
+// groups {l + 32 j} of K, so it holds its share of x (K / 32 floats, SiLU
+// already applied) in registers for the whole launch instead of re-reading it
+// from shared memory for every weight vector; each warp walks rows with a
+// stride of all warps, and the KC 16-byte loads of its next row are issued
+// before the arithmetic of the current one (two register buffers), so a warp
+// keeps about 2 x 6 KB of weights in flight. bf16 -> fp32 is a shift or a
+// mask, the products run as paired f32x2 FMAs into two partial sums.
+template <int F16, int KC>
+__device__ __forceinline__ void gemv_row_acc(const uint4 (&p)[KC], const float (&xv)[KC][8], float2& acc) {
+#pragma unroll
+  for (int j = 0; j < KC; ++j) {
+    const uint32_t u[4] = {p[j].x, p[j].y, p[j].z, p[j].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 w;
+      if (F16) {
+        w = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+      } else {
+        w = make_float2(__uint_as_float(u[i] << 16), __uint_as_float(u[i] & 0xffff0000u));
+      }
+      acc = ffma2(w, make_float2(xv[j][2 * i], xv[j][2 * i + 1]), acc);
+    }
+  }
+}
+
+template <int F16, int KC>
+__device__ __forceinline__ void gemv_row_load(const uint16_t* __restrict__ W, long long n, int lane, uint4 (&p)[KC]) {
+  const uint4* wr = reinterpret_cast<const uint4*>(W + n * (256LL * KC));
+#pragma unroll
+  for (int j = 0; j < KC; ++j)
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(p[j].x), "=r"(p[j].y), "=r"(p[j].z), "=r"(p[j].w)
+                 : "l"(wr + lane + 32 * j));
+}
+
+template <int F16, int KC>
+__device__ __forceinline__ void gemv_row_finish(float2 acc, long long n, int lane, const float* __restrict__ bias,
+                                                int act, float* __restrict__ y, long long bias_period) {
+  float v = warp_sum(acc.x + acc.y);
+  if (lane == 0) {
+    if (bias) v += bias[bias_period > 0 ? n % bias_period : n];
+    if (act == 1) v = v / (1.0f + __expf(-v));
+    else if (act == 2) v = tanhf(v);
+    y[n] = v;
+  }
+}
+
+template <int F16, int KC>
+__global__ void __launch_bounds__(128) gemv_rows_kernel(const uint16_t* __restrict__ W, long long N,
+                                                        const float* __restrict__ x, int pre,
+                                                        const float* __restrict__ bias, int act,
+                                                        float* __restrict__ y, long long bias_period) {
+  griddep_launch();
+  griddep_wait();
+  const int lane = threadIdx.x & 31;
+  float xv[KC][8];
+#pragma unroll
+  for (int j = 0; j < KC; ++j) {
+    const float4* xs = reinterpret_cast<const float4*>(x + 8 * (lane + 32 * j));
+    const float4 a = __ldg(xs), b = __ldg(xs + 1);
+    const float t[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[j][i] = pre ? t[i] / (1.0f + __expf(-t[i])) : t[i];
+  }
+  const long long stride = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  long long n = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  uint4 pa[KC], pb[KC];
+  if (n < N) gemv_row_load<F16, KC>(W, n, lane, pa);
+  while (n < N) {
+    const long long n1 = n + stride;
+    if (n1 < N) gemv_row_load<F16, KC>(W, n1, lane, pb);
+    float2 acc = make_float2(0.f, 0.f);
+    gemv_row_acc<F16, KC>(pa, xv, acc);
+    gemv_row_finish<F16, KC>(acc, n, lane, bias, act, y, bias_period);
+    if (n1 >= N) break;
+    const long long n2 = n1 + stride;
+    if (n2 < N) gemv_row_load<F16, KC>(W, n2, lane, pa);
+    acc = make_float2(0.f, 0.f);
+    gemv_row_acc<F16, KC>(pb, xv, acc);
+    gemv_row_finish<F16, KC>(acc, n1, lane, bias, act, y, bias_period);
+    n = n2;
+  }
+}
+
 // RMSNorm over short 16-bit rows (an image's pixels x channels, the Wan VAE's
 // channel norm): L lanes per row (L = 8, 16 or 32), each holding up to V
 // 16-byte vectors, so one warp keeps 32 / L rows' bytes in flight instead of
@@ -483,6 +656,35 @@ int modulate(const nd_modulate_args& a, cudaStream_t stream) {
   const int vs = a.vec_stride ? static_cast<int>(a.vec_stride) : static_cast<int>(a.width);
   const unsigned grid = static_cast<unsigned>((rows + 1) / 2);
   const int per_thread = (static_cast<int>(a.width) / 4 + 127) / 128;
+  if ((a.out_dtype == ND_BF16 || a.out_dtype == ND_F16) && (reinterpret_cast<uintptr_t>(a.y) & 7u) == 0 &&
+      (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) {
+    const int f16 = a.out_dtype == ND_F16;
+    uint16_t* y = static_cast<uint16_t*>(a.y);
+#define ND_MOD16(V, F)                                                                                        \
+  do {                                                                                                        \
+    int per_sm = 0;                                                                                           \
+    ND_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, modulate16_kernel<V, F>, 256, 0));         \
+    const unsigned g16 = static_cast<unsigned>(std::min<long long>(grid, static_cast<long long>(sm_count()) * \
+                                                                             std::max(per_sm, 1)));           \
+    ND_CUDA(launch_pdl(modulate16_kernel<V, F>, dim3(g16), dim3(256), 0, stream, a.x, a.ldx, y, a.ldy, rows,   \
+                       static_cast<int>(a.width), a.shift, a.scale, vs, split, a.eps, a.affine));            \
+  } while (0)
+#define ND_MOD16V(F)                      \
+    if (per_thread <= 1) ND_MOD16(1, F);  \
+    else if (per_thread <= 2) ND_MOD16(2, F); \
+    else if (per_thread <= 4) ND_MOD16(4, F); \
+    else if (per_thread <= 6) ND_MOD16(6, F); \
+    else ND_MOD16(8, F);
+    if (f16) {
+      ND_MOD16V(1)
+    } else {
+      ND_MOD16V(0)
+    }
+#undef ND_MOD16V
+#undef ND_MOD16
+    ND_CUDA(cudaGetLastError());
+    return ND_OK;
+  }
 #define ND_MOD(V) ND_CUDA(launch_pdl(modulate_kernel<V>, dim3(grid), dim3(256), 0, stream, a.x, a.ldx, a.y, a.ldy, a.out_dtype, rows, static_cast<int>(a.width), a.shift, a.scale, vs, split, a.eps, a.affine))
   if (per_thread <= 1) ND_MOD(1);
   else if (per_thread <= 2) ND_MOD(2);
@@ -568,6 +770,47 @@ int gemv(const nd_gemv_args& a, cudaStream_t stream) {
   long long blocks = (a.n + 7) / 8;
   const long long cap = static_cast<long long>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
+  if (a.w_dtype != ND_BF16X2 && nvec == 1 && a.k % 256 == 0 && a.k / 256 <= 12 &&
+      (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) {
+    // One input vector and K a multiple of 256: x in registers, two rows in flight per warp.
+    const int kc = static_cast<int>(a.k / 256);
+    const uint16_t* w = static_cast<const uint16_t*>(a.w);
+    const int pre = a.pre_silu ? 1 : 0;
+    // One wave of resident blocks (the register budget allows about two per SM).
+#define ND_GR(F, KC)                                                                                          \
+  do {                                                                                                        \
+    int per_sm = 0;                                                                                           \
+    ND_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_rows_kernel<F, KC>, 128, 0));         \
+    const long long cap = static_cast<long long>(sm_count()) * std::max(per_sm, 1);                           \
+    const unsigned g = static_cast<unsigned>(std::min<long long>((a.n + 3) / 4, cap));                       \
+    ND_CUDA(launch_pdl(gemv_rows_kernel<F, KC>, dim3(g), dim3(128), 0, stream, w, a.n, a.x, pre, a.bias,      \
+                       a.act, a.y, a.bias_period));                                                           \
+  } while (0)
+#define ND_GRK(F)                   \
+  switch (kc) {                     \
+    case 1: ND_GR(F, 1); break;     \
+    case 2: ND_GR(F, 2); break;     \
+    case 3: ND_GR(F, 3); break;     \
+    case 4: ND_GR(F, 4); break;     \
+    case 5: ND_GR(F, 5); break;     \
+    case 6: ND_GR(F, 6); break;     \
+    case 7: ND_GR(F, 7); break;     \
+    case 8: ND_GR(F, 8); break;     \
+    case 9: ND_GR(F, 9); break;     \
+    case 10: ND_GR(F, 10); break;   \
+    case 11: ND_GR(F, 11); break;   \
+    default: ND_GR(F, 12); break;   \
+  }
+    if (a.w_dtype == ND_F16) {
+      ND_GRK(1)
+    } else {
+      ND_GRK(0)
+    }
+#undef ND_GRK
+#undef ND_GR
+    ND_CUDA(cudaGetLastError());
+    return ND_OK;
+  }
   if (a.w_dtype != ND_BF16X2) {
     const unsigned g = static_cast<unsigned>(blocks);
     const uint16_t* w = static_cast<const uint16_t*>(a.w);
