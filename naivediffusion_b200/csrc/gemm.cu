@@ -6,6 +6,7 @@
 #include <string>
 
 #include "gemm2_sm100.cuh"
+#include "gemm2_w8_sm100.cuh"
 #include "gemm_sm100.cuh"
 #include "gemm_w8_sm100.cuh"
 #include "nd_internal.h"
@@ -72,6 +73,46 @@ int launch_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap
   cfg.gridDim = dim3(2 * std::min(tiles, max_pairs[dev & 63]));
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   ND_CUDA(cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, g));
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+// The int8 pair kernel (gemm2_w8_sm100.cuh), launched like launch_gemm2.
+template <int BN, int STAGES, int BSTAGES>
+int launch_gemm2_w8(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& tc, const GemmArgs& g,
+                    cudaStream_t stream) {
+  using L = Gemm2W8Smem<BN, STAGES, BSTAGES>;
+  auto kernel = gemm2_w8_sm100_kernel<BN, STAGES, BSTAGES>;
+  static int max_pairs[64] = {};
+  int dev = 0;
+  ND_CUDA(cudaGetDevice(&dev));
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(kW8Threads);
+  cfg.dynamicSmemBytes = L::kLaunchBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  if (!max_pairs[dev & 63]) {
+    int rc = check_register_split(reinterpret_cast<const void*>(kernel), kW8Threads, kW8RegsNeeded, "int8 linear");
+    if (rc) return rc;
+    ND_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kLaunchBytes));
+    cfg.gridDim = dim3(2 * sm_count());
+    cfg.numAttrs = 1;
+    int n = 0;
+    ND_CUDA(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
+    if (n <= 0) return fail(ND_ERR_UNSUPPORTED, "linear: no CTA pair fits on this GPU");
+    max_pairs[dev & 63] = n;
+  }
+  const int tiles = ((g.M + 255) / 256) * ((g.N + BN - 1) / BN);
+  cfg.gridDim = dim3(2 * std::min(tiles, max_pairs[dev & 63]));
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  ND_CUDA(cudaLaunchKernelEx(&cfg, kernel, ta, tw, tc, g));
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }
@@ -345,6 +386,13 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
   const int bn = (epi == ND_EPI_QK_NORM_ROPE || (n_all >= 256 && tiles256 >= sms)) ? 256 : 128;
   g.idesc = make_idesc_f16(128, bn, a.dtype == ND_BF16);
   if (w8) {
+    if (use_pairs(g, bn)) {
+      // Each CTA of a pair loads and widens [bn / 2 rows x 64 bytes].
+      g.idesc = make_idesc_f16(256, bn, a.dtype == ND_BF16);
+      rc = make_tmap_2d_typed(&tb, a.weight, ND_I8, groups * n_all, a.in_features, a.in_features, bn / 2, 64, 0);
+      if (rc) return rc;
+      return launch_gemm2_w8<256, 4, 4>(ta, tb, tc, g, stream);  // 4 raw + 4 widened slots
+    }
     // Raw int8 tiles [bn rows x 64 bytes], unswizzled (the converters swizzle).
     rc = make_tmap_2d_typed(&tb, a.weight, ND_I8, groups * n_all, a.in_features, a.in_features,
                             swiglu ? bn / 2 : bn, 64, 0);

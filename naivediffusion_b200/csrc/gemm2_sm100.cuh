@@ -49,9 +49,11 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Arrive on an mbarrier anywhere in the cluster (a shared::cluster address).
+// Arrive on an mbarrier anywhere in the cluster (a shared::cluster address),
+// with the default release semantics at CTA scope: a cluster-scope release
+// is a memory barrier the arriving warp stalls on.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
 // TMA loads into this CTA's shared memory whose completion is counted on a
