@@ -645,7 +645,7 @@ def run_ours(args):
     tpath = ROOT / "profiles" / "gemm_traffic.json"
     if args.config == "cfg3" and tpath.exists():
         traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
-    kernel = "gemm_sm100_kernel (tcgen05, all GEMM launches of a step)"
+    kernel = "gemm2_sm100_kernel (tcgen05 CTA pairs; gemm_sm100_kernel for the small GEMMs; all GEMM launches of a step)"
     if args.config in ("cfg5", "vae", "wan21", "wan22"):
         kernel = "gemm_sm100_kernel (tcgen05: conv3x3 implicit GEMMs and the linear layers)"
     elif args.config == "cfg4":
