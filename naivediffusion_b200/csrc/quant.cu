@@ -66,6 +66,12 @@ __global__ void __launch_bounds__(256) quantize_kernel(const void* __restrict__ 
   }
 }
 
+__device__ __forceinline__ float warp_sum_w8(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
 // y[b][n] = act(sum_k q[n][k] * scale(n, k) * pre(x[b][k]) + bias[n]) for int8
 // q; one warp per output row, 16 weights (one 16-byte load) per lane step.
 __global__ void __launch_bounds__(256) gemv_w8_kernel(const int8_t* __restrict__ W, long long N, int K,
@@ -150,6 +156,98 @@ __global__ void __launch_bounds__(256) gemv_w8_kernel(const int8_t* __restrict__
   }
 }
 
+// The int8 GEMV for one input vector and K = 512 * KC (cfg4's modulation
+// GEMV: 6.8 GB of int8 weights per step): as gemv_rows_kernel, lane l always
+// covers the same 16-column groups {l + 32 j}, so its 16 * KC values of x
+// (SiLU applied) stay in registers, and each warp keeps two rows' loads in
+// flight. The scale is constant over a lane's 16 weights (per output channel,
+// or a group of 16 k or more), so it multiplies each 16-term partial sum once:
+// sum_j s_j * sum_i q_i x_i.
+template <int KC>
+__device__ __forceinline__ void gemv_w8_row_load(const int8_t* __restrict__ W, long long n, int lane,
+                                                 uint4 (&p)[KC]) {
+  const uint4* wr = reinterpret_cast<const uint4*>(W + n * (512LL * KC));
+#pragma unroll
+  for (int j = 0; j < KC; ++j)
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(p[j].x), "=r"(p[j].y), "=r"(p[j].z), "=r"(p[j].w)
+                 : "l"(wr + lane + 32 * j));
+}
+
+template <int KC>
+__device__ __forceinline__ float gemv_w8_row_dot(const uint4 (&p)[KC], const float (&xv)[KC][16], long long n,
+                                                 int lane, const void* __restrict__ scales, int scale_f16,
+                                                 int group, int scale_cols) {
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < KC; ++j) {
+    const long long si = n * scale_cols + (16 * (lane + 32 * j)) / group;
+    const float s = scale_f16 ? __half2float(__ldg(static_cast<const __half*>(scales) + si))
+                              : __ldg(static_cast<const float*>(scales) + si);
+    const uint32_t w4[4] = {p[j].x, p[j].y, p[j].z, p[j].w};
+    float2 part = make_float2(0.f, 0.f);
+    const float2 m2 = make_float2(-8388736.0f, -8388736.0f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t u = w4[i] ^ 0x80808080u;  // exact int8 -> fp32 (magic 2^23 + 128 offset)
+      const float2 lo = fadd2(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u)),
+                                          __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541u))), m2);
+      const float2 hi = fadd2(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542u)),
+                                          __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543u))), m2);
+      part = ffma2(lo, make_float2(xv[j][4 * i], xv[j][4 * i + 1]), part);
+      part = ffma2(hi, make_float2(xv[j][4 * i + 2], xv[j][4 * i + 3]), part);
+    }
+    acc = fmaf(s, part.x + part.y, acc);
+  }
+  return acc;
+}
+
+template <int KC>
+__global__ void __launch_bounds__(128) gemv_w8_rows_kernel(const int8_t* __restrict__ W, long long N,
+                                                           const void* __restrict__ scales, int scale_f16,
+                                                           int group, int scale_cols, const float* __restrict__ x,
+                                                           int pre, const float* __restrict__ bias, int act,
+                                                           float* __restrict__ y, long long bias_period) {
+  griddep_launch();
+  griddep_wait();
+  const int lane = threadIdx.x & 31;
+  float xv[KC][16];
+#pragma unroll
+  for (int j = 0; j < KC; ++j) {
+    const float4* xs = reinterpret_cast<const float4*>(x + 16 * (lane + 32 * j));
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 a = __ldg(xs + q);
+      const float t[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) xv[j][4 * q + i] = pre ? t[i] / (1.0f + __expf(-t[i])) : t[i];
+    }
+  }
+  auto finish = [&](float v, long long n) {
+    v = warp_sum_w8(v);
+    if (lane == 0) {
+      if (bias) v += bias[bias_period > 0 ? n % bias_period : n];
+      if (act == 1) v = v / (1.0f + __expf(-v));
+      else if (act == 2) v = tanhf(v);
+      y[n] = v;
+    }
+  };
+  const long long stride = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  long long n = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  uint4 pa[KC], pb[KC];
+  if (n < N) gemv_w8_row_load<KC>(W, n, lane, pa);
+  while (n < N) {
+    const long long n1 = n + stride;
+    if (n1 < N) gemv_w8_row_load<KC>(W, n1, lane, pb);
+    finish(gemv_w8_row_dot<KC>(pa, xv, n, lane, scales, scale_f16, group, scale_cols), n);
+    if (n1 >= N) break;
+    const long long n2 = n1 + stride;
+    if (n2 < N) gemv_w8_row_load<KC>(W, n2, lane, pa);
+    finish(gemv_w8_row_dot<KC>(pb, xv, n1, lane, scales, scale_f16, group, scale_cols), n1);
+    n = n2;
+  }
+}
+
 }  // namespace
 
 int quantize_weights(const void* src, int src_dtype, int64_t rows, int64_t cols, int64_t group,
@@ -171,6 +269,37 @@ int gemv_w8(const nd_gemv_args& a, cudaStream_t stream) {
   if (group % 16 || a.k % group) return fail(ND_ERR_INVALID, "gemv: quant_group must be a multiple of 16 dividing k");
   const long long nvec = a.x_rows_per_vec > 0 ? (a.n + a.x_rows_per_vec - 1) / a.x_rows_per_vec : a.batch;
   const size_t shmem = static_cast<size_t>(a.k) * nvec * sizeof(float);
+  if (nvec == 1 && a.k % 512 == 0 && a.k / 512 <= 8 && (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0 &&
+      (reinterpret_cast<uintptr_t>(a.w) & 15u) == 0) {
+    // One input vector, K a multiple of 512: x in registers, two rows in flight per warp.
+    const int kc = static_cast<int>(a.k / 512);
+    const int8_t* w = static_cast<const int8_t*>(a.w);
+    const int pre = a.pre_silu ? 1 : 0;
+    const int f16 = a.scale_dtype == ND_F16;
+    const int g = static_cast<int>(group), sc = static_cast<int>(a.k / group);
+#define ND_GW8(KC)                                                                                           \
+  do {                                                                                                       \
+    int per_sm = 0;                                                                                          \
+    ND_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_w8_rows_kernel<KC>, 128, 0));        \
+    const long long cap = static_cast<long long>(sm_count()) * std::max(per_sm, 1);                          \
+    const unsigned grid = static_cast<unsigned>(std::min<long long>((a.n + 3) / 4, cap));                    \
+    ND_CUDA(launch_pdl(gemv_w8_rows_kernel<KC>, dim3(grid), dim3(128), 0, stream, w, a.n, a.scales, f16, g,  \
+                       sc, a.x, pre, a.bias, a.act, a.y, a.bias_period));                                    \
+  } while (0)
+    switch (kc) {
+      case 1: ND_GW8(1); break;
+      case 2: ND_GW8(2); break;
+      case 3: ND_GW8(3); break;
+      case 4: ND_GW8(4); break;
+      case 5: ND_GW8(5); break;
+      case 6: ND_GW8(6); break;
+      case 7: ND_GW8(7); break;
+      default: ND_GW8(8); break;
+    }
+#undef ND_GW8
+    ND_CUDA(cudaGetLastError());
+    return ND_OK;
+  }
   long long blocks = (a.n + 7) / 8;
   const long long cap = static_cast<long long>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
