@@ -117,11 +117,28 @@ int launch_gemm2_w8(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensor
   return ND_OK;
 }
 
-// Whether a 256-wide GEMM runs on CTA pairs: enough rows for the 256-row
+// Tile width: 256 unless the grid of 256-wide tiles leaves most SMs idle
+// (narrow outputs, few rows), or, for the linear layers, 256-wide tiles pad
+// the output columns more than 128-wide ones do (N = 320, 640, 1920: the
+// padding is computed and thrown away; the SDXL step's linear layers gained
+// 0.9 ms). The convolutions keep 256: at K = 9 Cin a 128-wide tile doubles
+// the A traffic per FLOP and measured slower (the SDXL step's convolutions
+// 3.84 -> 4.00 ms). (A 192-wide variant filled the last wave better at
+// N = 3072 but measured slower per tile on B200.)
+int pick_bn(int64_t rows, int64_t n, bool force256, bool pad_aware = true) {
+  if (force256) return 256;
+  const int64_t tiles256 = ((rows + 127) / 128) * ((n + 255) / 256);
+  if (n < 256 || tiles256 < sm_count()) return 128;
+  if (!pad_aware) return 256;
+  return (n + 255) / 256 * 256 > (n + 127) / 128 * 128 ? 128 : 256;
+}
+
+// Whether a GEMM runs on CTA pairs (256 x bn tiles): enough rows for the 256-row
 // tiles to fill the GPU, and no pair straddling two weight groups (the two
 // CTAs of a pair multiply by one W tile).
 bool use_pairs(const GemmArgs& g, int bn) {
-  if (bn != 256 || g.M < 1024) return false;
+  (void)bn;
+  if (g.M < 1024) return false;
   if (g.group_split >= g.M || g.shared_weights || g.row_groups) return true;
   return g.group_split % 256 == 0;
 }
@@ -247,15 +264,14 @@ int linear_split(const nd_linear_args& a, cudaStream_t stream) {
   g.status = device_status();
   if (!g.status) return fail(ND_ERR_CUDA, "linear: no device status word");
 
-  const int sms = sm_count();
   const int64_t n_all = g.N;
-  const int64_t tiles256 = ((a.rows + 127) / 128) * ((n_all + 255) / 256);
-  const int bn = (qk || (n_all >= 256 && tiles256 >= sms)) ? 256 : 128;
+  const int bn = pick_bn(a.rows, n_all, qk);
   if (use_pairs(g, bn)) {
     g.idesc = make_idesc_f16(256, bn, true);
     rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, K2, K2, bn / 2, 64, true);
     if (rc) return rc;
-    return launch_gemm2<256, 6>(ta, tb, tc, g, stream);
+    if (bn == 256) return launch_gemm2<256, 6>(ta, tb, tc, g, stream);
+    return launch_gemm2<128, 8>(ta, tb, tc, g, stream);
   }
   g.idesc = make_idesc_f16(128, bn, true);
   rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, K2, K2, swiglu ? bn / 2 : bn, 64, true);
@@ -377,16 +393,12 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
     g.w8_scale_f16 = a.scale_dtype == ND_F16;
   }
 
-  // Tile width: 256 unless the grid of 256-wide tiles leaves most SMs idle
-  // (narrow outputs, few rows); then 128. (A 192-wide variant filled the last
-  // wave better at N = 3072 but measured slower per tile on B200.)
-  const int sms = sm_count();
+  // Tile width: pick_bn.
   const int64_t n_all = g.N;
-  const int64_t tiles256 = ((a.rows + 127) / 128) * ((n_all + 255) / 256);
-  const int bn = (epi == ND_EPI_QK_NORM_ROPE || (n_all >= 256 && tiles256 >= sms)) ? 256 : 128;
+  const int bn = pick_bn(a.rows, n_all, epi == ND_EPI_QK_NORM_ROPE);
   g.idesc = make_idesc_f16(128, bn, a.dtype == ND_BF16);
   if (w8) {
-    if (use_pairs(g, bn)) {
+    if (bn == 256 && use_pairs(g, bn)) {
       // Each CTA of a pair loads and widens [bn / 2 rows x 64 bytes].
       g.idesc = make_idesc_f16(256, bn, a.dtype == ND_BF16);
       rc = make_tmap_2d_typed(&tb, a.weight, ND_I8, groups * n_all, a.in_features, a.in_features, bn / 2, 64, 0);
@@ -404,7 +416,8 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
     g.idesc = make_idesc_f16(256, bn, a.dtype == ND_BF16);
     rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, a.in_features, a.in_features, bn / 2, 64, true);
     if (rc) return rc;
-    return launch_gemm2<256, 6>(ta, tb, tc, g, stream);
+    if (bn == 256) return launch_gemm2<256, 6>(ta, tb, tc, g, stream);
+    return launch_gemm2<128, 8>(ta, tb, tc, g, stream);
   }
   rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, a.in_features, a.in_features, swiglu ? bn / 2 : bn, 64,
                     true);
@@ -484,10 +497,8 @@ int conv2d(const nd_conv_args& c, cudaStream_t stream) {
   g.head_dim = 128;
   g.status = device_status();
   if (!g.status) return fail(ND_ERR_CUDA, "conv2d: no device status word");
-  const int sms = sm_count();
-  const int64_t tiles256 = ((M + 127) / 128) * ((c.out_channels + 255) / 256);
-  const int bn = (c.out_channels >= 256 && tiles256 >= sms) ? 256 : 128;
-  if (use_pairs(g, bn)) {
+  const int bn = pick_bn(M, c.out_channels, false, false);
+  if (bn == 256 && use_pairs(g, bn)) {  // (128-wide conv tiles stay on single CTAs, as measured)
     g.idesc = make_idesc_f16(256, bn, c.dtype == ND_BF16);
     rc = make_tmap_2d(&tb, c.weight, 2, c.out_channels, K, K, bn / 2, 64, true);
     if (rc) return rc;

@@ -1,5 +1,5 @@
-"""The two-SM GEMM (clusters of two CTAs sharing 256 x 256 tiles, the path
-nd_op_linear / nd_op_conv2d take for 256-wide tiles over >= 1024 rows)
+"""The two-SM GEMM (clusters of two CTAs sharing 256 x 256 or 256 x 128
+tiles, the path nd_op_linear / nd_op_conv2d take over >= 1024 rows)
 against a torch fp32 reference of the same op, at the shapes where the pair
 logic has edges: the smallest paired row count, a row tail that leaves the
 second CTA of the last pair without rows, both weight groups' boundaries
@@ -36,7 +36,8 @@ def _data(m, n, k, dtype, seed=0, groups=1):
     return x.cuda(), w.cuda(), b.cuda()
 
 
-@pytest.mark.parametrize("m,n,k", [(1024, 256, 64), (1100, 768, 1024), (2048, 3072, 3072), (1536, 2304, 128)])
+@pytest.mark.parametrize("m,n,k", [(1024, 256, 64), (1100, 768, 1024), (2048, 3072, 3072), (1536, 2304, 128),
+                                   (2048, 640, 640), (1536, 1920, 640), (1024, 320, 320), (8192, 640, 1280)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_pair_store(cuda, m, n, k, dtype):
     from naivediffusion_b200 import ops
@@ -76,9 +77,10 @@ def test_pair_residual_gate_and_add(cuda):
     assert _rel(r - r0, ref) < 5e-3
 
 
-def test_pair_swiglu(cuda):
+@pytest.mark.parametrize("f", [1024, 640], ids=["256-wide", "128-wide"])
+def test_pair_swiglu(cuda, f):
     from naivediffusion_b200 import ops, _lib
-    m, f, k = 2048, 1024, 512
+    m, k = 2048, 512
     x, w, b = _data(m, 2 * f, k, torch.bfloat16, seed=7)
     y = ops.linear(x, w, b, epilogue=_lib.ND_EPI_SWIGLU)
     ops.sync()
@@ -114,11 +116,16 @@ def test_pair_qk_norm_rope_two_groups(cuda):
 
 
 def test_pair_conv3x3(cuda):
-    """A 320-channel SDXL level-0 convolution at 128 x 128, batch 2 (256-wide
-    tiles over 32768 output pixels: the pair path), against the oracle."""
+    """A 320-channel SDXL level-0 convolution at 128 x 128, batch 2 (32768
+    output pixels on CTA pairs with 256-wide tiles) and a 640-channel level-1
+    one, against the oracle."""
+    for b_, h, w_, cin, cout in ((2, 128, 128, 64, 320), (2, 64, 64, 128, 640)):
+        _conv_case(b_, h, w_, cin, cout)
+
+
+def _conv_case(b_, h, w_, cin, cout):
     from naivediffusion_b200 import ops
-    g = torch.Generator().manual_seed(9)
-    b_, h, w_, cin, cout = 2, 128, 128, 64, 320
+    g = torch.Generator().manual_seed(9 + cout)
     x = torch.randn(b_, h, w_, cin, generator=g).half()
     wt = (torch.randn(cout, cin, 3, 3, generator=g) * (1.0 / (3 * cin ** 0.5))).half()
     bias = torch.randn(cout, generator=g) * 0.1
