@@ -5,6 +5,7 @@ import ctypes as C
 import re
 from pathlib import Path
 
+import numpy as np
 import pytest
 
 from naivediffusion_b200 import _lib
@@ -81,6 +82,28 @@ def test_cfg3_algorithmic_flops():
     # 99.9 TFLOP per step: GEMMs 76.5 + joint attention 23.4 (+ embeddings).
     f = D.MMDiTConfig().flops_per_step()
     assert 99.8e12 < f < 100.1e12
+
+
+def test_cfg5_algorithmic_flops():
+    # 13.52 TFLOP per SDXL UNet step at batch 2: convolutions, the 70
+    # transformer blocks' GEMMs and attention, the time / add embeddings.
+    f = D.UNetConfig().flops_per_step()
+    assert 13.50e12 < f < 13.54e12
+    # linear in the batch; a one-block sample is a small fraction of the step
+    assert abs(D.UNetConfig(batch=1).flops_per_step() * 2 - f) < 1e6
+    one = D.UNetConfig(depth=(0, 1, 1), batch=1)
+    sample = one.resblock_flops(320, 320, 128 * 128) + one.transformer2d_flops(640, 64 * 64, 1)
+    assert 50 < f / sample < 100
+
+
+def test_synthetic_weights_prefix_filter_draws_the_same_values():
+    cfg = D.UNetConfig(width=64, depth=(0, 1, 1), latent_height=16, latent_width=16, context_width=128,
+                       add_width=256, time_width=64)
+    full = dict(D.synthetic_weights(cfg, seed=3))
+    part = dict(D.synthetic_weights(cfg, seed=3, only=("down_blocks.1.attentions.0.", "conv_in.")))
+    assert part and set(part) == {k for k in full if k.startswith(("down_blocks.1.attentions.0.", "conv_in."))}
+    for k, v in part.items():
+        np.testing.assert_array_equal(v, full[k])
 
 
 def test_device_open_fails_cleanly_without_gpu():
