@@ -22,8 +22,8 @@ import torch
 
 import oracle as O
 from naivediffusion_b200 import _lib
-from naivediffusion_b200.denoiser import (AnimaConfig, CudaDenoiser, Device, MMDiTConfig, UNetConfig,
-                                          build_denoiser, synthetic_weights)
+from naivediffusion_b200.denoiser import (AnimaConfig, CudaDenoiser, Device, MMDiTConfig, QwenImageConfig,
+                                          UNetConfig, build_denoiser, synthetic_weights)
 
 pytestmark = pytest.mark.gpu
 
@@ -177,3 +177,27 @@ def test_cfg5_unet_full_width(device):
     with build_denoiser(device, cfg, w) as d:
         y = d.predict(lat, 481.0, 0.0, {"context": ctx, "add": add})
     check(y, O.unet_forward(w, cfg, lat, 481.0, add, ctx), "cfg5 UNet")
+
+
+# ------------------------------------------------------- Qwen-Image 2.1 (f3)
+
+def test_qwen_image_block_full_width(device):
+    """One block of the reference's own Qwen-Image 2.1 single-stream DiT at its
+    released shape (4096 wide, 32 x 128 heads, SwiGLU 12288, 64-channel
+    latent at patch 1: 4096 image rows + 256 text rows, 4096-wide text
+    states), fp16 compute, with 40 real text rows under the causal text table
+    and the key count, against the oracle's composition of the reference's
+    step (which turns adjacent feature pairs on the file's weight order)."""
+    cfg = QwenImageConfig(blocks=1)
+    w = dict(synthetic_weights(cfg, seed=4))
+    rng = np.random.default_rng(4)
+    real = 40
+    lat = rng.standard_normal((1, cfg.latent_channels, cfg.latent_height, cfg.latent_width)).astype(np.float32)
+    ctx = np.zeros((1, cfg.context_rows, cfg.context_width), np.float32)
+    ctx[0, :real] = rng.standard_normal((real, cfg.context_width))
+    n_img = cfg.latent_height * cfg.latent_width
+    cond = {"context": ctx, "key_length": np.array([n_img + real], np.int32),
+            "text_mask": O.causal_table(real, cfg.context_rows)}
+    with build_denoiser(device, cfg, w) as d:
+        y = d.predict(lat, 0.0, 0.7, cond)
+    check(y, O.qwen_image_forward(w, cfg, lat, ctx[0], 0.7, key_len=n_img + real), "Qwen-Image 2.1 block")
