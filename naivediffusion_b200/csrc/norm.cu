@@ -115,17 +115,21 @@ __global__ void __launch_bounds__(256) modulate_kernel(const float* __restrict__
 // next GEMM), as a persistent loop: each block keeps one pair of rows (128
 // threads per row) in registers while the next pair's loads are already in
 // flight, so the grid is one wave of resident blocks with no tail and no
-// block launches per row pair. Same arithmetic as modulate_kernel: the mean,
-// then the centred second moment over the registers, then
-// (x - mean) * rstd * (1 + scale) + shift. The two block-wide reductions of
-// an iteration use a parity-indexed slot so the next iteration's writes
-// never race this one's reads.
+// block launches per row pair. A thread covers the same columns of every
+// row, so it keeps its columns of (1 + scale) and shift in registers (loaded
+// again only when a row's vector group differs from its previous row's), and
+// the arithmetic runs as paired f32x2 operations: inside the power-capped DiT
+// step the kernel is bound by instruction issue, not bytes. The statistics
+// are those of modulate_kernel (the mean, then the centred second moment over
+// the registers); the output is (x - mean) * (rstd * (1 + scale)) + shift.
+// The two block-wide reductions of an iteration use a parity-indexed slot so
+// the next iteration's writes never race this one's reads.
 template <int V, int F16OUT>
-__global__ void __launch_bounds__(256) modulate16_kernel(const float* __restrict__ x, long long ldx,
-                                                         uint16_t* __restrict__ y, long long ldy, int rows,
-                                                         int width, const float* __restrict__ shift,
-                                                         const float* __restrict__ scale, int vec_stride,
-                                                         int split, float eps, int affine) {
+__global__ void __launch_bounds__(256, V <= 6 ? 2 : 1) modulate16_kernel(const float* __restrict__ x, long long ldx,
+                                                            uint16_t* __restrict__ y, long long ldy, int rows,
+                                                            int width, const float* __restrict__ shift,
+                                                            const float* __restrict__ scale, int vec_stride,
+                                                            int split, float eps, int affine) {
   griddep_launch();
   griddep_wait();
   __shared__ float red[2][2][2][4];  // [parity][row of the pair][mean / second moment][warp]
@@ -144,6 +148,24 @@ __global__ void __launch_bounds__(256) modulate16_kernel(const float* __restrict
       v[i] = (row < rows && c < w4) ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
+  float4 k1[V], sb[V];  // this thread's columns of (1 + scale) and shift for vector group cur_g
+  int cur_g = -1;
+  auto load_vecs = [&](int g) {
+    const float4* sc = reinterpret_cast<const float4*>(scale + g * vec_stride);
+    const float4* sh = shift ? reinterpret_cast<const float4*>(shift + g * vec_stride) : nullptr;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = t + 128 * i;
+      float4 k = make_float4(0.f, 0.f, 0.f, 0.f), bb = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < w4) {
+        k = __ldg(sc + c);
+        if (sh) bb = __ldg(sh + c);
+      }
+      k1[i] = make_float4(one + k.x, one + k.y, one + k.z, one + k.w);
+      sb[i] = bb;
+    }
+    cur_g = g;
+  };
   float4 v[V], nv[V];
   int pair = blockIdx.x;
   if (pair < pairs) load_row(2 * pair + half, v);
@@ -152,42 +174,47 @@ __global__ void __launch_bounds__(256) modulate16_kernel(const float* __restrict
     if (next < pairs) load_row(2 * next + half, nv);
     const int row = 2 * pair + half;
     const int par = it & 1;
-    float s = 0.f;
+    float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < V; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-    s = warp_sum(s);
+    for (int i = 0; i < V; ++i) {
+      s2 = fadd2(s2, make_float2(v[i].x, v[i].y));
+      s2 = fadd2(s2, make_float2(v[i].z, v[i].w));
+    }
+    float s = warp_sum(s2.x + s2.y);
     if (lane == 0) red[par][half][0][w] = s;
     __syncthreads();
     const float mean = (red[par][half][0][0] + red[par][half][0][1] + red[par][half][0][2] + red[par][half][0][3]) / width;
-    float q = 0.f;
+    const float2 nm2 = make_float2(-mean, -mean);
+    float2 q2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       if (t + 128 * i < w4) {
-        const float a = v[i].x - mean, b = v[i].y - mean, cc = v[i].z - mean, d = v[i].w - mean;
-        q += (a * a + b * b) + (cc * cc + d * d);
+        const float2 d0 = fadd2(make_float2(v[i].x, v[i].y), nm2);
+        const float2 d1 = fadd2(make_float2(v[i].z, v[i].w), nm2);
+        q2 = ffma2(d0, d0, q2);
+        q2 = ffma2(d1, d1, q2);
       }
     }
-    q = warp_sum(q);
+    const float q = warp_sum(q2.x + q2.y);
     if (lane == 0) red[par][half][1][w] = q;
     __syncthreads();
     if (row < rows) {
       const float var = (red[par][half][1][0] + red[par][half][1][1] + red[par][half][1][2] + red[par][half][1][3]) / width;
       const float rstd = rsqrtf(var + eps);
       const int g = row >= split ? 1 : 0;
-      const float4* sc = reinterpret_cast<const float4*>(scale + g * vec_stride);
-      const float4* sh = shift ? reinterpret_cast<const float4*>(shift + g * vec_stride) : nullptr;
+      if (g != cur_g) load_vecs(g);
+      const float2 rs2 = make_float2(rstd, rstd);
       uint2* yr = reinterpret_cast<uint2*>(y + static_cast<long long>(row) * ldy);
 #pragma unroll
       for (int i = 0; i < V; ++i) {
         const int c = t + 128 * i;
         if (c < w4) {
-          const float4 k = __ldg(sc + c);
-          const float4 b = sh ? __ldg(sh + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-          const float ox = (v[i].x - mean) * rstd * (one + k.x) + b.x;
-          const float oy = (v[i].y - mean) * rstd * (one + k.y) + b.y;
-          const float oz = (v[i].z - mean) * rstd * (one + k.z) + b.z;
-          const float ow = (v[i].w - mean) * rstd * (one + k.w) + b.w;
-          yr[c] = F16OUT ? make_uint2(pack_f16(ox, oy), pack_f16(oz, ow)) : make_uint2(pack_bf16(ox, oy), pack_bf16(oz, ow));
+          const float2 o0 = ffma2(fadd2(make_float2(v[i].x, v[i].y), nm2), fmul2(make_float2(k1[i].x, k1[i].y), rs2),
+                                  make_float2(sb[i].x, sb[i].y));
+          const float2 o1 = ffma2(fadd2(make_float2(v[i].z, v[i].w), nm2), fmul2(make_float2(k1[i].z, k1[i].w), rs2),
+                                  make_float2(sb[i].z, sb[i].w));
+          yr[c] = F16OUT ? make_uint2(pack_f16(o0.x, o0.y), pack_f16(o1.x, o1.y))
+                         : make_uint2(pack_bf16(o0.x, o0.y), pack_bf16(o1.x, o1.y));
         }
       }
     }
