@@ -398,9 +398,22 @@ typedef struct nd_attention_args {
                            h / (heads / kv_heads) (CpuMath.Attention,
                            Tensors/CpuMath.cs:196-248); k and v are then
                            [rows, kv_heads * head_dim] */
+  void* workspace;      /* NULL, or nd_attention_workspace_bytes(head_dim) bytes,
+                           zero-filled once before first use (the kernel leaves
+                           it zeroed). With it, when the (query-tile pair x head
+                           x batch) units do not fill the last wave of SMs, the
+                           16-bit non-causal kernel splits the last wave's units
+                           along the keys and merges the pieces in a fixed order
+                           (bit-identical from run to run). One workspace per
+                           stream: launches that share one must be ordered. */
+  int64_t workspace_bytes;
 } nd_attention_args;
 
 ND_API int nd_op_attention(const nd_attention_args* args, void* stream);
+
+/* Bytes of the workspace above for head_dim 64 or 128 on the current device
+ * (0 for other head dims). */
+ND_API int64_t nd_attention_workspace_bytes(int head_dim);
 
 /* ------------------------------------------------------------ norms
  * adaLN modulation: y = LayerNorm(x, no affine) * (1 + scale) + shift

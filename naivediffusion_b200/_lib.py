@@ -82,6 +82,7 @@ class AttentionArgs(C.Structure):
         ("q", C.c_void_p), ("ldq", C.c_int64), ("k", C.c_void_p), ("ldk", C.c_int64),
         ("v", C.c_void_p), ("ldv", C.c_int64), ("out", C.c_void_p), ("ldo", C.c_int64),
         ("scale", C.c_float), ("out_dtype", C.c_int), ("kv_heads", C.c_int),
+        ("workspace", C.c_void_p), ("workspace_bytes", C.c_int64),
     ]
 
 
@@ -150,6 +151,8 @@ def lib() -> C.CDLL:
         L.nd_op_geglu.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int64, C.c_void_p]
         L.nd_op_conv2d.argtypes = [C.POINTER(ConvArgs), C.c_void_p]
         L.nd_op_attention.argtypes = [C.POINTER(AttentionArgs), C.c_void_p]
+        L.nd_attention_workspace_bytes.argtypes = [C.c_int]
+        L.nd_attention_workspace_bytes.restype = C.c_int64
         L.nd_op_sampler_step.argtypes = [C.POINTER(SamplerArgs), C.c_void_p]
         L.nd_op_modulate.argtypes = [C.POINTER(ModulateArgs), C.c_void_p]
         L.nd_op_rmsnorm.argtypes = [C.POINTER(RmsNormArgs), C.c_void_p]

@@ -179,6 +179,7 @@ struct Anima final : nd_denoiser {
     hid = S(static_cast<size_t>(M) * F * e * pw);
     tok_in = S(static_cast<size_t>(M) * cin * e * pw);
     tsin = static_cast<float*>(pinned(static_cast<size_t>(D) * 4));
+    if (desc.compute != ND_F32) alloc_attn_workspace(128);
     if (alloc_failed) return fail(ND_ERR_OOM, "anima: device allocation failed");
     ND_CUDA(cudaEventCreateWithFlags(&staged, cudaEventDisableTiming));
 
@@ -366,6 +367,7 @@ struct Anima final : nd_denoiser {
     a.ldv = ldkv;
     a.out = attn;
     a.ldo = static_cast<int64_t>(D) * pw;
+    use_attn_workspace(a);
     return attention(a, s);
   }
 

@@ -1,4 +1,5 @@
 // Host side of the tcgen05 flash-attention kernel (attention_sm100.cuh).
+#include <algorithm>
 #include <climits>
 #include <cmath>
 
@@ -7,6 +8,94 @@
 #include "nd_runtime.h"
 
 namespace nd {
+
+namespace {
+
+constexpr int64_t kAttnCounterBytes = 16384;  // one unsigned per split unit (at most 4096)
+
+int64_t attn_piece_bytes(int hd) { return 256 * (8 + 4 * static_cast<int64_t>(hd)); }
+
+// Sets the kernel's shared-memory limit and checks its register split, once
+// per device.
+template <int HD, bool SPLIT>
+int configure_attention() {
+  static bool configured[64] = {};
+  int dev = 0;
+  ND_CUDA(cudaGetDevice(&dev));
+  if (!configured[dev & 63]) {
+    auto kernel = attention_sm100_kernel<HD, SPLIT>;
+    int rc = check_register_split(reinterpret_cast<const void*>(kernel), kAttnThreads, kAttnRegsNeeded, "attention");
+    if (rc) return rc;
+    ND_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem<HD>::kLaunchBytes));
+    configured[dev & 63] = true;
+  }
+  return ND_OK;
+}
+
+template <int HD, bool SPLIT>
+int launch_attention(dim3 grid, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                     const AttnArgs& g, cudaStream_t stream) {
+  int rc = configure_attention<HD, SPLIT>();
+  if (rc) return rc;
+  ND_CUDA(launch_pdl(attention_sm100_kernel<HD, SPLIT>, grid, dim3(kAttnThreads), AttnSmem<HD>::kLaunchBytes, stream,
+                     tq, tk, tv, g));
+  ND_CUDA(cudaGetLastError());
+  return ND_OK;
+}
+
+// CTAs of the attention kernel resident at once on this device (one per SM:
+// 512 TMEM columns and the 384 x 168 register file each); 0 if unknown.
+template <int HD>
+int attn_slots() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  int& c = cached[dev & 63];
+  if (!c) {
+    if (configure_attention<HD, true>()) return 0;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attention_sm100_kernel<HD, true>, kAttnThreads,
+                                                      AttnSmem<HD>::kLaunchBytes) != cudaSuccess || per_sm <= 0)
+      return 0;
+    c = per_sm * sm_count();
+  }
+  return c;
+}
+
+// The split of the units past the last whole wave: each of the T tail units
+// runs as s CTAs over a 1/s share of the keys, so the tail takes
+// ceil(T s / slots) rounds of (n_kv / s + fixed) key-tile times instead of
+// one round of (n_kv + fixed). The fixed costs (Q load, pipeline fill and
+// drain; for pieces also the partial write and the merge) are counted in
+// key tiles. Returns 1 (no split) unless the model gains 10 %, and for tails
+// of more than half a wave: there the model's gain did not show (cfg3's
+// 84-unit tail of 148: 1.00x measured for a predicted 1.03x), while the
+// split kernel's extra registers cost its whole units ~3 %.
+int choose_split(int64_t units, int slots, int n_kv, int64_t max_pieces) {
+  if (slots <= 0) return 1;
+  const int64_t tail = units % slots;
+  if (tail == 0 || 2 * tail > slots) return 1;
+  const double fixed = 1.5, merge = 1.0;
+  const double base = n_kv + fixed;
+  int best = 1;
+  double best_cost = base;
+  for (int s = 2; s <= kAttnMaxSplit && 2 * s <= n_kv && tail * s <= max_pieces; ++s) {
+    const double rounds = static_cast<double>((tail * s + slots - 1) / slots);
+    const double cost = rounds * (static_cast<double>(n_kv) / s + fixed + merge);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best_cost < 0.9 * base ? best : 1;
+}
+
+}  // namespace
+
+int64_t attention_workspace_bytes(int hd) {
+  if (hd != 64 && hd != 128) return 0;
+  return kAttnCounterBytes + 2LL * sm_count() * attn_piece_bytes(hd);
+}
 
 int attention(const nd_attention_args& a, cudaStream_t stream) {
   if (a.dtype == ND_F32) return attention_f32(a, stream);
@@ -54,35 +143,40 @@ int attention(const nd_attention_args& a, cudaStream_t stream) {
   g.status = device_status();
   if (!g.status) return fail(ND_ERR_CUDA, "attention: no device status word");
 
-  dim3 grid(static_cast<unsigned>((a.q_rows + 255) / 256), static_cast<unsigned>(a.heads),
-            static_cast<unsigned>(a.batch));
-  int dev = 0;
-  ND_CUDA(cudaGetDevice(&dev));
-  if (hd == 128) {
-    static bool configured[64] = {};
-    if (!configured[dev & 63]) {
-      int rc = check_register_split(reinterpret_cast<const void*>(attention_sm100_kernel<128>), kAttnThreads,
-                                    kAttnRegsNeeded, "attention");
-      if (rc) return rc;
-      ND_CUDA(cudaFuncSetAttribute(attention_sm100_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   AttnSmem<128>::kLaunchBytes));
-      configured[dev & 63] = true;
+  const int64_t q_pairs = (a.q_rows + 255) / 256;
+  const int64_t units = q_pairs * a.heads * a.batch;
+  if (units > INT_MAX / 2) return fail(ND_ERR_INVALID, "attention: too many query tiles x heads x batch");
+  g.q_pairs = static_cast<int>(q_pairs);
+  g.heads = a.heads;
+  g.full_units = static_cast<int>(units);
+  g.split = 1;
+  int64_t ctas = units;
+  if (a.workspace && !a.causal) {
+    if (reinterpret_cast<uintptr_t>(a.workspace) & 15u)
+      return fail(ND_ERR_INVALID, "attention: workspace must be 16-byte aligned");
+    const int64_t max_pieces = (a.workspace_bytes - kAttnCounterBytes) / attn_piece_bytes(hd);
+    const int slots = hd == 128 ? attn_slots<128>() : attn_slots<64>();
+    const int n_kv = static_cast<int>((limit + 127) / 128);
+    const int split = max_pieces > 0 && slots > 0 ? choose_split(units, slots, n_kv, max_pieces) : 1;
+    const int64_t tail = slots > 0 ? units % slots : 0;
+    if (split > 1 && tail <= kAttnCounterBytes / 4) {
+      g.full_units = static_cast<int>(units - tail);
+      g.split = split;
+      ctas = g.full_units + tail * split;
+      uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+      g.counters = reinterpret_cast<unsigned*>(ws);
+      g.part_ml = reinterpret_cast<float2*>(ws + kAttnCounterBytes);
+      g.part_o = reinterpret_cast<float*>(ws + kAttnCounterBytes + max_pieces * 256 * 8);
     }
-    ND_CUDA(launch_pdl(attention_sm100_kernel<128>, grid, dim3(kAttnThreads), AttnSmem<128>::kLaunchBytes, stream, tq, tk, tv, g));
-  } else {
-    static bool configured[64] = {};
-    if (!configured[dev & 63]) {
-      int rc = check_register_split(reinterpret_cast<const void*>(attention_sm100_kernel<64>), kAttnThreads,
-                                    kAttnRegsNeeded, "attention");
-      if (rc) return rc;
-      ND_CUDA(cudaFuncSetAttribute(attention_sm100_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   AttnSmem<64>::kLaunchBytes));
-      configured[dev & 63] = true;
-    }
-    ND_CUDA(launch_pdl(attention_sm100_kernel<64>, grid, dim3(kAttnThreads), AttnSmem<64>::kLaunchBytes, stream, tq, tk, tv, g));
   }
-  ND_CUDA(cudaGetLastError());
-  return ND_OK;
+  if (g.split > 1) {
+    const dim3 grid(static_cast<unsigned>(ctas));
+    return hd == 128 ? launch_attention<128, true>(grid, tq, tk, tv, g, stream)
+                     : launch_attention<64, true>(grid, tq, tk, tv, g, stream);
+  }
+  const dim3 grid(static_cast<unsigned>(q_pairs), static_cast<unsigned>(a.heads), static_cast<unsigned>(a.batch));
+  return hd == 128 ? launch_attention<128, false>(grid, tq, tk, tv, g, stream)
+                   : launch_attention<64, false>(grid, tq, tk, tv, g, stream);
 }
 
 }  // namespace nd

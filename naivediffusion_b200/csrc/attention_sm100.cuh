@@ -41,7 +41,19 @@ struct AttnArgs {
   int out_f16;
   uint32_t idesc_s, idesc_pv, idesc_s64;
   unsigned* status;
+  // 1-D grid over units = query-tile pairs x heads x batch (pair fastest).
+  // Units [0, full_units) run whole, one CTA each; every later unit runs as
+  // `split` CTAs over consecutive key ranges, and the last of them to finish
+  // merges the pieces.
+  int q_pairs, heads;
+  int full_units, split;
+  float* part_o;      // [piece][tile][HD][128]: each piece's unnormalised O, row fastest
+  float2* part_ml;    // [piece][tile][128]: (running max in log2 units, row sum)
+  unsigned* counters; // [split unit]: pieces arrived (the merging piece resets it to 0)
 };
+
+// Largest split of one unit (the host never asks for more).
+constexpr int kAttnMaxSplit = 16;
 
 template <int HD>
 struct AttnSmem {
@@ -58,8 +70,7 @@ struct AttnSmem {
   static constexpr int kLaunchBytes = kTotal + 1024;
 };
 
-__device__ __forceinline__ void attn_store_row(void* out, long long ldo, long long row, int col,
-                                               const float (&v)[32], int f16) {
+__device__ __forceinline__ void attn_store_row(uint16_t* dst_row, int col, const float (&v)[32], int f16) {
   uint32_t p[16];
   if (f16) {
 #pragma unroll
@@ -68,7 +79,7 @@ __device__ __forceinline__ void attn_store_row(void* out, long long ldo, long lo
 #pragma unroll
     for (int i = 0; i < 16; ++i) p[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
   }
-  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + row * ldo + col);
+  uint4* dst = reinterpret_cast<uint4*>(dst_row + col);
 #pragma unroll
   for (int i = 0; i < 4; ++i) dst[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
 }
@@ -81,7 +92,10 @@ constexpr int kAttnRegsLow = 72;
 constexpr int kAttnRegsHigh = 216;
 constexpr int kAttnRegsNeeded = 128 * kAttnRegsLow + 256 * kAttnRegsHigh;
 
-template <int HD>
+// SPLIT: the 1-D grid of whole units and key-range pieces (AttnArgs::split);
+// otherwise a (query-tile pair, head, batch) grid of whole units, with none
+// of the pieces' code (it costs the d = 128 loop ~3 % in registers).
+template <int HD, bool SPLIT>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                            const __grid_constant__ CUtensorMap tmK,
@@ -113,15 +127,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
-  const int batch = blockIdx.z;
-  const int q_tile0 = blockIdx.x * 256;                      // within the batch item
+  int unit = 0, piece = 0, nsplit = 1, head, batch, q_tile0;  // q_tile0: within the batch item
+  if constexpr (SPLIT) {
+    unit = blockIdx.x;
+    if (unit >= a.full_units) {
+      nsplit = a.split;
+      piece = (unit - a.full_units) % nsplit;
+      unit = a.full_units + (unit - a.full_units) / nsplit;
+    }
+    head = (unit / a.q_pairs) % a.heads;
+    batch = unit / (a.q_pairs * a.heads);
+    q_tile0 = (unit % a.q_pairs) * 256;
+  } else {
+    head = blockIdx.y;
+    batch = blockIdx.z;
+    q_tile0 = blockIdx.x * 256;
+  }
   const long long q_row0 = static_cast<long long>(batch) * a.q_rows + q_tile0;
   const int kv_row0 = batch * a.kv_rows;
-  // Key tiles this CTA visits: all visible keys, or (causal) up to its last row.
+  // Key tiles this CTA visits: all visible keys, or (causal) up to its last
+  // row; a piece of a split unit takes its share [j_begin, j_begin + n_kv).
   int limit = a.key_limit;
   if (a.causal) limit = min(limit, q_tile0 + 256);
-  const int n_kv = (limit + 127) / 128;
+  const int n_all = (limit + 127) / 128;
+  const int j_begin = piece * n_all / nsplit;
+  const int n_kv = (piece + 1) * n_all / nsplit - j_begin;
+  // the piece's first key row, and the key limit counted from it (the roles
+  // below take these, so the piece offset is not one more live value)
+  const int kv_row_first = kv_row0 + j_begin * 128;
+  const int limit_rel = limit - j_begin * 128;
   const int col0 = head * HD;
   const int kv_col0 = (head / a.kv_group) * HD;
 
@@ -179,7 +213,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           ok = false;
           break;
         }
-        const int krow = kv_row0 + j * 128;
+        const int krow = kv_row_first + j * 128;
         mbar_arrive_expect_tx(k_full(st), L::kTile);
         for (int c = 0; c < L::kChunks; ++c)
           tma_load_2d(sbase + L::kK + st * L::kTile + c * 16384, &tmK, k_full(st),
@@ -315,10 +349,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int ew = warp & 3;        // TMEM lane quarter
     const int r = ew * 32 + lane;   // row within the tile
     const int q_in_batch = q_tile0 + t * 128 + r;
-    const long long q_row = q_row0 + t * 128 + r;
+    // this row's output (head columns included); null past the batch item's rows
+    uint16_t* const out_row = q_in_batch < a.q_rows
+        ? reinterpret_cast<uint16_t*>(a.out) + (q_row0 + t * 128 + r) * a.ldo + col0 : nullptr;
     const uint32_t lane_off = static_cast<uint32_t>(ew * 32) << 16;
     const uint32_t s_tm = tmem + lane_off + t * 128;
     const uint32_t o_tm = tmem + lane_off + 256 + t * HD;
+    // keys of this piece's block j visible to this row: vis_end - 128 j
+    // (the key count, and with causal the row's own position)
+    const int vis_end = a.causal ? min(limit, q_in_batch + 1) : limit_rel;  // causal launches are never split
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
@@ -338,8 +377,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (lane == 0) mbar_arrive(s_loaded(t));
       }
       // Masks: keys past the visible count (and past the end), causal.
-      int vis = limit - j * 128;
-      if (a.causal) vis = min(vis, q_in_batch + 1 - j * 128);
+      const int vis = vis_end - j * 128;
       if (vis < 128) {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -405,20 +443,88 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float rowsum = ((s4[0].x + s4[0].y) + (s4[1].x + s4[1].y)) + ((s4[2].x + s4[2].y) + (s4[3].x + s4[3].y));
       l = l * factor + rowsum;
     }
-    if (ok && n_kv > 0 && mbar_wait(o_full(t), 0, abort_flag, a.status, kStatusTimeoutEpilogue)) {
+    const bool have_o = ok && n_kv > 0 && mbar_wait(o_full(t), 0, abort_flag, a.status, kStatusTimeoutEpilogue);
+    if (have_o) {
       __syncwarp();
       tc_fence_after();
-      const float inv = 1.0f / l;
-      const bool row_ok = q_in_batch < a.q_rows;
+    }
+    // (the split position is re-derived from the block index and the
+    // arguments here rather than kept live through the softmax loop)
+    const int pidx = SPLIT ? static_cast<int>(blockIdx.x) - a.full_units : -1;
+    if (!SPLIT || pidx < 0) {
+      if (have_o) {
+        const float inv = 1.0f / l;
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(o_tm + c * 32, o);
-        tmem_ld_wait();
-        float v[32];
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_tm + c * 32, o);
+          tmem_ld_wait();
+          float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]) * inv;
-        if (row_ok) attn_store_row(a.out, a.ldo, q_row, col0 + c * 32, v, a.out_f16);
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]) * inv;
+          if (out_row) attn_store_row(out_row, c * 32, v, a.out_f16);
+        }
+      }
+    } else if constexpr (SPLIT) {
+      // A piece of a split unit: its unnormalised O and (m, l) go to the
+      // workspace (column-major per tile, so a warp's 32 rows are one
+      // 128-byte line per column), then it counts itself in. The last piece
+      // to arrive merges all of them in piece order.
+      const int ns = a.split;
+      if (have_o) {
+        float* po = a.part_o + (static_cast<size_t>(pidx) * 2 + t) * HD * 128 + r;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_tm + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) __stcg(po + (c * 32 + i) * 128, __uint_as_float(o[i]));
+        }
+        __stcg(&a.part_ml[(static_cast<size_t>(pidx) * 2 + t) * 128 + r], make_float2(m, l));
+      }
+      // Every piece arrives once, also after a timeout (its status is set and
+      // the merged rows are then not meaningful), so the count stays exact.
+      volatile int* is_last = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
+      __threadfence();
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      const unsigned split_unit = static_cast<unsigned>(pidx / ns);
+      if (threadIdx.x == 128) {
+        const unsigned prev = atomicAdd(&a.counters[split_unit], 1u);
+        const int last = prev == static_cast<unsigned>(ns - 1);
+        if (last) a.counters[split_unit] = 0u;  // every piece has counted: ready for the next launch
+        *is_last = last;
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (*is_last) {
+        __threadfence();
+        const int first = static_cast<int>(split_unit) * ns;
+        const float2* ml = a.part_ml + (static_cast<size_t>(first) * 2 + t) * 128 + r;
+        float mx = -INFINITY;
+        for (int i = 0; i < ns; ++i) mx = fmaxf(mx, __ldcg(ml + static_cast<size_t>(i) * 256).x);
+        float sum = 0.f;
+        for (int i = 0; i < ns; ++i) {
+          const float2 p = __ldcg(ml + static_cast<size_t>(i) * 256);
+          sum += fast_exp2(p.x - mx) * p.y;
+        }
+        const float inv = 1.0f / sum;
+        const float* po = a.part_o + (static_cast<size_t>(first) * 2 + t) * HD * 128 + r;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          float v[32];
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] = 0.f;
+#pragma unroll 1
+          for (int i = 0; i < ns; ++i) {
+            const float w = fast_exp2(__ldcg(ml + static_cast<size_t>(i) * 256).x - mx);
+            const float* src = po + static_cast<size_t>(i) * 2 * HD * 128 + c * 32 * 128;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) v[k] = fmaf(w, __ldcg(src + k * 128), v[k]);
+          }
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] *= inv;
+          if (out_row) attn_store_row(out_row, c * 32, v, a.out_f16);
+        }
       }
     }
   }

@@ -123,6 +123,18 @@ struct nd_denoiser {
   void* alloc(size_t bytes, bool weight);
   // Pinned host memory, freed with the denoiser (nullptr + alloc_failed on failure).
   void* pinned(size_t bytes);
+  // The attention workspace (zeroed by alloc; the kernel keeps it zeroed),
+  // shared by this denoiser's attention launches, which its one stream orders.
+  void* attn_ws = nullptr;
+  int64_t attn_ws_bytes = 0;
+  void alloc_attn_workspace(int head_dim) {
+    attn_ws_bytes = nd::attention_workspace_bytes(head_dim);
+    attn_ws = attn_ws_bytes > 0 ? alloc(static_cast<size_t>(attn_ws_bytes), false) : nullptr;
+  }
+  void use_attn_workspace(nd_attention_args& a) const {
+    a.workspace = attn_ws;
+    a.workspace_bytes = attn_ws ? attn_ws_bytes : 0;
+  }
   void add_slot(const std::string& name, int kind, int64_t rows, int64_t cols, void* dst,
                 bool required = true, void* scales = nullptr);
   // int8 storage of matrices (desc.weight_dtype == ND_I8): columns per scale

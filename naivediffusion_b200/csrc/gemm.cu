@@ -133,6 +133,27 @@ int pick_bn(int64_t rows, int64_t n, bool force256, bool pad_aware = true) {
   return (n + 255) / 256 * 256 > (n + 127) / 128 * 128 ? 128 : 256;
 }
 
+// Pair-tile width for the plain epilogues: 160 where 160-column tiles cut the
+// rounds of pair tiles enough to pay (the SDXL widths 320 / 640 / 1280, whose
+// 256-wide tiles pad or leave a near-empty last round and whose 128-wide ones
+// double the rounds). The cost of one 256 x bn pair tile per 64-deep k block,
+// per SM, is its MMA time (2 bn cycles) or, for narrow tiles, its operand
+// loads (128 A rows + bn / 2 W rows of 128 B at about 85 B per cycle); a
+// round of pair tiles is one per pair on the GPU. 160 must beat the width
+// `bn` by 15 %: a partial last round costs less than the model says (the
+// other SMs idle, the clock rises), which made 192-wide tiles at N = 3072
+// measure even where this model gives them 6 %.
+int pair_bn(int64_t rows, int64_t n, int bn) {
+  if (n < 160) return bn;
+  const int pairs = std::max(1, sm_count() / 2);
+  auto cost = [&](int w) {
+    const int64_t tiles = ((rows + 255) / 256) * ((n + w - 1) / w);
+    const double per = std::max(2.0 * w, (128.0 + w / 2) * 1.5);
+    return static_cast<double>((tiles + pairs - 1) / pairs) * per;
+  };
+  return cost(160) < 0.85 * cost(bn) ? 160 : bn;
+}
+
 // Whether a GEMM runs on CTA pairs (256 x bn tiles): enough rows for the 256-row
 // tiles to fill the GPU, and no pair straddling two weight groups (the two
 // CTAs of a pair multiply by one W tile).
@@ -413,10 +434,12 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
     return launch_gemm_w8<128, 6>(ta, tb, tc, g, stream);
   }
   if (use_pairs(g, bn)) {
-    g.idesc = make_idesc_f16(256, bn, a.dtype == ND_BF16);
-    rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, a.in_features, a.in_features, bn / 2, 64, true);
+    const int pbn = swiglu || epi == ND_EPI_QK_NORM_ROPE ? bn : pair_bn(a.rows, n_all, bn);
+    g.idesc = make_idesc_f16(256, pbn, a.dtype == ND_BF16);
+    rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, a.in_features, a.in_features, pbn / 2, 64, true);
     if (rc) return rc;
-    if (bn == 256) return launch_gemm2<256, 6>(ta, tb, tc, g, stream);
+    if (pbn == 256) return launch_gemm2<256, 6>(ta, tb, tc, g, stream);
+    if (pbn == 160) return launch_gemm2<160, 7>(ta, tb, tc, g, stream);
     return launch_gemm2<128, 8>(ta, tb, tc, g, stream);
   }
   rc = make_tmap_2d(&tb, a.weight, 2, groups * n_all, a.in_features, a.in_features, swiglu ? bn / 2 : bn, 64,
@@ -498,10 +521,14 @@ int conv2d(const nd_conv_args& c, cudaStream_t stream) {
   g.status = device_status();
   if (!g.status) return fail(ND_ERR_CUDA, "conv2d: no device status word");
   const int bn = pick_bn(M, c.out_channels, false, false);
-  if (bn == 256 && use_pairs(g, bn)) {  // (128-wide conv tiles stay on single CTAs, as measured)
-    g.idesc = make_idesc_f16(256, bn, c.dtype == ND_BF16);
-    rc = make_tmap_2d(&tb, c.weight, 2, c.out_channels, K, K, bn / 2, 64, true);
+  // Pairs with 256- or 160-wide tiles (128-wide conv tiles stay on single
+  // CTAs, as measured).
+  const int pbn = use_pairs(g, 256) ? pair_bn(M, c.out_channels, 256) : 0;
+  if (pbn == 160 || (pbn == 256 && bn == 256)) {
+    g.idesc = make_idesc_f16(256, pbn, c.dtype == ND_BF16);
+    rc = make_tmap_2d(&tb, c.weight, 2, c.out_channels, K, K, pbn / 2, 64, true);
     if (rc) return rc;
+    if (pbn == 160) return launch_gemm2<160, 7, true>(ta, tb, tc, g, stream);
     return launch_gemm2<256, 6, true>(ta, tb, tc, g, stream);
   }
   g.idesc = make_idesc_f16(128, bn, c.dtype == ND_BF16);

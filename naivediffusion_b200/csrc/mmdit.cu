@@ -191,6 +191,7 @@ struct MMDiT final : nd_denoiser {
     tok_in = S(static_cast<size_t>(n_img) * cin * esz() * pw);
     ctx_n = S(static_cast<size_t>(ctx) * cw * esz() * pw);
     tsin = static_cast<float*>(pinned(static_cast<size_t>(tw) * 4));
+    if (desc.compute != ND_F32) alloc_attn_workspace(128);
     if (alloc_failed) return fail(ND_ERR_OOM, "mmdit: device allocation failed");
     ND_CUDA(cudaEventCreateWithFlags(&staged, cudaEventDisableTiming));
 
@@ -448,6 +449,7 @@ struct MMDiT final : nd_denoiser {
       a.ldv = 3 * D;
       a.out = attn;
       a.ldo = static_cast<int64_t>(D) * pw;
+      use_attn_workspace(a);
       ND_OP("attention", 4.0 * M * keys * D, mD * 2 * 4, attention(a, s));
     }
     ND_OP("gemm.out", gemm_flops(M, D, D), gemm_bytes(M, 2.0 * D, D, mD * 8),

@@ -54,6 +54,8 @@ int dequantize(const int8_t* q, const void* scales, int scale_dtype, int64_t qua
 // count x threads covers `needed`.
 int check_register_split(const void* kernel, int threads, int needed, const char* what);
 int attention(const nd_attention_args& a, cudaStream_t stream);
+// Bytes of nd_attention_args::workspace for head_dim 64 / 128 (0 otherwise).
+int64_t attention_workspace_bytes(int head_dim);
 int attention_f32(const nd_attention_args& a, cudaStream_t stream);
 int sampler_step(const nd_sampler_args& a, cudaStream_t stream);
 int modulate(const nd_modulate_args& a, cudaStream_t stream);

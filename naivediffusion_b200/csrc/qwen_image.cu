@@ -174,6 +174,7 @@ struct QwenImage final : nd_denoiser {
     tok_in = S(static_cast<size_t>(n_img) * C * 2 * pw);
     ctx_n = S(static_cast<size_t>(R) * cw * 2 * pw);
     tsin = static_cast<float*>(pinned(static_cast<size_t>(2) * tw * 4));
+    if (desc.compute != ND_F32) alloc_attn_workspace(128);
     if (alloc_failed) return fail(ND_ERR_OOM, "qwen_image: device allocation failed");
     ND_CUDA(cudaEventCreateWithFlags(&staged, cudaEventDisableTiming));
 
@@ -410,6 +411,7 @@ struct QwenImage final : nd_denoiser {
     a.ldv = 3 * D;
     a.out = static_cast<uint8_t*>(attn) + q_row0 * static_cast<size_t>(D) * 2 * pw;
     a.ldo = static_cast<int64_t>(D) * pw;
+    use_attn_workspace(a);
     return attention(a, s);
   }
 

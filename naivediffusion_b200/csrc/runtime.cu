@@ -242,6 +242,8 @@ int nd_op_attention(const nd_attention_args* args, void* stream) {
   return nd::attention(*args, static_cast<cudaStream_t>(stream));
 }
 
+int64_t nd_attention_workspace_bytes(int head_dim) { return nd::attention_workspace_bytes(head_dim); }
+
 int nd_op_modulate(const nd_modulate_args* args, void* stream) {
   if (!args) return nd::fail(ND_ERR_INVALID, "nd_op_modulate: null args");
   return nd::modulate(*args, static_cast<cudaStream_t>(stream));

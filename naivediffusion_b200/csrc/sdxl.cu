@@ -389,6 +389,7 @@ struct Unet final : nd_denoiser {
       gsz = std::max(gsz, group_norm_scratch(B, level_h(l) * level_w(l), static_cast<int>(max_act / (static_cast<int64_t>(B) * level_h(l) * level_w(l))), kGroups));
     gn_scratch_bytes = gsz;
     gn_scratch = S(gsz);
+    if (desc.compute != ND_F32) alloc_attn_workspace(64);
     if (alloc_failed) return fail(ND_ERR_OOM, "sdxl: device allocation failed");
     ND_CUDA(cudaEventCreateWithFlags(&staged, cudaEventDisableTiming));
     return ND_OK;
@@ -597,6 +598,7 @@ struct Unet final : nd_denoiser {
     a.ldv = ldkv;
     a.out = ATT;
     a.ldo = static_cast<int64_t>(heads) * 64;
+    use_attn_workspace(a);
     return attention(a, s);
   }
 

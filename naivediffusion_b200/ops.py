@@ -148,13 +148,16 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *,
               out: torch.Tensor | None = None, batch: int = 1, key_limit: int = 0,
               causal: bool = False, scale: float = 0.0, head_dim: int = 128,
-              out_pairs: bool = False, kv_heads: int = 0) -> torch.Tensor:
+              out_pairs: bool = False, kv_heads: int = 0,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Flash attention over packed heads (Layers.Attend, Graph/Layers.cs:260-279).
 
     q: [batch * q_rows, >= heads*128] (row stride q.stride(0)); k, v likewise
     with kv_rows per item. Returns out [batch * q_rows, heads * 128].
     fp32 q/k/v run the fp32 attention; out_pairs then writes an ND_BF16X2 pair.
     kv_heads < heads: grouped-query attention (k, v [rows, kv_heads * head_dim]).
+    workspace: a zeroed uint8 tensor from attention_workspace(); with it the
+    last partial wave of query tiles is split along the keys.
     """
     q_rows = q.shape[0] // batch
     kv_rows = k.shape[0] // batch
@@ -177,8 +180,21 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *,
     a.out, a.ldo = out.data_ptr(), out.stride(0)
     a.scale = scale
     a.kv_heads = kv_heads
+    if workspace is not None:
+        if workspace.device != q.device or workspace.dtype != torch.uint8 or not workspace.is_contiguous():
+            raise ValueError("attention: workspace must be a contiguous uint8 tensor on q's device")
+        a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
     check(lib().nd_op_attention(C.byref(a), C.c_void_p(_stream())))
     return out
+
+
+def attention_workspace(head_dim: int = 128, device="cuda") -> torch.Tensor:
+    """A zeroed workspace for attention(..., workspace=) on `device` (one per
+    stream; the kernel leaves it zeroed)."""
+    n = int(lib().nd_attention_workspace_bytes(head_dim))
+    if n <= 0:
+        raise ValueError(f"attention_workspace: no workspace for head_dim {head_dim}")
+    return torch.zeros(n, dtype=torch.uint8, device=device)
 
 
 def modulate(x: torch.Tensor, shift: torch.Tensor | None, scale: torch.Tensor, *,

@@ -1,5 +1,5 @@
-"""The two-SM GEMM (clusters of two CTAs sharing 256 x 256 or 256 x 128
-tiles, the path nd_op_linear / nd_op_conv2d take over >= 1024 rows)
+"""The two-SM GEMM (clusters of two CTAs sharing 256 x 256, 256 x 160 or
+256 x 128 tiles, the path nd_op_linear / nd_op_conv2d take over >= 1024 rows)
 against a torch fp32 reference of the same op, at the shapes where the pair
 logic has edges: the smallest paired row count, a row tail that leaves the
 second CTA of the last pair without rows, both weight groups' boundaries
@@ -36,8 +36,11 @@ def _data(m, n, k, dtype, seed=0, groups=1):
     return x.cuda(), w.cuda(), b.cuda()
 
 
+# 160-wide pair tiles: (1536, 1920, 640), (8192, 640, 1280), (2048, 1280, 1280)
+# and (2048, 1200, 640), whose last 160-column tile is half empty.
 @pytest.mark.parametrize("m,n,k", [(1024, 256, 64), (1100, 768, 1024), (2048, 3072, 3072), (1536, 2304, 128),
-                                   (2048, 640, 640), (1536, 1920, 640), (1024, 320, 320), (8192, 640, 1280)])
+                                   (2048, 640, 640), (1536, 1920, 640), (1024, 320, 320), (8192, 640, 1280),
+                                   (2048, 1280, 1280), (2048, 1200, 640)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_pair_store(cuda, m, n, k, dtype):
     from naivediffusion_b200 import ops
@@ -60,9 +63,9 @@ def test_pair_row_groups(cuda, split):
     assert _rel(y, ref) < 2e-2 and _cos(y, ref) > 0.999
 
 
-def test_pair_residual_gate_and_add(cuda):
+@pytest.mark.parametrize("m,n,k", [(1280, 1536, 768), (2048, 1280, 5120)], ids=["128-wide", "160-wide"])
+def test_pair_residual_gate_and_add(cuda, m, n, k):
     from naivediffusion_b200 import ops, _lib
-    m, n, k = 1280, 1536, 768
     x, w, b = _data(m, n, k, torch.bfloat16, seed=6)
     ref = x.float() @ w.float().t() + b
     r0 = torch.randn(m, n, device="cuda")
@@ -117,9 +120,11 @@ def test_pair_qk_norm_rope_two_groups(cuda):
 
 def test_pair_conv3x3(cuda):
     """A 320-channel SDXL level-0 convolution at 128 x 128, batch 2 (32768
-    output pixels on CTA pairs with 256-wide tiles) and a 640-channel level-1
-    one, against the oracle."""
-    for b_, h, w_, cin, cout in ((2, 128, 128, 64, 320), (2, 64, 64, 128, 640)):
+    output pixels on CTA pairs with 160-wide tiles), a 640-channel level-1 one
+    and a 1280-channel level-2 one (160-wide), and a 1024-channel one that
+    keeps 256-wide pair tiles, against the oracle."""
+    for b_, h, w_, cin, cout in ((2, 128, 128, 64, 320), (2, 64, 64, 128, 640), (2, 32, 32, 128, 1280),
+                                 (2, 64, 64, 64, 1024)):
         _conv_case(b_, h, w_, cin, cout)
 
 
