@@ -647,9 +647,10 @@ def run_ours(args):
         traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
     kernel = "gemm2_sm100_kernel (tcgen05 CTA pairs; gemm_sm100_kernel for the small GEMMs; all GEMM launches of a step)"
     if args.config in ("cfg5", "vae", "wan21", "wan22"):
-        kernel = "gemm_sm100_kernel (tcgen05: conv3x3 implicit GEMMs and the linear layers)"
+        kernel = ("gemm2_sm100_kernel / gemm_sm100_kernel (tcgen05: conv3x3 implicit GEMMs and the linear layers; "
+                  "CTA pairs with 256- or 160-wide tiles over >= 1024 rows)")
     elif args.config == "cfg4":
-        kernel = "gemm_w8_sm100_kernel (tcgen05, int8 weights widened in the mainloop)"
+        kernel = "gemm2_w8_sm100_kernel (tcgen05 CTA pairs, int8 weights widened in the mainloop)"
     elif args.config == "cfg1":
         kernel = ("gemm_sm100_kernel on bf16 hi|lo pairs (3 MMA passes per logical product; "
                   "achieved counts the logical fp32 FLOPs)")
