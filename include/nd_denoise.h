@@ -473,8 +473,11 @@ ND_API int nd_op_gemv(const nd_gemv_args* args, void* stream);
  * (pixels, C/groups), then y = n * weight[c] + bias[c], optionally SiLU
  * (Layers.GroupNorm, src/NaiveDiffusion/Graph/Layers.cs:166-185, and the
  * ResBlocks' SiLU, Models/Sdxl/UNetModel.cs:230-254). x, y: [batch, pixels,
- * channels]; weight / bias may be NULL (1 / 0). Uses library-owned device scratch for its partial sums
- * (allocated on first use per device and grown when a larger shape needs it). */
+ * channels], batch <= 1024; weight / bias may be NULL (1 / 0). Uses
+ * library-owned device scratch for its partial sums (allocated zeroed on
+ * first use per device and grown when a larger shape needs it). Two
+ * launches: the partial sums (whose last block per image forms the group
+ * statistics) and the normalization. */
 ND_API int nd_op_group_norm(const void* x, void* y, int dtype, int batch, int pixels, int channels,
                             int groups, const float* weight, const float* bias, float eps,
                             int silu_after, void* stream);
@@ -485,12 +488,14 @@ ND_API int nd_op_group_norm(const void* x, void* y, int dtype, int batch, int pi
  * library, so it suits hosts that cannot let the library allocate: device
  * memory already fully committed (a serving pool, full weight residency), or
  * a pipeline that must not meet cudaFree's device-wide wait.
- *  - Limit: batch * ceil(pixels / 32) * groups * 8 (rounded up to 256)
- *    + batch * groups * 8 + 256 bytes must fit in 4 MiB (SDXL at 1024 x
- *    1024, batch 2: 0.26 MB; at 32 groups up to about 512 K pixels over the
- *    batch); larger shapes fail with ND_ERR_INVALID and launch nothing.
- *  - Nothing needs to start at zero: every partial sum and group statistic
- *    is written before it is read within the same call.
+ *  - Limit: 4096 + batch * ceil(pixels / 32) * groups * 8 (rounded up to
+ *    256) + batch * groups * 8 + 256 bytes must fit in 4 MiB (SDXL at 1024
+ *    x 1024, batch 2: 0.27 MB; at 32 groups up to about 512 K pixels over
+ *    the batch); larger shapes fail with ND_ERR_INVALID and launch nothing.
+ *  - The array's first 4 KB are one arrival counter per image (batch <=
+ *    1024): zero when the library loads, and every call leaves them zero
+ *    (the last block of each image resets its counter). Partial sums and
+ *    group statistics are written before they are read within a call.
  *  - The first call on each device looks up the array's address (with that
  *    device current); make that first call before any stream capture. The
  *    address stays valid for the life of the device's CUDA context: a process

@@ -19,10 +19,11 @@
 namespace nd {
 namespace {
 
-// Fixed scratch: batch x ceil(pixels / 32) x groups float pairs (8 bytes,
-// rounded up to 256) plus batch x groups float pairs plus 256 bytes of slack.
+// Fixed scratch: 4 KB of per-image arrival counters (zero at load; each call
+// leaves them zero), batch x ceil(pixels / 32) x groups float pairs (8 bytes,
+// rounded up to 256), batch x groups float pairs and 256 bytes of slack.
 // 4 MiB holds the SDXL UNet's GroupNorms at a 1024 x 1024 image and batch 2
-// (2 x 512 x 32 x 8 bytes = 0.26 MB) with room to spare.
+// (4 KB + 2 x 512 x 32 x 8 bytes = 0.27 MB) with room to spare.
 constexpr size_t kNoAllocScratchBytes = size_t{4} << 20;
 __device__ __align__(256) unsigned char g_gn_scratch[kNoAllocScratchBytes];
 

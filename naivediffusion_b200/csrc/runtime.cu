@@ -98,6 +98,11 @@ int op_scratch(size_t need, void** ptr, size_t* bytes) {
     g_op_scratch_bytes[dev & 63] = 0;
     void* p = nullptr;
     ND_CUDA(cudaMalloc(&p, need));
+    // zeroed: group_norm's arrival counters must start at zero
+    if (cudaMemset(p, 0, need) != cudaSuccess) {
+      cudaFree(p);
+      return fail(ND_ERR_CUDA, "op scratch: memset failed");
+    }
     g_op_scratch[dev & 63] = p;
     g_op_scratch_bytes[dev & 63] = need;
   }

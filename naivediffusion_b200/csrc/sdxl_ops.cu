@@ -3,8 +3,9 @@
 //
 // GroupNorm (Layers.GroupNorm, Graph/Layers.cs:166-185: mean-variance
 // normalization over (C/G, H, W) of each group, then the per-channel affine)
-// runs in three passes: per-chunk channel sums in fp64, per-group mean and
-// 1/sqrt(var + eps), then one vectorized pass applying it (fused with the SiLU
+// runs in two launches: per-block channel and group sums, whose last block per
+// image forms each group's mean and 1/sqrt(var + eps) in fp64, then one
+// vectorized pass applying it (fused with the SiLU
 // the ResBlocks put after it, UNetModel.ResnetBlock, Models/Sdxl/UNetModel.cs:230-254).
 #include <algorithm>
 #include <climits>
@@ -41,46 +42,46 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8], int f16) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// Per (image, chunk of pixels, group): sum and sum of squares.
-// Threads read 16-byte vectors (8 channels), consecutive threads on
-// consecutive vectors of a pixel row and several rows per pass, so every load
-// is coalesced; each thread sums its 8 channels in fp32, the block adds the
-// rows' sums per channel in shared memory and then each group's channels.
-// Small chunks give every SM blocks to run even at the UNet's smallest
-// levels; the per-group partials are combined in fp64 by gn_finalize_kernel.
-constexpr int kGnChunk = 32;
-constexpr int kGnMaxSlab = 2048;  // channels per block (static shared memory: 16 KB of channel sums)
+// Per (image, run of pixels): channel sums and sums of squares, then group
+// totals. One wave of blocks (about two per SM) each streams a long run of
+// pixels: threads read 16-byte vectors (8 channels), consecutive threads on
+// consecutive vectors of a pixel row and several rows per pass, eight loads
+// in flight, every load coalesced; each thread sums its 8 channels in fp32,
+// the block adds the pixel rows' sums per channel and then each group's
+// channels, in a fixed order. The last block of an image to write its
+// partials (one counter per image, reset by that block) adds them per group
+// in fp64 and writes the group's mean and 1/sqrt(var + eps).
+constexpr int kGnChunk = 32;           // fewest pixels per block (bounds the partials)
+constexpr int kGnMaxC = 3072;          // channels (shared memory: two sums per channel)
+constexpr int kGnCounterBytes = 4096;  // one arrival counter per image, at the start of the scratch
 
-// grid (pixel chunks, channel slabs, images): a slab is a run of whole groups
-// and whole 8-channel vectors, [slab * slab_c, ...) clipped to C.
-__global__ void __launch_bounds__(256) gn_partial_kernel(const void* __restrict__ x, int f16, int hw,
-                                                         int C, int G, int slab_c, int chunk,
-                                                         float2* __restrict__ part) {
+__global__ void __launch_bounds__(256) gn_stats_kernel(const void* __restrict__ x, int f16, int hw, int C, int G,
+                                                       int chunk, float2* __restrict__ part,
+                                                       unsigned* __restrict__ arrived, float eps,
+                                                       float2* __restrict__ stats) {
   griddep_launch();
   griddep_wait();
   __shared__ float red[256][17];
-  __shared__ float chs[2][kGnMaxSlab];
-  const int ck = blockIdx.x, b = blockIdx.z;
-  const int c_lo = blockIdx.y * slab_c, c_hi = min(C, c_lo + slab_c);
-  const int p0 = ck * chunk, p1 = min(hw, p0 + chunk);
-  const int nchunks = gridDim.x;
+  __shared__ float csum[2][kGnMaxC];
+  __shared__ int is_last;
+  const int blk = blockIdx.x, b = blockIdx.y, nblk = gridDim.x;
   const int c8 = C / 8;
-  const int v_lo = c_lo / 8, nv = (c_hi - c_lo) / 8;  // this slab's vectors
-  const int tpr = min(nv, 256);                        // threads per pixel row
-  const int rows = 256 / tpr;                          // pixel rows per pass
+  const int tpr = min(c8, 256);  // threads per pixel row
+  const int rows = 256 / tpr;    // pixel rows per pass
   const int t = threadIdx.x;
   const int pr = t / tpr;
+  const int p0 = blk * chunk, p1 = min(hw, p0 + chunk);
   const uint4* xv = reinterpret_cast<const uint4*>(x) + static_cast<long long>(b) * hw * c8;
-  for (int j0 = 0; j0 < nv; j0 += tpr) {
-    const int j = j0 + t % tpr;  // vector within the slab
+  for (int j0 = 0; j0 < c8; j0 += tpr) {  // (more than 2048 channels: vector runs of 256)
+    const int j = j0 + t % tpr;
     float s1[8], s2[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) s1[k] = s2[k] = 0.f;
-    if (pr < rows && j < nv) {
-#pragma unroll 4
+    if (pr < rows && j < c8) {
+#pragma unroll 8
       for (int p = p0 + pr; p < p1; p += rows) {
         float v[8];
-        unpack8(__ldg(xv + static_cast<long long>(p) * c8 + v_lo + j), f16, v);
+        unpack8(__ldg(xv + static_cast<long long>(p) * c8 + j), f16, v);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           s1[k] += v[k];
@@ -94,86 +95,67 @@ __global__ void __launch_bounds__(256) gn_partial_kernel(const void* __restrict_
       red[t][8 + k] = s2[k];
     }
     __syncthreads();
-    if (pr == 0 && j < nv) {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
+    for (int e = t; e < tpr * 8; e += 256) {  // e = vector of the run x 8 + channel
+      const int jj = e >> 3, k = e & 7;
+      if (j0 + jj < c8) {
         float a = 0.f, q = 0.f;
         for (int r = 0; r < rows; ++r) {
-          a += red[r * tpr + t][k];
-          q += red[r * tpr + t][8 + k];
+          a += red[r * tpr + jj][k];
+          q += red[r * tpr + jj][8 + k];
         }
-        chs[0][j * 8 + k] = a;
-        chs[1][j * 8 + k] = q;
+        csum[0][(j0 + jj) * 8 + k] = a;
+        csum[1][(j0 + jj) * 8 + k] = q;
       }
     }
     __syncthreads();
   }
   const int cg = C / G;
-  const int g_lo = c_lo / cg, g_hi = c_hi / cg;
-  for (int g = g_lo + t; g < g_hi; g += 256) {
+  for (int g = t; g < G; g += 256) {
     float a = 0.f, q = 0.f;
     for (int c = g * cg; c < (g + 1) * cg; ++c) {
-      a += chs[0][c - c_lo];
-      q += chs[1][c - c_lo];
+      a += csum[0][c];
+      q += csum[1][c];
     }
-    part[(static_cast<long long>(b) * nchunks + ck) * G + g] = make_float2(a, q);
+    part[(static_cast<long long>(b) * nblk + blk) * G + g] = make_float2(a, q);
   }
-}
-
-// Per (image, group): mean and 1/sqrt(var + eps) over hw x C/G values, the
-// chunks' partial sums added in fp64.
-__global__ void gn_finalize_kernel(const float2* __restrict__ part, int nchunks, int C, int G, int hw,
-                                   float eps, float2* __restrict__ stats) {
-  griddep_launch();
-  griddep_wait();
-  const int b = blockIdx.x / G, g = blockIdx.x % G;
-  __shared__ double red[2][8];
-  double s1 = 0.0, s2 = 0.0;
-#pragma unroll 4
-  for (int i = threadIdx.x; i < nchunks; i += blockDim.x) {
-    const float2 v = part[(static_cast<long long>(b) * nchunks + i) * G + g];
-    s1 += v.x;
-    s2 += v.y;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-  }
-  const int w = threadIdx.x >> 5;
-  if ((threadIdx.x & 31) == 0) {
-    red[0][w] = s1;
-    red[1][w] = s2;
+  __threadfence();
+  __syncthreads();
+  if (t == 0) {
+    const unsigned prev = atomicAdd(&arrived[b], 1u);
+    is_last = prev == static_cast<unsigned>(nblk - 1);
+    if (is_last) arrived[b] = 0u;  // every block of this image has counted
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    s1 = s2 = 0.0;
-    for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) {
-      s1 += red[0][k];
-      s2 += red[1][k];
+  if (!is_last) return;
+  __threadfence();
+  const double n = static_cast<double>(hw) * cg;
+  for (int g = t; g < G; g += 256) {
+    double s1 = 0.0, s2 = 0.0;
+    for (int i = 0; i < nblk; ++i) {
+      const float2 v = __ldcg(part + (static_cast<long long>(b) * nblk + i) * G + g);
+      s1 += v.x;
+      s2 += v.y;
     }
-    const double n = static_cast<double>(hw) * (C / G);
     const double mean = s1 / n;
     const double var = fmax(s2 / n - mean * mean, 0.0);
-    stats[blockIdx.x] = make_float2(static_cast<float>(mean), static_cast<float>(1.0 / sqrt(var + eps)));
+    stats[b * G + g] = make_float2(static_cast<float>(mean), static_cast<float>(1.0 / sqrt(var + eps)));
   }
 }
 
-// y = (x - mean_g) * rstd_g * w_c + b_c (then SiLU), one block per
-// (kGnApplyPixels pixels, image): each thread owns fixed 8-channel vectors, so
-// the per-channel factors are formed once and the loop is loads, 8 FMAs and
-// stores, with no index division.
-constexpr int kGnApplyPixels = 64;  // upper bound; the host picks fewer for enough blocks
-
+// y = (x - mean_g) * rstd_g * w_c + b_c (then SiLU), one block per (run of
+// pixels, image), about four blocks per SM: each thread owns fixed 8-channel
+// vectors, so the per-channel factors are formed once and the loop is loads
+// (four in flight), 8 FMAs (and SiLU: an exponential and a fast reciprocal
+// division) and stores, with no index division.
 __global__ void __launch_bounds__(256) gn_apply_kernel(const void* __restrict__ x, void* __restrict__ y,
-                                                       int f16, int hw, int C, int G, int pix_per_block,
+                                                       int f16, int hw, int C, int G, int chunk,
                                                        const float2* __restrict__ stats,
                                                        const float* __restrict__ w,
                                                        const float* __restrict__ bias, int silu_after) {
   griddep_launch();
   griddep_wait();
   const int b = blockIdx.y;
-  const int p0 = blockIdx.x * pix_per_block, p1 = min(hw, p0 + pix_per_block);
+  const int p0 = blockIdx.x * chunk, p1 = min(hw, p0 + chunk);
   const int c8 = C / 8;
   const int tpr = min(c8, 256);
   const int rows = 256 / tpr;
@@ -192,6 +174,7 @@ __global__ void __launch_bounds__(256) gn_apply_kernel(const void* __restrict__ 
       sc[k] = st.y * wc;
       sh[k] = (bias ? __ldg(bias + c) : 0.0f) - st.x * st.y * wc;
     }
+#pragma unroll 4
     for (int p = p0 + pr; p < p1; p += rows) {
       const long long i = base + static_cast<long long>(p) * c8 + cv;
       float v[8];
@@ -199,7 +182,7 @@ __global__ void __launch_bounds__(256) gn_apply_kernel(const void* __restrict__ 
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         float o = fmaf(v[k], sc[k], sh[k]);
-        if (silu_after) o = o / (1.0f + __expf(-o));
+        if (silu_after) o = __fdividef(o, 1.0f + __expf(-o));
         v[k] = o;
       }
       reinterpret_cast<uint4*>(y)[i] = pack8(v, f16);
@@ -306,41 +289,34 @@ int group_norm(const void* x, void* y, int dtype, int B, int HW, int C, int G, c
                cudaStream_t s) {
   if (dtype != ND_F16 && dtype != ND_BF16) return fail(ND_ERR_INVALID, "group_norm: dtype must be f16 or bf16");
   if (B <= 0 || HW <= 0 || C <= 0 || G <= 0 || C % G || C % 8) return fail(ND_ERR_INVALID, "group_norm: bad shape");
+  if (C > kGnMaxC) return fail(ND_ERR_UNSUPPORTED, "group_norm: more than 3072 channels");
+  if (B > kGnCounterBytes / 4) return fail(ND_ERR_UNSUPPORTED, "group_norm: batch above 1024");
   if (!x || !y) return fail(ND_ERR_INVALID, "group_norm: null operand");
-  // Pixel chunks of kGnChunk, or longer when that would make far more blocks
-  // than the SMs can hold at once (large images: fewer partials to combine).
-  const long long min_chunks = (HW + kGnChunk - 1) / kGnChunk;
-  const long long cap_blocks = 8LL * sm_count();
-  const int chunk = kGnChunk * static_cast<int>(std::max<long long>(1, (min_chunks * B + cap_blocks - 1) / cap_blocks));
-  const int nchunks = (HW + chunk - 1) / chunk;
-  // Channel slabs: whole groups and whole vectors (multiples of lcm(C/G, 8)),
-  // as many as it takes for ~4 blocks per SM, at most kGnMaxSlab channels.
-  const int cg = C / G;
-  int base = cg;
-  while (base % 8) base += cg;
-  if (base > kGnMaxSlab) return fail(ND_ERR_UNSUPPORTED, "group_norm: groups too wide");
-  const long long want = 4LL * sm_count();
-  long long slabs = std::max<long long>(1, std::min<long long>(C / base, (want + static_cast<long long>(nchunks) * B - 1) /
-                                                                            (static_cast<long long>(nchunks) * B)));
-  int slab_c = static_cast<int>(((C / base + slabs - 1) / slabs) * base);
-  while (slab_c > kGnMaxSlab) slab_c -= base;
-  slabs = (C + slab_c - 1) / slab_c;
-  if (B > 65535) return fail(ND_ERR_INVALID, "group_norm: batch above 65535");
-  const size_t part_bytes = static_cast<size_t>(B) * nchunks * G * sizeof(float2);
   if (scratch_bytes < group_norm_scratch(B, HW, C, G))
     return fail(ND_ERR_INVALID, "group_norm: scratch too small");
-  float2* part = static_cast<float2*>(scratch);
-  float2* stats = reinterpret_cast<float2*>(static_cast<uint8_t*>(scratch) + ((part_bytes + 255) & ~size_t{255}));
-  const int f16 = dtype == ND_F16;
-  ND_CUDA(launch_pdl(gn_partial_kernel, dim3(nchunks, static_cast<unsigned>(slabs), B), dim3(256), 0, s, x, f16, HW,
-                     C, G, slab_c, chunk, part));
-  ND_CUDA(launch_pdl(gn_finalize_kernel, dim3(B * G), dim3(256), 0, s, part, nchunks, C, G, HW, eps, stats));
-  const long long vectors = static_cast<long long>(B) * HW * (C / 8);
   const int rows = 256 / std::min(C / 8, 256);  // pixel rows a block covers per pass
-  const int ppb = static_cast<int>(std::max<long long>(
-      rows, std::min<long long>(kGnApplyPixels, vectors / (want * 256 * 2))));
-  ND_CUDA(launch_pdl(gn_apply_kernel, dim3((HW + ppb - 1) / ppb, B), dim3(256), 0, s, x, y, f16, HW, C, G, ppb,
-                     stats, w, bias, silu_after));
+  // Statistics: about two blocks per SM over all images, at least kGnChunk
+  // pixels each (so the partials fit the scratch bound).
+  const long long stat_blocks = std::max<long long>(1, 2LL * sm_count() / B);
+  const long long sc = std::max<long long>(kGnChunk, (HW + stat_blocks - 1) / stat_blocks);
+  const int chunk = static_cast<int>((sc + rows - 1) / rows * rows);
+  const int nblk = (HW + chunk - 1) / chunk;
+  // Scratch: the per-image arrival counters at a fixed place (zero before
+  // the first call; the last block of each image resets its counter, so
+  // calls of any shape find them zero), the partials and the statistics.
+  const size_t part_bytes = static_cast<size_t>(B) * nblk * G * sizeof(float2);
+  unsigned* arrived = static_cast<unsigned*>(scratch);
+  float2* part = reinterpret_cast<float2*>(static_cast<uint8_t*>(scratch) + kGnCounterBytes);
+  float2* stats = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(part) + ((part_bytes + 255) & ~size_t{255}));
+  const int f16 = dtype == ND_F16;
+  ND_CUDA(launch_pdl(gn_stats_kernel, dim3(nblk, B), dim3(256), 0, s, x, f16, HW, C, G, chunk, part, arrived, eps,
+                     stats));
+  // Normalization: about four blocks per SM.
+  const long long apply_blocks = std::max<long long>(1, 4LL * sm_count() / B);
+  const long long ac = (HW + apply_blocks - 1) / apply_blocks;
+  const int achunk = static_cast<int>((ac + rows - 1) / rows * rows);
+  ND_CUDA(launch_pdl(gn_apply_kernel, dim3((HW + achunk - 1) / achunk, B), dim3(256), 0, s, x, y, f16, HW, C, G,
+                     achunk, stats, w, bias, silu_after));
   return ND_OK;
 }
 
@@ -348,7 +324,7 @@ size_t group_norm_scratch(int B, int HW, int C, int G) {
   (void)C;
   const size_t nchunks = (static_cast<size_t>(HW) + kGnChunk - 1) / kGnChunk;
   const size_t part = static_cast<size_t>(B) * nchunks * G * sizeof(float2);
-  return ((part + 255) & ~size_t{255}) + static_cast<size_t>(B) * G * sizeof(float2) + 256;
+  return kGnCounterBytes + ((part + 255) & ~size_t{255}) + static_cast<size_t>(B) * G * sizeof(float2) + 256;
 }
 
 int geglu(const void* in, void* out, int dtype, int64_t rows, int64_t F, cudaStream_t s) {
