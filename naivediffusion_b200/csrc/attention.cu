@@ -17,13 +17,13 @@ int64_t attn_piece_bytes(int hd) { return 256 * (8 + 4 * static_cast<int64_t>(hd
 
 // Sets the kernel's shared-memory limit and checks its register split, once
 // per device.
-template <int HD, bool SPLIT>
+template <int HD, bool SPLIT, bool F16>
 int configure_attention() {
   static bool configured[64] = {};
   int dev = 0;
   ND_CUDA(cudaGetDevice(&dev));
   if (!configured[dev & 63]) {
-    auto kernel = attention_sm100_kernel<HD, SPLIT>;
+    auto kernel = attention_sm100_kernel<HD, SPLIT, F16>;
     int rc = check_register_split(reinterpret_cast<const void*>(kernel), kAttnThreads, kAttnRegsNeeded, "attention");
     if (rc) return rc;
     ND_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem<HD>::kLaunchBytes));
@@ -32,12 +32,12 @@ int configure_attention() {
   return ND_OK;
 }
 
-template <int HD, bool SPLIT>
+template <int HD, bool SPLIT, bool F16>
 int launch_attention(dim3 grid, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                      const AttnArgs& g, cudaStream_t stream) {
-  int rc = configure_attention<HD, SPLIT>();
+  int rc = configure_attention<HD, SPLIT, F16>();
   if (rc) return rc;
-  ND_CUDA(launch_pdl(attention_sm100_kernel<HD, SPLIT>, grid, dim3(kAttnThreads), AttnSmem<HD>::kLaunchBytes, stream,
+  ND_CUDA(launch_pdl(attention_sm100_kernel<HD, SPLIT, F16>, grid, dim3(kAttnThreads), AttnSmem<HD>::kLaunchBytes, stream,
                      tq, tk, tv, g));
   ND_CUDA(cudaGetLastError());
   return ND_OK;
@@ -52,9 +52,9 @@ int attn_slots() {
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
   int& c = cached[dev & 63];
   if (!c) {
-    if (configure_attention<HD, true>()) return 0;
+    if (configure_attention<HD, true, false>()) return 0;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attention_sm100_kernel<HD, true>, kAttnThreads,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attention_sm100_kernel<HD, true, false>, kAttnThreads,
                                                       AttnSmem<HD>::kLaunchBytes) != cudaSuccess || per_sm <= 0)
       return 0;
     c = per_sm * sm_count();
@@ -169,14 +169,21 @@ int attention(const nd_attention_args& a, cudaStream_t stream) {
       g.part_o = reinterpret_cast<float*>(ws + kAttnCounterBytes + max_pieces * 256 * 8);
     }
   }
+  const bool f16 = g.out_f16 != 0;
   if (g.split > 1) {
     const dim3 grid(static_cast<unsigned>(ctas));
-    return hd == 128 ? launch_attention<128, true>(grid, tq, tk, tv, g, stream)
-                     : launch_attention<64, true>(grid, tq, tk, tv, g, stream);
+    if (hd == 128)
+      return f16 ? launch_attention<128, true, true>(grid, tq, tk, tv, g, stream)
+                 : launch_attention<128, true, false>(grid, tq, tk, tv, g, stream);
+    return f16 ? launch_attention<64, true, true>(grid, tq, tk, tv, g, stream)
+               : launch_attention<64, true, false>(grid, tq, tk, tv, g, stream);
   }
   const dim3 grid(static_cast<unsigned>(q_pairs), static_cast<unsigned>(a.heads), static_cast<unsigned>(a.batch));
-  return hd == 128 ? launch_attention<128, false>(grid, tq, tk, tv, g, stream)
-                   : launch_attention<64, false>(grid, tq, tk, tv, g, stream);
+  if (hd == 128)
+    return f16 ? launch_attention<128, false, true>(grid, tq, tk, tv, g, stream)
+               : launch_attention<128, false, false>(grid, tq, tk, tv, g, stream);
+  return f16 ? launch_attention<64, false, true>(grid, tq, tk, tv, g, stream)
+             : launch_attention<64, false, false>(grid, tq, tk, tv, g, stream);
 }
 
 }  // namespace nd

@@ -95,7 +95,10 @@ constexpr int kAttnRegsNeeded = 128 * kAttnRegsLow + 256 * kAttnRegsHigh;
 // SPLIT: the 1-D grid of whole units and key-range pieces (AttnArgs::split);
 // otherwise a (query-tile pair, head, batch) grid of whole units, with none
 // of the pieces' code (it costs the d = 128 loop ~3 % in registers).
-template <int HD, bool SPLIT>
+// F16: fp16 operands (P packed to fp16), else bf16. A compile-time choice: a
+// run-time select packs every P pair both ways (two SFU conversions per pair
+// instead of one, on the unit the exponentials saturate).
+template <int HD, bool SPLIT, bool F16>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                            const __grid_constant__ CUtensorMap tmK,
@@ -430,7 +433,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                  sc2, nm2);
           const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
           s4[i & 3] = fadd2(s4[i & 3], p);
-          pk[i] = a.out_f16 ? pack_f16(p.x, p.y) : pack_bf16(p.x, p.y);
+          pk[i] = F16 ? pack_f16(p.x, p.y) : pack_bf16(p.x, p.y);
         }
         tmem_st16(s_tm + c * 16, pk);
         if ((c + 1) % (4 / kParts) == 0) {  // a part of the row's P is in TMEM: hand it over
@@ -462,7 +465,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           float v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]) * inv;
-          if (out_row) attn_store_row(out_row, c * 32, v, a.out_f16);
+          if (out_row) attn_store_row(out_row, c * 32, v, F16);
         }
       }
     } else if constexpr (SPLIT) {
@@ -523,7 +526,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
 #pragma unroll
           for (int k = 0; k < 32; ++k) v[k] *= inv;
-          if (out_row) attn_store_row(out_row, c * 32, v, a.out_f16);
+          if (out_row) attn_store_row(out_row, c * 32, v, F16);
         }
       }
     }

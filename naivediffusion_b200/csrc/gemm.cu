@@ -78,11 +78,11 @@ int launch_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap
 }
 
 // The int8 pair kernel (gemm2_w8_sm100.cuh), launched like launch_gemm2.
-template <int BN, int STAGES, int BSTAGES>
+template <int BN, int STAGES, int BSTAGES, bool F16>
 int launch_gemm2_w8(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& tc, const GemmArgs& g,
                     cudaStream_t stream) {
   using L = Gemm2W8Smem<BN, STAGES, BSTAGES>;
-  auto kernel = gemm2_w8_sm100_kernel<BN, STAGES, BSTAGES>;
+  auto kernel = gemm2_w8_sm100_kernel<BN, STAGES, BSTAGES, F16>;
   static int max_pairs[64] = {};
   int dev = 0;
   ND_CUDA(cudaGetDevice(&dev));
@@ -164,24 +164,23 @@ bool use_pairs(const GemmArgs& g, int bn) {
   return g.group_split % 256 == 0;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool F16>
 int launch_gemm_w8(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& tc,
                    const GemmArgs& g, cudaStream_t stream) {
   using L = GemmW8Smem<BN, STAGES>;
+  auto kernel = gemm_w8_sm100_kernel<BN, STAGES, F16>;
   static bool configured[64] = {};
   int dev = 0;
   ND_CUDA(cudaGetDevice(&dev));
   if (!configured[dev & 63]) {
-    int rc = check_register_split(reinterpret_cast<const void*>(gemm_w8_sm100_kernel<BN, STAGES>), kW8Threads,
-                                  kW8RegsNeeded, "int8 linear");
+    int rc = check_register_split(reinterpret_cast<const void*>(kernel), kW8Threads, kW8RegsNeeded, "int8 linear");
     if (rc) return rc;
-    ND_CUDA(cudaFuncSetAttribute(gemm_w8_sm100_kernel<BN, STAGES>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, L::kLaunchBytes));
+    ND_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kLaunchBytes));
     configured[dev & 63] = true;
   }
   const int tiles = ((g.M + 127) / 128) * ((g.N + BN - 1) / BN);
   const int grid = std::min(tiles, sm_count());
-  ND_CUDA(launch_pdl(gemm_w8_sm100_kernel<BN, STAGES>, dim3(grid), dim3(kW8Threads), L::kLaunchBytes, stream, ta, tw, tc, g));
+  ND_CUDA(launch_pdl(kernel, dim3(grid), dim3(kW8Threads), L::kLaunchBytes, stream, ta, tw, tc, g));
   ND_CUDA(cudaGetLastError());
   return ND_OK;
 }
@@ -424,14 +423,18 @@ int linear(const nd_linear_args& a, cudaStream_t stream) {
       g.idesc = make_idesc_f16(256, bn, a.dtype == ND_BF16);
       rc = make_tmap_2d_typed(&tb, a.weight, ND_I8, groups * n_all, a.in_features, a.in_features, bn / 2, 64, 0);
       if (rc) return rc;
-      return launch_gemm2_w8<256, 4, 4>(ta, tb, tc, g, stream);  // 4 raw + 4 widened slots
+      return g.out_f16 ? launch_gemm2_w8<256, 4, 4, true>(ta, tb, tc, g, stream)  // 4 raw + 4 widened slots
+                       : launch_gemm2_w8<256, 4, 4, false>(ta, tb, tc, g, stream);
     }
     // Raw int8 tiles [bn rows x 64 bytes], unswizzled (the converters swizzle).
     rc = make_tmap_2d_typed(&tb, a.weight, ND_I8, groups * n_all, a.in_features, a.in_features,
                             swiglu ? bn / 2 : bn, 64, 0);
     if (rc) return rc;
-    if (bn == 256) return launch_gemm_w8<256, 4>(ta, tb, tc, g, stream);
-    return launch_gemm_w8<128, 6>(ta, tb, tc, g, stream);
+    if (bn == 256)
+      return g.out_f16 ? launch_gemm_w8<256, 4, true>(ta, tb, tc, g, stream)
+                       : launch_gemm_w8<256, 4, false>(ta, tb, tc, g, stream);
+    return g.out_f16 ? launch_gemm_w8<128, 6, true>(ta, tb, tc, g, stream)
+                     : launch_gemm_w8<128, 6, false>(ta, tb, tc, g, stream);
   }
   if (use_pairs(g, bn)) {
     const int pbn = swiglu || epi == ND_EPI_QK_NORM_ROPE ? bn : pair_bn(a.rows, n_all, bn);

@@ -49,7 +49,9 @@ struct Gemm2W8Smem {
   static constexpr int kConverters = 8;           // warps 4..11 of each CTA
 };
 
-template <int BN, int STAGES, int BSTAGES>
+// F16: fp16 activations (W widened to fp16), else bf16; a compile-time
+// choice, so each widened pair is packed one way only.
+template <int BN, int STAGES, int BSTAGES, bool F16>
 __global__ void __launch_bounds__(kW8Threads, 1)
     gemm2_w8_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                           const __grid_constant__ CUtensorMap tmW,
@@ -280,8 +282,8 @@ __global__ void __launch_bounds__(kW8Threads, 1)
             const float2 hi = fadd2(make_float2(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7542u)),
                                                 __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7543u))), m2);
             const float2 a = fmul2(lo, s2), b = fmul2(hi, s2);
-            p[2 * i] = args.out_f16 ? pack_f16(a.x, a.y) : pack_bf16(a.x, a.y);
-            p[2 * i + 1] = args.out_f16 ? pack_f16(b.x, b.y) : pack_bf16(b.x, b.y);
+            p[2 * i] = F16 ? pack_f16(a.x, a.y) : pack_bf16(a.x, a.y);
+            p[2 * i + 1] = F16 ? pack_f16(b.x, b.y) : pack_bf16(b.x, b.y);
           }
           const uint32_t dst = b_buf(bstage) + r * 128;
           st_shared_v4(dst + (((2 * q) ^ (r & 7)) << 4), p[0], p[1], p[2], p[3]);

@@ -55,7 +55,8 @@ constexpr int kGnChunk = 32;           // fewest pixels per block (bounds the pa
 constexpr int kGnMaxC = 3072;          // channels (shared memory: two sums per channel)
 constexpr int kGnCounterBytes = 4096;  // one arrival counter per image, at the start of the scratch
 
-__global__ void __launch_bounds__(256) gn_stats_kernel(const void* __restrict__ x, int f16, int hw, int C, int G,
+template <int f16>  // fp16 (1) or bf16 (0) x, fixed at compile time so no conversion runs both ways
+__global__ void __launch_bounds__(256) gn_stats_kernel(const void* __restrict__ x, int hw, int C, int G,
                                                        int chunk, float2* __restrict__ part,
                                                        unsigned* __restrict__ arrived, float eps,
                                                        float2* __restrict__ stats) {
@@ -147,8 +148,9 @@ __global__ void __launch_bounds__(256) gn_stats_kernel(const void* __restrict__ 
 // vectors, so the per-channel factors are formed once and the loop is loads
 // (four in flight), 8 FMAs (and SiLU: an exponential and a fast reciprocal
 // division) and stores, with no index division.
+template <int f16>
 __global__ void __launch_bounds__(256) gn_apply_kernel(const void* __restrict__ x, void* __restrict__ y,
-                                                       int f16, int hw, int C, int G, int chunk,
+                                                       int hw, int C, int G, int chunk,
                                                        const float2* __restrict__ stats,
                                                        const float* __restrict__ w,
                                                        const float* __restrict__ bias, int silu_after) {
@@ -309,14 +311,14 @@ int group_norm(const void* x, void* y, int dtype, int B, int HW, int C, int G, c
   float2* part = reinterpret_cast<float2*>(static_cast<uint8_t*>(scratch) + kGnCounterBytes);
   float2* stats = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(part) + ((part_bytes + 255) & ~size_t{255}));
   const int f16 = dtype == ND_F16;
-  ND_CUDA(launch_pdl(gn_stats_kernel, dim3(nblk, B), dim3(256), 0, s, x, f16, HW, C, G, chunk, part, arrived, eps,
-                     stats));
+  ND_CUDA(launch_pdl(f16 ? gn_stats_kernel<1> : gn_stats_kernel<0>, dim3(nblk, B), dim3(256), 0, s, x, HW, C, G,
+                     chunk, part, arrived, eps, stats));
   // Normalization: about four blocks per SM.
   const long long apply_blocks = std::max<long long>(1, 4LL * sm_count() / B);
   const long long ac = (HW + apply_blocks - 1) / apply_blocks;
   const int achunk = static_cast<int>((ac + rows - 1) / rows * rows);
-  ND_CUDA(launch_pdl(gn_apply_kernel, dim3((HW + achunk - 1) / achunk, B), dim3(256), 0, s, x, y, f16, HW, C, G,
-                     achunk, stats, w, bias, silu_after));
+  ND_CUDA(launch_pdl(f16 ? gn_apply_kernel<1> : gn_apply_kernel<0>, dim3((HW + achunk - 1) / achunk, B), dim3(256), 0,
+                     s, x, y, HW, C, G, achunk, stats, w, bias, silu_after));
   return ND_OK;
 }
 
