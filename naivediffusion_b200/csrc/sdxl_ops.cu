@@ -129,17 +129,31 @@ __global__ void __launch_bounds__(256) gn_stats_kernel(const void* __restrict__ 
   __syncthreads();
   if (!is_last) return;
   __threadfence();
+  // Eight threads per group, each over every eighth block's partial, then a
+  // fixed shuffle tree: the same order every run.
   const double n = static_cast<double>(hw) * cg;
-  for (int g = t; g < G; g += 256) {
+  const int sub = t & 7;
+  for (int g0 = 0; g0 < G; g0 += 32) {
+    const int g = g0 + (t >> 3);
     double s1 = 0.0, s2 = 0.0;
-    for (int i = 0; i < nblk; ++i) {
-      const float2 v = __ldcg(part + (static_cast<long long>(b) * nblk + i) * G + g);
-      s1 += v.x;
-      s2 += v.y;
+    if (g < G) {
+#pragma unroll 4
+      for (int i = sub; i < nblk; i += 8) {
+        const float2 v = __ldcg(part + (static_cast<long long>(b) * nblk + i) * G + g);
+        s1 += v.x;
+        s2 += v.y;
+      }
     }
-    const double mean = s1 / n;
-    const double var = fmax(s2 / n - mean * mean, 0.0);
-    stats[b * G + g] = make_float2(static_cast<float>(mean), static_cast<float>(1.0 / sqrt(var + eps)));
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    if (g < G && sub == 0) {
+      const double mean = s1 / n;
+      const double var = fmax(s2 / n - mean * mean, 0.0);
+      stats[b * G + g] = make_float2(static_cast<float>(mean), static_cast<float>(1.0 / sqrt(var + eps)));
+    }
   }
 }
 
