@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(256) modulate_kernel(const float* __restrict__
 // the arithmetic runs as paired f32x2 operations: inside the power-capped DiT
 // step the kernel is bound by instruction issue, not bytes. The statistics
 // are those of modulate_kernel (the mean, then the centred second moment over
-// the registers); the output is (x - mean) * (rstd * (1 + scale)) + shift.
+// the registers); the output is (x * rstd - mean * rstd) * (1 + scale) + shift.
 // The two block-wide reductions of an iteration use a parity-indexed slot so
 // the next iteration's writes never race this one's reads.
 template <int V, int F16OUT>
@@ -203,15 +203,18 @@ __global__ void __launch_bounds__(256, V <= 6 ? 2 : 1) modulate16_kernel(const f
       const float rstd = rsqrtf(var + eps);
       const int g = row >= split ? 1 : 0;
       if (g != cur_g) load_vecs(g);
+      // n = x * rstd - mean * rstd, y = n * (1 + scale) + shift: two paired
+      // FMAs per two values
       const float2 rs2 = make_float2(rstd, rstd);
+      const float2 nb2 = make_float2(-mean * rstd, -mean * rstd);
       uint2* yr = reinterpret_cast<uint2*>(y + static_cast<long long>(row) * ldy);
 #pragma unroll
       for (int i = 0; i < V; ++i) {
         const int c = t + 128 * i;
         if (c < w4) {
-          const float2 o0 = ffma2(fadd2(make_float2(v[i].x, v[i].y), nm2), fmul2(make_float2(k1[i].x, k1[i].y), rs2),
+          const float2 o0 = ffma2(ffma2(make_float2(v[i].x, v[i].y), rs2, nb2), make_float2(k1[i].x, k1[i].y),
                                   make_float2(sb[i].x, sb[i].y));
-          const float2 o1 = ffma2(fadd2(make_float2(v[i].z, v[i].w), nm2), fmul2(make_float2(k1[i].z, k1[i].w), rs2),
+          const float2 o1 = ffma2(ffma2(make_float2(v[i].z, v[i].w), rs2, nb2), make_float2(k1[i].z, k1[i].w),
                                   make_float2(sb[i].z, sb[i].w));
           yr[c] = F16OUT ? make_uint2(pack_f16(o0.x, o0.y), pack_f16(o1.x, o1.y))
                          : make_uint2(pack_bf16(o0.x, o0.y), pack_bf16(o1.x, o1.y));
