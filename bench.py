@@ -1,6 +1,6 @@
 #!/usr/bin/env python
 """Headline benchmark: one Qwen-Image-style dual-stream DiT denoiser step at
-1024x1344 in bf16 (60 blocks x 3072, 24 heads,
+1024x1344 in bf16 (benchmark configuration 3: 60 blocks x 3072, 24 heads,
 MLP 12288, 5376 image + 256 text tokens), per B200, images sharded one per GPU.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -21,11 +21,11 @@ Rank 0 prints ONE JSON line.
           layer arithmetic) on a bounded sample: one block at full size,
           extrapolated to a step
 
---config picks another BASELINE configuration for the same line (default
+--config picks another benchmark configuration for the same line (default
 cfg3, the headline): cfg1 one Anima block in fp32, cfg2 the 28-block Anima
 step (two CFG branches), cfg4 cfg3 with int8 per-channel weights, cfg5 the
 SDXL UNet (fp16, two CFG branches), vae the SDXL VAE decoder (a 128 x 128
-latent to a 1024 x 1024 image; not a BASELINE configuration: the step after
+latent to a 1024 x 1024 image; not a benchmark configuration: the step after
 the denoiser).
 
 --impl reference times that CPU restatement alone (the reference is C# over
@@ -113,7 +113,7 @@ class Clocks:
 
 
 def _configs():
-    """BASELINE configurations: (model config, workload text, dtype, metric)."""
+    """benchmark configurations: (model config, workload text, dtype, metric)."""
     from naivediffusion_b200 import _lib
     from naivediffusion_b200.denoiser import (AnimaConfig, MMDiTConfig, QwenImageConfig, UNetConfig,
                                               VaeDecoderConfig, WanVaeConfig)
@@ -714,7 +714,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["cfg3", "cfg1", "cfg2", "cfg4", "cfg5", "vae", "vae_tiled", "qwen21", "wan21",
                                          "wan22", *TEXT_CONFIGS], default="cfg3",
-                    help="BASELINE configuration (default cfg3, the headline)")
+                    help="benchmark configuration (default cfg3, the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle sample")
     ap.add_argument("--cfg-pairs", action="store_true",
                     help="two-branch configurations (cfg2, cfg5): two ranks per image, one CFG branch each")
@@ -722,7 +722,7 @@ def main():
     if args.impl == "reference":
         if args.config in TEXT_CONFIGS:
             print(json.dumps({"impl": "reference", "unavailable": f"{args.config}: the text towers are not a "
-                              "BASELINE configuration; no bounded CPU sample is timed"}))
+                              "benchmark configuration; no bounded CPU sample is timed"}))
             return 0
         if args.config == "vae_tiled":
             print(json.dumps({"impl": "reference", "unavailable": "vae_tiled has no bounded CPU sample of the decode"}))

@@ -151,7 +151,7 @@ struct nd_denoiser {
     return q8() && rows * cols >= 65536 && cols % qgroup(cols) == 0 && cols % 16 == 0;
   }
   // Allocate a matrix kind of `rows` x `cols` (sub-matrices of `per_rows`
-  // rows each stacked; the int8 rule is judged per sub-matrix).
+  // rows each stacked; the int8 rule applies per sub-matrix).
   nd::Mat alloc_mat(int64_t rows, int64_t cols, int64_t per_rows);
 
   virtual int build() = 0;          // allocate weights + scratch, register slots

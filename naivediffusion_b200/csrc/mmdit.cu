@@ -1,4 +1,4 @@
-// The Qwen-Image-style dual-stream DiT (MMDiT) denoiser step: the BASELINE
+// The Qwen-Image-style dual-stream DiT (MMDiT) denoiser step: the benchmark
 // configuration the headline number is quoted on (60 blocks x 3072, 24 heads,
 // GELU-tanh MLP 12288, 16-channel latent patchified 2x2, 3584-wide text).
 //

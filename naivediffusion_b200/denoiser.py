@@ -77,7 +77,7 @@ def _bind() -> C.CDLL:
 
 @dataclass
 class MMDiTConfig:
-    """A Qwen-Image-style dual-stream DiT. Defaults
+    """A Qwen-Image-style dual-stream DiT. Defaults: benchmark configuration 3
     (60 blocks x 3072, 24 x 128 heads, MLP 12288, 16 x 128 x 168 latent in 2x2
     patches = 5376 image tokens, 256 text rows of 3584, bf16)."""
     width: int = 3072
@@ -322,7 +322,7 @@ class LlmAdapterConfig:
 
 @dataclass
 class AnimaConfig:
-    """The Anima (Cosmos-Predict2 2B) DiT. Defaults
+    """The Anima (Cosmos-Predict2 2B) DiT. Defaults: benchmark configuration 2
     (28 blocks x 2048, 16 x 128 heads, exact-GELU MLP 8192, low-rank adaLN
     256, 16 x 128 x 128 latent in 2x2 patches = 4096 tokens, cross-attention
     to 256 x 1024 text rows, batch 2 = the CFG branches, bf16)."""
@@ -396,7 +396,7 @@ class AnimaConfig:
 
 @dataclass
 class UNetConfig:
-    """The SDXL UNet. Defaults: BASELINE configuration 5 (levels 320 / 640 /
+    """The SDXL UNet. Defaults: benchmark configuration 5 (levels 320 / 640 /
     1280 with transformer depths 0 / 2 / 10, 64-wide heads, 2 resnets per
     level, cross-attention to 77 x 2048 text rows, add embedding 2816, 4 x 128
     x 128 latent, batch 2 = the CFG branches, fp16)."""
@@ -818,7 +818,7 @@ def synthetic_weights(cfg, seed: int = 0, only: tuple | None = None):
 
 def synthetic_weights_device(cfg, seed: int = 0, device="cuda"):
     """The same distributions as synthetic_weights, drawn on the GPU (a full
-    BASELINE-size model is 20 G parameters): one torch generator per tensor
+    benchmark-size model is 20 G parameters): one torch generator per tensor
     name. Yields (name, CUDA tensor): matrices in the compute dtype, vectors fp32."""
     import torch
     dt = {_lib.ND_BF16: torch.bfloat16, _lib.ND_F16: torch.float16}.get(cfg.compute, torch.float32)

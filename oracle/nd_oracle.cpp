@@ -463,7 +463,7 @@ struct nd_oracle_mmdit_stream {
   const float *down_w, *down_b;            // [D, F], [D]
 };
 
-// The BASELINE configuration-3 block. The reference has no dual-stream
+// The benchmark configuration-3 block. The reference has no dual-stream
 // Qwen-Image model (QwenImageCheckpoint refuses it); this block is composed
 // from the reference's own primitives in the order its single-stream
 // QwenImageDit.Block uses them (Models/QwenImage/QwenImageDit.cs:309-425):

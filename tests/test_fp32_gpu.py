@@ -140,7 +140,7 @@ def test_anima_fp32_step_within_1e4(device):
 
 
 def test_anima_fp32_cfg1_block_within_1e4(device):
-    """BASELINE configuration 1 in full: one Anima block, fp32, D 2048, 16 x 128
+    """benchmark configuration 1 in full: one Anima block, fp32, D 2048, 16 x 128
     heads, 1024 image tokens with 3-D RoPE, cross-attention to 256 x 1024,
     GELU MLP 8192, low-rank adaLN rank 256 (plus the embedder and final layer
     the denoiser step always runs)."""

@@ -1,4 +1,4 @@
-"""Parity at the BASELINE configurations' real widths: one block of each
+"""Parity at the benchmark configurations' real widths: one block of each
 benchmarked model at its full width, token count and batch, and the joint
 attention at the cfg3 shape, through the C ABI against the CPU oracle.
 
@@ -99,7 +99,7 @@ def test_cfg3_block_full_width_key_count(device, cfg3_case):
                          ids=["per-channel-f32", "g32-f16"])
 def test_cfg4_int8_block_full_width(device, cfg3_case, group, scale_dtype):
     """cfg4: the cfg3 block with int8 weights quantized on the device from the
-    seeded bf16 weights (per output channel with fp32 scales, the BASELINE
+    seeded bf16 weights (per output channel with fp32 scales, the benchmark
     configuration; and the reference's G = 32 fp16 scales), against the
     oracle run on the dequantized weights."""
     w, lat, ctx = cfg3_case
