@@ -345,22 +345,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, for the half of the softmax exponentials the SFU
-// does not take. Range reduction by the round-to-nearest magic constant
-// 1.5 * 2^23 (x = j + f, j integer, |f| <= 1/2; j lands in the low mantissa
-// bits of x + 1.5 * 2^23), 2^f by a degree-3 polynomial whose coefficients
-// were fitted here for relative error 7.5e-5 on [-1/2, 1/2], and 2^j added to
-// the exponent field. Relative error <= 1.5e-4 on [-126, 8]; x < -126 gives 0.
-__device__ __forceinline__ float poly_exp2(float x) {
-  const float xc = fmaxf(x, -126.0f);
-  const float t = xc + 12582912.0f;
-  const float j = t - 12582912.0f;
-  const float f = xc - j;
-  const float p = fmaf(fmaf(fmaf(0.0551716648f, f, 0.2426111400f), f, 0.6932609677f), f, 0.9999280572f);
-  const float r = __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-  return x < -126.0f ? 0.0f : r;
-}
-
 // Programmatic dependent launch: let the next kernel in the stream be
 // scheduled now (its CTAs fill SMs this grid no longer needs and run their
 // prologue), and wait until the previous kernel's grid has completed and its
